@@ -1,0 +1,137 @@
+// Shared device helpers for the exact integer engine (sm_100a).
+//
+// Integer semantics follow the reference program exactly (exact_llm.py:25-46, :97-124 of
+// novain-shibu/exact-llm; SPEC.md:18-28).  All int64 arithmetic wraps modulo 2^64, like
+// numpy's, so every result is bit-identical to the reference's numpy int64 result.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#define EXB_DEV __device__ __forceinline__
+
+namespace exb {
+
+// error bits reported through the engine's device error word
+enum : int {
+  ERR_V_RANGE = 1,        // |V| >= 2^31: the int32 V cache cannot hold the value exactly
+  ERR_WAIT_TIMEOUT = 2,   // a bounded device wait gave up
+  ERR_FREIVALDS = 4,      // a Freivalds self-check failed
+  ERR_BOUNDS = 8,         // an index/size check failed inside a kernel
+  ERR_SHIFT_RANGE = 16,   // a shift count outside [-63, 63] (numpy semantics not representable)
+};
+
+// round-half-up arithmetic shift right (n > 0); n <= 0 is a left shift (exact_llm.py:25-34).
+// Sum and left shift are done in uint64 so overflow wraps exactly like numpy int64.
+EXB_DEV int64_t shr64(int64_t a, int n) {
+  if (n <= 0) {
+    int m = -n;
+    return m >= 64 ? 0 : (int64_t)((uint64_t)a << m);
+  }
+  if (n >= 64) return a < 0 ? -1 : 0;                 // only reachable for pathological inputs
+  uint64_t s = (uint64_t)a + (1ull << (n - 1));
+  return ((int64_t)s) >> n;
+}
+
+// bit length of a non-negative value (exact_llm.py:35-40)
+EXB_DEV int bitlen64(uint64_t m) { return m ? 64 - __clzll((long long)m) : 0; }
+
+EXB_DEV uint64_t uabs64(int64_t a) { return a < 0 ? (uint64_t)0 - (uint64_t)a : (uint64_t)a; }
+
+// floor division by a positive divisor (numpy // on int64)
+EXB_DEV int64_t floordiv64(int64_t a, int64_t b) {
+  int64_t q = a / b;
+  int64_t r = a - q * b;
+  return (r != 0 && a < 0) ? q - 1 : q;
+}
+
+// floor(sqrt(double(n))) with one correction step each way (exact_llm.py:97-99)
+EXB_DEV int64_t isqrt_ref(int64_t n) {
+  int64_t r = (int64_t)floor(sqrt(__ll2double_rn(n)));
+  if (r * r > n) r -= 1;
+  if ((r + 1) * (r + 1) <= n) r += 1;
+  return r;
+}
+
+// qrow clip bound (exact_llm.py:41-46)
+constexpr int64_t QLIM = 32767;
+EXB_DEV int qrow_shift(uint64_t amax) { int s = bitlen64(amax) - 15; return s > 0 ? s : 0; }
+EXB_DEV int16_t qrow_value(int64_t x, int s) {
+  int64_t v = shr64(x, s);
+  v = v > QLIM ? QLIM : (v < -QLIM ? -QLIM : v);
+  return (int16_t)v;
+}
+
+// exp table lookup for the integer softmax (exact_llm.py:109-115); d >= 0
+constexpr int EXP_LEN = 256 * 40 + 2;
+EXB_DEV int64_t exp_lookup(const int32_t* __restrict__ T, int64_t d) {
+  if (d >= (40ll << 16)) return 0;
+  int64_t i = d >> 8;
+  if (i > EXP_LEN - 2) i = EXP_LEN - 2;
+  int64_t fr = d & 255;
+  int64_t a = T[i], b = T[i + 1];
+  return a - shr64((a - b) * fr, 8);
+}
+
+// SiLU / sigmoid tables on [-16, 16) at 1/256 steps (exact_llm.py:118-124; moe_exact_kaggle.py:420-424)
+constexpr int SILU_LEN = 32 * 256 + 2;
+EXB_DEV int64_t table_interp(const int32_t* __restrict__ T, int64_t x, int64_t hi_value) {
+  const int64_t lo = -(16ll << 16), hi = (16ll << 16);
+  if (x >= hi) return hi_value;
+  if (x < lo) return 0;
+  int64_t t = x + hi;                       // clip is a no-op inside the range
+  int64_t i = t >> 8, fr = t & 255;
+  int64_t a = T[i], b = T[i + 1];
+  return a + shr64((b - a) * fr, 8);
+}
+EXB_DEV int64_t isilu_dev(const int32_t* T, int64_t x) { return table_interp(T, x, x); }
+EXB_DEV int64_t isig_dev(const int32_t* T, int64_t x) { return table_interp(T, x, 1ll << 16); }
+
+// ---------------------------------------------------------------- block reductions
+template <int NT>
+EXB_DEV uint64_t block_max_u64(uint64_t v, uint64_t* red) {
+  for (int o = 16; o > 0; o >>= 1) { uint64_t w = __shfl_xor_sync(0xffffffffu, v, o); v = w > v ? w : v; }
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  if (wid == 0) {
+    v = lane < NT / 32 ? red[lane] : 0;
+    for (int o = 16; o > 0; o >>= 1) { uint64_t w = __shfl_xor_sync(0xffffffffu, v, o); v = w > v ? w : v; }
+    if (lane == 0) red[32] = v;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+template <int NT>
+EXB_DEV int64_t block_sum_i64(int64_t v, uint64_t* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[wid] = (uint64_t)v;
+  __syncthreads();
+  if (wid == 0) {
+    v = lane < NT / 32 ? (int64_t)red[lane] : 0;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[32] = (uint64_t)v;
+  }
+  __syncthreads();
+  return (int64_t)red[32];
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels launched with the PDL attribute may start while the previous kernel drains; they
+// must call pdl_wait() before touching data the previous kernel produced.
+EXB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+EXB_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+EXB_DEV void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  // fire-and-forget L2 prefetch of a 16-byte aligned range (no completion to wait for)
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+EXB_DEV void set_err(int* err, int bit) { if (err) atomicOr(err, bit); }
+
+// Freivalds primes p1 = 2^31 - 1, p2 = 2147483629 (experiments/gpu_engine_trace_verify_kaggle.py:782)
+EXB_DEV unsigned long long fr_prime(int i) { return i ? 2147483629ull : 2147483647ull; }
+
+}  // namespace exb

@@ -1,0 +1,888 @@
+// The exact integer model engine behind the C ABI (include/exactb200.h).
+//
+// Replaces the reference's torch engine (exact_torch.py TModel, experiments GraphDecoder and
+// TLinG) with a native runtime: weights in one HBM arena in fused layouts (q|k|v rows
+// concatenated, gate/up rows interleaved), a static KV cache (K int16 + int8 shift, V int32),
+// CUDA-graph replay of each decode/prefill step (one graph per step shape, position and token
+// read from device memory, as in GraphDecoder), on-device greedy feedback, trace capture written
+// directly by the GEMV epilogues, and the Freivalds self-check accumulated inside the GEMVs.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "exactb200.h"
+#include "common.cuh"
+#include "exb_internal.h"
+
+using namespace exb;
+
+static thread_local std::string g_err;
+
+#define FAIL(code, msg)     \
+  do {                      \
+    g_err = (msg);          \
+    return (code);          \
+  } while (0)
+#define CK(call)                                                                    \
+  do {                                                                              \
+    cudaError_t e_ = (call);                                                        \
+    if (e_ != cudaSuccess) {                                                        \
+      g_err = std::string(#call) + " -> " + cudaGetErrorString(e_);                 \
+      return EXB_ECUDA;                                                             \
+    }                                                                               \
+  } while (0)
+
+static constexpr int RMAX = 4;          // activation rows per GEMV pass (CUDA-core decode path)
+static constexpr int EXP_LEN_H = 256 * 40 + 2, SILU_LEN_H = 32 * 256 + 2;
+
+static int bitlen_host(uint64_t v) { int b = 0; while (v) { ++b; v >>= 1; } return b; }
+
+struct LinInfo {                        // one logical linear (reference naming) inside a fused matrix
+  std::string name;
+  int N = 0, K = 0;
+  int row0 = 0, row_step = 1;           // its rows in the fused matrix
+  LinW* fused = nullptr;                // owning fused matrix
+  int trace_off = 0;
+  int mbits = 0;
+  int32_t* fr_r = nullptr;              // (2, N)
+  int32_t* fr_d = nullptr;              // (2, K)
+  unsigned long long* fr_acc = nullptr; // (RMAX, 4)
+};
+
+struct LayerDev {
+  int64_t* g1 = nullptr;
+  int64_t* g2 = nullptr;
+  LinW qkv, o, gu, down;
+  int li[7];                            // q, k, v, o, gate, up, down -> index into lins
+};
+
+struct exb_model {
+  exb_config c{};
+  bool group = true;
+  bool finalized = false;
+  bool pdl = true;
+  bool trace_on = false, fr_on = false;
+  int n_lin = 0;
+  int Nqkv = 0, KMAX = 0, NMAX = 0;
+  char* warena = nullptr; size_t wbytes = 0, woff = 0;
+  char* rarena = nullptr; size_t rbytes = 0, roff = 0;
+  int8_t* emb = nullptr; int64_t* emb_q16 = nullptr;
+  int64_t* gf = nullptr;
+  LinW head;
+  std::vector<LayerDev> L;
+  std::vector<LinInfo> lins;            // trace order
+  int32_t *exp_t = nullptr, *silu_t = nullptr, *sig_t = nullptr, *cos_t = nullptr, *sin_t = nullptr;
+  cudaStream_t st = nullptr;
+  // runtime buffers
+  int32_t *row_ids = nullptr, *row_seq = nullptr, *row_pos = nullptr;      // exb_forward rows (RMAX)
+  int32_t *gen_ids = nullptr, *gen_seq = nullptr, *gen_pos = nullptr;      // generate rows (max_batch)
+  int32_t* gen_step = nullptr; int32_t* gen_tokens = nullptr; int gen_cap = 0;
+  int64_t *x = nullptr, *qkv = nullptr, *ao = nullptr, *hb = nullptr, *logits = nullptr, *rawb = nullptr;
+  int16_t* xq = nullptr; int32_t* xs = nullptr;
+  int16_t* qq = nullptr; int32_t* qs = nullptr;
+  int32_t* next_tok = nullptr;
+  unsigned long long* head_part = nullptr; unsigned int* head_ticket = nullptr;
+  int head_grid = 0;
+  int64_t* trace = nullptr; int64_t trace_row = 0;
+  unsigned long long* fr_acc = nullptr;
+  int* fr_fail = nullptr; int* err = nullptr;
+  int16_t* kc = nullptr; int8_t* ks = nullptr; int32_t* vc = nullptr;
+  size_t kv_layer_elems = 0;           // B * KV * Smax * hd
+  // host state
+  std::vector<int> seq_len;
+  std::vector<int64_t> trace_host; int64_t trace_rows = 0;
+  int64_t fr_checks = 0;
+  std::map<uint64_t, cudaGraphExec_t> graphs;
+  int32_t *h_ids = nullptr, *h_seq = nullptr, *h_pos = nullptr;           // pinned staging
+};
+
+// ------------------------------------------------------------------------------------------ helpers
+template <typename T>
+static T* walloc(exb_model* m, size_t n) {
+  size_t off = (m->woff + 255) & ~size_t(255);
+  m->woff = off + n * sizeof(T);
+  return m->warena ? reinterpret_cast<T*>(m->warena + off) : nullptr;
+}
+template <typename T>
+static T* ralloc(exb_model* m, size_t n) {
+  size_t off = (m->roff + 255) & ~size_t(255);
+  m->roff = off + n * sizeof(T);
+  return m->rarena ? reinterpret_cast<T*>(m->rarena + off) : nullptr;
+}
+
+static void plan_weights(exb_model* m) {
+  const exb_config& c = m->c;
+  const int D = c.D, Hd = c.H * c.hd, I = c.I;
+  m->woff = 0;
+  m->L.assign(c.NL, LayerDev());
+  auto mk = [&](LinW& W, int N, int K, bool bias) {
+    W.N = N; W.K = K;
+    W.w = walloc<int8_t>(m, (size_t)N * K);
+    if (m->group) W.Mg = walloc<int32_t>(m, (size_t)N * (K / 128));
+    else W.Mc = walloc<int64_t>(m, N);
+    W.b = bias ? walloc<int64_t>(m, N) : nullptr;
+  };
+  for (int i = 0; i < c.NL; ++i) {
+    LayerDev& Ld = m->L[i];
+    Ld.g1 = walloc<int64_t>(m, D);
+    Ld.g2 = walloc<int64_t>(m, D);
+    mk(Ld.qkv, m->Nqkv, D, true);
+    mk(Ld.o, D, Hd, false);
+    mk(Ld.gu, 2 * I, D, false);
+    mk(Ld.down, D, I, false);
+  }
+  m->emb = walloc<int8_t>(m, (size_t)c.V * D);
+  m->gf = walloc<int64_t>(m, D);
+  m->head.N = c.V; m->head.K = D;
+  m->head.w = c.tie ? m->emb : walloc<int8_t>(m, (size_t)c.V * D);
+  m->head.Mc = walloc<int64_t>(m, c.V);
+  m->exp_t = walloc<int32_t>(m, EXP_LEN_H);
+  m->silu_t = walloc<int32_t>(m, SILU_LEN_H);
+  m->sig_t = walloc<int32_t>(m, SILU_LEN_H);
+  m->cos_t = walloc<int32_t>(m, (size_t)c.rope_len * (c.hd / 2));
+  m->sin_t = walloc<int32_t>(m, (size_t)c.rope_len * (c.hd / 2));
+}
+
+static void plan_lins(exb_model* m) {
+  const exb_config& c = m->c;
+  m->lins.clear();
+  int off = 0;
+  auto add = [&](const std::string& nm, LinW* f, int N, int K, int row0, int step) {
+    LinInfo li; li.name = nm; li.N = N; li.K = K; li.row0 = row0; li.row_step = step; li.fused = f;
+    li.trace_off = off; off += N;
+    m->lins.push_back(li);
+    return (int)m->lins.size() - 1;
+  };
+  const int qn = c.H * c.hd, kn = c.KV * c.hd;
+  for (int i = 0; i < c.NL; ++i) {
+    LayerDev& Ld = m->L[i];
+    std::string p = "L" + std::to_string(i) + ".";
+    Ld.li[0] = add(p + "q", &Ld.qkv, qn, c.D, 0, 1);
+    Ld.li[1] = add(p + "k", &Ld.qkv, kn, c.D, qn, 1);
+    Ld.li[2] = add(p + "v", &Ld.qkv, kn, c.D, qn + kn, 1);
+    Ld.li[3] = add(p + "o", &Ld.o, c.D, qn, 0, 1);
+    Ld.li[4] = add(p + "gate", &Ld.gu, c.I, c.D, 0, 2);
+    Ld.li[5] = add(p + "up", &Ld.gu, c.I, c.D, 1, 2);
+    Ld.li[6] = add(p + "down", &Ld.down, c.D, c.I, 0, 1);
+  }
+  add("head", &m->head, c.V, c.D, 0, 1);
+  m->n_lin = (int)m->lins.size();
+  m->trace_row = off;
+}
+
+static void plan_runtime(exb_model* m) {
+  const exb_config& c = m->c;
+  m->roff = 0;
+  m->row_ids = ralloc<int32_t>(m, 3 * RMAX);              // ids | seq | pos, one block (one H2D copy)
+  m->row_seq = m->row_ids ? m->row_ids + RMAX : nullptr;
+  m->row_pos = m->row_ids ? m->row_ids + 2 * RMAX : nullptr;
+  m->gen_ids = ralloc<int32_t>(m, c.max_batch); m->gen_seq = ralloc<int32_t>(m, c.max_batch);
+  m->gen_pos = ralloc<int32_t>(m, c.max_batch); m->gen_step = ralloc<int32_t>(m, 1);
+  m->x = ralloc<int64_t>(m, (size_t)RMAX * c.D);
+  m->xq = ralloc<int16_t>(m, (size_t)RMAX * m->KMAX);
+  m->xs = ralloc<int32_t>(m, RMAX);
+  m->qkv = ralloc<int64_t>(m, (size_t)RMAX * m->Nqkv);
+  m->qq = ralloc<int16_t>(m, (size_t)RMAX * c.H * c.hd);
+  m->qs = ralloc<int32_t>(m, (size_t)RMAX * c.H);
+  m->ao = ralloc<int64_t>(m, (size_t)RMAX * c.H * c.hd);
+  m->hb = ralloc<int64_t>(m, (size_t)RMAX * c.I);
+  m->logits = ralloc<int64_t>(m, (size_t)RMAX * c.V);
+  m->rawb = ralloc<int64_t>(m, (size_t)RMAX * m->NMAX);
+  m->next_tok = ralloc<int32_t>(m, RMAX);
+  m->head_part = ralloc<unsigned long long>(m, (size_t)m->head_grid * RMAX * 2);
+  m->head_ticket = ralloc<unsigned int>(m, 1);
+  m->trace = ralloc<int64_t>(m, (size_t)RMAX * m->trace_row);
+  m->fr_acc = ralloc<unsigned long long>(m, (size_t)m->n_lin * RMAX * 4);
+  m->fr_fail = ralloc<int>(m, 1);
+  m->err = ralloc<int>(m, 1);
+  m->kv_layer_elems = (size_t)c.max_batch * c.KV * c.max_seq * c.hd;
+  m->kc = ralloc<int16_t>(m, m->kv_layer_elems * c.NL);
+  m->vc = ralloc<int32_t>(m, m->kv_layer_elems * c.NL);
+  m->ks = ralloc<int8_t>(m, (size_t)c.max_batch * c.KV * c.max_seq * c.NL);
+}
+
+// ------------------------------------------------------------------------------------------ step
+// One forward pass of R (<= RMAX) rows through every layer and the head.  Rows read their token,
+// sequence slot and position from device arrays, so the enqueued work is identical for every
+// step and can be captured once into a CUDA graph.
+static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const int32_t* seq, const int32_t* pos,
+                                bool want_logits, cudaStream_t st) {
+  const exb_config& c = m->c;
+  const bool pdl = m->pdl;
+  cudaError_t e;
+#define RUN(x)                     \
+  do {                             \
+    e = (x);                       \
+    if (e != cudaSuccess) return e; \
+  } while (0)
+  if (m->fr_on) RUN(cudaMemsetAsync(m->fr_acc, 0, sizeof(unsigned long long) * m->n_lin * RMAX * 4, st));
+  if (m->emb_q16) RUN(launch_embed64(m->emb_q16, ids, R, c.D, m->x, st, false));   // general Q16 rows
+  else RUN(launch_embed(m->emb, c.emb_shift, ids, R, c.D, m->x, st, false));        // int8 rows << shift
+  const int Hd = c.H * c.hd;
+  AttnArgs aa;
+  aa.qkv = m->qkv; aa.ldqkv = m->Nqkv; aa.row_seq = seq; aa.row_pos = pos;
+  aa.cos_t = m->cos_t; aa.sin_t = m->sin_t; aa.qq = m->qq; aa.qs = m->qs; aa.exp_t = m->exp_t;
+  aa.out = m->ao; aa.ldo = Hd; aa.R = R; aa.H = c.H; aa.KV = c.KV; aa.hd = c.hd; aa.Smax = c.max_seq;
+  aa.Tmax = c.rope_len; aa.err = m->err;
+  // INV = round(2^16 / sqrt(hd)) (exact_llm.py:164): correctly rounded sqrt and division, ties to even
+  aa.inv = (int64_t)std::nearbyint(65536.0 / std::sqrt((double)c.hd));
+  auto trace_ptr = [&](int li) -> int64_t* { return m->trace_on ? m->trace + m->lins[li].trace_off : nullptr; };
+  auto set_fr = [&](GemvArgs& g, std::initializer_list<int> lis, int nseg_start_override = -1) {
+    (void)nseg_start_override;
+    if (!m->fr_on) return;
+    int s = 0;
+    for (int li : lis) {
+      const LinInfo& L = m->lins[li];
+      g.fr_seg_start[s] = L.row_step == 1 ? L.row0 : 0;
+      g.fr_r[s] = L.fr_r;
+      g.fr_d[s] = L.fr_d;
+      g.fr_acc[s] = L.fr_acc;
+      ++s;
+    }
+    g.fr_nseg = s;
+  };
+  for (int i = 0; i < c.NL; ++i) {
+    LayerDev& Ld = m->L[i];
+    const size_t kvoff = m->kv_layer_elems * i;
+    aa.kc = m->kc + kvoff; aa.vc = m->vc + kvoff;
+    aa.ks = m->ks + (size_t)c.max_batch * c.KV * c.max_seq * i;
+    // attention block
+    RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    {
+      GemvArgs g; g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = Ld.qkv; g.R = R; g.epi = EPI_STORE;
+      g.out = m->qkv; g.ldo = m->Nqkv; g.raw = trace_ptr(Ld.li[0]); g.ldr = (int)m->trace_row; g.err = m->err;
+      set_fr(g, {Ld.li[0], Ld.li[1], Ld.li[2]});
+      RUN(launch_gemv(g, st, pdl));
+    }
+    RUN(launch_rope_cache(aa, st, pdl));
+    RUN(launch_attn_decode(aa, st, pdl));
+    RUN(launch_quant(m->ao, Hd, R, Hd, m->xq, m->KMAX, m->xs, st, pdl));
+    {
+      GemvArgs g; g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = Ld.o; g.R = R; g.epi = EPI_RESID;
+      g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[3]); g.ldr = (int)m->trace_row; g.err = m->err;
+      set_fr(g, {Ld.li[3]});
+      RUN(launch_gemv(g, st, pdl));
+    }
+    // MLP block
+    RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    {
+      GemvArgs g; g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = Ld.gu; g.R = R; g.epi = EPI_SWIGLU;
+      g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.err = m->err;
+      g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]); g.ldr = (int)m->trace_row;
+      set_fr(g, {Ld.li[4], Ld.li[5]});
+      RUN(launch_gemv(g, st, pdl));
+    }
+    RUN(launch_quant(m->hb, c.I, R, c.I, m->xq, m->KMAX, m->xs, st, pdl));
+    {
+      GemvArgs g; g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = Ld.down; g.R = R; g.epi = EPI_RESID;
+      g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[6]); g.ldr = (int)m->trace_row; g.err = m->err;
+      set_fr(g, {Ld.li[6]});
+      RUN(launch_gemv(g, st, pdl));
+    }
+  }
+  RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+  {
+    GemvArgs g; g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = m->head; g.R = R; g.epi = EPI_HEAD;
+    g.out = want_logits ? m->logits : nullptr; g.ldo = c.V; g.err = m->err;
+    g.raw = trace_ptr(m->n_lin - 1); g.ldr = (int)m->trace_row;
+    g.head_part = m->head_part; g.head_ticket = m->head_ticket; g.next_tok = m->next_tok; g.grid = m->head_grid;
+    set_fr(g, {m->n_lin - 1});
+    RUN(launch_gemv(g, st, pdl));
+  }
+  if (m->fr_on) RUN(launch_fr_check(m->fr_acc, m->n_lin * RMAX, m->fr_fail, m->err, st, false));
+  // note: fr_acc rows beyond R stay zero and compare equal
+#undef RUN
+  return cudaSuccess;
+}
+
+__global__ void k_advance(int B, int32_t* ids, int32_t* pos, const int32_t* next, int32_t* step, int32_t* tokens,
+                          int cap) {
+  const int r = threadIdx.x;
+  const int s = *step;
+  __syncthreads();
+  if (r < B) {
+    ids[r] = next[r];
+    pos[r] += 1;
+    if (s < cap) tokens[(size_t)s * B + r] = next[r];
+  }
+  __syncthreads();
+  if (r == 0) *step = s + 1;
+}
+
+// --- graph cache: key = (R, row-array base, logits, advance, trace, freivalds)
+static int run_step(exb_model* m, int R, const int32_t* ids, const int32_t* seq, const int32_t* pos, bool want_logits,
+                    int advanceB) {
+  const uint64_t key = ((uint64_t)R) | ((uint64_t)(want_logits ? 1 : 0) << 8) | ((uint64_t)(advanceB) << 9) |
+                       ((uint64_t)(m->trace_on ? 1 : 0) << 20) | ((uint64_t)(m->fr_on ? 1 : 0) << 21) |
+                       ((uint64_t)((const char*)ids - (const char*)m->rarena) << 24);
+  auto it = m->graphs.find(key);
+  if (it == m->graphs.end()) {
+    cudaGraph_t graph;
+    CK(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = enqueue_step(m, R, ids, seq, pos, want_logits, m->st);
+    if (e == cudaSuccess && advanceB > 0) {
+      k_advance<<<1, 32, 0, m->st>>>(advanceB, const_cast<int32_t*>(ids), const_cast<int32_t*>(pos), m->next_tok,
+                                     m->gen_step, m->gen_tokens, m->gen_cap);
+      e = cudaGetLastError();
+    }
+    cudaError_t e2 = cudaStreamEndCapture(m->st, &graph);
+    if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("step capture: ") + cudaGetErrorString(e));
+    if (e2 != cudaSuccess) FAIL(EXB_ECUDA, std::string("end capture: ") + cudaGetErrorString(e2));
+    cudaGraphExec_t ge;
+    e = cudaGraphInstantiate(&ge, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    it = m->graphs.emplace(key, ge).first;
+  }
+  CK(cudaGraphLaunch(it->second, m->st));
+  return EXB_OK;
+}
+
+static int check_device_errors(exb_model* m) {
+  int bits = 0;
+  CK(cudaMemcpyAsync(&bits, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->st));
+  CK(cudaStreamSynchronize(m->st));
+  if (bits & ~ERR_FREIVALDS) {
+    char buf[128];
+    snprintf(buf, sizeof buf, "device error bits 0x%x (1: |V|>=2^31, 2: wait timeout, 8: bounds)", bits);
+    FAIL(EXB_EDEVICE, buf);
+  }
+  return EXB_OK;
+}
+
+// ------------------------------------------------------------------------------------------ C ABI
+extern "C" {
+
+const char* exb_last_error(void) { return g_err.c_str(); }
+int exb_version(void) { return 1; }
+
+int exb_gen_tensor(int kind, uint64_t seed, uint64_t stream_id, int64_t n, int64_t K, void* out, void* stream) {
+  CK(gen_tensor(kind, seed, stream_id, n, K, out, (cudaStream_t)stream));
+  return EXB_OK;
+}
+
+int exb_gemv(const int16_t* x16, const int8_t* wT, const int64_t* Mg, int K, int N, int64_t* out, void* stream) {
+  if (!x16 || !wT || !Mg || !out || K <= 0 || N <= 0 || K % 128) FAIL(EXB_EINVAL, "exb_gemv: bad arguments (K % 128 == 0 required)");
+  if (((uintptr_t)x16 | (uintptr_t)wT) & 15) FAIL(EXB_EINVAL, "exb_gemv: x16 and wT must be 16-byte aligned");
+  CK(launch_gemv_op(x16, wT, Mg, K, N, out, (cudaStream_t)stream));
+  return EXB_OK;
+}
+
+size_t exb_linear_g128_scratch_bytes(int R, int K) {
+  return ((size_t)R * K * sizeof(int16_t) + 255) / 256 * 256 + (size_t)R * sizeof(int32_t);
+}
+
+static int linear_common(const int64_t* x, int R, int K, const LinW& L, int64_t* y, int64_t* raw, void* scratch,
+                         cudaStream_t st, bool channel) {
+  int16_t* xq = (int16_t*)scratch;
+  int32_t* xs = (int32_t*)((char*)scratch + ((size_t)R * K * sizeof(int16_t) + 255) / 256 * 256);
+  CK(launch_quant(x, K, R, K, xq, K, xs, st, false));
+  for (int r0 = 0; r0 < R; r0 += RMAX) {
+    const int rr = R - r0 < RMAX ? R - r0 : RMAX;
+    GemvArgs g;
+    g.xq = xq + (size_t)r0 * K; g.xs = xs + r0; g.ldx = K; g.L = L; g.R = rr;
+    g.epi = channel ? EPI_RAW : EPI_STORE;
+    g.out = channel ? nullptr : y + (size_t)r0 * L.N; g.ldo = L.N;
+    g.raw = raw ? raw + (size_t)r0 * L.N : nullptr; g.ldr = L.N;
+    CK(launch_gemv(g, st, false));
+  }
+  if (channel) CK(launch_requant_channel(raw, L.N, R, L, y, L.N, xs, EPI_STORE, st, false));
+  return EXB_OK;
+}
+
+int exb_linear_g128(const int64_t* x, int R, int K, const int8_t* w_NK, const int32_t* M_NG, const int64_t* bias,
+                    int N, int64_t* y, int64_t* tot_out, void* scratch, void* stream) {
+  if (!x || !w_NK || !M_NG || !y || !scratch || R <= 0 || K <= 0 || N <= 0 || K % 128)
+    FAIL(EXB_EINVAL, "exb_linear_g128: bad arguments (K % 128 == 0 required)");
+  if (((uintptr_t)w_NK | (uintptr_t)scratch) & 15) FAIL(EXB_EINVAL, "exb_linear_g128: w and scratch must be 16-byte aligned");
+  LinW L; L.w = w_NK; L.Mg = M_NG; L.b = bias; L.N = N; L.K = K;
+  return linear_common(x, R, K, L, y, tot_out, scratch, (cudaStream_t)stream, false);
+}
+
+int exb_linear_channel(const int64_t* x, int R, int K, const int8_t* w_NK, const int64_t* M, const int64_t* bias,
+                       int N, int64_t* y, int64_t* acc_out, void* scratch, void* stream) {
+  if (!x || !w_NK || !M || !y || !acc_out || !scratch || R <= 0 || K <= 0 || N <= 0 || K % 16)
+    FAIL(EXB_EINVAL, "exb_linear_channel: bad arguments (K % 16 == 0 and acc_out required)");
+  if (((uintptr_t)w_NK | (uintptr_t)scratch) & 15) FAIL(EXB_EINVAL, "exb_linear_channel: w and scratch must be 16-byte aligned");
+  std::vector<int64_t> hM(N);
+  LinW L; L.w = w_NK; L.Mc = M; L.b = bias; L.N = N; L.K = K;
+  // Mbits = bitlen(max M) over the layer (exact_llm.py:87)
+  CK(cudaMemcpy(hM.data(), M, sizeof(int64_t) * N, cudaMemcpyDeviceToHost));
+  int64_t mx = 0;
+  for (int64_t v : hM) mx = v > mx ? v : mx;
+  L.mbits = bitlen_host((uint64_t)mx);
+  return linear_common(x, R, K, L, y, acc_out, scratch, (cudaStream_t)stream, true);
+}
+
+int exb_model_create(const exb_config* cfg, exb_model** out) {
+  if (!cfg || !out) FAIL(EXB_EINVAL, "null argument");
+  const exb_config& c = *cfg;
+  if (c.D <= 0 || c.H <= 0 || c.KV <= 0 || c.hd <= 0 || c.I <= 0 || c.V <= 0 || c.NL <= 0) FAIL(EXB_EINVAL, "bad dims");
+  if (c.H % c.KV || c.H / c.KV > 8) FAIL(EXB_EINVAL, "H must be a multiple of KV with at most 8 query heads per KV head");
+  if (c.hd % 16 || c.hd > 128) FAIL(EXB_EINVAL, "head_dim must be a multiple of 16 and <= 128");
+  if (c.n_experts) FAIL(EXB_EINVAL, "MoE models are not supported by this build");
+  if (c.max_batch <= 0 || c.max_seq <= 0 || c.rope_len < c.max_seq) FAIL(EXB_EINVAL, "bad capacities");
+  const int gk = c.lin_kind == 0 ? 128 : 16;
+  if (c.D % gk || (c.H * c.hd) % gk || c.I % gk) FAIL(EXB_EINVAL, "D, H*hd and I must be multiples of 128 (group) or 16 (channel)");
+  exb_model* m = new exb_model();
+  m->c = c;
+  m->group = c.lin_kind == 0;
+  m->Nqkv = (c.H + 2 * c.KV) * c.hd;
+  m->KMAX = std::max(std::max(c.D, c.H * c.hd), c.I);
+  m->NMAX = std::max(std::max(m->Nqkv, 2 * c.I), c.V);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  m->head_grid = 4 * sms;
+  plan_weights(m);
+  m->wbytes = m->woff;
+  plan_lins(m);
+  plan_runtime(m);
+  m->rbytes = m->roff + (size_t)m->n_lin * ((2 * (size_t)m->NMAX + 2 * (size_t)m->KMAX) * 4 + 512) + 4096;
+  cudaError_t e = cudaMalloc(&m->warena, m->wbytes);
+  if (e == cudaSuccess) e = cudaMalloc(&m->rarena, m->rbytes);
+  if (e != cudaSuccess) {
+    cudaFree(m->warena);
+    delete m;
+    FAIL(EXB_ENOMEM, std::string("device allocation failed: ") + cudaGetErrorString(e));
+  }
+  plan_weights(m);
+  plan_lins(m);
+  plan_runtime(m);
+  cudaMemset(m->rarena, 0, m->rbytes);
+  cudaMemset(m->warena, 0, m->wbytes);
+  cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking);
+  cudaMallocHost(&m->h_ids, sizeof(int32_t) * RMAX * 3);
+  m->h_seq = m->h_ids + RMAX; m->h_pos = m->h_ids + 2 * RMAX;
+  m->seq_len.assign(c.max_batch, 0);
+  *out = m;
+  return EXB_OK;
+}
+
+void exb_model_destroy(exb_model* m) {
+  if (!m) return;
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  if (m->st) cudaStreamSynchronize(m->st);
+  cudaFree(m->warena);
+  cudaFree(m->rarena);
+  cudaFree(m->gen_tokens);
+  cudaFree(m->emb_q16);
+  if (m->h_ids) cudaFreeHost(m->h_ids);
+  if (m->st) cudaStreamDestroy(m->st);
+  delete m;
+}
+
+static int to_i32_device(exb_model* m, const int64_t* h, size_t n, int32_t* d) {
+  std::vector<int32_t> t(n);
+  for (size_t i = 0; i < n; ++i) {
+    if (h[i] > INT32_MAX || h[i] < INT32_MIN) FAIL(EXB_EINVAL, "table value does not fit int32");
+    t[i] = (int32_t)h[i];
+  }
+  CK(cudaMemcpyAsync(d, t.data(), n * 4, cudaMemcpyHostToDevice, m->st));
+  CK(cudaStreamSynchronize(m->st));
+  return EXB_OK;
+}
+
+int exb_model_set_tables(exb_model* m, const int64_t* exp_t, const int64_t* silu_t, const int64_t* sig_t,
+                         const int64_t* cos_t, const int64_t* sin_t) {
+  if (!m || !exp_t || !silu_t || !cos_t || !sin_t) FAIL(EXB_EINVAL, "null table");
+  int rc;
+  if ((rc = to_i32_device(m, exp_t, EXP_LEN_H, m->exp_t))) return rc;
+  if ((rc = to_i32_device(m, silu_t, SILU_LEN_H, m->silu_t))) return rc;
+  if (sig_t && (rc = to_i32_device(m, sig_t, SILU_LEN_H, m->sig_t))) return rc;
+  const size_t n = (size_t)m->c.rope_len * (m->c.hd / 2);
+  if ((rc = to_i32_device(m, cos_t, n, m->cos_t))) return rc;
+  if ((rc = to_i32_device(m, sin_t, n, m->sin_t))) return rc;
+  return EXB_OK;
+}
+
+// copy a logical (N, K) tensor into fused rows row0 + i*step (row pitch = elem*K bytes)
+static int put_rows(exb_model* m, void* dst_base, size_t row_bytes, int row0, int step, const void* src, int N) {
+  char* dst = (char*)dst_base + (size_t)row0 * row_bytes;
+  CK(cudaMemcpy2DAsync(dst, row_bytes * step, src, row_bytes, row_bytes, N, cudaMemcpyHostToDevice, m->st));
+  return EXB_OK;
+}
+
+static LinInfo* find_lin(exb_model* m, const std::string& nm) {
+  for (auto& l : m->lins)
+    if (l.name == nm) return &l;
+  return nullptr;
+}
+
+int exb_model_set_tensor(exb_model* m, const char* name_c, const void* host, size_t bytes) {
+  if (!m || !name_c || !host) FAIL(EXB_EINVAL, "null argument");
+  const exb_config& c = m->c;
+  const std::string name(name_c);
+  auto need = [&](size_t n) -> bool { return bytes == n; };
+  if (name == "emb_q16") {
+    if (!need((size_t)c.V * c.D * 8)) FAIL(EXB_EINVAL, "emb_q16: wrong size");
+    if (!m->emb_q16) CK(cudaMalloc(&m->emb_q16, bytes));
+    CK(cudaMemcpyAsync(m->emb_q16, host, bytes, cudaMemcpyHostToDevice, m->st));
+  } else if (name == "emb") {
+    if (!need((size_t)c.V * c.D)) FAIL(EXB_EINVAL, "emb: wrong size");
+    CK(cudaMemcpyAsync(m->emb, host, bytes, cudaMemcpyHostToDevice, m->st));
+  } else if (name == "gf") {
+    if (!need((size_t)c.D * 8)) FAIL(EXB_EINVAL, "gf: wrong size");
+    CK(cudaMemcpyAsync(m->gf, host, bytes, cudaMemcpyHostToDevice, m->st));
+  } else if (name == "head.w") {
+    if (c.tie) FAIL(EXB_EINVAL, "head.w: tied model");
+    if (!need((size_t)c.V * c.D)) FAIL(EXB_EINVAL, "head.w: wrong size");
+    CK(cudaMemcpyAsync((void*)m->head.w, host, bytes, cudaMemcpyHostToDevice, m->st));
+  } else if (name == "head.M") {
+    if (!need((size_t)c.V * 8)) FAIL(EXB_EINVAL, "head.M: wrong size");
+    CK(cudaMemcpyAsync((void*)m->head.Mc, host, bytes, cudaMemcpyHostToDevice, m->st));
+  } else {
+    // L{i}.xxx
+    if (name.size() < 3 || name[0] != 'L') FAIL(EXB_EINVAL, "unknown tensor " + name);
+    const size_t dot = name.find('.');
+    const int li = atoi(name.substr(1, dot - 1).c_str());
+    if (li < 0 || li >= c.NL || dot == std::string::npos) FAIL(EXB_EINVAL, "bad layer in " + name);
+    LayerDev& Ld = m->L[li];
+    const std::string rest = name.substr(dot + 1);
+    if (rest == "g1" || rest == "g2") {
+      if (!need((size_t)c.D * 8)) FAIL(EXB_EINVAL, name + ": wrong size");
+      CK(cudaMemcpyAsync(rest == "g1" ? Ld.g1 : Ld.g2, host, bytes, cudaMemcpyHostToDevice, m->st));
+    } else {
+      const size_t d2 = rest.find('.');
+      if (d2 == std::string::npos) FAIL(EXB_EINVAL, "unknown tensor " + name);
+      LinInfo* L = find_lin(m, name.substr(0, dot + 1 + d2));
+      if (!L) FAIL(EXB_EINVAL, "unknown linear in " + name);
+      const std::string part = rest.substr(d2 + 1);
+      LinW& F = *L->fused;
+      if (part == "w") {
+        if (!need((size_t)L->N * L->K)) FAIL(EXB_EINVAL, name + ": wrong size");
+        return put_rows(m, (void*)F.w, (size_t)L->K, L->row0, L->row_step, host, L->N);
+      } else if (part == "M") {
+        if (m->group) {
+          if (!need((size_t)L->N * (L->K / 128) * 4)) FAIL(EXB_EINVAL, name + ": wrong size (int32 N x K/128)");
+          return put_rows(m, (void*)F.Mg, (size_t)(L->K / 128) * 4, L->row0, L->row_step, host, L->N);
+        }
+        if (!need((size_t)L->N * 8)) FAIL(EXB_EINVAL, name + ": wrong size (int64 N)");
+        return put_rows(m, (void*)F.Mc, 8, L->row0, L->row_step, host, L->N);
+      } else if (part == "b") {
+        if (!F.b) FAIL(EXB_EINVAL, name + ": this linear has no bias");
+        if (!need((size_t)L->N * 8)) FAIL(EXB_EINVAL, name + ": wrong size");
+        return put_rows(m, (void*)F.b, 8, L->row0, L->row_step, host, L->N);
+      } else {
+        FAIL(EXB_EINVAL, "unknown tensor " + name);
+      }
+    }
+  }
+  return EXB_OK;
+}
+
+// Stream ids of the synthetic generator (same numbering as the test oracle's generator).
+static uint64_t layer_stream(int li, int off) { return (uint64_t)li * 64 + off; }
+
+int exb_model_generate(exb_model* m, uint64_t seed) {
+  if (!m) FAIL(EXB_EINVAL, "null model");
+  const exb_config& c = m->c;
+  size_t maxn = (size_t)c.V * c.D;
+  for (auto& l : m->lins) maxn = std::max(maxn, (size_t)l.N * l.K);
+  void* tmp = nullptr;
+  CK(cudaMallocAsync(&tmp, maxn * 8, m->st));
+  static const std::map<std::string, int> LS = {{"q", 2}, {"k", 5}, {"v", 8}, {"o", 11}, {"gate", 14}, {"up", 17}, {"down", 20}};
+  for (auto& L : m->lins) {
+    if (L.name == "head") continue;
+    const int li = atoi(L.name.c_str() + 1);
+    const std::string nm = L.name.substr(L.name.find('.') + 1);
+    const uint64_t s0 = layer_stream(li, LS.at(nm));
+    LinW& F = *L.fused;
+    CK(gen_tensor(GEN_WEIGHT, seed, s0, (int64_t)L.N * L.K, L.K, tmp, m->st));
+    CK(cudaMemcpy2DAsync((char*)F.w + (size_t)L.row0 * L.K, (size_t)L.K * L.row_step, tmp, L.K, L.K, L.N,
+                         cudaMemcpyDeviceToDevice, m->st));
+    if (m->group) {
+      const int G = L.K / 128;
+      CK(gen_tensor(GEN_SCALE32, seed, s0 + 1, (int64_t)L.N * G, L.K, tmp, m->st));
+      CK(cudaMemcpy2DAsync((char*)F.Mg + (size_t)L.row0 * G * 4, (size_t)G * 4 * L.row_step, tmp, (size_t)G * 4,
+                           (size_t)G * 4, L.N, cudaMemcpyDeviceToDevice, m->st));
+    } else {
+      CK(gen_tensor(GEN_SCALE64, seed, s0 + 1, L.N, L.K, tmp, m->st));
+      CK(cudaMemcpy2DAsync((char*)F.Mc + (size_t)L.row0 * 8, (size_t)8 * L.row_step, tmp, 8, 8, L.N,
+                           cudaMemcpyDeviceToDevice, m->st));
+    }
+    if (F.b) {
+      CK(gen_tensor(GEN_BIAS, seed, s0 + 2, L.N, 0, tmp, m->st));
+      CK(cudaMemcpy2DAsync((char*)F.b + (size_t)L.row0 * 8, (size_t)8 * L.row_step, tmp, 8, 8, L.N,
+                           cudaMemcpyDeviceToDevice, m->st));
+    }
+  }
+  for (int i = 0; i < c.NL; ++i) {
+    CK(gen_tensor(GEN_GAIN, seed, layer_stream(i, 0), c.D, 0, m->L[i].g1, m->st));
+    CK(gen_tensor(GEN_GAIN, seed, layer_stream(i, 1), c.D, 0, m->L[i].g2, m->st));
+  }
+  const uint64_t S_EMB = 1ull << 20;
+  CK(gen_tensor(GEN_WEIGHT, seed, S_EMB, (int64_t)c.V * c.D, c.D, m->emb, m->st));
+  CK(gen_tensor(GEN_GAIN, seed, S_EMB + 1, c.D, 0, m->gf, m->st));
+  if (!c.tie) CK(gen_tensor(GEN_WEIGHT, seed, S_EMB + 2, (int64_t)c.V * c.D, c.D, (void*)m->head.w, m->st));
+  CK(gen_tensor(GEN_SCALE64, seed, S_EMB + 3, c.V, c.D, (void*)m->head.Mc, m->st));
+  CK(cudaFreeAsync(tmp, m->st));
+  CK(cudaStreamSynchronize(m->st));
+  return EXB_OK;
+}
+
+int exb_model_finalize(exb_model* m) {
+  if (!m) FAIL(EXB_EINVAL, "null model");
+  const exb_config& c = m->c;
+  CK(cudaStreamSynchronize(m->st));
+  // per-channel drop rule (exact_llm.py:93): provably inactive when
+  // bitlen(K * 32767 * 127) + bitlen(max M) <= 62 for every row
+  for (auto& L : m->lins) {
+    LinW& F = *L.fused;
+    if (F.Mc) {
+      // logical rows of this linear inside the fused scale vector
+      std::vector<int64_t> h((size_t)F.N);
+      CK(cudaMemcpy(h.data(), F.Mc, 8 * (size_t)F.N, cudaMemcpyDeviceToHost));
+      int64_t mx = 0;
+      for (int i = 0; i < L.N; ++i) mx = std::max(mx, h[(size_t)L.row0 + (size_t)i * L.row_step]);
+      L.mbits = bitlen_host((uint64_t)mx);
+      const int accbits = bitlen_host((uint64_t)L.K * 32767ull * 127ull);
+      if (accbits + L.mbits > 62) F.nodrop = false;
+      F.mbits = std::max(F.mbits, L.mbits);
+    }
+  }
+  CK(cudaStreamSynchronize(m->st));
+  for (auto& L : m->lins)
+    if (L.fused->Mc && !L.fused->nodrop)
+      FAIL(EXB_EINVAL, "per-channel linear " + L.name + " may trigger the overflow drop rule; the fused decode path "
+                       "requires bitlen(K*32767*127) + bitlen(max M) <= 62");
+  m->finalized = true;
+  (void)c;
+  return EXB_OK;
+}
+
+int exb_seq_reset(exb_model* m, int seq) {
+  if (!m || seq < 0 || seq >= m->c.max_batch) FAIL(EXB_EINVAL, "bad sequence slot");
+  m->seq_len[seq] = 0;
+  return EXB_OK;
+}
+int exb_seq_len(exb_model* m, int seq) {
+  if (!m || seq < 0 || seq >= m->c.max_batch) return -1;
+  return m->seq_len[seq];
+}
+
+int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, int64_t* logits, int32_t* next) {
+  if (!m || !m->finalized) FAIL(EXB_EINVAL, "model not finalized");
+  if (n <= 0 || !ids || !seqs) FAIL(EXB_EINVAL, "bad rows");
+  const exb_config& c = m->c;
+  std::vector<int> pos(n);
+  std::vector<int> len = m->seq_len;
+  for (int i = 0; i < n; ++i) {
+    if (seqs[i] < 0 || seqs[i] >= c.max_batch) FAIL(EXB_EINVAL, "bad sequence slot");
+    if (ids[i] < 0 || ids[i] >= c.V) FAIL(EXB_EINVAL, "token id out of range");
+    pos[i] = len[seqs[i]]++;
+    if (pos[i] >= c.max_seq) FAIL(EXB_EINVAL, "sequence longer than max_seq");
+  }
+  if (m->trace_on) { m->trace_host.assign((size_t)n * m->trace_row, 0); m->trace_rows = n; }
+  CK(cudaMemsetAsync(m->err, 0, sizeof(int), m->st));
+  for (int r0 = 0; r0 < n; r0 += RMAX) {
+    const int R = std::min(RMAX, n - r0);
+    for (int r = 0; r < R; ++r) { m->h_ids[r] = ids[r0 + r]; m->h_seq[r] = seqs[r0 + r]; m->h_pos[r] = pos[r0 + r]; }
+    CK(cudaMemcpyAsync(m->row_ids, m->h_ids, sizeof(int32_t) * RMAX * 3, cudaMemcpyHostToDevice, m->st));
+    int rc = run_step(m, R, m->row_ids, m->row_seq, m->row_pos, logits != nullptr, 0);
+    if (rc) return rc;
+    if (logits) CK(cudaMemcpyAsync(logits + (size_t)r0 * c.V, m->logits, sizeof(int64_t) * R * c.V, cudaMemcpyDeviceToHost, m->st));
+    if (next) CK(cudaMemcpyAsync(next + r0, m->next_tok, sizeof(int32_t) * R, cudaMemcpyDeviceToHost, m->st));
+    if (m->trace_on)
+      CK(cudaMemcpyAsync(m->trace_host.data() + (size_t)r0 * m->trace_row, m->trace, sizeof(int64_t) * R * m->trace_row,
+                         cudaMemcpyDeviceToHost, m->st));
+    if (m->fr_on) m->fr_checks += (int64_t)R * m->n_lin;
+    // the pinned staging buffer is reused by the next chunk: wait for its copy
+    CK(cudaStreamSynchronize(m->st));
+  }
+  m->seq_len = len;
+  return check_device_errors(m);
+}
+
+static int ensure_gen(exb_model* m, int B, int steps) {
+  if (m->gen_cap < B * steps) {
+    cudaFree(m->gen_tokens);
+    m->gen_tokens = nullptr;
+    CK(cudaMalloc(&m->gen_tokens, sizeof(int32_t) * (size_t)B * steps));
+    m->gen_cap = B * steps;
+    // graphs bake the token buffer pointer: drop the generate graphs
+    for (auto it = m->graphs.begin(); it != m->graphs.end();) {
+      if ((it->first >> 9) & 0x7ff) { cudaGraphExecDestroy(it->second); it = m->graphs.erase(it); }
+      else ++it;
+    }
+  }
+  return EXB_OK;
+}
+
+static int generate_common(exb_model* m, int B, const int32_t* ids_dev_or_null, const int32_t* ids_host, int steps,
+                           int32_t* tokens_host, int64_t* logits_host, int32_t* tokens_dev) {
+  if (!m || !m->finalized) FAIL(EXB_EINVAL, "model not finalized");
+  const exb_config& c = m->c;
+  if (B <= 0 || B > RMAX || B > c.max_batch) FAIL(EXB_EINVAL, "generate: 1 <= B <= 4 in this build");
+  if (steps <= 0) return EXB_OK;
+  for (int b = 0; b < B; ++b)
+    if (m->seq_len[b] + steps > c.max_seq) FAIL(EXB_EINVAL, "generate: max_seq exceeded");
+  int rc = ensure_gen(m, B, steps);
+  if (rc) return rc;
+  std::vector<int32_t> seq(B), pos(B);
+  for (int b = 0; b < B; ++b) { seq[b] = b; pos[b] = m->seq_len[b]; }
+  CK(cudaMemsetAsync(m->err, 0, sizeof(int), m->st));
+  if (ids_dev_or_null) CK(cudaMemcpyAsync(m->gen_ids, ids_dev_or_null, 4 * B, cudaMemcpyDeviceToDevice, m->st));
+  else CK(cudaMemcpyAsync(m->gen_ids, ids_host, 4 * B, cudaMemcpyHostToDevice, m->st));
+  CK(cudaMemcpyAsync(m->gen_seq, seq.data(), 4 * B, cudaMemcpyHostToDevice, m->st));
+  CK(cudaMemcpyAsync(m->gen_pos, pos.data(), 4 * B, cudaMemcpyHostToDevice, m->st));
+  CK(cudaMemsetAsync(m->gen_step, 0, 4, m->st));
+  if (m->trace_on) { m->trace_host.assign((size_t)B * steps * m->trace_row, 0); m->trace_rows = (int64_t)B * steps; }
+  for (int s = 0; s < steps; ++s) {
+    rc = run_step(m, B, m->gen_ids, m->gen_seq, m->gen_pos, logits_host != nullptr, B);
+    if (rc) return rc;
+    if (logits_host)
+      CK(cudaMemcpyAsync(logits_host + (size_t)s * B * c.V, m->logits, sizeof(int64_t) * B * c.V, cudaMemcpyDeviceToHost, m->st));
+    if (m->trace_on)
+      CK(cudaMemcpyAsync(m->trace_host.data() + (size_t)s * B * m->trace_row, m->trace, sizeof(int64_t) * B * m->trace_row,
+                         cudaMemcpyDeviceToHost, m->st));
+    if (m->fr_on) m->fr_checks += (int64_t)B * m->n_lin;
+  }
+  if (tokens_dev) CK(cudaMemcpyAsync(tokens_dev, m->gen_tokens, sizeof(int32_t) * B * steps, cudaMemcpyDeviceToDevice, m->st));
+  if (tokens_host) CK(cudaMemcpyAsync(tokens_host, m->gen_tokens, sizeof(int32_t) * B * steps, cudaMemcpyDeviceToHost, m->st));
+  for (int b = 0; b < B; ++b) m->seq_len[b] += steps;
+  if (tokens_host || logits_host || m->trace_on) return check_device_errors(m);
+  return EXB_OK;
+}
+
+int exb_generate(exb_model* m, int B, const int32_t* first_ids, int steps, int32_t* tokens, int64_t* logits) {
+  if (!first_ids || !tokens) FAIL(EXB_EINVAL, "null argument");
+  return generate_common(m, B, nullptr, first_ids, steps, tokens, logits, nullptr);
+}
+
+int exb_generate_device(exb_model* m, int B, const int32_t* ids_dev, int steps, int32_t* tokens_dev) {
+  if (!ids_dev || !tokens_dev) FAIL(EXB_EINVAL, "null argument");
+  return generate_common(m, B, ids_dev, nullptr, steps, nullptr, nullptr, tokens_dev);
+}
+
+int exb_trace_enable(exb_model* m, int on) {
+  if (!m) FAIL(EXB_EINVAL, "null model");
+  m->trace_on = on != 0;
+  return EXB_OK;
+}
+int64_t exb_trace_row_len(exb_model* m) { return m ? m->trace_row : -1; }
+int exb_trace_read(exb_model* m, int64_t* host, int64_t n) {
+  if (!m || !host) FAIL(EXB_EINVAL, "null argument");
+  const int64_t have = (int64_t)m->trace_host.size();
+  if (n != have) FAIL(EXB_EINVAL, "trace size mismatch: expected " + std::to_string(have));
+  memcpy(host, m->trace_host.data(), sizeof(int64_t) * n);
+  return EXB_OK;
+}
+
+int exb_freivalds_set_keys(exb_model* m, const int32_t* r_host, int64_t n) {
+  if (!m || !r_host) FAIL(EXB_EINVAL, "null argument");
+  int64_t need = 0;
+  for (auto& L : m->lins) need += 2 * (int64_t)L.N;
+  if (n != need) FAIL(EXB_EINVAL, "freivalds keys: expected " + std::to_string(need) + " r values");
+  // key storage lives in the runtime arena's tail
+  size_t off = (m->roff + 255) & ~size_t(255);
+  int64_t pos = 0;
+  unsigned long long* acc_base = m->fr_acc;
+  int idx = 0;
+  for (auto& L : m->lins) {
+    L.fr_r = (int32_t*)(m->rarena + off); off += ((size_t)2 * L.N * 4 + 255) & ~size_t(255);
+    L.fr_d = (int32_t*)(m->rarena + off); off += ((size_t)2 * L.K * 4 + 255) & ~size_t(255);
+    if (off > m->rbytes) FAIL(EXB_ENOMEM, "freivalds key storage exhausted");
+    CK(cudaMemcpyAsync(L.fr_r, r_host + pos, sizeof(int32_t) * 2 * L.N, cudaMemcpyHostToDevice, m->st));
+    pos += 2 * L.N;
+    const LinW& F = *L.fused;
+    CK(launch_fr_keys(F.w, F.Mg, L.N, L.K, L.row0, L.row_step, L.fr_r, L.fr_d, m->st));
+    L.fr_acc = acc_base + (size_t)idx * RMAX * 4;
+    ++idx;
+  }
+  CK(cudaStreamSynchronize(m->st));
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  m->graphs.clear();
+  return EXB_OK;
+}
+
+int exb_freivalds_read_keys(exb_model* m, int32_t* d_host, int64_t n) {
+  if (!m || !d_host) FAIL(EXB_EINVAL, "null argument");
+  int64_t need = 0;
+  for (auto& L : m->lins) need += 2 * (int64_t)L.K;
+  if (n != need) FAIL(EXB_EINVAL, "freivalds read: expected " + std::to_string(need));
+  int64_t pos = 0;
+  for (auto& L : m->lins) {
+    if (!L.fr_d) FAIL(EXB_EINVAL, "keys not set");
+    CK(cudaMemcpy(d_host + pos, L.fr_d, sizeof(int32_t) * 2 * L.K, cudaMemcpyDeviceToHost));
+    pos += 2 * L.K;
+  }
+  return EXB_OK;
+}
+
+int exb_freivalds_enable(exb_model* m, int on) {
+  if (!m) FAIL(EXB_EINVAL, "null model");
+  if (on && (m->lins.empty() || !m->lins[0].fr_r)) FAIL(EXB_EINVAL, "set keys first");
+  m->fr_on = on != 0;
+  if (on) { CK(cudaMemset(m->fr_fail, 0, sizeof(int))); m->fr_checks = 0; }
+  return EXB_OK;
+}
+
+int exb_freivalds_status(exb_model* m, int64_t* checks, int64_t* failures) {
+  if (!m) FAIL(EXB_EINVAL, "null model");
+  int f = 0;
+  CK(cudaStreamSynchronize(m->st));
+  CK(cudaMemcpy(&f, m->fr_fail, sizeof(int), cudaMemcpyDeviceToHost));
+  if (checks) *checks = m->fr_checks;
+  if (failures) *failures = f;
+  return EXB_OK;
+}
+
+int exb_device_errors(exb_model* m, int* bits) {
+  if (!m || !bits) FAIL(EXB_EINVAL, "null argument");
+  CK(cudaStreamSynchronize(m->st));
+  CK(cudaMemcpy(bits, m->err, sizeof(int), cudaMemcpyDeviceToHost));
+  return EXB_OK;
+}
+
+int exb_bench_linear(exb_model* m, int layer, int which, int R, int reps, float* avg_ms, double* bytes) {
+  if (!m || !m->finalized || layer < 0 || layer >= m->c.NL || which < 0 || which > 4 || R < 1 || R > RMAX || reps < 1)
+    FAIL(EXB_EINVAL, "exb_bench_linear: bad arguments");
+  LayerDev& Ld = m->L[layer];
+  GemvArgs g;
+  g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.R = R; g.err = m->err;
+  const exb_config& c = m->c;
+  switch (which) {
+    case 0: g.L = Ld.qkv; g.epi = EPI_STORE; g.out = m->qkv; g.ldo = m->Nqkv; break;
+    case 1: g.L = Ld.o; g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; break;
+    case 2: g.L = Ld.gu; g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; break;
+    case 3: g.L = Ld.down; g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; break;
+    default:
+      g.L = m->head; g.epi = EPI_HEAD; g.out = nullptr; g.head_part = m->head_part; g.head_ticket = m->head_ticket;
+      g.next_tok = m->next_tok; g.grid = m->head_grid; break;
+  }
+  // keep the activations in range: zero input rows (timing does not depend on values)
+  CK(cudaMemsetAsync(m->xq, 0, sizeof(int16_t) * (size_t)RMAX * m->KMAX, m->st));
+  CK(cudaMemsetAsync(m->xs, 0, sizeof(int32_t) * RMAX, m->st));
+  cudaEvent_t e0, e1;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventCreate(&e1));
+  CK(launch_gemv(g, m->st, false));  // warm-up
+  CK(cudaEventRecord(e0, m->st));
+  for (int i = 0; i < reps; ++i) CK(launch_gemv(g, m->st, false));
+  CK(cudaEventRecord(e1, m->st));
+  CK(cudaEventSynchronize(e1));
+  float ms = 0;
+  CK(cudaEventElapsedTime(&ms, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (avg_ms) *avg_ms = ms / reps;
+  if (bytes) {
+    const LinW& L = g.L;
+    double b = (double)L.N * L.K + (L.Mg ? 4.0 * L.N * (L.K / 128) : 8.0 * L.N) + (L.b ? 8.0 * L.N : 0) +
+               2.0 * R * L.K;
+    const int nout = which == 2 ? L.N / 2 : (which == 4 ? 0 : L.N);
+    b += 8.0 * R * nout * ((which == 1 || which == 3) ? 2 : 1);   // residual: read + write
+    *bytes = b;
+  }
+  return EXB_OK;
+}
+
+void* exb_model_stream(exb_model* m) { return m ? (void*)m->st : nullptr; }
+size_t exb_model_weight_bytes(exb_model* m) { return m ? m->wbytes : 0; }
+
+}  // extern "C"

@@ -1,0 +1,104 @@
+// Internal (C++) interfaces between the engine and its kernels.  Not part of the C ABI.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace exb {
+
+enum GenKind { GEN_WEIGHT = 0, GEN_SCALE32 = 1, GEN_SCALE64 = 2, GEN_BIAS = 3, GEN_GAIN = 4 };
+cudaError_t gen_tensor(int kind, uint64_t seed, uint64_t stream, int64_t n, int64_t K, void* out, cudaStream_t st);
+int64_t isqrt_host(int64_t n);
+
+// One linear layer in HBM.  Weights are (N, K) row-major int8 = one contiguous K-byte row per
+// output column.  Group-128 layers carry int32 scales (N, K/128); per-channel layers carry int64
+// scales (N,).  For a fused SwiGLU pair the rows are interleaved: row 2j = gate j, 2j+1 = up j.
+struct LinW {
+  const int8_t* w = nullptr;
+  const int32_t* Mg = nullptr;     // group-128 scales (N, K/128) or nullptr
+  const int64_t* Mc = nullptr;     // per-channel scales (N) or nullptr
+  const int64_t* b = nullptr;      // bias (N) Q16 or nullptr
+  int N = 0, K = 0;
+  int mbits = 0;                   // per-channel: bitlen(max M)
+  bool nodrop = true;              // per-channel: the drop rule can never trigger (host-proven)
+};
+
+enum Epi {
+  EPI_STORE = 0,     // out[r, n] = requant(tot)
+  EPI_RESID = 1,     // out[r, n] += requant(tot)       (residual add)
+  EPI_SWIGLU = 2,    // rows interleaved gate/up: out[r, j] = shr(isilu(y_gate) * y_up, 16)
+  EPI_RAW = 3,       // raw accumulator only
+  EPI_HEAD = 4,      // out[r, n] = requant(acc) (optional) + greedy argmax per row
+};
+
+struct GemvArgs {
+  const int16_t* xq = nullptr;     // (R, ldx) int16 activations
+  const int32_t* xs = nullptr;     // (R) qrow shifts
+  int ldx = 0;
+  LinW L;
+  int R = 1;
+  int epi = EPI_STORE;
+  int64_t* out = nullptr; int ldo = 0;
+  int64_t* raw = nullptr; int ldr = 0;          // trace / raw output (row stride ldr)
+  int64_t* raw2 = nullptr;                      // SwiGLU: raw of the up rows
+  const int32_t* silu_t = nullptr;
+  // Freivalds self-check, per LOGICAL linear ("segment") of a fused GEMV.  Segment rows of the
+  // accumulator are (lhs_p1, lhs_p2, rhs_p1, rhs_p2), one row per activation row:
+  //   lhs += sum_n r_p[n] * (tot_n mod P_p),   rhs += sum_k d_p[k] * (xq_k mod P_p)
+  // RPU == 1: segment s covers fused columns [seg_start[s], seg_start[s] + seg_n[s]);
+  // SwiGLU (RPU == 2): segment 0 = gate rows, segment 1 = up rows (local index = pair index).
+  int fr_nseg = 0;
+  int fr_seg_start[3] = {0, 0, 0};
+  const int32_t* fr_r[3] = {nullptr, nullptr, nullptr};     // (2, n_seg) values in [0, P)
+  const int32_t* fr_d[3] = {nullptr, nullptr, nullptr};     // (2, K)
+  unsigned long long* fr_acc[3] = {nullptr, nullptr, nullptr};
+  // greedy head
+  unsigned long long* head_part = nullptr;      // (grid, R, 2) partial (value, index)
+  unsigned int* head_ticket = nullptr;          // last-CTA counter
+  int32_t* next_tok = nullptr;                  // (R)
+  int* err = nullptr;
+  int grid = 0;
+};
+
+cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_gemv_op(const int16_t* x16, const int8_t* wT, const int64_t* Mg, int K, int N, int64_t* out,
+                           cudaStream_t st);
+
+// per-row kernels
+cudaError_t launch_embed(const int8_t* emb, int emb_shift, const int32_t* ids, int R, int D, int64_t* x,
+                         cudaStream_t st, bool pdl);
+cudaError_t launch_embed64(const int64_t* emb_q16, const int32_t* ids, int R, int D, int64_t* x, cudaStream_t st,
+                           bool pdl);
+cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
+                          int32_t* xs, cudaStream_t st, bool pdl);
+cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, int ldq, int32_t* xs,
+                         cudaStream_t st, bool pdl);
+cudaError_t launch_requant_channel(const int64_t* acc, int ld, int R, const LinW& L, int64_t* out, int ldo,
+                                   const int32_t* xs, int epi, cudaStream_t st, bool pdl);
+
+// attention
+struct AttnArgs {
+  const int64_t* qkv = nullptr; int ldqkv = 0;  // (R, (H + 2KV) hd) projected q|k|v (before RoPE)
+  const int32_t* row_seq = nullptr;             // (R) sequence slot of each row
+  const int32_t* row_pos = nullptr;             // (R) absolute position of each row
+  const int32_t* cos_t = nullptr;               // (Tmax, hd/2) Q16
+  const int32_t* sin_t = nullptr;
+  int16_t* kc = nullptr;                        // K cache (B, KV, Smax, hd) int16 (this layer)
+  int8_t* ks = nullptr;                         // K shifts (B, KV, Smax)
+  int32_t* vc = nullptr;                        // V cache (B, KV, Smax, hd) int32
+  int16_t* qq = nullptr;                        // (R, H, hd) quantised roped q
+  int32_t* qs = nullptr;                        // (R, H) q shifts
+  const int32_t* exp_t = nullptr;
+  int64_t* out = nullptr; int ldo = 0;          // (R, H*hd)
+  int R = 0, H = 0, KV = 0, hd = 0, Smax = 0, Tmax = 0;
+  int64_t inv = 0;                              // round(2^16 / sqrt(hd))
+  int* err = nullptr;
+};
+cudaError_t launch_rope_cache(const AttnArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
+
+cudaError_t launch_fr_keys(const int8_t* w, const int32_t* Mg, int N, int K, int row0, int row_step,
+                           const int32_t* r, int32_t* d, cudaStream_t st);
+cudaError_t launch_fr_check(const unsigned long long* acc, int nchecks, int* fail_count, int* err,
+                            cudaStream_t st, bool pdl);
+
+}  // namespace exb

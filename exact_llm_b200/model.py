@@ -1,0 +1,218 @@
+"""Host-side model API mirroring the reference's model/engine interface.
+
+Reference interfaces (novain-shibu/exact-llm) and their counterparts here:
+
+  IntModel(get, c); model(ids) -> int64 (T, V)          exact_llm.py:141-180      ExactModel.__call__
+  TModel.forward(ids, cache, last_only); new_cache()     exact_torch.py:140,171-193 ExactModel.forward / new_cache
+  GraphDecoder.step(token) (CUDA graph, static cache)    speed_fair_kaggle.py:590-645 ExactModel.step / generate
+  TRACE['rec'][name] / flat per-step buffer              gpu_engine_trace_verify_kaggle.py:746,
+                                                         prover_commit_cost_gpu_kaggle.py:741-742  ExactModel.trace
+  keys_group / keys_channel / fr                         gpu_engine_trace_verify_kaggle.py:803-834 freivalds_*
+
+All compute runs in libexactb200.so (sm_100a CUDA kernels); this module only moves host
+arrays and calls the C ABI.  Outputs are numpy int64 Q16 logits exactly as the reference returns.
+"""
+import ctypes
+
+import numpy as np
+
+from . import tables
+from ._lib import Config, check, lib, ptr
+
+LIN_NAMES = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+class Cache:
+    """A KV-cache sequence slot (TModel.new_cache equivalent, exact_torch.py:140)."""
+
+    def __init__(self, model, slot):
+        self.model, self.slot = model, slot
+
+    @property
+    def n(self):
+        return lib.exb_seq_len(self.model.h, self.slot)
+
+
+class ExactModel:
+    """Exact integer Qwen2-family model on one B200.
+
+    ``c`` uses the reference's config keys (D, H, KV, hd, I, V, NL, theta, tie) plus
+    ``lin`` ("group" for group-128 GQLin layers, "channel" for per-channel QLin layers).
+    """
+
+    def __init__(self, c, max_batch=1, max_seq=None, rope_len=None, emb_shift=9, tie=None):
+        self.c = dict(c)
+        self.max_batch = int(max_batch)
+        self.max_seq = int(max_seq or c.get("T", 4096))
+        self.rope_len = int(rope_len or max(self.max_seq, c.get("T", 0)))
+        cfg = Config(D=c["D"], H=c["H"], KV=c["KV"], hd=c["hd"], I=c["I"], V=c["V"], NL=c["NL"],
+                     tie=int(c.get("tie", False) if tie is None else tie),
+                     lin_kind=0 if c.get("lin", "group") == "group" else 1, n_experts=int(c.get("NE", 0)),
+                     topk=int(c.get("TOPK", 0)), moe_I=int(c.get("MI", 0)), shared_I=int(c.get("SI", 0)),
+                     max_batch=self.max_batch, max_seq=self.max_seq, rope_len=self.rope_len, emb_shift=emb_shift)
+        h = ctypes.c_void_p()
+        check(lib.exb_model_create(ctypes.byref(cfg), ctypes.byref(h)))
+        self.h = h
+        cos, sin = tables.rope_tables(self.rope_len, c["hd"], c["theta"])
+        half = c["hd"] // 2
+        self._tab = [np.ascontiguousarray(t) for t in (tables.exp_table(), tables.silu_table(), tables.sig_table(),
+                                                       cos[:, :half], sin[:, :half])]
+        check(lib.exb_model_set_tables(self.h, *[ptr(t, ctypes.c_int64) for t in self._tab]))
+        self._finalized = False
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def synthetic(cls, c, seed, **kw):
+        """Seeded synthetic integer model generated directly in HBM."""
+        m = cls(c, **kw)
+        check(lib.exb_model_generate(m.h, int(seed)))
+        m.finalize()
+        return m
+
+    @classmethod
+    def from_tensors(cls, c, tensors, **kw):
+        """Integer artifact given as {name: array} (names as in include/exactb200.h)."""
+        m = cls(c, **kw)
+        for name, arr in tensors.items():
+            m.set_tensor(name, arr)
+        m.finalize()
+        return m
+
+    def set_tensor(self, name, arr):
+        a = np.ascontiguousarray(arr)
+        check(lib.exb_model_set_tensor(self.h, name.encode(), ptr(a), a.nbytes))
+
+    def finalize(self):
+        check(lib.exb_model_finalize(self.h))
+        self._finalized = True
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib.exb_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def weight_bytes(self):
+        return lib.exb_model_weight_bytes(self.h)
+
+    @property
+    def stream(self):
+        return lib.exb_model_stream(self.h)
+
+    # ------------------------------------------------------------------ reference-style API
+    def new_cache(self, slot=0):
+        check(lib.exb_seq_reset(self.h, slot))
+        return Cache(self, slot)
+
+    def forward(self, ids, cache=None, last_only=False, want_logits=True):
+        """TModel.forward: logits (T, V) of the new tokens (or (1, V) with last_only)."""
+        if cache is None:
+            cache = self.new_cache(0)
+        ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        T = len(ids)
+        self._rows = T
+        seqs = np.full(T, cache.slot, np.int32)
+        logits = np.empty((T, self.c["V"]), np.int64) if want_logits else None
+        nxt = np.empty(T, np.int32)
+        check(lib.exb_forward(self.h, T, ptr(ids, ctypes.c_int32), ptr(seqs, ctypes.c_int32),
+                              ptr(logits, ctypes.c_int64), ptr(nxt, ctypes.c_int32)))
+        self.last_next = nxt
+        if logits is None:
+            return None
+        return logits[-1:] if last_only else logits
+
+    def __call__(self, ids):
+        """IntModel.__call__: full causal forward of a fresh sequence -> int64 (T, V) Q16 logits."""
+        return self.forward(ids, self.new_cache(0))
+
+    def forward_rows(self, ids, seqs, want_logits=True):
+        """Rows of several sequences in one call (row i appends ids[i] to sequence seqs[i])."""
+        ids = np.ascontiguousarray(np.asarray(ids, np.int32).reshape(-1))
+        seqs = np.ascontiguousarray(np.asarray(seqs, np.int32).reshape(-1))
+        self._rows = len(ids)
+        logits = np.empty((len(ids), self.c["V"]), np.int64) if want_logits else None
+        nxt = np.empty(len(ids), np.int32)
+        check(lib.exb_forward(self.h, len(ids), ptr(ids, ctypes.c_int32), ptr(seqs, ctypes.c_int32),
+                              ptr(logits, ctypes.c_int64), ptr(nxt, ctypes.c_int32)))
+        return logits, nxt
+
+    def generate(self, first_ids, steps, want_logits=False):
+        """Greedy decode of sequences 0..B-1 with on-device token feedback (GraphDecoder loop).
+        Returns tokens (B, steps) and, if asked, logits (steps, B, V)."""
+        first = np.ascontiguousarray(np.asarray(first_ids, np.int32).reshape(-1))
+        B = len(first)
+        self._rows = B * int(steps)
+        toks = np.empty((steps, B), np.int32)
+        logits = np.empty((steps, B, self.c["V"]), np.int64) if want_logits else None
+        check(lib.exb_generate(self.h, B, ptr(first, ctypes.c_int32), int(steps), ptr(toks, ctypes.c_int32),
+                               ptr(logits, ctypes.c_int64)))
+        return (toks.T.copy(), logits) if want_logits else toks.T.copy()
+
+    def greedy(self, prompt, steps, want_logits=True):
+        """Prefill ``prompt`` in slot 0, then ``steps`` greedy tokens: (prefill logits, step logits, tokens),
+        the first generated token being argmax of the prompt's last row (exact_llm.py:262-268)."""
+        lg = self.forward(prompt, self.new_cache(0))
+        first = int(self.last_next[-1])
+        if steps <= 0:
+            return lg, [], []
+        toks, rows = self.generate([first], steps, want_logits=True)
+        # generate() feeds token t and returns the argmax of its logits as token t+1
+        tokens = [first] + [int(t) for t in toks[0, :-1]]
+        return lg, [rows[s, 0] for s in range(steps)], tokens
+
+    # ------------------------------------------------------------------ trace + Freivalds
+    def trace_enable(self, on=True):
+        check(lib.exb_trace_enable(self.h, int(on)))
+
+    @property
+    def trace_row_len(self):
+        return int(lib.exb_trace_row_len(self.h))
+
+    def trace(self):
+        """Raw accumulators of the last call's rows: int64 (rows, trace_row_len) in the order
+        L0.q, L0.k, L0.v, L0.o, L0.gate, L0.up, L0.down, L1.q, ..., head."""
+        n = self._rows
+        out = np.empty(n * self.trace_row_len, np.int64)
+        check(lib.exb_trace_read(self.h, ptr(out, ctypes.c_int64), out.size))
+        return out.reshape(n, self.trace_row_len)
+
+    def linear_sizes(self):
+        c = self.c
+        out = []
+        for i in range(c["NL"]):
+            out += [(f"L{i}.q", c["H"] * c["hd"], c["D"]), (f"L{i}.k", c["KV"] * c["hd"], c["D"]),
+                    (f"L{i}.v", c["KV"] * c["hd"], c["D"]), (f"L{i}.o", c["D"], c["H"] * c["hd"]),
+                    (f"L{i}.gate", c["I"], c["D"]), (f"L{i}.up", c["I"], c["D"]), (f"L{i}.down", c["D"], c["I"])]
+        out.append(("head", c["V"], c["D"]))
+        return out
+
+    def freivalds_set_keys(self, r_list):
+        """r_list: per linear (trace order) an int array (2, N) of r values in [0, p)."""
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(r, np.int64).reshape(-1) for r in r_list]).astype(np.int32))
+        check(lib.exb_freivalds_set_keys(self.h, ptr(flat, ctypes.c_int32), flat.size))
+
+    def freivalds_keys(self):
+        sizes = self.linear_sizes()
+        n = sum(2 * K for _, _, K in sizes)
+        out = np.empty(n, np.int32)
+        check(lib.exb_freivalds_read_keys(self.h, ptr(out, ctypes.c_int32), n))
+        res, pos = [], 0
+        for _, _, K in sizes:
+            res.append(out[pos:pos + 2 * K].reshape(2, K).astype(np.int64))
+            pos += 2 * K
+        return res
+
+    def freivalds_enable(self, on=True):
+        check(lib.exb_freivalds_enable(self.h, int(on)))
+
+    def freivalds_status(self):
+        a, b = ctypes.c_int64(), ctypes.c_int64()
+        check(lib.exb_freivalds_status(self.h, ctypes.byref(a), ctypes.byref(b)))
+        return a.value, b.value
+

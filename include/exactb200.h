@@ -1,0 +1,150 @@
+/* exactb200.h -- C ABI of the B200-native exact integer forward pass.
+ *
+ * Drop-in boundary for the hot path of novain-shibu/exact-llm: the exact integer model
+ * (exact_llm.py IntModel / exact_torch.py TModel / experiments GraphDecoder) and the exact
+ * group-128 GEMV operator (experiments/speed_fair_kaggle.py "exact::gemv").  Plain pointers and
+ * sizes only; no torch types.  Every entry point returns 0 on success and a non-zero code on
+ * failure; exb_last_error() returns the message of the calling thread's last failure.
+ *
+ * Integer conventions (SPEC.md v0.4 of the reference): activations and logits are int64 Q16;
+ * weights int8; group-128 scales int32 (< 2^27); per-channel scales and biases int64.
+ * Weight matrices are (N, K) = (out, in) row-major.
+ */
+#ifndef EXACTB200_H
+#define EXACTB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* error codes */
+#define EXB_OK 0
+#define EXB_EINVAL 1     /* bad argument / size / unsupported shape */
+#define EXB_ECUDA 2      /* CUDA runtime error */
+#define EXB_EDEVICE 3    /* the device reported a numeric-range, bounds or wait-timeout error */
+#define EXB_ENOMEM 4
+
+typedef struct exb_model exb_model;
+
+/* Model architecture.  Mirrors the config dict of exact_llm.open_hf (exact_llm.py:227-230)
+ * plus the integer-engine capacities. */
+typedef struct exb_config {
+  int D, H, KV, hd, I, V, NL;  /* hidden, query heads, KV heads, head dim, MLP, vocab, layers */
+  int tie;                     /* 1: the head is the embedding matrix (Qwen2.5-0.5B) */
+  int lin_kind;                /* 0: group-128 linears (GQLin), 1: per-channel linears (QLin) */
+  int n_experts, topk;         /* MoE (Qwen1.5-MoE): 0 for dense models */
+  int moe_I, shared_I;
+  int max_batch;               /* sequence slots of the KV cache */
+  int max_seq;                 /* KV positions per sequence (Smax) */
+  int rope_len;                /* rows of the cos/sin tables (>= max_seq) */
+  int emb_shift;               /* x = emb_int8 << emb_shift gives Q16 embeddings */
+} exb_config;
+
+const char* exb_last_error(void);
+int exb_version(void);
+
+/* --------------------------------------------------------------------- operator level */
+
+/* exact::gemv drop-in (experiments/speed_fair_kaggle.py:686-702):
+ * out[n] = sum_g Mg[n,g] * sum_{k in g} x16[k] * wT[n,k]   (int64, exact).
+ * Device pointers; K % 128 == 0; 16-byte aligned x16 and wT; launches on `stream`. */
+int exb_gemv(const int16_t* x16, const int8_t* wT, const int64_t* Mg, int K, int N, int64_t* out, void* stream);
+
+/* GQLin.__call__ (experiments/speed_fair_kaggle.py:722-725) on R rows of device int64 Q16 input:
+ * xq, s = qrow(x); tot = sum_g M_g (xq_g . W_g); y = shr(tot, 28 - s) + b.
+ * w_NK int8 (N, K); M_NG int32 (N, K/128); bias int64 (N) or NULL; y int64 (R, N);
+ * tot_out int64 (R, N) or NULL.  `scratch` holds R*K int16 + R int32 device bytes
+ * (exb_linear_g128_scratch_bytes). */
+size_t exb_linear_g128_scratch_bytes(int R, int K);
+int exb_linear_g128(const int64_t* x, int R, int K, const int8_t* w_NK, const int32_t* M_NG, const int64_t* bias,
+                    int N, int64_t* y, int64_t* tot_out, void* scratch, void* stream);
+
+/* QLin.__call__ (exact_llm.py:89-96) with the per-row drop rule, on device buffers.
+ * w_NK int8 (N, K); M int64 (N); acc_out int64 (R, N) is required (the drop rule needs the
+ * whole row); scratch as for exb_linear_g128. */
+int exb_linear_channel(const int64_t* x, int R, int K, const int8_t* w_NK, const int64_t* M, const int64_t* bias,
+                       int N, int64_t* y, int64_t* acc_out, void* scratch, void* stream);
+
+/* --------------------------------------------------------------------- model level */
+
+int exb_model_create(const exb_config* cfg, exb_model** out);
+void exb_model_destroy(exb_model* m);
+
+/* Integer tables shipped with the model (SPEC.md section 1): exp (10242 entries, Q24), SiLU and
+ * sigmoid (8194 entries, Q16), RoPE cos/sin (rope_len x hd/2, Q16).  Host int64 arrays. */
+int exb_model_set_tables(exb_model* m, const int64_t* exp_t, const int64_t* silu_t, const int64_t* sig_t,
+                         const int64_t* cos_t, const int64_t* sin_t);
+
+/* Upload one named tensor of the integer artifact from host memory.  Names:
+ *   emb (int8 V x D), gf (int64 D), head.w (int8 V x D, untied only), head.M (int64 V),
+ *   L{i}.g1 / L{i}.g2 (int64 D),
+ *   L{i}.{q,k,v,o,gate,up,down}.w (int8 N x K), .M (int32 N x K/128 group | int64 N channel), .b (int64 N),
+ *   MoE: L{i}.{router,sgate,sg,su,sd}.{w,M}, L{i}.e{e}.{g,u,d}.{w,M}. */
+int exb_model_set_tensor(exb_model* m, const char* name, const void* host, size_t bytes);
+
+/* Fill every tensor with the seeded synthetic integer generator, directly in HBM. */
+int exb_model_generate(exb_model* m, uint64_t seed);
+
+/* Upload done: derive fused layouts and range proofs.  Must precede any forward call. */
+int exb_model_finalize(exb_model* m);
+
+/* Empty a sequence slot (its next token gets position 0). */
+int exb_seq_reset(exb_model* m, int seq);
+int exb_seq_len(exb_model* m, int seq);
+
+/* TModel.forward(ids, cache) (exact_torch.py:171-193) for several sequences at once: row i
+ * appends token ids[i] to sequence seqs[i] (rows of one sequence in order).  HOST buffers:
+ * logits (n x V int64) may be NULL; next (n int32, greedy argmax, lowest index on ties) may be NULL. */
+int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, int64_t* logits, int32_t* next);
+
+/* Greedy generation with the token fed back on the device (GraphDecoder.step loop,
+ * experiments/speed_fair_kaggle.py:639-645).  Sequences 0..B-1 continue from their current
+ * length with first_ids (B); writes tokens (B x steps, host) and optionally every step's logits
+ * (steps x B x V, host) -- NULL skips the copy. */
+int exb_generate(exb_model* m, int B, const int32_t* first_ids, int steps, int32_t* tokens, int64_t* logits);
+
+/* Same loop on device buffers only (ids_dev B int32 in, tokens_dev B x steps int32 out), on the
+ * model's stream; no host synchronisation. */
+int exb_generate_device(exb_model* m, int B, const int32_t* ids_dev, int steps, int32_t* tokens_dev);
+
+/* Trace capture (experiments/prover_commit_cost_gpu_kaggle.py:727-742): when on, every forward
+ * row records the raw accumulator of every linear (tot for group-128, acc for per-channel) in
+ * call order L0.q,k,v,o,gate,up,down, L1..., head.  exb_trace_row_len gives int64 per row. */
+int exb_trace_enable(exb_model* m, int on);
+int64_t exb_trace_row_len(exb_model* m);
+/* copy the trace of the last forward/decode step's rows (rows x row_len int64) to host */
+int exb_trace_read(exb_model* m, int64_t* host, int64_t n);
+
+/* Freivalds self-check on every linear (experiments/gpu_engine_trace_verify_kaggle.py:803-834):
+ * r_host holds, for each linear in trace order, 2 x N values in [0, p) for p = 2^31-1 and
+ * 2147483629 (int32).  The device builds d_p = (W*M)^T r_p mod p and, on every later forward,
+ * checks sum_n r_n (t_n mod p) == sum_k d_k (xq_k mod p) (mod p) per row and linear. */
+int exb_freivalds_set_keys(exb_model* m, const int32_t* r_host, int64_t n);
+int exb_freivalds_read_keys(exb_model* m, int32_t* d_host, int64_t n);   /* 2 x K per linear */
+int exb_freivalds_enable(exb_model* m, int on);
+int exb_freivalds_status(exb_model* m, int64_t* checks, int64_t* failures);
+
+/* device error word: bit 1 |V| >= 2^31 (V cache range), 2 wait timeout, 4 Freivalds, 8 bounds */
+int exb_device_errors(exb_model* m, int* bits);
+
+/* Time one layer's fused linear kernel alone: `reps` back-to-back launches on the model's stream
+ * between CUDA events; *avg_ms = mean duration of one launch.  which: 0 q|k|v, 1 o, 2 gate|up,
+ * 3 down, 4 head.  *bytes = algorithmic bytes one launch must move (weights + scales + activations
+ * + outputs). */
+int exb_bench_linear(exb_model* m, int layer, int which, int R, int reps, float* avg_ms, double* bytes);
+
+/* raw pointers for benchmarks / interop */
+void* exb_model_stream(exb_model* m);
+size_t exb_model_weight_bytes(exb_model* m);
+
+/* Synthetic tensor generator on the device (same integers as the test oracle's generator).
+ * kind: 0 int8 weight, 1 int32 scale, 2 int64 scale, 3 int64 bias, 4 int64 gain. */
+int exb_gen_tensor(int kind, uint64_t seed, uint64_t stream_id, int64_t n, int64_t K, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

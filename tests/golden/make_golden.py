@@ -1,0 +1,351 @@
+"""Generate the golden fixtures under tests/golden/ by RUNNING THE REFERENCE's own code.
+
+Usage:  python tests/golden/make_golden.py --ref <path to the exact-llm checkout> [--only NAME ...]
+
+The reference (novain-shibu/exact-llm) is a Python project; this script imports its
+``exact_llm.py`` and executes, from its experiment scripts, only the class/function
+definitions the hot path needs (the scripts' top-level code downloads checkpoints):
+
+  * ``GQLin``                         experiments/speed_fair_kaggle.py:713-725
+  * ``SIG_T``/``isig``                 experiments/moe_exact_kaggle.py:419-424
+  * ``MoEInt``                         experiments/moe_exact_kaggle.py:433-482
+  * ``P1, P2``                         experiments/gpu_engine_trace_verify_kaggle.py:782
+  * ``keys_group/keys_channel/fr``     experiments/gpu_engine_trace_verify_kaggle.py:802-819, 830-834
+  * the tiny preflight model           experiments/_pre_tiny.py:1-15
+  * the G1 GEMV known-answer inputs    experiments/speed_fair_kaggle.py:704-708
+
+Synthetic integer weights come from ``oracle.synth`` and are handed to the reference's
+classes through ``__new__`` (no float checkpoint is involved).  Nothing here is imported
+by the product or by the GPU tests at run time: they read only the committed outputs.
+"""
+import argparse
+import hashlib
+import json
+import os
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from oracle import synth  # noqa: E402
+from oracle.exact_oracle import h16  # noqa: E402
+
+OUT_JSON = os.path.join(HERE, "golden.json")
+
+
+def load_reference(ref):
+    sys.path.insert(0, ref)
+    import exact_llm as ex
+
+    def exec_lines(rel, a, b, ns):
+        with open(os.path.join(ref, rel)) as f:
+            lines = f.readlines()
+        exec(compile("".join(lines[a - 1:b]), f"{rel}:{a}-{b}", "exec"), ns)
+
+    exec_lines("experiments/speed_fair_kaggle.py", 713, 725, ex.__dict__)           # G_, GQLin
+    exec_lines("experiments/moe_exact_kaggle.py", 419, 424, ex.__dict__)            # SIG_T, isig
+    fr_ns = dict(ex.__dict__)
+    exec_lines("experiments/gpu_engine_trace_verify_kaggle.py", 782, 782, fr_ns)    # P1, P2
+    exec_lines("experiments/gpu_engine_trace_verify_kaggle.py", 802, 819, fr_ns)    # rng, keys_group/channel
+    exec_lines("experiments/gpu_engine_trace_verify_kaggle.py", 830, 834, fr_ns)    # fr
+    ex._fr_ns = fr_ns
+    ex._exec_lines = exec_lines
+    return ex
+
+
+# ----------------------------------------------------------------------------- reference objects
+def ref_gqlin(ex, lin):
+    g = ex.GQLin.__new__(ex.GQLin)
+    g.w = np.ascontiguousarray(lin.w.T)                    # reference layout (K, N)
+    g.M = np.ascontiguousarray(lin.M.T)                    # (G, N)
+    g.groups = [(a, a + 128) for a in range(0, lin.K, 128)]
+    g.b = lin.b
+    return g
+
+
+def ref_qlin(ex, lin):
+    q = ex.QLin.__new__(ex.QLin)
+    q.w = np.ascontiguousarray(lin.w.T)
+    q.M = lin.M
+    q.Mbits = int(ex.bitlen(np.array([q.M.max()]))[0])
+    q.b = lin.b
+    return q
+
+
+def ref_lin(ex, lin):
+    return ref_gqlin(ex, lin) if lin.kind == "group" else ref_qlin(ex, lin)
+
+
+class Recorder:
+    """Wraps a reference linear and records its integer accumulator (tot / acc) per call,
+    the way the reference's trace capture does (gpu_engine_trace_verify_kaggle.py:746)."""
+
+    def __init__(self, ex, inner, name, log):
+        self.ex, self.inner, self.name, self.log = ex, inner, name, log
+
+    def __call__(self, x):
+        ex = self.ex
+        y = self.inner(x)
+        xq, s = ex.qrow(x, 15)
+        if isinstance(self.inner, ex.GQLin):
+            raw = np.zeros((x.shape[0], self.inner.w.shape[1]), np.int64)
+            for gi, (a, b) in enumerate(self.inner.groups):
+                raw += ex.exact_mm(xq[:, a:b], self.inner.w[a:b]) * self.inner.M[gi]
+            chk = ex.shr(raw, 28 - s)
+        else:
+            raw = ex.exact_mm(xq, self.inner.w)
+            q = self.inner
+            drop = np.maximum(ex.bitlen(np.abs(raw).max(-1, keepdims=True)) + q.Mbits - 62, 0)
+            chk = ex.shr(ex.shr(raw, drop) * q.M, 28 - s - drop)
+        if self.inner.b is not None:
+            chk = chk + self.inner.b
+        assert np.array_equal(chk, y), "recorded accumulator does not reproduce the reference output"
+        if self.log is not None:
+            self.log.append((self.name, raw))
+        return y
+
+
+def ref_int_model(ex, om, record=None):
+    c = dict(om.c)
+    m = ex.IntModel.__new__(ex.IntModel)
+    m.c = c
+    m.emb = om.emb_i8.astype(np.float64) / 128.0          # rint(emb * 2^16) == emb_i8 << 9 exactly
+    m.layers = []
+    for li, L in enumerate(om.layers):
+        d = dict(g1=L["g1"], g2=L["g2"])
+        for nm in ("q", "k", "v", "o", "gate", "up", "down"):
+            inner = ref_lin(ex, L[nm])
+            d[nm] = Recorder(ex, inner, f"L{li}.{nm}", record) if record is not None else inner
+        m.layers.append(d)
+    m.gf = om.gf
+    head = ref_qlin(ex, om.head)
+    m.head = Recorder(ex, head, "head", record) if record is not None else head
+    cos, sin = ex.rope_tables(c["T"], c["hd"], c["theta"])
+    m.cos = np.rint(cos * ex.ONE).astype(np.int64)
+    m.sin = np.rint(sin * ex.ONE).astype(np.int64)
+    return m
+
+
+def ref_moe_model(ex, om):
+    c = dict(om.c)
+    ns = dict(ex.__dict__)
+    ns.update(c=c, NE=c["NE"], TOPK=c["TOPK"])
+    ex._exec_lines("experiments/moe_exact_kaggle.py", 433, 482, ns)                # class MoEInt
+    MoEInt = ns["MoEInt"]
+    m = MoEInt.__new__(MoEInt)
+    m.c = c
+    m.emb = om.emb_i8.astype(np.float64) / 128.0
+    m.layers = []
+    for L in om.layers:
+        d = dict(g1=L["g1"], g2=L["g2"])
+        for nm in ("q", "k", "v", "o", "router", "sgate", "sg", "su", "sd"):
+            d[nm] = ref_qlin(ex, L[nm])
+        d["ex"] = [tuple(ref_qlin(ex, t) for t in e) for e in L["ex"]]
+        m.layers.append(d)
+    m.gf = om.gf
+    m.head = ref_qlin(ex, om.head)
+    cos, sin = ex.rope_tables(c["T"], c["hd"], c["theta"])
+    m.cos = np.rint(cos * ex.ONE).astype(np.int64)
+    m.sin = np.rint(sin * ex.ONE).astype(np.int64)
+    return m
+
+
+def step_digest_hex(flat):
+    arr = np.ascontiguousarray(flat, dtype=np.int64)
+    step = (len(arr) + 3) // 4
+    parts = [hashlib.sha256(arr[i * step:(i + 1) * step].tobytes()).digest() for i in range(4)]
+    return hashlib.sha256(b"".join(parts)).hexdigest()
+
+
+# ----------------------------------------------------------------------------- fixture builders
+def g_tables(ex, G):
+    out = dict(EXP_T=h16(ex.EXP_T), SILU_T=h16(ex.SILU_T), SIG_T=h16(ex.SIG_T), rope={})
+    for T, hd, th in ((4352, 64, 1e6), (4352, 128, 1e6), (4352, 64, 1e4), (64, 16, 1e4)):
+        cos, sin = ex.rope_tables(T, hd, th)
+        out["rope"][f"{T}_{hd}_{th:g}"] = [h16(np.rint(cos * ex.ONE).astype(np.int64)),
+                                           h16(np.rint(sin * ex.ONE).astype(np.int64))]
+    G["tables"] = out
+
+
+def g_gemv_kat(ex, G):
+    """The reference's G1 kernel known-answer test (speed_fair_kaggle.py:704-711): same seeded
+    torch inputs, expected output from its own int64 expression."""
+    import torch
+    g = torch.Generator().manual_seed(0)
+    res = []
+    for K_, N_ in ((896, 896), (896, 4864), (4864, 896), (1536, 8960), (8960, 1536), (896, 151936)):
+        x = torch.randint(-32767, 32768, (K_,), generator=g, dtype=torch.int64)
+        w = torch.randint(-127, 128, (K_, N_), generator=g, dtype=torch.int64)
+        Mg = torch.randint(1, 1 << 27, (N_, K_ // 128), generator=g, dtype=torch.int64)
+        ref = ((x.view(K_ // 128, 128, 1) * w.view(K_ // 128, 128, N_)).sum(1) * Mg.T).sum(0)
+        res.append(dict(K=K_, N=N_, out=h16(ref.numpy()), x=h16(x.numpy()), w=h16(w.numpy()), Mg=h16(Mg.numpy())))
+    G["gemv_kat"] = res
+
+
+LINEAR_SHAPES = ((3584, 4608), (3584, 3584), (3584, 37888), (18944, 3584))
+LINEAR_ROWS = (1, 16, 256, 2048)
+
+
+def g_linear(ex, G):
+    """BASELINE config 2 through the reference GQLin at every (K, N, M)."""
+    res = []
+    for K, N in LINEAR_SHAPES:
+        for R in LINEAR_ROWS:
+            t0 = time.time()
+            x, lin = synth.linear_case(1000 + K + N, K, N, R)
+            rec = []
+            y = Recorder(ex, ref_gqlin(ex, lin), "lin", rec)(x)
+            res.append(dict(K=K, N=N, R=R, seed=1000 + K + N, y=h16(y), tot=h16(rec[0][1]),
+                            y_row0=[int(v) for v in y[0, :8]], ref_s=round(time.time() - t0, 3)))
+            print("linear", K, N, R, res[-1]["ref_s"], flush=True)
+    G["linear"] = res
+
+
+def _dense_case(ex, G, key, cfg, seed, T, steps, prompt_seed, save_npz=False):
+    om = synth.build_model(cfg, seed)
+    ids = [int(t) for t in synth.prompt_ids(prompt_seed, 1, T, cfg["V"])[0]]
+    rec = []
+    rm = ref_int_model(ex, om, rec)
+    t0 = time.time()
+    lg = rm(ids)
+    pre_s = time.time() - t0
+    n_lin = len(rec)
+    prefill_trace = [(nm, raw) for nm, raw in rec]
+    toks, rows_h, digests = [], [], []
+    cur = list(ids)
+    nxt = int(lg[-1].argmax())
+    rows = []
+    for t in range(steps):                                  # the reference's decode: full recompute
+        toks.append(nxt)
+        cur.append(nxt)
+        rec.clear()
+        full = rm(cur)
+        row = full[-1]
+        rows.append(row)
+        rows_h.append(h16(row))
+        # per-step flat trace = last row of every accumulator, in call order
+        digests.append(step_digest_hex(np.concatenate([raw[-1] for _, raw in rec])))
+        nxt = int(row.argmax())
+    ent = dict(config=cfg, seed=seed, prompt=ids, prefill=h16(lg), prefill_last=h16(lg[-1]),
+               tokens=toks, rows=rows_h, trace_digests=digests, n_linears=n_lin,
+               prefill_trace={nm: h16(raw) for nm, raw in prefill_trace}, prefill_s=round(pre_s, 2))
+    if save_npz:
+        np.savez_compressed(os.path.join(HERE, f"{key}.npz"), prefill=lg, rows=np.array(rows),
+                            **{f"tr_{nm}": raw for nm, raw in prefill_trace})
+    G.setdefault("models", {})[key] = ent
+    print(key, "prefill", h16(lg), "tokens", toks[:8], round(pre_s, 2), flush=True)
+    return om, rm, ids, prefill_trace
+
+
+def g_models(ex, G):
+    _dense_case(ex, G, "tiny-g128", synth.config("tiny-g128"), 1, 12, 8, 3, save_npz=True)
+    _dense_case(ex, G, "tiny-ch", synth.config("tiny-ch"), 2, 10, 6, 4, save_npz=True)
+
+
+def g_config1(ex, G):
+    """0.5B architecture, 32 prompt ids, 64 greedy steps (reference full recompute)."""
+    _dense_case(ex, G, "qwen2.5-0.5b", synth.config("qwen2.5-0.5b"), 5, 32, 64, 5)
+
+
+def g_big_layers(ex, G):
+    """7B / 14B shapes with reduced depth (every kernel shape of configs 3 and 5)."""
+    _dense_case(ex, G, "qwen2.5-7b-L2", synth.config("qwen2.5-7b", NL=2), 7, 8, 3, 7)
+    _dense_case(ex, G, "qwen2.5-14b-L1", synth.config("qwen2.5-14b", NL=1), 14, 6, 2, 14)
+
+
+def g_freivalds(ex, G):
+    """Reference keys (rng seeded 2026, in layer/linear order) for tiny-g128; honest trace passes,
+    a +-1 or +p tamper fails (gpu_engine_trace_verify_kaggle.py:802-872)."""
+    cfg = synth.config("tiny-g128")
+    om = synth.build_model(cfg, 1)
+    rec = []
+    rm = ref_int_model(ex, om, rec)
+    ids = [int(t) for t in synth.prompt_ids(3, 1, 12, cfg["V"])[0]]
+    rm(ids)
+    fr_ns = dict(ex._fr_ns)
+    fr_ns["rng"] = np.random.default_rng(2026)
+    keys = {}
+    for li, L in enumerate(rm.layers):
+        for nm in ("q", "k", "v", "o", "gate", "up", "down"):
+            keys[f"L{li}.{nm}"] = fr_ns["keys_group"](L[nm].inner)
+    keys["head"] = fr_ns["keys_channel"](rm.head.inner)
+    ent = {}
+    for nm, ks in keys.items():
+        ent[nm] = [dict(p=int(p), r=h16(r), d=h16(d)) for p, r, d in ks]
+    G["freivalds"] = dict(keys=ent, model="tiny-g128", seed=1, prompt=ids)
+    np.savez_compressed(os.path.join(HERE, "freivalds_tiny.npz"),
+                        **{f"{nm}|{i}|r": k[1] for nm, ks in keys.items() for i, k in enumerate(ks)},
+                        **{f"{nm}|{i}|d": k[2] for nm, ks in keys.items() for i, k in enumerate(ks)})
+
+
+def g_pre_tiny(ex, G):
+    """The reference's own tiny fixture (experiments/_pre_tiny.py), float -> int conversion by
+    the reference's QLin; its hash for windows[0][:32] pins conversion + forward."""
+    ns = dict(ex.__dict__)
+    ex._exec_lines("experiments/_pre_tiny.py", 1, 15, ns)
+    get, c, windows = ns["get"], ns["c"], ns["windows"]
+    m = ex.IntModel(get, c)
+    ids = windows[0][:32]
+    lg = m(ids)
+    arrs = dict(emb=np.asarray(get("model.embed_tokens.weight"), np.float64), gf=m.gf, head_w=m.head.w,
+                head_M=m.head.M, ids=np.array(ids), logits=lg)
+    for li, L in enumerate(m.layers):
+        arrs[f"L{li}.g1"], arrs[f"L{li}.g2"] = L["g1"], L["g2"]
+        for nm in ("q", "k", "v", "o", "gate", "up", "down"):
+            arrs[f"L{li}.{nm}.w"] = L[nm].w
+            arrs[f"L{li}.{nm}.M"] = L[nm].M
+            if L[nm].b is not None:
+                arrs[f"L{li}.{nm}.b"] = L[nm].b
+    np.savez_compressed(os.path.join(HERE, "pre_tiny.npz"), **arrs)
+    G["pre_tiny"] = dict(config=c, logits=h16(lg), ids=[int(t) for t in ids])
+    print("pre_tiny", h16(lg), flush=True)
+
+
+def g_moe(ex, G):
+    for key, cfg, seed, T, steps in (("tiny-moe", synth.config("tiny-moe"), 3, 10, 4, ),
+                                     ("qwen1.5-moe-L1", synth.config("qwen1.5-moe-a2.7b", NL=1), 4, 8, 2)):
+        om = synth.build_model(cfg, seed)
+        rm = ref_moe_model(ex, om)
+        ids = [int(t) for t in synth.prompt_ids(seed, 1, T, cfg["V"])[0]]
+        st = {}
+        lg = rm(ids, st)
+        sels = {str(k): np.concatenate(v).tolist() for k, v in st.items()}
+        cur = list(ids)
+        toks, rows_h = [], []
+        nxt = int(lg[-1].argmax())
+        for _ in range(steps):
+            toks.append(nxt)
+            cur.append(nxt)
+            row = rm(cur)[-1]
+            rows_h.append(h16(row))
+            nxt = int(row.argmax())
+        G.setdefault("moe", {})[key] = dict(config=cfg, seed=seed, prompt=ids, prefill=h16(lg), sel=sels,
+                                            tokens=toks, rows=rows_h)
+        print(key, h16(lg), toks, flush=True)
+
+
+BUILDERS = dict(tables=g_tables, gemv_kat=g_gemv_kat, models=g_models, freivalds=g_freivalds,
+                pre_tiny=g_pre_tiny, moe=g_moe, linear=g_linear, config1=g_config1, big=g_big_layers)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", required=True, help="path of the exact-llm reference checkout")
+    ap.add_argument("--only", nargs="*", default=None)
+    a = ap.parse_args()
+    ex = load_reference(a.ref)
+    G = json.load(open(OUT_JSON)) if os.path.exists(OUT_JSON) else {}
+    for name, fn in BUILDERS.items():
+        if a.only and name not in a.only:
+            continue
+        t0 = time.time()
+        fn(ex, G)
+        print(f"[{name}] {time.time() - t0:.1f}s", flush=True)
+        with open(OUT_JSON, "w") as f:
+            json.dump(G, f, indent=1, sort_keys=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,227 @@
+"""CUDA path vs the reference: bit-exact parity through the C ABI (needs a B200).
+
+Every expected value here was recorded from the reference's own code (tests/golden) or is
+computed by the numpy oracle, which those fixtures pin."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from oracle import exact_oracle as eo
+from oracle import synth
+from tests.conftest import GOLDEN_DIR
+from tests.helpers import oracle_tensors
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch_cuda(cuda_ok):
+    import torch
+    return torch
+
+
+def _lib():
+    from exact_llm_b200 import _lib
+    return _lib
+
+
+def _stream(torch):
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+# ------------------------------------------------------------------ operator level
+def test_gemv_known_answer(golden, torch_cuda):
+    """The reference's own G1 kernel test (experiments/speed_fair_kaggle.py:704-711), all six shapes."""
+    torch = torch_cuda
+    L = _lib()
+    g = torch.Generator().manual_seed(0)
+    for case in golden["gemv_kat"]:
+        K, N = case["K"], case["N"]
+        x = torch.randint(-32767, 32768, (K,), generator=g, dtype=torch.int64)
+        w = torch.randint(-127, 128, (K, N), generator=g, dtype=torch.int64)
+        Mg = torch.randint(1, 1 << 27, (N, K // 128), generator=g, dtype=torch.int64)
+        ref = ((x.view(K // 128, 128, 1) * w.view(K // 128, 128, N)).sum(1) * Mg.T).sum(0)
+        xd = x.to(torch.int16).cuda()
+        wd = w.to(torch.int8).T.contiguous().cuda()
+        Md = Mg.cuda()
+        out = torch.empty(N, dtype=torch.int64, device="cuda")
+        L.check(L.lib.exb_gemv(L.ptr(xd), L.ptr(wd), L.ptr(Md), K, N, L.ptr(out), _stream(torch)))
+        got = out.cpu()
+        assert torch.equal(got, ref), (K, N)
+        assert eo.h16(got.numpy()) == case["out"]
+
+
+def _gen(torch, kind, seed, stream, n, K, dtype):
+    L = _lib()
+    out = torch.empty(n, dtype=dtype, device="cuda")
+    L.check(L.lib.exb_gen_tensor(kind, seed, stream, n, K, L.ptr(out), _stream(torch)))
+    return out
+
+
+def test_device_generator_matches_oracle(torch_cuda):
+    torch = torch_cuda
+    for kind, fn, dt, K in ((0, lambda: synth.gen_weight(5, 77, 300, 256).reshape(-1), torch.int8, 256),
+                            (1, lambda: synth.gen_scale(5, 78, 999, 3584), torch.int32, 3584),
+                            (2, lambda: synth.gen_scale(5, 79, 999, 896), torch.int64, 896),
+                            (3, lambda: synth.gen_bias(5, 80, 777), torch.int64, 0),
+                            (4, lambda: synth.gen_gain(5, 81, 777), torch.int64, 0)):
+        want = fn()
+        got = _gen(torch, kind, 5, 77 + kind, want.size, K, dt).cpu().numpy()
+        assert np.array_equal(got.astype(np.int64), want.astype(np.int64)), kind
+
+
+@pytest.mark.parametrize("K,N", [(3584, 4608), (3584, 3584), (3584, 37888), (18944, 3584)])
+def test_linear_config2(golden, torch_cuda, K, N):
+    """exact int8 x int8 linear with group-128 requant at M in {1, 16, 256, 2048},
+    against hashes of the reference GQLin's outputs."""
+    torch = torch_cuda
+    L = _lib()
+    cases = [c for c in golden["linear"] if c["K"] == K and c["N"] == N]
+    assert len(cases) == 4
+    seed = cases[0]["seed"]
+    w = _gen(torch, 0, seed, 7, N * K, K, torch.int8)
+    M = _gen(torch, 1, seed, 8, N * (K // 128), K, torch.int32)
+    for case in cases:
+        R = case["R"]
+        x = torch.from_numpy(np.random.default_rng(seed).integers(-128, 128, (R, K)).astype(np.int64)).cuda()
+        y = torch.empty((R, N), dtype=torch.int64, device="cuda")
+        tot = torch.empty((R, N), dtype=torch.int64, device="cuda")
+        scratch = torch.empty(L.lib.exb_linear_g128_scratch_bytes(R, K), dtype=torch.uint8, device="cuda")
+        L.check(L.lib.exb_linear_g128(L.ptr(x), R, K, L.ptr(w), L.ptr(M), None, N, L.ptr(y), L.ptr(tot),
+                                      L.ptr(scratch), _stream(torch)))
+        yh, th = y.cpu().numpy(), tot.cpu().numpy()
+        assert eo.h16(th) == case["tot"], (K, N, R)
+        assert eo.h16(yh) == case["y"], (K, N, R)
+        assert [int(v) for v in yh[0, :8]] == case["y_row0"]
+
+
+@pytest.mark.parametrize("scale_bits", [18, 40])
+def test_linear_channel_drop_rule(torch_cuda, scale_bits):
+    """Per-channel linear incl. the per-row overflow drop rule (exact_llm.py:89-96); 40-bit scales
+    force drop > 0 on every row."""
+    torch = torch_cuda
+    L = _lib()
+    rng = np.random.default_rng(scale_bits)
+    R, K, N = 5, 896, 1000
+    x = rng.integers(-(1 << 40), 1 << 40, (R, K)).astype(np.int64)
+    w = rng.integers(-127, 128, (N, K)).astype(np.int8)
+    M = rng.integers(1 << (scale_bits - 1), 1 << scale_bits, N).astype(np.int64)
+    b = rng.integers(-(1 << 14), 1 << 14, N).astype(np.int64)
+    lin = eo.ChannelLinear(w, M, b)
+    want = lin(x)
+    acc_want = lin.raw(eo.qrow(x)[0])
+    if scale_bits == 40:
+        assert (eo.bitlen(np.abs(acc_want).max(-1)) + lin.Mbits - 62).min() > 0
+    xd, wd, Md, bd = (torch.from_numpy(a).cuda() for a in (x, w, M, b))
+    y = torch.empty((R, N), dtype=torch.int64, device="cuda")
+    acc = torch.empty((R, N), dtype=torch.int64, device="cuda")
+    scratch = torch.empty(L.lib.exb_linear_g128_scratch_bytes(R, K), dtype=torch.uint8, device="cuda")
+    L.check(L.lib.exb_linear_channel(L.ptr(xd), R, K, L.ptr(wd), L.ptr(Md), L.ptr(bd), N, L.ptr(y), L.ptr(acc),
+                                     L.ptr(scratch), _stream(torch)))
+    assert np.array_equal(acc.cpu().numpy(), acc_want)
+    assert np.array_equal(y.cpu().numpy(), want)
+
+
+# ------------------------------------------------------------------ model level
+def _engine_from_oracle(om, **kw):
+    from exact_llm_b200 import ExactModel
+    return ExactModel.from_tensors(om.c, oracle_tensors(om), **kw)
+
+
+@pytest.mark.parametrize("key", ["tiny-g128", "tiny-ch"])
+def test_tiny_model_prefill_decode_trace(golden, cuda_ok, key):
+    g = golden["models"][key]
+    om = synth.build_model(dict(g["config"]), g["seed"])
+    ref = np.load(os.path.join(GOLDEN_DIR, f"{key}.npz"))
+    m = _engine_from_oracle(om, max_batch=2, max_seq=64)
+    m.trace_enable(True)
+    lg = m(g["prompt"])
+    assert np.array_equal(lg, ref["prefill"])
+    tr = m.trace()
+    sizes = m.linear_sizes()
+    off = 0
+    for name, N, _ in sizes:
+        assert eo.h16(np.ascontiguousarray(tr[:, off:off + N])) == g["prefill_trace"][name], name
+        off += N
+    m.trace_enable(False)
+    pre, rows, toks = m.greedy(g["prompt"], len(g["tokens"]))
+    assert toks == g["tokens"]
+    assert np.array_equal(np.array(rows), ref["rows"])
+
+
+def test_tiny_decode_trace_digests(golden, cuda_ok):
+    g = golden["models"]["tiny-g128"]
+    om = synth.build_model(dict(g["config"]), g["seed"])
+    m = _engine_from_oracle(om, max_batch=1, max_seq=64)
+    lg = m(g["prompt"])
+    first = int(lg[-1].argmax())
+    m.trace_enable(True)
+    m.generate([first], len(g["trace_digests"]))
+    tr = m.trace()
+    for step, want in enumerate(g["trace_digests"]):
+        assert eo.step_digest(tr[step]).hex() == want, step
+
+
+def test_pre_tiny_reference_fixture(golden, cuda_ok):
+    """The reference's own tiny model (float -> int by its QLin; hd = 16): hash eb3c5426052399f8."""
+    from exact_llm_b200 import ExactModel
+    z = np.load(os.path.join(GOLDEN_DIR, "pre_tiny.npz"))
+    c = dict(golden["pre_tiny"]["config"])
+    c["lin"] = "channel"
+    t = {"emb_q16": np.rint(z["emb"] * eo.ONE).astype(np.int64), "gf": z["gf"], "head.w": z["head_w"].T,
+         "head.M": z["head_M"], "emb": np.zeros((c["V"], c["D"]), np.int8)}
+    for i in range(c["NL"]):
+        t[f"L{i}.g1"], t[f"L{i}.g2"] = z[f"L{i}.g1"], z[f"L{i}.g2"]
+        for nm in eo.LIN_NAMES:
+            t[f"L{i}.{nm}.w"] = np.ascontiguousarray(z[f"L{i}.{nm}.w"].T)
+            t[f"L{i}.{nm}.M"] = z[f"L{i}.{nm}.M"]
+            if f"L{i}.{nm}.b" in z:
+                t[f"L{i}.{nm}.b"] = z[f"L{i}.{nm}.b"]
+    m = ExactModel.from_tensors(c, t, max_batch=1, max_seq=64, tie=False)
+    lg = m(golden["pre_tiny"]["ids"])
+    assert eo.h16(lg) == "eb3c5426052399f8"
+
+
+@pytest.mark.parametrize("key", ["qwen2.5-0.5b", "qwen2.5-7b-L2", "qwen2.5-14b-L1"])
+def test_synthetic_models_vs_reference(golden, cuda_ok, key):
+    """BASELINE config 1 (0.5B: 32 prompt ids + 64 greedy steps) and the 7B / 14B layer shapes,
+    weights generated in HBM, against the reference IntModel run on the same integers."""
+    from exact_llm_b200 import ExactModel
+    if key not in golden["models"]:
+        pytest.skip(f"fixture {key} not recorded")
+    g = golden["models"][key]
+    c = dict(g["config"])
+    m = ExactModel.synthetic(c, g["seed"], max_batch=1, max_seq=len(g["prompt"]) + len(g["tokens"]) + 8)
+    pre, rows, toks = m.greedy(g["prompt"], len(g["tokens"]))
+    assert eo.h16(pre) == g["prefill"]
+    assert toks == g["tokens"]
+    assert [eo.h16(r) for r in rows] == g["rows"]
+
+
+def test_freivalds_keys_and_self_check(golden, cuda_ok):
+    """Device keys equal the reference keys (rng seeded 2026); honest steps pass every check;
+    a corrupted weight is caught (experiments/gpu_engine_trace_verify_kaggle.py:803-872)."""
+    g = golden["models"]["tiny-g128"]
+    om = synth.build_model(dict(g["config"]), g["seed"])
+    m = _engine_from_oracle(om, max_batch=1, max_seq=64)
+    lins = [L[nm] for L in om.layers for nm in eo.LIN_NAMES] + [om.head]
+    rs = eo.draw_keys(lins, 2026)
+    m.freivalds_set_keys([np.stack([r for _, r in pr]) for pr in rs])
+    d_dev = m.freivalds_keys()
+    names = [n for n, _, _ in m.linear_sizes()]
+    for nm, d, pr in zip(names, d_dev, rs):
+        want = golden["freivalds"]["keys"][nm]
+        assert eo.h16(d[0]) == want[0]["d"] and eo.h16(d[1]) == want[1]["d"], nm
+    m.freivalds_enable(True)
+    m(g["prompt"])
+    checks, fails = m.freivalds_status()
+    assert checks == len(g["prompt"]) * len(names) and fails == 0
+    # corrupt one weight of L1.down after the keys were built: the self-check must fail
+    w = om.layers[1]["down"].w.copy()
+    w[3, 5] = np.int8(w[3, 5] + (1 if w[3, 5] < 127 else -1))
+    m.set_tensor("L1.down.w", w)
+    m(g["prompt"])
+    _, fails = m.freivalds_status()
+    assert fails > 0
