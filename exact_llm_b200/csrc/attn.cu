@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "exb_internal.h"
+#include "rowdev.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -27,54 +28,18 @@ constexpr int ATT_THREADS = 256;
 constexpr int REP_MAX = 8;          // query heads per KV head handled by one cluster
 
 // ---------------------------------------------------------------- RoPE + cache write + q quantisation
-__global__ void __launch_bounds__(128) k_rope_cache(const AttnArgs a) {
-  __shared__ uint64_t red[33];
+// Standalone form of rope_cache_rows (the decode path runs it as the q|k|v GEMV's last-CTA tail).
+__global__ void __launch_bounds__(256) k_rope_cache(const AttnArgs a) {
   pdl_wait();
-  const int r = blockIdx.x, j = blockIdx.y, d = threadIdx.x;
-  const int hd = a.hd, half = hd >> 1, rep = a.H / a.KV;
-  const int pos = a.row_pos[r], seq = a.row_seq[r];
-  if (pos < 0 || pos >= a.Smax || pos >= a.Tmax) {
-    if (d == 0) set_err(a.err, ERR_BOUNDS);
-    return;
-  }
-  const int64_t* row = a.qkv + (size_t)r * a.ldqkv;
-  int64_t c = 0, s = 0;
-  if (d < hd) {
-    c = a.cos_t[(size_t)pos * half + (d % half)];
-    s = a.sin_t[(size_t)pos * half + (d % half)];
-  }
-  auto rope1 = [&](const int64_t* x) -> int64_t {
-    if (d >= hd) return 0;
-    const int64_t rot = d < half ? (int64_t)(0ull - (uint64_t)x[d + half]) : x[d - half];
-    return shr64((int64_t)((uint64_t)x[d] * (uint64_t)c + (uint64_t)rot * (uint64_t)s), 16);
-  };
-  // key head j: RoPE, per-row quantisation, cache write; value head j: cache write
-  const int64_t kr = rope1(row + (size_t)(a.H + j) * hd);
-  const int sk = qrow_shift(block_max_u64<128>(d < hd ? uabs64(kr) : 0, red));
-  const size_t cidx = ((size_t)seq * a.KV + j) * a.Smax + pos;
-  if (d < hd) {
-    a.kc[cidx * hd + d] = qrow_value(kr, sk);
-    const int64_t v = row[(size_t)(a.H + a.KV + j) * hd + d];
-    if (v > INT32_MAX || v < INT32_MIN) set_err(a.err, ERR_V_RANGE);
-    a.vc[cidx * hd + d] = (int32_t)v;
-  }
-  if (d == 0) a.ks[cidx] = (int8_t)sk;
-  // query heads of this KV group: RoPE + per-row quantisation
-  for (int i = 0; i < rep; ++i) {
-    const int h = j * rep + i;
-    const int64_t qr = rope1(row + (size_t)h * hd);
-    const int sq = qrow_shift(block_max_u64<128>(d < hd ? uabs64(qr) : 0, red));
-    if (d < hd) a.qq[((size_t)r * a.H + h) * hd + d] = qrow_value(qr, sq);
-    if (d == 0) a.qs[(size_t)r * a.H + h] = sq;
-  }
   pdl_launch_dependents();
+  rope_cache_rows<256>(a);
 }
 
 cudaError_t launch_rope_cache(const AttnArgs& a, cudaStream_t st, bool pdl) {
   if (a.hd > 128 || (a.hd & 1) || a.H % a.KV) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.R, a.KV);
-  cfg.blockDim = dim3(128);
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(256);
   cfg.stream = st;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -85,9 +50,11 @@ cudaError_t launch_rope_cache(const AttnArgs& a, cudaStream_t st, bool pdl) {
 }
 
 // ---------------------------------------------------------------- decode attention (one cluster per row x KV head)
-EXB_DEV int64_t dot_i16(const int16_t* __restrict__ a, const int16_t* __restrict__ b, int hd) {
+template <int HD>
+EXB_DEV int64_t dot_i16(const int16_t* __restrict__ a, const int16_t* __restrict__ b) {
   int64_t acc = 0;
-  for (int d = 0; d < hd; d += 8) {
+#pragma unroll
+  for (int d = 0; d < HD; d += 8) {
     const int4 x = *reinterpret_cast<const int4*>(a + d);
     const int4 y = *reinterpret_cast<const int4*>(b + d);
     const int xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
@@ -101,6 +68,7 @@ EXB_DEV int64_t dot_i16(const int16_t* __restrict__ a, const int16_t* __restrict
   return acc;
 }
 
+template <int HD>
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a, int SCmax) {
   extern __shared__ __align__(16) unsigned char sm[];
   __shared__ int64_t lmax[REP_MAX], lsum[REP_MAX], gmax[REP_MAX], gsum[REP_MAX];
@@ -109,7 +77,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
   const int c = (int)cluster.block_rank();
   const int j = blockIdx.y, r = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int hd = a.hd, rep = a.H / a.KV;
+  constexpr int hd = HD;
+  const int rep = a.H / a.KV;
 
   int16_t* qs_sm = reinterpret_cast<int16_t*>(sm);                                  // rep*hd
   int64_t* sc = reinterpret_cast<int64_t*>(sm + ((rep * hd * 2 + 15) & ~15));      // rep*SCmax
@@ -117,6 +86,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
   int64_t* pv = pout + (size_t)rep * hd;                                             // ATT_THREADS*REP_MAX
 
   pdl_wait();
+  pdl_launch_dependents();
   const int pos = a.row_pos[r], seq = a.row_seq[r];
   const int S = pos + 1;
   const int chunk = (S + CL - 1) / CL;
@@ -132,7 +102,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
   // phase 1: scores of this CTA's positions, local max per head
   for (int e = tid; e < rep * n; e += ATT_THREADS) {
     const int i = e / n, t = t0 + (e - i * n);
-    const int64_t acc = dot_i16(qs_sm + i * hd, a.kc + (cbase + t) * hd, hd);
+    const int64_t acc = dot_i16<HD>(qs_sm + i * hd, a.kc + (cbase + t) * hd);
     sc[(size_t)i * SCmax + (t - t0)] =
         shr64((int64_t)((uint64_t)acc * (uint64_t)a.inv), 32 - qsh[i] - (int)a.ks[cbase + t]);
   }
@@ -183,6 +153,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
     int64_t acc[REP_MAX];
 #pragma unroll
     for (int i = 0; i < REP_MAX; ++i) acc[i] = 0;
+#pragma unroll 8
     for (int t = part; t < n; t += nparts) {
       const int64_t v = a.vc[(cbase + t0 + t) * hd + d];
 #pragma unroll
@@ -204,14 +175,30 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
   {
     const int tot = rep * hd, per = (tot + CL - 1) / CL;
     const int e0 = c * per, e1 = min(tot, e0 + per);
+    uint64_t om = 0;
     for (int e = e0 + tid; e < e1; e += ATT_THREADS) {
       int64_t s = 0;
       for (int cc = 0; cc < CL; ++cc) s += cluster.map_shared_rank(pout, cc)[e];
-      a.out[(size_t)r * a.ldo + (size_t)j * rep * hd + e] = shr64(s, 20);
+      const int64_t o = shr64(s, 20);
+      a.out[(size_t)r * a.ldo + (size_t)j * rep * hd + e] = o;
+      const uint64_t u = uabs64(o);
+      om = u > om ? u : om;
+    }
+    if (a.amax_out) {
+      // per-row max |out| for the o-projection's row quantisation (exact_llm.py:41-46)
+      for (int o = 16; o > 0; o >>= 1) { const uint64_t w = __shfl_xor_sync(0xffffffffu, om, o); om = w > om ? w : om; }
+      if (lane == 0 && om) atomicMax(a.amax_out + r, (unsigned long long)om);
     }
   }
   cluster.sync();                                        // peers' shared memory stays alive until read
-  pdl_launch_dependents();
+  // last CTA of the grid: qrow of the complete output rows for the o projection
+  if (a.xq_out && last_cta(a.ticket, gridDim.x * gridDim.y * gridDim.z)) {
+    for (int rr = 0; rr < a.R; ++rr) {
+      const int s = qrow_shift(__ldcg(a.amax_out + rr));
+      row_quant_known<ATT_THREADS>(a.out + (size_t)rr * a.ldo, a.H * hd, s, a.xq_out + (size_t)rr * a.ldq);
+      if (tid == 0) a.xs_out[rr] = s;
+    }
+  }
 }
 
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
@@ -221,7 +208,10 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const size_t smem = (size_t)((rep * a.hd * 2 + 15) & ~15) + (size_t)rep * SCmax * 8 + (size_t)rep * a.hd * 8 +
                       (size_t)ATT_THREADS * REP_MAX * 8;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  void (*kern)(const AttnArgs, int) = a.hd == 128 ? k_attn_decode<128> : a.hd == 64 ? k_attn_decode<64>
+                                    : a.hd == 32 ? k_attn_decode<32> : k_attn_decode<16>;
+  if (a.hd != 128 && a.hd != 64 && a.hd != 32 && a.hd != 16) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CL, a.KV, a.R);
@@ -233,7 +223,7 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_attn_decode, a, SCmax);
+  return cudaLaunchKernelEx(&cfg, kern, a, SCmax);
 }
 
 }  // namespace exb

@@ -44,6 +44,20 @@ EXB_DEV int64_t floordiv64(int64_t a, int64_t b) {
   return (r != 0 && a < 0) ? q - 1 : q;
 }
 
+// floor(a / b) for b > 0, exact for every int64 a: a double-precision estimate, a second
+// estimate on the (small) remainder, then integer corrections until 0 <= a - q*b < b.  About 30
+// instructions instead of the ~hundreds of a software 64-bit division.
+EXB_DEV int64_t floordiv_fast(int64_t a, int64_t b) {
+  const double db = (double)b;
+  int64_t q = (int64_t)floor(__ll2double_rn(a) / db);
+  int64_t r = (int64_t)((uint64_t)a - (uint64_t)q * (uint64_t)b);
+  q += (int64_t)floor(__ll2double_rn(r) / db);
+  r = (int64_t)((uint64_t)a - (uint64_t)q * (uint64_t)b);
+  for (int i = 0; i < 4 && r < 0; ++i) { q -= 1; r += b; }
+  for (int i = 0; i < 4 && r >= b; ++i) { q += 1; r -= b; }
+  return q;
+}
+
 // floor(sqrt(double(n))) with one correction step each way (exact_llm.py:97-99)
 EXB_DEV int64_t isqrt_ref(int64_t n) {
   int64_t r = (int64_t)floor(sqrt(__ll2double_rn(n)));
@@ -134,4 +148,44 @@ EXB_DEV void set_err(int* err, int bit) { if (err) atomicOr(err, bit); }
 // Freivalds primes p1 = 2^31 - 1, p2 = 2147483629 (experiments/gpu_engine_trace_verify_kaggle.py:782)
 EXB_DEV unsigned long long fr_prime(int i) { return i ? 2147483629ull : 2147483647ull; }
 
+}  // namespace exb
+
+// ---------------------------------------------------------------- mbarrier + bulk async copy (sm_90+)
+namespace exb {
+EXB_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+EXB_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+EXB_DEV void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+EXB_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+EXB_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+EXB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after ~`limit` polls (each try_wait may itself suspend for a while).
+// Returns false on timeout; the caller records ERR_WAIT_TIMEOUT and stops.
+EXB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 24)) {
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+// global -> shared bulk copy (16-byte aligned addresses, size multiple of 16), completion counted
+// in bytes on `bar`
+EXB_DEV void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst_smem)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+EXB_DEV void named_sync(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
 }  // namespace exb

@@ -85,6 +85,8 @@ struct exb_model {
   int16_t* xq = nullptr; int32_t* xs = nullptr;
   int16_t* qq = nullptr; int32_t* qs = nullptr;
   int32_t* next_tok = nullptr;
+  unsigned long long *amax_o = nullptr, *amax_h = nullptr;   // per-row max |x| published by producers
+  unsigned int* ticket = nullptr;                            // last-CTA election counter
   unsigned long long* head_part = nullptr; unsigned int* head_ticket = nullptr;
   int head_grid = 0;
   int64_t* trace = nullptr; int64_t trace_row = 0;
@@ -122,7 +124,10 @@ static void plan_weights(exb_model* m) {
   auto mk = [&](LinW& W, int N, int K, bool bias) {
     W.N = N; W.K = K;
     W.w = walloc<int8_t>(m, (size_t)N * K);
-    if (m->group) W.Mg = walloc<int32_t>(m, (size_t)N * (K / 128));
+    if (m->group) {
+      W.ldm = ((K / 128) + 3) & ~3;          // scale rows padded to 16 bytes (bulk-copy alignment)
+      W.Mg = walloc<int32_t>(m, (size_t)N * W.ldm);
+    }
     else W.Mc = walloc<int64_t>(m, N);
     W.b = bias ? walloc<int64_t>(m, N) : nullptr;
   };
@@ -193,6 +198,9 @@ static void plan_runtime(exb_model* m) {
   m->logits = ralloc<int64_t>(m, (size_t)RMAX * c.V);
   m->rawb = ralloc<int64_t>(m, (size_t)RMAX * m->NMAX);
   m->next_tok = ralloc<int32_t>(m, RMAX);
+  m->amax_o = ralloc<unsigned long long>(m, RMAX);
+  m->amax_h = ralloc<unsigned long long>(m, RMAX);
+  m->ticket = ralloc<unsigned int>(m, 4);
   m->head_part = ralloc<unsigned long long>(m, (size_t)m->head_grid * RMAX * 2);
   m->head_ticket = ralloc<unsigned int>(m, 1);
   m->trace = ralloc<int64_t>(m, (size_t)RMAX * m->trace_row);
@@ -220,8 +228,8 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     if (e != cudaSuccess) return e; \
   } while (0)
   if (m->fr_on) RUN(cudaMemsetAsync(m->fr_acc, 0, sizeof(unsigned long long) * m->n_lin * RMAX * 4, st));
-  if (m->emb_q16) RUN(launch_embed64(m->emb_q16, ids, R, c.D, m->x, st, false));   // general Q16 rows
-  else RUN(launch_embed(m->emb, c.emb_shift, ids, R, c.D, m->x, st, false));        // int8 rows << shift
+  RUN(launch_embed_norm(m->emb, m->emb_q16, c.emb_shift, ids, R, c.D, m->L[0].g1, m->x, m->xq, m->KMAX, m->xs,
+                        st, false));
   const int Hd = c.H * c.hd;
   AttnArgs aa;
   aa.qkv = m->qkv; aa.ldqkv = m->Nqkv; aa.row_seq = seq; aa.row_pos = pos;
@@ -245,50 +253,61 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     }
     g.fr_nseg = s;
   };
+  // Per layer, five kernels.  Every GEMV reads ready int16 rows (xq, xs); the last CTA of each
+  // producer builds them for the next GEMV:
+  //   q|k|v GEMV    tail: RoPE, K/V cache write, quantised query rows
+  //   attention     cluster per (row, KV head); tail: qrow(out) (shift from the published max)
+  //   o GEMV        x += o(...);            tail: irms(x, g2) + qrow
+  //   gate|up GEMV  h = shr(isilu(g)*u, 16); tail: qrow(h) (shift from the published max)
+  //   down GEMV     x += down(h);           tail: irms(x, next g1 or gf) + qrow
+  aa.amax_out = m->amax_o; aa.ticket = m->ticket + 1; aa.xq_out = m->xq; aa.ldq = m->KMAX; aa.xs_out = m->xs;
   for (int i = 0; i < c.NL; ++i) {
     LayerDev& Ld = m->L[i];
     const size_t kvoff = m->kv_layer_elems * i;
     aa.kc = m->kc + kvoff; aa.vc = m->vc + kvoff;
     aa.ks = m->ks + (size_t)c.max_batch * c.KV * c.max_seq * i;
-    // attention block
-    RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    auto base = [&](GemvArgs& g, const LinW& L) {
+      g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = L; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
+      g.ticket = m->ticket; g.tail_xq = m->xq; g.tail_ldq = m->KMAX; g.tail_xs = m->xs;
+    };
     {
-      GemvArgs g; g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = Ld.qkv; g.R = R; g.epi = EPI_STORE;
-      g.out = m->qkv; g.ldo = m->Nqkv; g.raw = trace_ptr(Ld.li[0]); g.ldr = (int)m->trace_row; g.err = m->err;
+      GemvArgs g; base(g, Ld.qkv);
+      g.epi = EPI_STORE; g.out = m->qkv; g.ldo = m->Nqkv; g.raw = trace_ptr(Ld.li[0]);
+      g.zero = m->amax_o; g.nzero = RMAX; g.tail = TAIL_ROPE; g.rope = aa;
       set_fr(g, {Ld.li[0], Ld.li[1], Ld.li[2]});
       RUN(launch_gemv(g, st, pdl));
     }
-    RUN(launch_rope_cache(aa, st, pdl));
     RUN(launch_attn_decode(aa, st, pdl));
-    RUN(launch_quant(m->ao, Hd, R, Hd, m->xq, m->KMAX, m->xs, st, pdl));
     {
-      GemvArgs g; g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = Ld.o; g.R = R; g.epi = EPI_RESID;
-      g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[3]); g.ldr = (int)m->trace_row; g.err = m->err;
+      GemvArgs g; base(g, Ld.o);
+      g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[3]);
+      g.zero = m->amax_h; g.nzero = RMAX;
+      g.tail = TAIL_NORM; g.tail_x = m->x; g.tail_ldx = c.D; g.tail_K = c.D; g.tail_gain = Ld.g2;
       set_fr(g, {Ld.li[3]});
       RUN(launch_gemv(g, st, pdl));
     }
-    // MLP block
-    RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     {
-      GemvArgs g; g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = Ld.gu; g.R = R; g.epi = EPI_SWIGLU;
-      g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.err = m->err;
-      g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]); g.ldr = (int)m->trace_row;
+      GemvArgs g; base(g, Ld.gu);
+      g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.amax_out = m->amax_h;
+      g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]);
+      g.tail = TAIL_QUANT; g.tail_x = m->hb; g.tail_ldx = c.I; g.tail_K = c.I; g.tail_amax = m->amax_h;
       set_fr(g, {Ld.li[4], Ld.li[5]});
       RUN(launch_gemv(g, st, pdl));
     }
-    RUN(launch_quant(m->hb, c.I, R, c.I, m->xq, m->KMAX, m->xs, st, pdl));
     {
-      GemvArgs g; g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = Ld.down; g.R = R; g.epi = EPI_RESID;
-      g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[6]); g.ldr = (int)m->trace_row; g.err = m->err;
+      GemvArgs g; base(g, Ld.down);
+      g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[6]);
+      g.tail = TAIL_NORM; g.tail_x = m->x; g.tail_ldx = c.D; g.tail_K = c.D;
+      g.tail_gain = i + 1 < c.NL ? m->L[i + 1].g1 : m->gf;
       set_fr(g, {Ld.li[6]});
       RUN(launch_gemv(g, st, pdl));
     }
   }
-  RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
   {
-    GemvArgs g; g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = m->head; g.R = R; g.epi = EPI_HEAD;
-    g.out = want_logits ? m->logits : nullptr; g.ldo = c.V; g.err = m->err;
-    g.raw = trace_ptr(m->n_lin - 1); g.ldr = (int)m->trace_row;
+    GemvArgs g;
+    g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = m->head; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
+    g.epi = EPI_HEAD; g.out = want_logits ? m->logits : nullptr; g.ldo = c.V;
+    g.raw = trace_ptr(m->n_lin - 1);
     g.head_part = m->head_part; g.head_ticket = m->head_ticket; g.next_tok = m->next_tok; g.grid = m->head_grid;
     set_fr(g, {m->n_lin - 1});
     RUN(launch_gemv(g, st, pdl));
@@ -372,14 +391,18 @@ int exb_gemv(const int16_t* x16, const int8_t* wT, const int64_t* Mg, int K, int
   return EXB_OK;
 }
 
-size_t exb_linear_g128_scratch_bytes(int R, int K) {
-  return ((size_t)R * K * sizeof(int16_t) + 255) / 256 * 256 + (size_t)R * sizeof(int32_t);
+static size_t xq_bytes(int R, int K) { return ((size_t)R * K * sizeof(int16_t) + 255) / 256 * 256; }
+static size_t xs_bytes(int R) { return ((size_t)R * sizeof(int32_t) + 255) / 256 * 256; }
+
+size_t exb_linear_g128_scratch_bytes(int R, int K, int N) {
+  const size_t ldm = (size_t)(((K / 128) + 3) & ~3);
+  return xq_bytes(R, K) + xs_bytes(R) + (size_t)N * ldm * 4;
 }
 
 static int linear_common(const int64_t* x, int R, int K, const LinW& L, int64_t* y, int64_t* raw, void* scratch,
                          cudaStream_t st, bool channel) {
   int16_t* xq = (int16_t*)scratch;
-  int32_t* xs = (int32_t*)((char*)scratch + ((size_t)R * K * sizeof(int16_t) + 255) / 256 * 256);
+  int32_t* xs = (int32_t*)((char*)scratch + xq_bytes(R, K));
   CK(launch_quant(x, K, R, K, xq, K, xs, st, false));
   for (int r0 = 0; r0 < R; r0 += RMAX) {
     const int rr = R - r0 < RMAX ? R - r0 : RMAX;
@@ -400,6 +423,16 @@ int exb_linear_g128(const int64_t* x, int R, int K, const int8_t* w_NK, const in
     FAIL(EXB_EINVAL, "exb_linear_g128: bad arguments (K % 128 == 0 required)");
   if (((uintptr_t)w_NK | (uintptr_t)scratch) & 15) FAIL(EXB_EINVAL, "exb_linear_g128: w and scratch must be 16-byte aligned");
   LinW L; L.w = w_NK; L.Mg = M_NG; L.b = bias; L.N = N; L.K = K;
+  const int G = K / 128;
+  L.ldm = G;
+  if ((G % 4) || ((uintptr_t)M_NG & 15)) {
+    // the kernel copies scale rows with 16-byte bulk copies: re-pitch them into the scratch
+    int32_t* Mp = (int32_t*)((char*)scratch + xq_bytes(R, K) + xs_bytes(R));
+    L.ldm = (G + 3) & ~3;
+    CK(cudaMemcpy2DAsync(Mp, (size_t)L.ldm * 4, M_NG, (size_t)G * 4, (size_t)G * 4, N, cudaMemcpyDeviceToDevice,
+                         (cudaStream_t)stream));
+    L.Mg = Mp;
+  }
   return linear_common(x, R, K, L, y, tot_out, scratch, (cudaStream_t)stream, false);
 }
 
@@ -437,7 +470,7 @@ int exb_model_create(const exb_config* cfg, exb_model** out) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  m->head_grid = 4 * sms;
+  m->head_grid = std::min(sms, c.V);                 // the GEMV runs one CTA per SM
   plan_weights(m);
   m->wbytes = m->woff;
   plan_lins(m);
@@ -500,10 +533,13 @@ int exb_model_set_tables(exb_model* m, const int64_t* exp_t, const int64_t* silu
   return EXB_OK;
 }
 
-// copy a logical (N, K) tensor into fused rows row0 + i*step (row pitch = elem*K bytes)
-static int put_rows(exb_model* m, void* dst_base, size_t row_bytes, int row0, int step, const void* src, int N) {
-  char* dst = (char*)dst_base + (size_t)row0 * row_bytes;
-  CK(cudaMemcpy2DAsync(dst, row_bytes * step, src, row_bytes, row_bytes, N, cudaMemcpyHostToDevice, m->st));
+// copy a logical (N x row_bytes) host tensor into fused rows row0 + i*step of a device matrix whose
+// rows are dst_row_bytes apart
+static int put_rows(exb_model* m, void* dst_base, size_t dst_row_bytes, int row0, int step, const void* src, int N,
+                    size_t row_bytes = 0, cudaMemcpyKind kind = cudaMemcpyHostToDevice) {
+  if (!row_bytes) row_bytes = dst_row_bytes;
+  char* dst = (char*)dst_base + (size_t)row0 * dst_row_bytes;
+  CK(cudaMemcpy2DAsync(dst, dst_row_bytes * step, src, row_bytes, row_bytes, N, kind, m->st));
   return EXB_OK;
 }
 
@@ -559,7 +595,7 @@ int exb_model_set_tensor(exb_model* m, const char* name_c, const void* host, siz
       } else if (part == "M") {
         if (m->group) {
           if (!need((size_t)L->N * (L->K / 128) * 4)) FAIL(EXB_EINVAL, name + ": wrong size (int32 N x K/128)");
-          return put_rows(m, (void*)F.Mg, (size_t)(L->K / 128) * 4, L->row0, L->row_step, host, L->N);
+          return put_rows(m, (void*)F.Mg, (size_t)F.ldm * 4, L->row0, L->row_step, host, L->N, (size_t)(L->K / 128) * 4);
         }
         if (!need((size_t)L->N * 8)) FAIL(EXB_EINVAL, name + ": wrong size (int64 N)");
         return put_rows(m, (void*)F.Mc, 8, L->row0, L->row_step, host, L->N);
@@ -598,8 +634,9 @@ int exb_model_generate(exb_model* m, uint64_t seed) {
     if (m->group) {
       const int G = L.K / 128;
       CK(gen_tensor(GEN_SCALE32, seed, s0 + 1, (int64_t)L.N * G, L.K, tmp, m->st));
-      CK(cudaMemcpy2DAsync((char*)F.Mg + (size_t)L.row0 * G * 4, (size_t)G * 4 * L.row_step, tmp, (size_t)G * 4,
-                           (size_t)G * 4, L.N, cudaMemcpyDeviceToDevice, m->st));
+      int rc = put_rows(m, (void*)F.Mg, (size_t)F.ldm * 4, L.row0, L.row_step, tmp, L.N, (size_t)G * 4,
+                        cudaMemcpyDeviceToDevice);
+      if (rc) return rc;
     } else {
       CK(gen_tensor(GEN_SCALE64, seed, s0 + 1, L.N, L.K, tmp, m->st));
       CK(cudaMemcpy2DAsync((char*)F.Mc + (size_t)L.row0 * 8, (size_t)8 * L.row_step, tmp, 8, 8, L.N,
@@ -790,7 +827,7 @@ int exb_freivalds_set_keys(exb_model* m, const int32_t* r_host, int64_t n) {
     CK(cudaMemcpyAsync(L.fr_r, r_host + pos, sizeof(int32_t) * 2 * L.N, cudaMemcpyHostToDevice, m->st));
     pos += 2 * L.N;
     const LinW& F = *L.fused;
-    CK(launch_fr_keys(F.w, F.Mg, L.N, L.K, L.row0, L.row_step, L.fr_r, L.fr_d, m->st));
+    CK(launch_fr_keys(F.w, F.Mg, F.ldm, L.N, L.K, L.row0, L.row_step, L.fr_r, L.fr_d, m->st));
     L.fr_acc = acc_base + (size_t)idx * RMAX * 4;
     ++idx;
   }

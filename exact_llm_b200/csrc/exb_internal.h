@@ -14,7 +14,8 @@ int64_t isqrt_host(int64_t n);
 // scales (N,).  For a fused SwiGLU pair the rows are interleaved: row 2j = gate j, 2j+1 = up j.
 struct LinW {
   const int8_t* w = nullptr;
-  const int32_t* Mg = nullptr;     // group-128 scales (N, K/128) or nullptr
+  const int32_t* Mg = nullptr;     // group-128 scales (N, ldm), ldm >= K/128, rows 16-byte aligned
+  int ldm = 0;                     // row pitch of Mg in int32 (a multiple of 4)
   const int64_t* Mc = nullptr;     // per-channel scales (N) or nullptr
   const int64_t* b = nullptr;      // bias (N) Q16 or nullptr
   int N = 0, K = 0;
@@ -22,6 +23,27 @@ struct LinW {
   bool nodrop = true;              // per-channel: the drop rule can never trigger (host-proven)
 };
 
+// attention
+struct AttnArgs {
+  const int64_t* qkv = nullptr; int ldqkv = 0;  // (R, (H + 2KV) hd) projected q|k|v (before RoPE)
+  const int32_t* row_seq = nullptr;             // (R) sequence slot of each row
+  const int32_t* row_pos = nullptr;             // (R) absolute position of each row
+  const int32_t* cos_t = nullptr;               // (Tmax, hd/2) Q16
+  const int32_t* sin_t = nullptr;
+  int16_t* kc = nullptr;                        // K cache (B, KV, Smax, hd) int16 (this layer)
+  int8_t* ks = nullptr;                         // K shifts (B, KV, Smax)
+  int32_t* vc = nullptr;                        // V cache (B, KV, Smax, hd) int32
+  int16_t* qq = nullptr;                        // (R, H, hd) quantised roped q
+  int32_t* qs = nullptr;                        // (R, H) q shifts
+  const int32_t* exp_t = nullptr;
+  int64_t* out = nullptr; int ldo = 0;          // (R, H*hd)
+  int R = 0, H = 0, KV = 0, hd = 0, Smax = 0, Tmax = 0;
+  int64_t inv = 0;                              // round(2^16 / sqrt(hd))
+  unsigned long long* amax_out = nullptr;       // per-row max |out| (atomicMax), for the next qrow
+  unsigned int* ticket = nullptr;
+  int16_t* xq_out = nullptr; int ldq = 0; int32_t* xs_out = nullptr;   // last CTA: qrow(out) rows
+  int* err = nullptr;
+};
 enum Epi {
   EPI_STORE = 0,     // out[r, n] = requant(tot)
   EPI_RESID = 1,     // out[r, n] += requant(tot)       (residual add)
@@ -30,10 +52,28 @@ enum Epi {
   EPI_HEAD = 4,      // out[r, n] = requant(acc) (optional) + greedy argmax per row
 };
 
+// Work done by the LAST CTA of a GEMV to finish (elected with an atomic ticket, no spinning):
+// it turns the kernel's complete output rows into the int16 input rows of the next GEMV.
+enum Tail {
+  TAIL_NONE = 0,
+  TAIL_NORM = 1,     // xq, s = qrow(irms(tail_x, tail_gain))      (after a residual add)
+  TAIL_QUANT = 2,    // xq = clip(shr(tail_x, s)), s from tail_amax (published by this kernel)
+  TAIL_ROPE = 3,     // RoPE + KV-cache write + query rows (after the q|k|v GEMV)
+};
+
 struct GemvArgs {
-  const int16_t* xq = nullptr;     // (R, ldx) int16 activations
-  const int32_t* xs = nullptr;     // (R) qrow shifts
+  const int16_t* xq = nullptr;     // XIN_Q16: (R, ldx) int16 activations
+  const int32_t* xs = nullptr;     // XIN_Q16: (R) qrow shifts
   int ldx = 0;
+  unsigned long long* amax_out = nullptr;       // epilogue: per-row max |output| (atomicMax)
+  unsigned long long* zero = nullptr; int nzero = 0;   // CTA 0 clears these words (for a later producer)
+  int tail = TAIL_NONE;
+  unsigned int* ticket = nullptr;
+  const int64_t* tail_x = nullptr; int tail_ldx = 0; int tail_K = 0;
+  const int64_t* tail_gain = nullptr;
+  const unsigned long long* tail_amax = nullptr;
+  int16_t* tail_xq = nullptr; int tail_ldq = 0; int32_t* tail_xs = nullptr;
+  AttnArgs rope;
   LinW L;
   int R = 1;
   int epi = EPI_STORE;
@@ -60,6 +100,7 @@ struct GemvArgs {
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl);
+int gemv_grid(int N, bool swiglu);
 cudaError_t launch_gemv_op(const int16_t* x16, const int8_t* wT, const int64_t* Mg, int K, int N, int64_t* out,
                            cudaStream_t st);
 
@@ -75,28 +116,14 @@ cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, i
 cudaError_t launch_requant_channel(const int64_t* acc, int ld, int R, const LinW& L, int64_t* out, int ldo,
                                    const int32_t* xs, int epi, cudaStream_t st, bool pdl);
 
-// attention
-struct AttnArgs {
-  const int64_t* qkv = nullptr; int ldqkv = 0;  // (R, (H + 2KV) hd) projected q|k|v (before RoPE)
-  const int32_t* row_seq = nullptr;             // (R) sequence slot of each row
-  const int32_t* row_pos = nullptr;             // (R) absolute position of each row
-  const int32_t* cos_t = nullptr;               // (Tmax, hd/2) Q16
-  const int32_t* sin_t = nullptr;
-  int16_t* kc = nullptr;                        // K cache (B, KV, Smax, hd) int16 (this layer)
-  int8_t* ks = nullptr;                         // K shifts (B, KV, Smax)
-  int32_t* vc = nullptr;                        // V cache (B, KV, Smax, hd) int32
-  int16_t* qq = nullptr;                        // (R, H, hd) quantised roped q
-  int32_t* qs = nullptr;                        // (R, H) q shifts
-  const int32_t* exp_t = nullptr;
-  int64_t* out = nullptr; int ldo = 0;          // (R, H*hd)
-  int R = 0, H = 0, KV = 0, hd = 0, Smax = 0, Tmax = 0;
-  int64_t inv = 0;                              // round(2^16 / sqrt(hd))
-  int* err = nullptr;
-};
 cudaError_t launch_rope_cache(const AttnArgs& a, cudaStream_t st, bool pdl);
+// attention; when xq_out is set, the last CTA also writes qrow(out) (shift from amax_out)
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_embed_norm(const int8_t* emb, const int64_t* emb_q16, int emb_shift, const int32_t* ids, int R,
+                              int D, const int64_t* g, int64_t* x, int16_t* xq, int ldq, int32_t* xs,
+                              cudaStream_t st, bool pdl);
 
-cudaError_t launch_fr_keys(const int8_t* w, const int32_t* Mg, int N, int K, int row0, int row_step,
+cudaError_t launch_fr_keys(const int8_t* w, const int32_t* Mg, int ldm, int N, int K, int row0, int row_step,
                            const int32_t* r, int32_t* d, cudaStream_t st);
 cudaError_t launch_fr_check(const unsigned long long* acc, int nchecks, int* fail_count, int* err,
                             cudaStream_t st, bool pdl);

@@ -5,6 +5,7 @@
 // QLin requant + per-row drop rule :89-96 (SPEC.md:28), embedding rows :163.
 #include "common.cuh"
 #include "exb_internal.h"
+#include "rowdev.cuh"
 
 namespace exb {
 
@@ -56,49 +57,58 @@ cudaError_t launch_embed64(const int64_t* emb, const int32_t* ids, int R, int D,
   return launch_simple((const void*)k_embed64, dim3(R), dim3(256), 0, st, pdl, args);
 }
 
-// ---------------------------------------------------------------- irms + qrow
-// a = irms(x, g) (exact_llm.py:100-106), then xq, s = qrow(a) (:41-46).
+// ---------------------------------------------------------------- embedding + first irms/qrow
+// x = emb[id] (int8 << shift, or general int64 Q16 rows); xq, s = qrow(irms(x, g)).
+__global__ void __launch_bounds__(ROW_THREADS) k_embed_norm(const int8_t* __restrict__ emb,
+                                                            const int64_t* __restrict__ emb_q16, int shift,
+                                                            const int32_t* __restrict__ ids, int D,
+                                                            const int64_t* __restrict__ g, int64_t* __restrict__ x,
+                                                            int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs) {
+  extern __shared__ int64_t ys[];
+  __shared__ uint64_t red[33];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int r = blockIdx.x;
+  const size_t row = (size_t)ids[r] * D;
+  uint64_t m = 0;
+  for (int i = threadIdx.x; i < D; i += ROW_THREADS) {
+    const int64_t v = emb_q16 ? emb_q16[row + i] : (int64_t)emb[row + i] << shift;
+    ys[i] = v;
+    x[(size_t)r * D + i] = v;
+    const uint64_t a = uabs64(v);
+    m = a > m ? a : m;
+  }
+  row_norm_q_staged<ROW_THREADS>(g, D, xq + (size_t)r * ldq, xs + r, ys, red, m);
+}
+
+cudaError_t launch_embed_norm(const int8_t* emb, const int64_t* emb_q16, int emb_shift, const int32_t* ids, int R,
+                              int D, const int64_t* g, int64_t* x, int16_t* xq, int ldq, int32_t* xs,
+                              cudaStream_t st, bool pdl) {
+  const size_t smem = (size_t)D * 8;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_embed_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  void* args[] = {(void*)&emb, (void*)&emb_q16, (void*)&emb_shift, (void*)&ids, (void*)&D, (void*)&g, (void*)&x,
+                  (void*)&xq, (void*)&ldq, (void*)&xs};
+  return launch_simple((const void*)k_embed_norm, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
+}
+
+// ---------------------------------------------------------------- irms + qrow, qrow (one CTA per row)
 __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restrict__ x, int ldx,
                                                         const int64_t* __restrict__ g, int D,
                                                         int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs) {
   extern __shared__ int64_t ys[];
   __shared__ uint64_t red[33];
   pdl_wait();
-  const int r = blockIdx.x;
-  const int64_t* xr = x + (size_t)r * ldx;
-  uint64_t m = 0;
-  for (int i = threadIdx.x; i < D; i += ROW_THREADS) { uint64_t v = uabs64(xr[i]); m = v > m ? v : m; }
-  m = block_max_u64<ROW_THREADS>(m, red);
-  int k = bitlen64(m) - 24;
-  k = k > 0 ? k : 0;
-  uint64_t ss = 0;
-  for (int i = threadIdx.x; i < D; i += ROW_THREADS) {
-    const int64_t v = shr64(xr[i], k);
-    ss += (uint64_t)v * (uint64_t)v;
-  }
-  const int64_t sum = block_sum_i64<ROW_THREADS>((int64_t)ss, red);
-  const int64_t ms = floordiv64(sum, D) + 1;
-  int64_t rt = isqrt_ref(ms);
-  rt = rt > 1 ? rt : 1;
-  const int64_t den = (int64_t)((uint64_t)rt << k);
-  uint64_t m2 = 0;
-  for (int i = threadIdx.x; i < D; i += ROW_THREADS) {
-    const int64_t y = floordiv64((int64_t)((uint64_t)xr[i] << 16), den);
-    const int64_t a = shr64((int64_t)((uint64_t)y * (uint64_t)g[i]), 16);
-    ys[i] = a;
-    const uint64_t v = uabs64(a);
-    m2 = v > m2 ? v : m2;
-  }
-  m2 = block_max_u64<ROW_THREADS>(m2, red);
-  const int s = qrow_shift(m2);
-  for (int i = threadIdx.x; i < D; i += ROW_THREADS) xq[(size_t)r * ldq + i] = qrow_value(ys[i], s);
-  if (threadIdx.x == 0) xs[r] = s;
   pdl_launch_dependents();
+  const int r = blockIdx.x;
+  row_norm_q<ROW_THREADS>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, ys, red);
 }
 
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
                           int32_t* xs, cudaStream_t st, bool pdl) {
-  const size_t smem = (size_t)D * 8;
+  const size_t smem = (size_t)D * 16;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_norm_q, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -107,26 +117,26 @@ cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, in
   return launch_simple((const void*)k_norm_q, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
 }
 
-// ---------------------------------------------------------------- qrow only
 __global__ void __launch_bounds__(ROW_THREADS) k_quant(const int64_t* __restrict__ x, int ldx, int K,
                                                        int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs) {
+  extern __shared__ int64_t ys[];
   __shared__ uint64_t red[33];
   pdl_wait();
-  const int r = blockIdx.x;
-  const int64_t* xr = x + (size_t)r * ldx;
-  uint64_t m = 0;
-  for (int i = threadIdx.x; i < K; i += ROW_THREADS) { uint64_t v = uabs64(xr[i]); m = v > m ? v : m; }
-  m = block_max_u64<ROW_THREADS>(m, red);
-  const int s = qrow_shift(m);
-  for (int i = threadIdx.x; i < K; i += ROW_THREADS) xq[(size_t)r * ldq + i] = qrow_value(xr[i], s);
-  if (threadIdx.x == 0) xs[r] = s;
   pdl_launch_dependents();
+  const int r = blockIdx.x;
+  row_quant<ROW_THREADS>(x + (size_t)r * ldx, K, xq + (size_t)r * ldq, xs + r, ys, red);
 }
 
 cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, int ldq, int32_t* xs,
                          cudaStream_t st, bool pdl) {
+  const size_t smem = (size_t)K * 8;
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
   void* args[] = {(void*)&x, (void*)&ldx, (void*)&K, (void*)&xq, (void*)&ldq, (void*)&xs};
-  return launch_simple((const void*)k_quant, dim3(R), dim3(ROW_THREADS), 0, st, pdl, args);
+  return launch_simple((const void*)k_quant, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
 }
 
 // ---------------------------------------------------------------- per-channel requant, general drop rule

@@ -56,15 +56,15 @@ int exb_gemv(const int16_t* x16, const int8_t* wT, const int64_t* Mg, int K, int
 /* GQLin.__call__ (experiments/speed_fair_kaggle.py:722-725) on R rows of device int64 Q16 input:
  * xq, s = qrow(x); tot = sum_g M_g (xq_g . W_g); y = shr(tot, 28 - s) + b.
  * w_NK int8 (N, K); M_NG int32 (N, K/128); bias int64 (N) or NULL; y int64 (R, N);
- * tot_out int64 (R, N) or NULL.  `scratch` holds R*K int16 + R int32 device bytes
- * (exb_linear_g128_scratch_bytes). */
-size_t exb_linear_g128_scratch_bytes(int R, int K);
+ * tot_out int64 (R, N) or NULL.  `scratch` = exb_linear_g128_scratch_bytes(R, K, N) device bytes
+ * (quantised rows, shifts, and a 16-byte-pitched copy of the scales when K/128 is not a multiple of 4). */
+size_t exb_linear_g128_scratch_bytes(int R, int K, int N);
 int exb_linear_g128(const int64_t* x, int R, int K, const int8_t* w_NK, const int32_t* M_NG, const int64_t* bias,
                     int N, int64_t* y, int64_t* tot_out, void* scratch, void* stream);
 
 /* QLin.__call__ (exact_llm.py:89-96) with the per-row drop rule, on device buffers.
  * w_NK int8 (N, K); M int64 (N); acc_out int64 (R, N) is required (the drop rule needs the
- * whole row); scratch as for exb_linear_g128. */
+ * whole row); scratch of exb_linear_g128_scratch_bytes(R, K, 0) bytes. */
 int exb_linear_channel(const int64_t* x, int R, int K, const int8_t* w_NK, const int64_t* M, const int64_t* bias,
                        int N, int64_t* y, int64_t* acc_out, void* scratch, void* stream);
 

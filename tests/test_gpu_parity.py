@@ -88,7 +88,7 @@ def test_linear_config2(golden, torch_cuda, K, N):
         x = torch.from_numpy(np.random.default_rng(seed).integers(-128, 128, (R, K)).astype(np.int64)).cuda()
         y = torch.empty((R, N), dtype=torch.int64, device="cuda")
         tot = torch.empty((R, N), dtype=torch.int64, device="cuda")
-        scratch = torch.empty(L.lib.exb_linear_g128_scratch_bytes(R, K), dtype=torch.uint8, device="cuda")
+        scratch = torch.empty(L.lib.exb_linear_g128_scratch_bytes(R, K, N), dtype=torch.uint8, device="cuda")
         L.check(L.lib.exb_linear_g128(L.ptr(x), R, K, L.ptr(w), L.ptr(M), None, N, L.ptr(y), L.ptr(tot),
                                       L.ptr(scratch), _stream(torch)))
         yh, th = y.cpu().numpy(), tot.cpu().numpy()
@@ -117,7 +117,7 @@ def test_linear_channel_drop_rule(torch_cuda, scale_bits):
     xd, wd, Md, bd = (torch.from_numpy(a).cuda() for a in (x, w, M, b))
     y = torch.empty((R, N), dtype=torch.int64, device="cuda")
     acc = torch.empty((R, N), dtype=torch.int64, device="cuda")
-    scratch = torch.empty(L.lib.exb_linear_g128_scratch_bytes(R, K), dtype=torch.uint8, device="cuda")
+    scratch = torch.empty(L.lib.exb_linear_g128_scratch_bytes(R, K, 0), dtype=torch.uint8, device="cuda")
     L.check(L.lib.exb_linear_channel(L.ptr(xd), R, K, L.ptr(wd), L.ptr(Md), L.ptr(bd), N, L.ptr(y), L.ptr(acc),
                                      L.ptr(scratch), _stream(torch)))
     assert np.array_equal(acc.cpu().numpy(), acc_want)
