@@ -211,8 +211,14 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   void (*kern)(const AttnArgs, int) = a.hd == 128 ? k_attn_decode<128> : a.hd == 64 ? k_attn_decode<64>
                                     : a.hd == 32 ? k_attn_decode<32> : k_attn_decode<16>;
   if (a.hd != 128 && a.hd != 64 && a.hd != 32 && a.hd != 16) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+  // raised once to the full budget and never lowered (see the GEMV launcher)
+  static bool attr_set[4] = {false, false, false, false};
+  const int ti = a.hd == 128 ? 0 : a.hd == 64 ? 1 : a.hd == 32 ? 2 : 3;
+  if (!attr_set[ti]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set[ti] = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CL, a.KV, a.R);
   cfg.blockDim = dim3(ATT_THREADS);

@@ -217,19 +217,27 @@ static void plan_runtime(exb_model* m) {
 // One forward pass of R (<= RMAX) rows through every layer and the head.  Rows read their token,
 // sequence slot and position from device arrays, so the enqueued work is identical for every
 // step and can be captured once into a CUDA graph.
+static std::vector<cudaEvent_t>* g_prof = nullptr;   // profiling: an event after every launch
+
 static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const int32_t* seq, const int32_t* pos,
                                 bool want_logits, cudaStream_t st) {
   const exb_config& c = m->c;
-  const bool pdl = m->pdl;
+  const bool pdl = m->pdl && !g_prof;
   cudaError_t e;
-#define RUN(x)                     \
-  do {                             \
-    e = (x);                       \
-    if (e != cudaSuccess) return e; \
+#define RUN(x)                                                    \
+  do {                                                            \
+    e = (x);                                                      \
+    if (e != cudaSuccess) return e;                               \
+    if (g_prof) {                                                 \
+      cudaEvent_t ev;                                             \
+      cudaEventCreate(&ev);                                       \
+      cudaEventRecord(ev, st);                                    \
+      g_prof->push_back(ev);                                      \
+    }                                                             \
   } while (0)
   if (m->fr_on) RUN(cudaMemsetAsync(m->fr_acc, 0, sizeof(unsigned long long) * m->n_lin * RMAX * 4, st));
-  RUN(launch_embed_norm(m->emb, m->emb_q16, c.emb_shift, ids, R, c.D, m->L[0].g1, m->x, m->xq, m->KMAX, m->xs,
-                        st, false));
+  if (m->emb_q16) RUN(launch_embed64(m->emb_q16, ids, R, c.D, m->x, st, false));   // general Q16 rows
+  else RUN(launch_embed(m->emb, c.emb_shift, ids, R, c.D, m->x, st, false));        // int8 rows << shift
   const int Hd = c.H * c.hd;
   AttnArgs aa;
   aa.qkv = m->qkv; aa.ldqkv = m->Nqkv; aa.row_seq = seq; aa.row_pos = pos;
@@ -253,59 +261,61 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     }
     g.fr_nseg = s;
   };
-  // Per layer, five kernels.  Every GEMV reads ready int16 rows (xq, xs); the last CTA of each
-  // producer builds them for the next GEMV:
-  //   q|k|v GEMV    tail: RoPE, K/V cache write, quantised query rows
-  //   attention     cluster per (row, KV head); tail: qrow(out) (shift from the published max)
-  //   o GEMV        x += o(...);            tail: irms(x, g2) + qrow
-  //   gate|up GEMV  h = shr(isilu(g)*u, 16); tail: qrow(h) (shift from the published max)
-  //   down GEMV     x += down(h);           tail: irms(x, next g1 or gf) + qrow
-  aa.amax_out = m->amax_o; aa.ticket = m->ticket + 1; aa.xq_out = m->xq; aa.ldq = m->KMAX; aa.xs_out = m->xs;
+  // Per layer: every GEMV builds its own int16 input rows in its prologue (in parallel in every
+  // CTA, overlapping the L2 prefetch of its weights); producers publish per-row maxima for qrow.
+  //   q|k|v GEMV    in: irms(x, g1) + qrow
+  //   rope/cache    RoPE, K/V cache write, quantised query rows
+  //   attention     cluster per (row, KV head); publishes max |out| per row
+  //   o GEMV        in: qrow(out);            x += o(...)
+  //   gate|up GEMV  in: irms(x, g2) + qrow;  h = shr(isilu(g)*u, 16), publishes max |h| per row
+  //   down GEMV     in: qrow(h);              x += down(h)
+  aa.amax_out = m->amax_o;
   for (int i = 0; i < c.NL; ++i) {
     LayerDev& Ld = m->L[i];
     const size_t kvoff = m->kv_layer_elems * i;
     aa.kc = m->kc + kvoff; aa.vc = m->vc + kvoff;
     aa.ks = m->ks + (size_t)c.max_batch * c.KV * c.max_seq * i;
     auto base = [&](GemvArgs& g, const LinW& L) {
-      g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = L; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
-      g.ticket = m->ticket; g.tail_xq = m->xq; g.tail_ldq = m->KMAX; g.tail_xs = m->xs;
+      g.L = L; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
     };
     {
       GemvArgs g; base(g, Ld.qkv);
+      g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g1;
       g.epi = EPI_STORE; g.out = m->qkv; g.ldo = m->Nqkv; g.raw = trace_ptr(Ld.li[0]);
-      g.zero = m->amax_o; g.nzero = RMAX; g.tail = TAIL_ROPE; g.rope = aa;
+      g.zero = m->amax_o; g.nzero = RMAX;
       set_fr(g, {Ld.li[0], Ld.li[1], Ld.li[2]});
       RUN(launch_gemv(g, st, pdl));
     }
+    RUN(launch_rope_cache(aa, st, pdl));
     RUN(launch_attn_decode(aa, st, pdl));
     {
       GemvArgs g; base(g, Ld.o);
+      g.xin = XIN_QUANT; g.x64 = m->ao; g.ldx64 = Hd; g.amax_in = m->amax_o;
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[3]);
       g.zero = m->amax_h; g.nzero = RMAX;
-      g.tail = TAIL_NORM; g.tail_x = m->x; g.tail_ldx = c.D; g.tail_K = c.D; g.tail_gain = Ld.g2;
       set_fr(g, {Ld.li[3]});
       RUN(launch_gemv(g, st, pdl));
     }
     {
       GemvArgs g; base(g, Ld.gu);
+      g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g2;
       g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.amax_out = m->amax_h;
       g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]);
-      g.tail = TAIL_QUANT; g.tail_x = m->hb; g.tail_ldx = c.I; g.tail_K = c.I; g.tail_amax = m->amax_h;
       set_fr(g, {Ld.li[4], Ld.li[5]});
       RUN(launch_gemv(g, st, pdl));
     }
     {
       GemvArgs g; base(g, Ld.down);
+      g.xin = XIN_QUANT; g.x64 = m->hb; g.ldx64 = c.I; g.amax_in = m->amax_h;
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[6]);
-      g.tail = TAIL_NORM; g.tail_x = m->x; g.tail_ldx = c.D; g.tail_K = c.D;
-      g.tail_gain = i + 1 < c.NL ? m->L[i + 1].g1 : m->gf;
       set_fr(g, {Ld.li[6]});
       RUN(launch_gemv(g, st, pdl));
     }
   }
   {
     GemvArgs g;
-    g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX; g.L = m->head; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
+    g.L = m->head; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
+    g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = m->gf;
     g.epi = EPI_HEAD; g.out = want_logits ? m->logits : nullptr; g.ldo = c.V;
     g.raw = trace_ptr(m->n_lin - 1);
     g.head_part = m->head_part; g.head_ticket = m->head_ticket; g.next_tok = m->next_tok; g.grid = m->head_grid;
@@ -470,7 +480,7 @@ int exb_model_create(const exb_config* cfg, exb_model** out) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  m->head_grid = std::min(sms, c.V);                 // the GEMV runs one CTA per SM
+  m->head_grid = std::min(2 * sms, (c.V + 3) / 4);   // the GEMV runs two CTAs per SM
   plan_weights(m);
   m->wbytes = m->woff;
   plan_lins(m);
@@ -917,6 +927,38 @@ int exb_bench_linear(exb_model* m, int layer, int which, int R, int reps, float*
     *bytes = b;
   }
   return EXB_OK;
+}
+
+int exb_profile_step(exb_model* m, int B, float* ms_out, int max_n, int* n_out) {
+  if (!m || !m->finalized || B < 1 || B > RMAX || !ms_out || !n_out) FAIL(EXB_EINVAL, "exb_profile_step: bad arguments");
+  std::vector<int32_t> h(3 * RMAX, 0);
+  for (int b = 0; b < B; ++b) { h[b] = 0; h[RMAX + b] = b; h[2 * RMAX + b] = m->seq_len[b]; }
+  for (int b = 0; b < B; ++b)
+    if (m->seq_len[b] >= m->c.max_seq) FAIL(EXB_EINVAL, "exb_profile_step: sequence full");
+  CK(cudaMemcpyAsync(m->row_ids, h.data(), sizeof(int32_t) * 3 * RMAX, cudaMemcpyHostToDevice, m->st));
+  std::vector<cudaEvent_t> evs;
+  cudaEvent_t e0;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventRecord(e0, m->st));
+  g_prof = &evs;
+  cudaError_t e = enqueue_step(m, B, m->row_ids, m->row_seq, m->row_pos, false, m->st);
+  g_prof = nullptr;
+  CK(cudaStreamSynchronize(m->st));
+  int n = 0;
+  cudaEvent_t prev = e0;
+  for (auto ev : evs) {
+    float ms = 0;
+    cudaEventElapsedTime(&ms, prev, ev);
+    if (n < max_n) ms_out[n] = ms;
+    ++n;
+    if (prev != e0) cudaEventDestroy(prev);
+    prev = ev;
+  }
+  if (prev != e0) cudaEventDestroy(prev);
+  cudaEventDestroy(e0);
+  *n_out = n;
+  if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("profile step: ") + cudaGetErrorString(e));
+  return check_device_errors(m);   // the step wrote position seq_len (not advanced): harmless
 }
 
 void* exb_model_stream(exb_model* m) { return m ? (void*)m->st : nullptr; }

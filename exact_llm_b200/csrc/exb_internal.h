@@ -61,10 +61,22 @@ enum Tail {
   TAIL_ROPE = 3,     // RoPE + KV-cache write + query rows (after the q|k|v GEMV)
 };
 
+// How a GEMV obtains its int16 activation rows (every CTA stages all R rows in shared memory).
+enum XIn {
+  XIN_Q16 = 0,       // xq (R, ldx) int16 + shifts xs (R), already quantised
+  XIN_NORM = 1,      // x64 rows: xq, s = qrow(irms(x, gain))          (every CTA computes it)
+  XIN_QUANT = 2,     // x64 rows: xq = clip(shr(x, s)), s from the producer's published max |x|
+};
+
 struct GemvArgs {
   const int16_t* xq = nullptr;     // XIN_Q16: (R, ldx) int16 activations
   const int32_t* xs = nullptr;     // XIN_Q16: (R) qrow shifts
   int ldx = 0;
+  int xin = XIN_Q16;
+  const int64_t* x64 = nullptr; int ldx64 = 0;  // XIN_NORM / XIN_QUANT source rows (int64 Q16)
+  const int64_t* gain = nullptr;                // XIN_NORM gains
+  const unsigned long long* amax_in = nullptr;  // XIN_QUANT per-row max |x|
+  int rb = 0;                                   // columns per warp block (0: chosen by the launcher)
   unsigned long long* amax_out = nullptr;       // epilogue: per-row max |output| (atomicMax)
   unsigned long long* zero = nullptr; int nzero = 0;   // CTA 0 clears these words (for a later producer)
   int tail = TAIL_NONE;

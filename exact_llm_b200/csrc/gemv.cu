@@ -8,32 +8,29 @@
 // capture, Freivalds left/right-hand sides) and an optional last-CTA tail that builds the next
 // GEMV's int16 input rows (RMSNorm + qrow, qrow, or RoPE + KV-cache write).
 //
-// B200 design: one CTA per SM.  Every CTA owns a contiguous range of output columns, i.e. one
-// contiguous range of weight bytes (weights are (N, K) row-major, one K-byte row per column),
-// cut into stages of a few columns.  Each of the 8 warps owns every 8th stage and its own slots of
-// a shared-memory ring: it streams its stages with bulk asynchronous copies (cp.async.bulk,
-// completion counted on an mbarrier per slot) -- weight rows and their group scales in one
-// transaction -- so HBM traffic needs no registers, warps never wait on each other, and the
-// first stages are requested before the programmatic-dependent-launch wait (weights never depend
-// on the previous kernel).  Lane l handles the 16-byte chunks l, l+32, ... of a column: 16 MACs =
-// 8 dp2a (int16 x int8 -> int32, exact since 16 * 32767 * 127 < 2^31), each chunk's int32 times
-// its group scale into an int64 lane total, lanes combined by 64-bit shuffles; then lane u runs
-// the epilogue of the stage's column u, so epilogue latencies overlap.  Integer addition is
-// associative, so this order gives the reference's modulo-2^64 int64 result bit for bit.  Every
-// mbarrier wait is bounded.
+// B200 design (from a read-bandwidth calibration on this pool: plain 128-bit loads from 2 CTAs x
+// 512 threads per SM stream HBM at ~98% of the measured copy peak, bulk-copy rings at ~85%):
+// every CTA owns a contiguous range of output columns = one contiguous range of weight bytes
+// (weights are (N, K) row-major, one K-byte row per column).  Each warp takes blocks of RB
+// columns; lane l loads the 16-byte chunks l, l+32, ... of a column in batches of up to 8
+// independent 128-bit non-allocating loads (their group scales alongside), computes 16 MACs per
+// chunk as 8 dp2a (int16 x int8 -> int32, exact since 16 * 32767 * 127 < 2^31) against the int16
+// activations in shared memory, and multiplies each chunk's int32 by its group scale into an int64
+// lane partial.  The RB columns' partials are combined across the warp by recursive halving
+// (RB - 1 + 5 - log2 RB 64-bit shuffles instead of 5 RB), which leaves column b's total in lane
+// b * 32/RB, and those RB lanes run the epilogues in parallel.  The CTA's first weight bytes are
+// prefetched into L2 before the programmatic-dependent-launch wait.  Integer addition is
+// associative, so this order gives the reference's modulo-2^64 int64 result bit for bit.
 #include "common.cuh"
 #include "exb_internal.h"
 #include "rowdev.cuh"
 
 namespace exb {
 
-constexpr int NCW = 8;                          // warps; each streams and consumes its own stages
-constexpr int XREG_CHUNKS = 8;                  // K <= 32 * 16 * 8 = 4096: activations live in registers
-constexpr int L2_AHEAD = 2;                     // ring generations prefetched into L2 ahead of the copies
-constexpr int GEMV_THREADS = 32 * NCW;
-constexpr int STAGE_BYTES = 24 * 1024;          // target weight bytes per stage
-constexpr int MAX_STAGES = 32;
-constexpr int BAR_BYTES = MAX_STAGES * 8;       // full[] mbarriers at the start of shared memory
+constexpr int NCW = 16;                         // warps per CTA
+constexpr int GEMV_THREADS = 32 * NCW;          // 2 CTAs per SM (64 registers per thread)
+constexpr int PREFETCH_BYTES = 64 * 1024;       // per-CTA L2 prefetch before the PDL wait
+constexpr int DYN_SMEM_MAX = 200 * 1024;        // dynamic shared memory budget of one CTA
 
 EXB_DEV int4 ldg_stream(const int4* p) {
   int4 v;
@@ -69,17 +66,21 @@ EXB_DEV int64_t requant1(const LinW& L, int n, int64_t tot, int s) {
   return y;
 }
 
-struct GemvPlan {        // host-computed stage geometry (passed by value)
-  int SR;                // weight rows per stage (multiple of RPU)
-  int NS;                // stages in the ring
-  int stage_bytes;       // bytes per ring slot (weights + scales, 128-aligned)
-  int xs_bytes;          // bytes of the staged int16 activations (128-aligned)
+// Per-(epilogue lane, activation row) accumulators, kept in shared memory to spare registers.
+struct EpiState {
+  unsigned long long frl[3][2];   // Freivalds left-hand side residue sums (segment, prime)
+  uint64_t omax;                  // max |output| (SwiGLU)
+  int64_t best_v;                 // greedy argmax value / index
+  int best_n;
 };
 
 // Epilogue of one output unit (1 column, or a gate/up pair) for activation row r.
 template <int RPU>
-EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, int sh, uint64_t& omax,
-                           unsigned long long (&frl)[3][2], int64_t& best_v, int& best_n) {
+EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, int sh, EpiState& E) {
+  uint64_t& omax = E.omax;
+  unsigned long long (&frl)[3][2] = E.frl;
+  int64_t& best_v = E.best_v;
+  int& best_n = E.best_n;
   if (RPU == 2) {
     // SwiGLU pair: fused row 2u = gate u, 2u + 1 = up u (exact_llm.py:179)
     const int64_t yg = requant1(a.L, 2 * ug, t2[0], sh);
@@ -127,232 +128,196 @@ EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, 
   }
 }
 
-template <int R, int RPU, bool GROUP, bool XREG>
-__global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const GemvArgs a, const GemvPlan P) {
+// Sum V int64 values over the warp by recursive halving; payload of P int64 per value.
+// On return lane l holds the totals of value (l / (32 / V)).
+template <int V, int P>
+EXB_DEV void warp_reduce_halving(int64_t (&v)[V][P]) {
+  const int lane = threadIdx.x & 31;
+  int cnt = V;
+#pragma unroll
+  for (int step = 16; step >= 1; step >>= 1) {
+    if (cnt > 1) {
+      const int half = cnt >> 1;
+      const bool upper = (lane & step) != 0;
+#pragma unroll
+      for (int i = 0; i < V / 2; ++i) {
+        if (i < half) {
+#pragma unroll
+          for (int p = 0; p < P; ++p) {
+            const int64_t send = upper ? v[i][p] : v[i + half][p];
+            const int64_t keep = upper ? v[i + half][p] : v[i][p];
+            v[i][p] = (int64_t)((uint64_t)keep + (uint64_t)__shfl_xor_sync(0xffffffffu, send, step));
+          }
+        }
+      }
+      cnt = half;
+    } else {
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+        v[0][p] = (int64_t)((uint64_t)v[0][p] + (uint64_t)__shfl_xor_sync(0xffffffffu, v[0][p], step));
+    }
+  }
+}
+
+template <int R, int RPU, bool GROUP, int RB>
+__global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);                 // [MAX_STAGES]
-  int16_t* xs = reinterpret_cast<int16_t*>(smem_raw + BAR_BYTES);         // R x K int16
-  unsigned char* ring = smem_raw + BAR_BYTES + P.xs_bytes;                // NS x stage_bytes
+  int16_t* xs = reinterpret_cast<int16_t*>(smem_raw);                    // R x K int16 (tail: D int64 x 2)
   __shared__ unsigned long long red[NCW][R][6];
   __shared__ unsigned long long head_best[NCW][R][2];
   __shared__ uint64_t rred[33];
   __shared__ int sh_s[R];
-  __shared__ int abort_flag;
+  __shared__ EpiState est[NCW][RB][R];
+  constexpr int CPL = RB == 1 ? 8 : 4;              // chunks per lane per load batch
+  constexpr int PAY = R * RPU;                      // int64 totals per column block entry
 
   const int K = a.L.K, C = K >> 4, ldm = a.L.ldm;
   const int units = a.L.N / RPU;
   const int ulo = (int)((int64_t)units * blockIdx.x / gridDim.x);
   const int uhi = (int)((int64_t)units * (blockIdx.x + 1) / gridDim.x);
-  const int row0 = ulo * RPU, nrows = (uhi - ulo) * RPU;
-  const int nst = (nrows + P.SR - 1) / P.SR;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nact = P.NS < NCW ? P.NS : NCW;         // warps that stream (all, unless the ring is tiny)
-  const int NSW = P.NS / nact;                      // ring slots owned by each streaming warp
-  const int SU = P.SR / RPU;                        // units per full stage
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < P.NS; ++i) mbar_init(&full[i], 1);
-    abort_flag = 0;
-    mbar_fence_init();
-  }
-  __syncthreads();
-
-  // stage s belongs to warp s % nact; that warp's j-th stage (j = s / nact) lives in slot
-  // warp * NSW + j % NSW and completes phase (j / NSW) of that slot's mbarrier
-  auto issue = [&](int s) {
-    const int j = s / nact, slot = warp * NSW + j % NSW;
-    const int r0 = row0 + s * P.SR;
-    const int rows = min(P.SR, nrows - s * P.SR);
-    const uint32_t wb = (uint32_t)rows * K, mb = GROUP ? (uint32_t)rows * ldm * 4 : 0;
-    unsigned char* dst = ring + (size_t)slot * P.stage_bytes;
-    mbar_expect_tx(&full[slot], wb + mb);
-    bulk_g2s(dst, a.L.w + (size_t)r0 * K, wb, &full[slot]);
-    if (GROUP) bulk_g2s(dst + (size_t)P.SR * K, a.L.Mg + (size_t)r0 * ldm, mb, &full[slot]);
-  };
-  // HBM latency under full load is several microseconds -- more than the shared-memory ring can
-  // cover -- so each warp also asks L2 for its stages L2_AHEAD ring generations ahead; the
-  // bulk copies into shared memory then mostly hit L2.
-  auto prefetch = [&](int s) {
-    if (s >= nst) return;
-    const int r0 = row0 + s * P.SR;
-    const int rows = min(P.SR, nrows - s * P.SR);
-    prefetch_l2_bulk(a.L.w + (size_t)r0 * K, (uint32_t)rows * K);
-    if (GROUP) prefetch_l2_bulk(a.L.Mg + (size_t)r0 * ldm, (uint32_t)rows * ldm * 4);
-  };
-  // Weights never depend on the previous kernel: fill every warp's ring before the PDL wait.
-  int issued = 0;                                   // stages issued by this warp (lane 0)
-  if (lane == 0 && warp < nact) {
-    for (int j = 0; j < NSW && warp + j * nact < nst; ++j) { issue(warp + j * nact); issued = j + 1; }
-    for (int j = NSW; j < NSW * (1 + L2_AHEAD); ++j) prefetch(warp + j * nact);
+  // Weights never depend on the previous kernel: pull this CTA's first bytes into L2 before the
+  // PDL wait (fire-and-forget; no completion to wait for).
+  if (threadIdx.x == 0 && uhi > ulo) {
+    const char* w0 = reinterpret_cast<const char*>(a.L.w) + (size_t)ulo * RPU * K;
+    size_t bytes = (size_t)(uhi - ulo) * RPU * K;
+    bytes = bytes > PREFETCH_BYTES ? PREFETCH_BYTES : bytes;
+    for (size_t off = 0; off < bytes; off += 16384)
+      prefetch_l2_bulk(w0 + off, (uint32_t)(bytes - off < 16384 ? bytes - off : 16384));
   }
 
-  int64_t best_v[R];
-  int best_n[R];
-  uint64_t omax[R];
-  unsigned long long frl[R][3][2];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    best_v[r] = INT64_MIN;
-    best_n[r] = 0x7fffffff;
-    omax[r] = 0;
-#pragma unroll
-    for (int q = 0; q < 3; ++q) frl[r][q][0] = frl[r][q][1] = 0;
-  }
+  if (lane < RB)
+    for (int r = 0; r < R; ++r) {
+      EpiState& E = est[warp][lane][r];
+      for (int q = 0; q < 3; ++q) E.frl[q][0] = E.frl[q][1] = 0;
+      E.omax = 0;
+      E.best_v = INT64_MIN;
+      E.best_n = 0x7fffffff;
+    }
 
   pdl_wait();
   if (blockIdx.x == 0 && a.zero)
     for (int i = threadIdx.x; i < a.nzero; i += GEMV_THREADS) a.zero[i] = 0;
-  {
+  if (a.xin == XIN_Q16) {
     const int n16 = K >> 3;                                   // int4 per activation row
     for (int i = threadIdx.x; i < R * n16; i += GEMV_THREADS) {
       const int r = i / n16, c = i - r * n16;
       reinterpret_cast<int4*>(xs + (size_t)r * K)[c] = reinterpret_cast<const int4*>(a.xq + (size_t)r * a.ldx)[c];
     }
     if (threadIdx.x < R) sh_s[threadIdx.x] = a.xs[threadIdx.x];
+  } else if (a.xin == XIN_NORM) {
+    // xq, s = qrow(irms(x, g)) for every row, computed by this CTA (exact_llm.py:100-106, 41-46)
+    int64_t* ys = reinterpret_cast<int64_t*>(smem_raw + (((size_t)R * K * 2 + 127) & ~(size_t)127));
+    for (int r = 0; r < R; ++r)
+      row_norm_q<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, xs + (size_t)r * K, &sh_s[r], ys, rred);
+  } else {
+    // xq = clip(shr(x, s)) with s from the producer's published row max (exact_llm.py:41-46)
+    for (int r = 0; r < R; ++r) {
+      const int s = qrow_shift(__ldcg(a.amax_in + r));
+      row_quant_known<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, K, s, xs + (size_t)r * K);
+      if (threadIdx.x == 0) sh_s[r] = s;
+    }
   }
   __syncthreads();
+  pdl_launch_dependents();
   int sh[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) sh[r] = sh_s[r];
-  // XREG (R == 1, K <= 4096): a lane always multiplies the same activation chunks
-  // lane + 32 i, so they are loaded once into registers instead of from shared memory per column
-  int4 xr_a[XREG ? XREG_CHUNKS : 1], xr_b[XREG ? XREG_CHUNKS : 1];
-  if (XREG) {
-#pragma unroll
-    for (int i = 0; i < XREG_CHUNKS; ++i) {
-      const int ch = lane + 32 * i;
-      if (ch < C) {
-        const int4* xp = reinterpret_cast<const int4*>(xs + 16 * ch);
-        xr_a[i] = xp[0];
-        xr_b[i] = xp[1];
-      } else {
-        xr_a[i] = xr_b[i] = make_int4(0, 0, 0, 0);
-      }
-    }
-  }
 
-  for (int j = 0; warp < nact; ++j) {
-    const int s = warp + j * nact;
-    if (s >= nst) break;
-    const int slot = warp * NSW + j % NSW;
-    if (!mbar_wait(&full[slot], (j / NSW) & 1)) { abort_flag = 1; break; }
-    const unsigned char* st = ring + (size_t)slot * P.stage_bytes;
-    const int su = min(P.SR, nrows - s * P.SR) / RPU;
-    int64_t mine[R][RPU];                           // lane u keeps unit u's totals
-    for (int u = 0; u < su; ++u) {
-      int64_t tot[R][RPU];
+  const int nblk = (uhi - ulo + RB - 1) / RB;
+  for (int blk = warp; blk < nblk; blk += NCW) {
+    const int u0 = ulo + blk * RB;
+    int64_t acc[RB][PAY];
 #pragma unroll
-      for (int r = 0; r < R; ++r)
+    for (int b = 0; b < RB; ++b)
 #pragma unroll
-        for (int q = 0; q < RPU; ++q) tot[r][q] = 0;
-      if (XREG) {
-        // R == 1: activations in registers; chunk i of this lane is lane + 32 i
-        int64_t tot2[RPU];
+      for (int p = 0; p < PAY; ++p) acc[b][p] = 0;
 #pragma unroll
-        for (int q = 0; q < RPU; ++q) tot2[q] = 0;
+    for (int b = 0; b < RB; ++b) {
+      const int u = u0 + b;
+      if (u < uhi) {
 #pragma unroll
-        for (int i = 0; i < XREG_CHUNKS; ++i) {
-          const int ch = lane + 32 * i;
-          if (ch < C) {
+        for (int q = 0; q < RPU; ++q) {
+          const int n = u * RPU + q;
+          const int4* wrow = reinterpret_cast<const int4*>(a.L.w + (size_t)n * K);
+          const int32_t* mrow = GROUP ? a.L.Mg + (size_t)n * ldm : nullptr;
+          for (int c0 = 0; c0 < C; c0 += 32 * CPL) {
+            int4 wv[CPL];
+            int32_t mv[CPL];
 #pragma unroll
-            for (int q = 0; q < RPU; ++q) {
-              const int lr = u * RPU + q;
-              const int4 wv = reinterpret_cast<const int4*>(st + (size_t)lr * K)[ch];
-              const int32_t mv = GROUP ? reinterpret_cast<const int32_t*>(st + (size_t)P.SR * K)[lr * ldm + (ch >> 3)] : 1;
-              const int p = dot16(wv, xr_a[i], xr_b[i]);
-              const uint64_t term = (uint64_t)(GROUP ? (int64_t)p * mv : (int64_t)p);
-              // two independent accumulators (even / odd chunks); uint64 wraps like numpy int64
-              if (i & 1) tot2[q] = (int64_t)((uint64_t)tot2[q] + term);
-              else tot[0][q] = (int64_t)((uint64_t)tot[0][q] + term);
+            for (int i = 0; i < CPL; ++i) {
+              const int ch = c0 + lane + 32 * i;
+              if (ch < C) {
+                wv[i] = ldg_stream(wrow + ch);
+                mv[i] = GROUP ? __ldg(mrow + (ch >> 3)) : 1;
+              } else {
+                wv[i] = make_int4(0, 0, 0, 0);
+                mv[i] = 0;
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+              const int ch = c0 + lane + 32 * i;
+              if (ch < C) {
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                  const int4* xp = reinterpret_cast<const int4*>(xs + (size_t)r * K + 16 * ch);
+                  const int p = dot16(wv[i], xp[0], xp[1]);
+                  // uint64 accumulation: any overflow wraps like numpy int64
+                  acc[b][r * RPU + q] = (int64_t)((uint64_t)acc[b][r * RPU + q] +
+                                                  (uint64_t)(GROUP ? (int64_t)p * mv[i] : (int64_t)p));
+                }
+              }
             }
           }
         }
-#pragma unroll
-        for (int q = 0; q < RPU; ++q) tot[0][q] = (int64_t)((uint64_t)tot[0][q] + (uint64_t)tot2[q]);
-      } else {
-#pragma unroll 4
-      for (int ch = lane; ch < C; ch += 32) {
-        int4 wv[RPU];
-        int32_t mv[RPU];
-#pragma unroll
-        for (int q = 0; q < RPU; ++q) {
-          const int lr = u * RPU + q;                           // row within the stage
-          wv[q] = reinterpret_cast<const int4*>(st + (size_t)lr * K)[ch];
-          mv[q] = GROUP ? reinterpret_cast<const int32_t*>(st + (size_t)P.SR * K)[lr * ldm + (ch >> 3)] : 1;
-        }
+      }
+    }
+    warp_reduce_halving<RB, PAY>(acc);
+    // lane b * (32 / RB) holds the totals of column block entry b: run its epilogue
+    if ((lane & (32 / RB - 1)) == 0) {
+      const int b = lane / (32 / RB);
+      const int ug = u0 + b;
+      if (ug < uhi) {
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          const int4* xp = reinterpret_cast<const int4*>(xs + (size_t)r * K + 16 * ch);
-          const int4 xa = xp[0], xb = xp[1];
+          int64_t t2[RPU];
 #pragma unroll
-          for (int q = 0; q < RPU; ++q) {
-            const int p = dot16(wv[q], xa, xb);
-            // uint64 accumulation: any overflow wraps like numpy int64
-            tot[r][q] = (int64_t)((uint64_t)tot[r][q] + (uint64_t)(GROUP ? (int64_t)p * mv[q] : (int64_t)p));
-          }
+          for (int q = 0; q < RPU; ++q) t2[q] = acc[0][r * RPU + q];
+          unit_epilogue<RPU>(a, ug, r, t2, sh[r], est[warp][b][r]);
         }
       }
-      }
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int q = 0; q < RPU; ++q) {
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1)
-            tot[r][q] = (int64_t)((uint64_t)tot[r][q] + (uint64_t)__shfl_xor_sync(0xffffffffu, tot[r][q], o));
-          if (lane == u) mine[r][q] = tot[r][q];    // every lane holds the sum after the butterfly
-        }
     }
-    // slot fully read: hand it back to the bulk-copy engine for this warp's stage j + NSW
-    __syncwarp();
-    if (lane == 0 && s + NSW * nact < nst) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(s + NSW * nact);
-      issued = j + NSW + 1;
-      prefetch(s + NSW * nact * (1 + L2_AHEAD));
-    }
-    // epilogues of this stage's units in parallel: lane u finishes unit u
-    if (lane < su) {
-      const int ug = ulo + s * SU + lane;
-#pragma unroll
-      for (int r = 0; r < R; ++r) unit_epilogue<RPU>(a, ug, r, mine[r], sh[r], omax[r], frl[r], best_v[r], best_n[r]);
-    }
-    if (*(volatile int*)&abort_flag) break;
   }
-  __syncthreads();
-  if (abort_flag) {
-    // a bounded wait gave up: record it, let every copy this warp issued land (bounded), stop
-    if (lane == 0) {
-      set_err(a.err, ERR_WAIT_TIMEOUT);
-      for (int j = 0; j < issued; ++j) mbar_wait(&full[warp * NSW + j % NSW], (j / NSW) & 1, 1u << 20);
-    }
-    __syncthreads();
-    return;
-  }
-  // fold the per-lane epilogue state into lane 0 of each warp
+  __syncwarp();
+  // fold this warp's epilogue states (one per column-block entry) into lane-0 values
+  uint64_t omax[R];
+  int64_t best_v[R];
+  int best_n[R];
+  unsigned long long frl[R][3][2];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
+    omax[r] = 0;
+    best_v[r] = INT64_MIN;
+    best_n[r] = 0x7fffffff;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const uint64_t om = __shfl_xor_sync(0xffffffffu, omax[r], o);
-      omax[r] = om > omax[r] ? om : omax[r];
-      const int64_t bv = __shfl_xor_sync(0xffffffffu, best_v[r], o);
-      const int bn = __shfl_xor_sync(0xffffffffu, best_n[r], o);
-      if (bv > best_v[r] || (bv == best_v[r] && bn < best_n[r])) { best_v[r] = bv; best_n[r] = bn; }
+    for (int q = 0; q < 3; ++q) frl[r][q][0] = frl[r][q][1] = 0;
+    for (int b = 0; b < RB; ++b) {
+      const EpiState& E = est[warp][b][r];
+      omax[r] = E.omax > omax[r] ? E.omax : omax[r];
+      if (E.best_v > best_v[r] || (E.best_v == best_v[r] && E.best_n < best_n[r])) { best_v[r] = E.best_v; best_n[r] = E.best_n; }
 #pragma unroll
-      for (int q = 0; q < 3; ++q) {
-        frl[r][q][0] += __shfl_xor_sync(0xffffffffu, frl[r][q][0], o);
-        frl[r][q][1] += __shfl_xor_sync(0xffffffffu, frl[r][q][1], o);
-      }
+      for (int q = 0; q < 3; ++q) { frl[r][q][0] += E.frl[q][0]; frl[r][q][1] += E.frl[q][1]; }
     }
   }
-  pdl_launch_dependents();
+  __syncthreads();
 
   // ---- per-row max |output| for the consumer's qrow (SwiGLU output)
   if (a.amax_out) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      const uint64_t v = block_max_u64<GEMV_THREADS>(omax[r], rred);
+      const uint64_t v = block_max_u64<GEMV_THREADS>(lane == 0 ? omax[r] : 0, rred);
       if (threadIdx.x == 0 && v) atomicMax(a.amax_out + r, (unsigned long long)v);
     }
   }
@@ -426,7 +391,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const GemvArgs a, cons
   // ---- last CTA: build the next GEMV's int16 input rows from this kernel's complete output;
   // the activation staging area and the ring (contiguous) are free now and stage the row.
   if (a.tail != TAIL_NONE && last_cta(a.ticket, gridDim.x)) {
-    int64_t* ys = reinterpret_cast<int64_t*>(smem_raw + BAR_BYTES);
+    int64_t* ys = reinterpret_cast<int64_t*>(smem_raw);
     if (a.tail == TAIL_ROPE) {
       rope_cache_rows<GEMV_THREADS>(a.rope);
     } else if (a.tail == TAIL_NORM) {
@@ -444,11 +409,18 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const GemvArgs a, cons
   }
 }
 
-template <int R, int RPU, bool GROUP, bool XREG>
-static cudaError_t launch_t(const GemvArgs& a, const GemvPlan& P, size_t smem, cudaStream_t st, bool pdl) {
-  auto kern = k_gemv<R, RPU, GROUP, XREG>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+template <int R, int RPU, bool GROUP, int RB>
+static cudaError_t launch_t(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
+  auto kern = k_gemv<R, RPU, GROUP, RB>;
+  // The max-dynamic-shared-memory attribute is raised once to the full budget and never lowered:
+  // launches of one instantiation use different sizes, and a captured graph node (or a profiler
+  // replay) must never find a smaller maximum than it was launched with.
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_SMEM_MAX);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.grid);
   cfg.blockDim = dim3(GEMV_THREADS);
@@ -459,18 +431,16 @@ static cudaError_t launch_t(const GemvArgs& a, const GemvPlan& P, size_t smem, c
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, a, P);
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 template <int RPU, bool GROUP>
-static cudaError_t launch_r(const GemvArgs& a, const GemvPlan& P, size_t smem, cudaStream_t st, bool pdl) {
+static cudaError_t launch_r(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
   switch (a.R) {
-    case 1:
-      return a.L.K <= 32 * 16 * XREG_CHUNKS ? launch_t<1, RPU, GROUP, true>(a, P, smem, st, pdl)
-                                            : launch_t<1, RPU, GROUP, false>(a, P, smem, st, pdl);
-    case 2: return launch_t<2, RPU, GROUP, false>(a, P, smem, st, pdl);
-    case 3: return launch_t<3, RPU, GROUP, false>(a, P, smem, st, pdl);
-    case 4: return launch_t<4, RPU, GROUP, false>(a, P, smem, st, pdl);
+    case 1: return a.rb == 1 ? launch_t<1, RPU, GROUP, 1>(a, smem, st, pdl) : launch_t<1, RPU, GROUP, 4>(a, smem, st, pdl);
+    case 2: return launch_t<2, RPU, GROUP, 2>(a, smem, st, pdl);
+    case 3: return launch_t<3, RPU, GROUP, 1>(a, smem, st, pdl);
+    case 4: return launch_t<4, RPU, GROUP, 1>(a, smem, st, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -488,8 +458,9 @@ static int sm_count() {
 
 int gemv_grid(int N, bool swiglu) {
   const int units = swiglu ? N / 2 : N;
-  const int sms = sm_count();
-  return units < sms ? units : sms;
+  const int ctas = 2 * sm_count();                 // 2 CTAs of 512 threads per SM
+  const int g = (units + 3) / 4;                   // at least 4 columns per CTA
+  return g < ctas ? (g > 0 ? g : 1) : ctas;
 }
 
 cudaError_t launch_gemv(const GemvArgs& a0, cudaStream_t st, bool pdl) {
@@ -497,42 +468,24 @@ cudaError_t launch_gemv(const GemvArgs& a0, cudaStream_t st, bool pdl) {
   const bool group = a.L.Mg != nullptr;
   const int RPU = a.epi == EPI_SWIGLU ? 2 : 1;
   if ((group ? a.L.K % 128 : a.L.K % 16) != 0 || a.L.N <= 0 || a.R < 1 || a.R > 4) return cudaErrorInvalidValue;
-  if (group && (a.L.ldm < a.L.K / 128 || a.L.ldm % 4 || ((uintptr_t)a.L.Mg & 15))) return cudaErrorInvalidValue;
-  if (((uintptr_t)a.L.w & 15) || ((uintptr_t)a.xq & 15) || (a.ldx % 8)) return cudaErrorInvalidValue;
+  if (group && (a.L.ldm < a.L.K / 128)) return cudaErrorInvalidValue;
+  if (a.xin == XIN_Q16 && (((uintptr_t)a.xq & 15) || (a.ldx % 8))) return cudaErrorInvalidValue;
+  if (a.xin != XIN_Q16 && (((uintptr_t)a.x64 & 15) || (a.ldx64 & 1) || (a.L.K & 1))) return cudaErrorInvalidValue;
+  if ((uintptr_t)a.L.w & 15) return cudaErrorInvalidValue;
   if (RPU == 2 && (a.L.N & 1)) return cudaErrorInvalidValue;
   if (a.grid <= 0) a.grid = gemv_grid(a.L.N, RPU == 2);
-  GemvPlan P;
-  const int K = a.L.K;
-  const size_t budget = 200 * 1024;
-  P.xs_bytes = ((a.R * K * 2) + 127) & ~127;
-  if ((size_t)P.xs_bytes + BAR_BYTES >= budget) return cudaErrorInvalidValue;
-  const size_t avail = budget - BAR_BYTES - P.xs_bytes;
-  const int row_bytes = K + (group ? a.L.ldm * 4 : 0);
-  // stage size: two slots per consumer warp when that leaves at least one unit per stage
-  size_t target = avail / (2 * NCW);
-  if (target < (size_t)RPU * row_bytes) target = avail / NCW;
-  P.SR = (int)(target / row_bytes);
-  if (P.SR > STAGE_BYTES / K) P.SR = STAGE_BYTES / K;
-  {  // spread a CTA's columns over all consumer warps
+  if (a.rb <= 0) {
+    // one column per warp when the grid has a warp for (nearly) every column: every load of the
+    // kernel is then issued in one round; otherwise blocks of 4 columns amortise the reduction
     const int units = a.L.N / RPU;
-    const int rows_cta = ((units + a.grid - 1) / a.grid) * RPU;
-    const int per_warp = ((rows_cta + NCW - 1) / NCW + RPU - 1) / RPU * RPU;
-    if (P.SR > per_warp) P.SR = per_warp;
+    a.rb = units <= a.grid * NCW * 2 ? 1 : 4;
   }
-  if (P.SR > 32 * RPU) P.SR = 32 * RPU;            // lane u finishes unit u of a stage
-  if (P.SR < RPU) P.SR = RPU;
-  P.SR -= P.SR % RPU;
-  P.stage_bytes = (P.SR * row_bytes + 127) & ~127;
-  int NS = (int)(avail / P.stage_bytes);
-  if (NS > MAX_STAGES) NS = MAX_STAGES;
-  if (NS >= NCW) NS -= NS % NCW;                   // every streaming warp owns NS / min(NS, 8) slots
-  const size_t need_tail = a.tail == TAIL_NORM ? (size_t)a.tail_K * 16 : 0;
-  if (NS < 1) return cudaErrorInvalidValue;
-  if ((size_t)P.xs_bytes + (size_t)NS * P.stage_bytes < need_tail) return cudaErrorInvalidValue;
-  P.NS = NS;
-  const size_t smem = BAR_BYTES + P.xs_bytes + (size_t)NS * P.stage_bytes;
-  if (RPU == 2) return group ? launch_r<2, true>(a, P, smem, st, pdl) : launch_r<2, false>(a, P, smem, st, pdl);
-  return group ? launch_r<1, true>(a, P, smem, st, pdl) : launch_r<1, false>(a, P, smem, st, pdl);
+  size_t smem = (((size_t)a.R * a.L.K * 2 + 127) & ~(size_t)127);
+  if (a.xin == XIN_NORM) smem += (size_t)a.L.K * 16;                                       // row + gains
+  if (a.tail == TAIL_NORM && smem < (size_t)a.tail_K * 16) smem = (size_t)a.tail_K * 16;   // tail stages row + gains
+  if (smem > DYN_SMEM_MAX) return cudaErrorInvalidValue;
+  if (RPU == 2) return group ? launch_r<2, true>(a, smem, st, pdl) : launch_r<2, false>(a, smem, st, pdl);
+  return group ? launch_r<1, true>(a, smem, st, pdl) : launch_r<1, false>(a, smem, st, pdl);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -564,9 +517,12 @@ cudaError_t launch_gemv_op(const int16_t* x16, const int8_t* wT, const int64_t* 
                            cudaStream_t st) {
   if (K % 128 != 0 || N <= 0) return cudaErrorInvalidValue;
   const size_t smem = (size_t)K * 2;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemv_op, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > DYN_SMEM_MAX) return cudaErrorInvalidValue;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemv_op, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_SMEM_MAX);
     if (e != cudaSuccess) return e;
+    attr_set = true;
   }
   int blocks = (N + 7) / 8;
   if (blocks > 148 * 8) blocks = 148 * 8;

@@ -136,6 +136,11 @@ int exb_device_errors(exb_model* m, int* bits);
  * + outputs). */
 int exb_bench_linear(exb_model* m, int layer, int which, int R, int reps, float* avg_ms, double* bytes);
 
+/* Profiling: run one decode step for sequences 0..B-1 kernel by kernel (no graph, no programmatic
+ * launch overlap) with a CUDA event after every launch; ms_out[i] = duration of launch i.  The step
+ * writes the KV cache at each sequence's current length without advancing it. */
+int exb_profile_step(exb_model* m, int B, float* ms_out, int max_n, int* n_out);
+
 /* raw pointers for benchmarks / interop */
 void* exb_model_stream(exb_model* m);
 size_t exb_model_weight_bytes(exb_model* m);
