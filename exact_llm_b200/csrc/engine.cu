@@ -21,6 +21,7 @@
 using namespace exb;
 
 static thread_local std::string g_err;
+void exb::set_last_error(const std::string& msg) { g_err = msg; }
 
 #define FAIL(code, msg)     \
   do {                      \

@@ -3,7 +3,12 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <string>
+
 namespace exb {
+
+// message returned by exb_last_error() for the calling thread
+void set_last_error(const std::string& msg);
 
 enum GenKind { GEN_WEIGHT = 0, GEN_SCALE32 = 1, GEN_SCALE64 = 2, GEN_BIAS = 3, GEN_GAIN = 4 };
 cudaError_t gen_tensor(int kind, uint64_t seed, uint64_t stream, int64_t n, int64_t K, void* out, cudaStream_t st);

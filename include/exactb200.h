@@ -62,6 +62,21 @@ size_t exb_linear_g128_scratch_bytes(int R, int K, int N);
 int exb_linear_g128(const int64_t* x, int R, int K, const int8_t* w_NK, const int32_t* M_NG, const int64_t* bias,
                     int N, int64_t* y, int64_t* tot_out, void* scratch, void* stream);
 
+/* exb_linear_g128 without caller scratch, for callers that cannot allocate device memory: hosts
+ * that fix their HBM budget at start-up (every byte reserved for weights and KV caches) and plugin
+ * hosts that own the allocator.  No counterpart in the reference (its torch path allocates per
+ * call).  Same arguments and bit-identical results as exb_linear_g128, minus `scratch`.
+ * The scratch is a fixed array inside the library: every GPU that loads it holds about 8 MiB until
+ * exit.  Limits: R * K <= EXB_NOALLOC_MAX_XQ and R <= EXB_NOALLOC_MAX_ROWS (else EXB_EINVAL, nothing
+ * launched).  The first call on a device looks the array's device address up (make it before any
+ * stream capture on that device).  All calls on a device share the array: calls whose GPU work
+ * overlaps (different streams, no ordering) race and must be ordered by the caller.  Calls no
+ * cudaMalloc, cudaFree or allocating library routine. */
+#define EXB_NOALLOC_MAX_XQ (1 << 22)
+#define EXB_NOALLOC_MAX_ROWS 4096
+int exb_linear_g128_noalloc(const int64_t* x, int R, int K, const int8_t* w_NK, const int32_t* M_NG,
+                            const int64_t* bias, int N, int64_t* y, int64_t* tot_out, void* stream);
+
 /* QLin.__call__ (exact_llm.py:89-96) with the per-row drop rule, on device buffers.
  * w_NK int8 (N, K); M int64 (N); acc_out int64 (R, N) is required (the drop rule needs the
  * whole row); scratch of exb_linear_g128_scratch_bytes(R, K, 0) bytes. */
