@@ -26,19 +26,20 @@ namespace exb {
 constexpr int CL = 8;               // CTAs per cluster (portable cluster size)
 constexpr int ATT_THREADS = 256;
 constexpr int REP_MAX = 8;          // query heads per KV head handled by one cluster
+constexpr int ATT_TILE = 64;        // key/value positions staged in shared memory at a time
 
 // ---------------------------------------------------------------- RoPE + cache write + q quantisation
 // Standalone form of rope_cache_rows (the decode path runs it as the q|k|v GEMV's last-CTA tail).
 __global__ void __launch_bounds__(256) k_rope_cache(const AttnArgs a) {
   pdl_wait();
   pdl_launch_dependents();
-  rope_cache_rows<256>(a);
+  rope_cache_rows<256>(a, blockIdx.x * 8, gridDim.x * 8);
 }
 
 cudaError_t launch_rope_cache(const AttnArgs& a, cudaStream_t st, bool pdl) {
   if (a.hd > 128 || (a.hd & 1) || a.H % a.KV) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
+  cfg.gridDim = dim3((a.R * (a.KV + a.H) + 7) / 8);      // one warp per (row, head) task
   cfg.blockDim = dim3(256);
   cfg.stream = st;
   cudaLaunchAttribute at[1];
@@ -84,6 +85,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
   int64_t* sc = reinterpret_cast<int64_t*>(sm + ((rep * hd * 2 + 15) & ~15));      // rep*SCmax
   int64_t* pout = sc + (size_t)rep * SCmax;                                          // rep*hd
   int64_t* pv = pout + (size_t)rep * hd;                                             // ATT_THREADS*REP_MAX
+  int16_t* ktile = reinterpret_cast<int16_t*>(pv + (size_t)ATT_THREADS * REP_MAX);   // ATT_TILE x (hd + 8)
+  int32_t* vtile = reinterpret_cast<int32_t*>(ktile + (size_t)ATT_TILE * (hd + 8));   // ATT_TILE x hd
 
   pdl_wait();
   pdl_launch_dependents();
@@ -99,12 +102,25 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
   if (tid < rep) qsh[tid] = a.qs[(size_t)r * a.H + j * rep + tid];
   __syncthreads();
 
-  // phase 1: scores of this CTA's positions, local max per head
-  for (int e = tid; e < rep * n; e += ATT_THREADS) {
-    const int i = e / n, t = t0 + (e - i * n);
-    const int64_t acc = dot_i16<HD>(qs_sm + i * hd, a.kc + (cbase + t) * hd);
-    sc[(size_t)i * SCmax + (t - t0)] =
-        shr64((int64_t)((uint64_t)acc * (uint64_t)a.inv), 32 - qsh[i] - (int)a.ks[cbase + t]);
+  // phase 1: scores of this CTA's positions, local max per head.  Key rows are staged in shared
+  // memory one tile at a time (all loads in flight together; rows padded by 16 bytes so the
+  // 128-bit reads of 8 consecutive rows hit distinct banks).
+  for (int tt = 0; tt < n; tt += ATT_TILE) {
+    const int nt = min(ATT_TILE, n - tt);
+    const int per_row = hd / 8;                                         // int4 per key row
+    for (int e = tid; e < nt * per_row; e += ATT_THREADS) {
+      const int t = e / per_row, c4 = e - t * per_row;
+      *reinterpret_cast<int4*>(ktile + (size_t)t * (hd + 8) + c4 * 8) =
+          reinterpret_cast<const int4*>(a.kc + (cbase + t0 + tt + t) * hd)[c4];
+    }
+    __syncthreads();
+    for (int e = tid; e < rep * nt; e += ATT_THREADS) {
+      const int i = e / nt, t = e - i * nt;
+      const int64_t acc = dot_i16<HD>(qs_sm + i * hd, ktile + (size_t)t * (hd + 8));
+      sc[(size_t)i * SCmax + tt + t] =
+          shr64((int64_t)((uint64_t)acc * (uint64_t)a.inv), 32 - qsh[i] - (int)a.ks[cbase + t0 + tt + t]);
+    }
+    __syncthreads();
   }
   __syncthreads();
   if (warp < rep) {
@@ -153,12 +169,24 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
     int64_t acc[REP_MAX];
 #pragma unroll
     for (int i = 0; i < REP_MAX; ++i) acc[i] = 0;
-#pragma unroll 8
-    for (int t = part; t < n; t += nparts) {
-      const int64_t v = a.vc[(cbase + t0 + t) * hd + d];
+    // value rows staged in shared memory one tile at a time
+    for (int tt = 0; tt < n; tt += ATT_TILE) {
+      const int nt = min(ATT_TILE, n - tt);
+      const int per_row = hd / 4;                                       // int4 per value row
+      for (int e = tid; e < nt * per_row; e += ATT_THREADS) {
+        const int t = e / per_row, c4 = e - t * per_row;
+        reinterpret_cast<int4*>(vtile)[(size_t)t * per_row + c4] =
+            reinterpret_cast<const int4*>(a.vc + (cbase + t0 + tt + t) * hd)[c4];
+      }
+      __syncthreads();
+#pragma unroll 4
+      for (int t = part; t < nt; t += nparts) {
+        const int64_t v = vtile[(size_t)t * hd + d];
 #pragma unroll
-      for (int i = 0; i < REP_MAX; ++i)
-        if (i < rep) acc[i] += sc[(size_t)i * SCmax + t] * v;
+        for (int i = 0; i < REP_MAX; ++i)
+          if (i < rep) acc[i] += sc[(size_t)i * SCmax + tt + t] * v;
+      }
+      __syncthreads();
     }
 #pragma unroll
     for (int i = 0; i < REP_MAX; ++i) pv[(size_t)tid * REP_MAX + i] = acc[i];
@@ -204,9 +232,9 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const int rep = a.H / a.KV;
   if (rep > REP_MAX || a.H % a.KV || ATT_THREADS % a.hd || a.hd % 8) return cudaErrorInvalidValue;
-  const int SCmax = (a.Smax + CL - 1) / CL;
+  const int SCmax = (((a.Smax + CL - 1) / CL) + 1) & ~1;   // even: keeps the tiles after sc 16-byte aligned
   const size_t smem = (size_t)((rep * a.hd * 2 + 15) & ~15) + (size_t)rep * SCmax * 8 + (size_t)rep * a.hd * 8 +
-                      (size_t)ATT_THREADS * REP_MAX * 8;
+                      (size_t)ATT_THREADS * REP_MAX * 8 + (size_t)ATT_TILE * (a.hd + 8) * 2 + (size_t)ATT_TILE * a.hd * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   void (*kern)(const AttnArgs, int) = a.hd == 128 ? k_attn_decode<128> : a.hd == 64 ? k_attn_decode<64>
                                     : a.hd == 32 ? k_attn_decode<32> : k_attn_decode<16>;

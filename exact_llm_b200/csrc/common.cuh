@@ -58,6 +58,18 @@ EXB_DEV int64_t floordiv_fast(int64_t a, int64_t b) {
   return q;
 }
 
+// floor(a / b) for b > 0 with a precomputed inv = 1.0 / b: the same estimate + exact integer
+// correction as floordiv_fast, with multiplications instead of double divisions.
+EXB_DEV int64_t floordiv_recip(int64_t a, int64_t b, double inv) {
+  int64_t q = (int64_t)floor(__ll2double_rn(a) * inv);
+  int64_t r = (int64_t)((uint64_t)a - (uint64_t)q * (uint64_t)b);
+  q += (int64_t)floor(__ll2double_rn(r) * inv);
+  r = (int64_t)((uint64_t)a - (uint64_t)q * (uint64_t)b);
+  for (int i = 0; i < 4 && r < 0; ++i) { q -= 1; r += b; }
+  for (int i = 0; i < 4 && r >= b; ++i) { q += 1; r -= b; }
+  return q;
+}
+
 // floor(sqrt(double(n))) with one correction step each way (exact_llm.py:97-99)
 EXB_DEV int64_t isqrt_ref(int64_t n) {
   int64_t r = (int64_t)floor(sqrt(__ll2double_rn(n)));

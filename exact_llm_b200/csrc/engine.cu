@@ -262,14 +262,18 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     }
     g.fr_nseg = s;
   };
-  // Per layer: every GEMV builds its own int16 input rows in its prologue (in parallel in every
-  // CTA, overlapping the L2 prefetch of its weights); producers publish per-row maxima for qrow.
-  //   q|k|v GEMV    in: irms(x, g1) + qrow
+  // Per layer (every kernel chained with programmatic dependent launch, so each GEMV is resident
+  // and pulling its weights into L2 while the small kernel before it runs):
+  //   norm          xq, s = qrow(irms(x, g1))               (one CTA per row)
+  //   q|k|v GEMV    -> q|k|v rows
   //   rope/cache    RoPE, K/V cache write, quantised query rows
   //   attention     cluster per (row, KV head); publishes max |out| per row
-  //   o GEMV        in: qrow(out);            x += o(...)
-  //   gate|up GEMV  in: irms(x, g2) + qrow;  h = shr(isilu(g)*u, 16), publishes max |h| per row
-  //   down GEMV     in: qrow(h);              x += down(h)
+  //   quant         xq = qrow(out) with the published max   (row split over CTAs)
+  //   o GEMV        x += o(...)
+  //   norm          xq, s = qrow(irms(x, g2))
+  //   gate|up GEMV  h = shr(isilu(g)*u, 16); publishes max |h| per row
+  //   quant         xq = qrow(h)
+  //   down GEMV     x += down(h)
   aa.amax_out = m->amax_o;
   for (int i = 0; i < c.NL; ++i) {
     LayerDev& Ld = m->L[i];
@@ -278,10 +282,11 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     aa.ks = m->ks + (size_t)c.max_batch * c.KV * c.max_seq * i;
     auto base = [&](GemvArgs& g, const LinW& L) {
       g.L = L; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
+      g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX;
     };
+    RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     {
       GemvArgs g; base(g, Ld.qkv);
-      g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g1;
       g.epi = EPI_STORE; g.out = m->qkv; g.ldo = m->Nqkv; g.raw = trace_ptr(Ld.li[0]);
       g.zero = m->amax_o; g.nzero = RMAX;
       set_fr(g, {Ld.li[0], Ld.li[1], Ld.li[2]});
@@ -289,34 +294,35 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     }
     RUN(launch_rope_cache(aa, st, pdl));
     RUN(launch_attn_decode(aa, st, pdl));
+    RUN(launch_quant_known(m->ao, Hd, R, Hd, m->amax_o, m->xq, m->KMAX, m->xs, st, pdl));
     {
       GemvArgs g; base(g, Ld.o);
-      g.xin = XIN_QUANT; g.x64 = m->ao; g.ldx64 = Hd; g.amax_in = m->amax_o;
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[3]);
       g.zero = m->amax_h; g.nzero = RMAX;
       set_fr(g, {Ld.li[3]});
       RUN(launch_gemv(g, st, pdl));
     }
+    RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     {
       GemvArgs g; base(g, Ld.gu);
-      g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g2;
       g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.amax_out = m->amax_h;
       g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]);
       set_fr(g, {Ld.li[4], Ld.li[5]});
       RUN(launch_gemv(g, st, pdl));
     }
+    RUN(launch_quant_known(m->hb, c.I, R, c.I, m->amax_h, m->xq, m->KMAX, m->xs, st, pdl));
     {
       GemvArgs g; base(g, Ld.down);
-      g.xin = XIN_QUANT; g.x64 = m->hb; g.ldx64 = c.I; g.amax_in = m->amax_h;
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[6]);
       set_fr(g, {Ld.li[6]});
       RUN(launch_gemv(g, st, pdl));
     }
   }
+  RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
   {
     GemvArgs g;
     g.L = m->head; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
-    g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = m->gf;
+    g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX;
     g.epi = EPI_HEAD; g.out = want_logits ? m->logits : nullptr; g.ldo = c.V;
     g.raw = trace_ptr(m->n_lin - 1);
     g.head_part = m->head_part; g.head_ticket = m->head_ticket; g.next_tok = m->next_tok; g.grid = m->head_grid;

@@ -130,6 +130,8 @@ cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, in
                           int32_t* xs, cudaStream_t st, bool pdl);
 cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, int ldq, int32_t* xs,
                          cudaStream_t st, bool pdl);
+cudaError_t launch_quant_known(const int64_t* x, int ldx, int R, int K, const unsigned long long* amax, int16_t* xq,
+                               int ldq, int32_t* xs, cudaStream_t st, bool pdl);
 cudaError_t launch_requant_channel(const int64_t* acc, int ld, int R, const LinW& L, int64_t* out, int ldo,
                                    const int32_t* xs, int epi, cudaStream_t st, bool pdl);
 

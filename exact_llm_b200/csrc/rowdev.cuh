@@ -36,9 +36,10 @@ EXB_DEV void row_norm_q_staged(const int64_t* __restrict__ g, int D, int16_t* __
   int64_t rt = isqrt_ref(ms);
   rt = rt > 1 ? rt : 1;
   const int64_t den = (int64_t)((uint64_t)rt << k);
+  const double inv = 1.0 / (double)den;
   uint64_t m2 = 0;
   for (int i = threadIdx.x; i < D; i += NT) {
-    const int64_t y = floordiv_fast((int64_t)((uint64_t)ys[i] << 16), den);
+    const int64_t y = floordiv_recip((int64_t)((uint64_t)ys[i] << 16), den, inv);
     const int64_t gi = gs ? gs[i] : __ldg(g + i);
     const int64_t a = shr64((int64_t)((uint64_t)y * (uint64_t)gi), 16);
     ys[i] = a;
@@ -111,12 +112,13 @@ EXB_DEV void row_quant_known(const int64_t* __restrict__ xr, int K, int s, int16
 // RoPE + cache write for rows 0..R-1; one warp per (row, head) task.  Heads 0..KV-1 are the
 // key heads (RoPE, per-row quantisation, K and V cache write), heads KV..KV+H-1 the query heads
 // (RoPE + per-row quantisation into qq/qs).
+// Tasks are split over the grid: this CTA's warps take tasks first_task + warp, + stride, ...
 template <int NT>
-EXB_DEV void rope_cache_rows(const AttnArgs& a) {
+EXB_DEV void rope_cache_rows(const AttnArgs& a, int first_task = 0, int stride = NT / 32) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hd = a.hd, half = hd >> 1;
   const int tasks = a.R * (a.KV + a.H);
-  for (int t = warp; t < tasks; t += NT / 32) {
+  for (int t = first_task + warp; t < tasks; t += stride) {
     const int r = t / (a.KV + a.H), h = t - r * (a.KV + a.H);
     const int pos = a.row_pos[r], seq = a.row_seq[r];
     if (pos < 0 || pos >= a.Smax || pos >= a.Tmax) {

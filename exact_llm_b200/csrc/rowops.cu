@@ -145,6 +145,35 @@ cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, i
   return launch_simple((const void*)k_quant, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
 }
 
+// ---------------------------------------------------------------- qrow with a published row max
+// xq = clip(shr(x, s)), s = max(bitlen(amax[r]) - 15, 0); grid (slices, R): every CTA converts a
+// slice of a row, so a long row (e.g. the 18944-wide MLP activation) is converted in parallel.
+__global__ void __launch_bounds__(256) k_quant_known(const int64_t* __restrict__ x, int ldx, int K,
+                                                     const unsigned long long* __restrict__ amax,
+                                                     int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int r = blockIdx.y;
+  const int s = qrow_shift(__ldcg(amax + r));
+  const int per = ((K + gridDim.x - 1) / gridDim.x + 1) & ~1;      // even slice length
+  const int k0 = blockIdx.x * per, k1 = min(K, k0 + per);
+  const longlong2* x2 = reinterpret_cast<const longlong2*>(x + (size_t)r * ldx);
+  short2* q2 = reinterpret_cast<short2*>(xq + (size_t)r * ldq);
+  for (int i = (k0 >> 1) + threadIdx.x; i < (k1 >> 1); i += 256) {
+    const longlong2 v = __ldcg(x2 + i);
+    q2[i] = make_short2(qrow_value(v.x, s), qrow_value(v.y, s));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) xs[r] = s;
+}
+
+cudaError_t launch_quant_known(const int64_t* x, int ldx, int R, int K, const unsigned long long* amax, int16_t* xq,
+                               int ldq, int32_t* xs, cudaStream_t st, bool pdl) {
+  if ((K & 1) || (ldx & 1) || (ldq & 1)) return cudaErrorInvalidValue;
+  int slices = (K + 2047) / 2048;
+  void* args[] = {(void*)&x, (void*)&ldx, (void*)&K, (void*)&amax, (void*)&xq, (void*)&ldq, (void*)&xs};
+  return launch_simple((const void*)k_quant_known, dim3(slices, R), dim3(256), 0, st, pdl, args);
+}
+
 // ---------------------------------------------------------------- per-channel requant, general drop rule
 // drop = max(bitlen(max_row |acc|) + Mbits - 62, 0); y = shr(shr(acc, drop) * M, 28 - s - drop) + b
 // (exact_llm.py:93-96).  Used when the host cannot prove drop == 0 for every input.
