@@ -182,7 +182,7 @@ def run_ours(a, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
-    c = configs.arch(a.model)
+    c = configs.arch(a.model, **({"NL": a.layers} if a.layers else {}))
     B, K, W = a.batch, a.steps, a.warmup
     max_seq = PROMPT + W + 2 * K + 16
     m = ExactModel.synthetic(c, 1234, max_batch=B, max_seq=max_seq)
@@ -253,7 +253,7 @@ def run_ours(a, rank, world, local_rank):
         "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8 x int16 -> int64", "data": "synthetic",
         "config": {"workload": f"{a.model}-arch greedy decode, batch {B}, after a {PROMPT}-token uniform prompt",
-                   "batch": B, "prompt": PROMPT, "decode_steps": K,
+                   "batch": B, "prompt": PROMPT, "decode_steps": K, "layers": c["NL"],
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "no flush: 7.3 GB of weights stream from HBM every step (L2 126 MB)"},
         "decode_hbm": {"bytes_per_step": sb, "achieved_gbs": step_gbs, "peak_gbs": hbm, "frac": step_gbs / hbm,
@@ -288,7 +288,10 @@ def main():
     ap.add_argument("--model", default="qwen2.5-7b")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens before decode (profiling uses a short one)")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures only)")
     a = ap.parse_args()
+    globals()["PROMPT"] = a.prompt
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

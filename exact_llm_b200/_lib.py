@@ -7,7 +7,8 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libexactb200.so")
+# EXB_LIB selects another build of the same library (e.g. one compiled with different tuning macros)
+LIB_PATH = os.environ.get("EXB_LIB") or os.path.join(HERE, "libexactb200.so")
 
 c_i32p = ctypes.POINTER(ctypes.c_int32)
 c_i64p = ctypes.POINTER(ctypes.c_int64)
@@ -54,11 +55,14 @@ SIGNATURES = {
     "exb_freivalds_read_keys": (ctypes.c_int, [ctypes.c_void_p, c_i32p, ctypes.c_int64]),
     "exb_freivalds_enable": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "exb_freivalds_status": (ctypes.c_int, [ctypes.c_void_p, c_i64p, c_i64p]),
+    "exb_set_option": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int64]),
     "exb_device_errors": (ctypes.c_int, [ctypes.c_void_p, c_i32p]),
     "exb_bench_linear": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)]),
     "exb_profile_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float), ctypes.c_int,
                                         ctypes.POINTER(ctypes.c_int)]),
+    "exb_profile_persistent": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint64),
+                                              ctypes.c_int64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "exb_model_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
     "exb_model_weight_bytes": (ctypes.c_size_t, [ctypes.c_void_p]),
     "exb_gen_tensor": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64,

@@ -32,6 +32,12 @@ EXB_DEV int64_t shr64(int64_t a, int n) {
   return ((int64_t)s) >> n;
 }
 
+// shr64 for a shift count known to lie in [0, 63]: branch-free (same result as shr64 there)
+EXB_DEV int64_t shr_nn(int64_t a, int n) {
+  const uint64_t bias = n > 0 ? (1ull << ((n - 1) & 63)) : 0ull;
+  return ((int64_t)((uint64_t)a + bias)) >> n;
+}
+
 // bit length of a non-negative value (exact_llm.py:35-40)
 EXB_DEV int bitlen64(uint64_t m) { return m ? 64 - __clzll((long long)m) : 0; }
 
@@ -82,7 +88,7 @@ EXB_DEV int64_t isqrt_ref(int64_t n) {
 constexpr int64_t QLIM = 32767;
 EXB_DEV int qrow_shift(uint64_t amax) { int s = bitlen64(amax) - 15; return s > 0 ? s : 0; }
 EXB_DEV int16_t qrow_value(int64_t x, int s) {
-  int64_t v = shr64(x, s);
+  int64_t v = shr_nn(x, s);                        // 0 <= s <= 49 (qrow_shift of a 64-bit max)
   v = v > QLIM ? QLIM : (v < -QLIM ? -QLIM : v);
   return (int16_t)v;
 }
@@ -112,6 +118,20 @@ EXB_DEV int64_t table_interp(const int32_t* __restrict__ T, int64_t x, int64_t h
 EXB_DEV int64_t isilu_dev(const int32_t* T, int64_t x) { return table_interp(T, x, x); }
 EXB_DEV int64_t isig_dev(const int32_t* T, int64_t x) { return table_interp(T, x, 1ll << 16); }
 
+// ---------------------------------------------------------------- warp / block reductions
+// 64-bit warp max and sum from 32-bit single-instruction warp reductions (redux.sync)
+EXB_DEV uint64_t warp_max_u64(uint64_t v) {
+  const unsigned hi = __reduce_max_sync(0xffffffffu, (unsigned)(v >> 32));
+  const unsigned lo = __reduce_max_sync(0xffffffffu, (unsigned)(v >> 32) == hi ? (unsigned)v : 0u);
+  return ((uint64_t)hi << 32) | lo;
+}
+EXB_DEV uint64_t warp_sum_u64(uint64_t v) {
+  // three 22-bit digits: a warp sum of each fits in 27 bits; recombined modulo 2^64
+  const unsigned d0 = __reduce_add_sync(0xffffffffu, (unsigned)(v & 0x3fffffu));
+  const unsigned d1 = __reduce_add_sync(0xffffffffu, (unsigned)((v >> 22) & 0x3fffffu));
+  const unsigned d2 = __reduce_add_sync(0xffffffffu, (unsigned)(v >> 44));
+  return (uint64_t)d0 + ((uint64_t)d1 << 22) + ((uint64_t)d2 << 44);
+}
 // ---------------------------------------------------------------- block reductions
 template <int NT>
 EXB_DEV uint64_t block_max_u64(uint64_t v, uint64_t* red) {

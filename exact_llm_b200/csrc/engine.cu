@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -38,6 +39,7 @@ void exb::set_last_error(const std::string& msg) { g_err = msg; }
   } while (0)
 
 static constexpr int RMAX = 4;          // activation rows per GEMV pass (CUDA-core decode path)
+static constexpr int STEP_ROWS = 2;     // rows the persistent step kernel takes (batch <= 2)
 static constexpr int EXP_LEN_H = 256 * 40 + 2, SILU_LEN_H = 32 * 256 + 2;
 
 static int bitlen_host(uint64_t v) { int b = 0; while (v) { ++b; v >>= 1; } return b; }
@@ -101,6 +103,12 @@ struct exb_model {
   int64_t fr_checks = 0;
   std::map<uint64_t, cudaGraphExec_t> graphs;
   int32_t *h_ids = nullptr, *h_seq = nullptr, *h_pos = nullptr;           // pinned staging
+  // persistent decode-step kernel (step.cu): per-layer descriptors and accumulators
+  bool step_on = false;
+  int pf_bytes = 64 * 1024;
+  StepLayer* step_layers = nullptr;
+  int64_t* s_att = nullptr; long long* s_gmax = nullptr; unsigned long long* s_gsum = nullptr;
+  unsigned long long* s_amax_h = nullptr; int16_t* s_hq = nullptr; unsigned int* s_bar = nullptr;
 };
 
 // ------------------------------------------------------------------------------------------ helpers
@@ -212,6 +220,13 @@ static void plan_runtime(exb_model* m) {
   m->kc = ralloc<int16_t>(m, m->kv_layer_elems * c.NL);
   m->vc = ralloc<int32_t>(m, m->kv_layer_elems * c.NL);
   m->ks = ralloc<int8_t>(m, (size_t)c.max_batch * c.KV * c.max_seq * c.NL);
+  m->step_layers = ralloc<StepLayer>(m, c.NL);
+  m->s_att = ralloc<int64_t>(m, (size_t)c.NL * STEP_ROWS * c.H * c.hd);
+  m->s_gmax = ralloc<long long>(m, (size_t)c.NL * STEP_ROWS * c.H);
+  m->s_gsum = ralloc<unsigned long long>(m, (size_t)c.NL * STEP_ROWS * c.H);
+  m->s_amax_h = ralloc<unsigned long long>(m, (size_t)c.NL * STEP_ROWS);
+  m->s_hq = ralloc<int16_t>(m, (size_t)STEP_ROWS * c.I);
+  m->s_bar = ralloc<unsigned int>(m, 2);
 }
 
 // ------------------------------------------------------------------------------------------ step
@@ -219,6 +234,34 @@ static void plan_runtime(exb_model* m) {
 // sequence slot and position from device arrays, so the enqueued work is identical for every
 // step and can be captured once into a CUDA graph.
 static std::vector<cudaEvent_t>* g_prof = nullptr;   // profiling: an event after every launch
+
+// Arguments of the persistent step kernel, when it can run this step: group-128 model, R <= 2
+// rows, no trace or Freivalds capture (those stay on the per-kernel path), int8 embedding rows.
+static bool step_args(exb_model* m, int R, const int32_t* ids, const int32_t* seq, const int32_t* pos,
+                      bool want_logits, StepArgs& a) {
+  const exb_config& c = m->c;
+  if (!m->step_on || !m->group || m->trace_on || m->fr_on || m->emb_q16 || R < 1 || R > STEP_ROWS) return false;
+  a.layers = m->step_layers; a.NL = c.NL; a.R = R; a.D = c.D; a.H = c.H; a.KV = c.KV; a.hd = c.hd; a.I = c.I;
+  a.V = c.V; a.Nqkv = m->Nqkv; a.Smax = c.max_seq; a.Tmax = c.rope_len; a.max_batch = c.max_batch;
+  a.emb = m->emb; a.emb_shift = c.emb_shift; a.gf = m->gf; a.head = m->head;
+  a.ids = ids; a.seq = seq; a.pos = pos;
+  a.exp_t = m->exp_t; a.silu_t = m->silu_t; a.cos_t = m->cos_t; a.sin_t = m->sin_t;
+  a.inv = (int64_t)std::nearbyint(65536.0 / std::sqrt((double)c.hd));
+  a.kc = m->kc; a.ks = m->ks; a.vc = m->vc; a.kv_layer_elems = m->kv_layer_elems;
+  a.ks_layer_elems = (size_t)c.max_batch * c.KV * c.max_seq;
+  a.x = m->x; a.qkv = m->qkv; a.hb = m->hb; a.hq = m->s_hq;
+  a.att = m->s_att; a.gmax = m->s_gmax; a.gsum = m->s_gsum; a.amax_h = m->s_amax_h;
+  a.logits = want_logits ? m->logits : nullptr;
+  a.head_part = m->head_part; a.head_ticket = m->head_ticket; a.next_tok = m->next_tok;
+  a.bar = m->s_bar; a.err = m->err; a.pf_bytes = m->pf_bytes; a.KMAX = m->KMAX;
+  // the attention split depends on the grid, the grid on the shared memory the split needs
+  a.att_split = 1; a.att_chunk_max = 1;
+  const int g0 = step_grid(a, nullptr);
+  if (g0 <= 0 || g0 > m->head_grid) return false;
+  a.att_split = std::max(1, std::min(32, g0 / (R * c.KV)));
+  a.att_chunk_max = (c.max_seq + a.att_split - 1) / a.att_split;
+  return step_grid(a, nullptr) == g0;
+}
 
 static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const int32_t* seq, const int32_t* pos,
                                 bool want_logits, cudaStream_t st) {
@@ -236,6 +279,14 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       g_prof->push_back(ev);                                      \
     }                                                             \
   } while (0)
+  if (!g_prof) {
+    StepArgs sa;
+    if (step_args(m, R, ids, seq, pos, want_logits, sa)) {
+      RUN(cudaMemsetAsync(m->s_bar, 0, 2 * sizeof(unsigned int), st));
+      RUN(launch_step(sa, st));
+      return cudaSuccess;
+    }
+  }
   if (m->fr_on) RUN(cudaMemsetAsync(m->fr_acc, 0, sizeof(unsigned long long) * m->n_lin * RMAX * 4, st));
   if (m->emb_q16) RUN(launch_embed64(m->emb_q16, ids, R, c.D, m->x, st, false));   // general Q16 rows
   else RUN(launch_embed(m->emb, c.emb_shift, ids, R, c.D, m->x, st, false));        // int8 rows << shift
@@ -704,8 +755,15 @@ int exb_model_finalize(exb_model* m) {
     if (L.fused->Mc && !L.fused->nodrop)
       FAIL(EXB_EINVAL, "per-channel linear " + L.name + " may trigger the overflow drop rule; the fused decode path "
                        "requires bitlen(K*32767*127) + bitlen(max M) <= 62");
+  std::vector<StepLayer> sl(c.NL);
+  for (int i = 0; i < c.NL; ++i) {
+    sl[i].qkv = m->L[i].qkv; sl[i].o = m->L[i].o; sl[i].gu = m->L[i].gu; sl[i].down = m->L[i].down;
+    sl[i].g1 = m->L[i].g1; sl[i].g2 = m->L[i].g2;
+  }
+  CK(cudaMemcpy(m->step_layers, sl.data(), sizeof(StepLayer) * c.NL, cudaMemcpyHostToDevice));
+  if (const char* v = getenv("EXB_STEP")) m->step_on = atoi(v) != 0;
+  if (const char* v = getenv("EXB_PF_KB")) m->pf_bytes = std::max(0, atoi(v)) * 1024;
   m->finalized = true;
-  (void)c;
   return EXB_OK;
 }
 
@@ -752,18 +810,15 @@ int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, in
   return check_device_errors(m);
 }
 
+// The token buffer holds max_batch x max_seq tokens (no call can produce more), allocated once:
+// the captured generate graphs bake its address, so it must never move.
 static int ensure_gen(exb_model* m, int B, int steps) {
-  if (m->gen_cap < B * steps) {
-    cudaFree(m->gen_tokens);
-    m->gen_tokens = nullptr;
-    CK(cudaMalloc(&m->gen_tokens, sizeof(int32_t) * (size_t)B * steps));
-    m->gen_cap = B * steps;
-    // graphs bake the token buffer pointer: drop the generate graphs
-    for (auto it = m->graphs.begin(); it != m->graphs.end();) {
-      if ((it->first >> 9) & 0x7ff) { cudaGraphExecDestroy(it->second); it = m->graphs.erase(it); }
-      else ++it;
-    }
+  if (!m->gen_tokens) {
+    const size_t cap = (size_t)m->c.max_batch * m->c.max_seq;
+    CK(cudaMalloc(&m->gen_tokens, sizeof(int32_t) * cap));
+    m->gen_cap = (int)cap;
   }
+  if ((size_t)B * steps > (size_t)m->gen_cap) FAIL(EXB_EINVAL, "generate: more tokens than max_batch x max_seq");
   return EXB_OK;
 }
 
@@ -884,6 +939,49 @@ int exb_freivalds_status(exb_model* m, int64_t* checks, int64_t* failures) {
   if (checks) *checks = m->fr_checks;
   if (failures) *failures = f;
   return EXB_OK;
+}
+
+int exb_set_option(exb_model* m, const char* name, int64_t value) {
+  if (!m || !name) FAIL(EXB_EINVAL, "null argument");
+  const std::string n(name);
+  if (n == "step") m->step_on = value != 0;
+  else if (n == "pf_kb") {
+    if (value < 0 || value > 1024) FAIL(EXB_EINVAL, "pf_kb: 0..1024");
+    m->pf_bytes = (int)value * 1024;
+  } else FAIL(EXB_EINVAL, "unknown option " + n);
+  CK(cudaStreamSynchronize(m->st));
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  m->graphs.clear();
+  return EXB_OK;
+}
+
+int exb_profile_persistent(exb_model* m, int B, uint64_t* host, int64_t n, int* nbar, int* grid) {
+  if (!m || !m->finalized || B < 1 || B > STEP_ROWS || !host || !nbar || !grid)
+    FAIL(EXB_EINVAL, "exb_profile_persistent: bad arguments");
+  for (int b = 0; b < B; ++b)
+    if (m->seq_len[b] >= m->c.max_seq) FAIL(EXB_EINVAL, "exb_profile_persistent: sequence full");
+  std::vector<int32_t> h(3 * RMAX, 0);
+  for (int b = 0; b < B; ++b) { h[RMAX + b] = b; h[2 * RMAX + b] = m->seq_len[b]; }
+  CK(cudaMemcpyAsync(m->row_ids, h.data(), sizeof(int32_t) * 3 * RMAX, cudaMemcpyHostToDevice, m->st));
+  StepArgs sa;
+  if (!step_args(m, B, m->row_ids, m->row_seq, m->row_pos, false, sa))
+    FAIL(EXB_EINVAL, "exb_profile_persistent: the persistent kernel does not take this model/step");
+  const int g = step_grid(sa, nullptr);
+  const int nb = 1 + 8 * m->c.NL;
+  if (n < (int64_t)3 * nb * g) FAIL(EXB_EINVAL, "exb_profile_persistent: buffer too small");
+  unsigned long long* d = nullptr;
+  CK(cudaMalloc(&d, sizeof(unsigned long long) * 3 * nb * g));
+  CK(cudaMemsetAsync(d, 0, sizeof(unsigned long long) * 3 * nb * g, m->st));
+  sa.prof = d;
+  CK(cudaMemsetAsync(m->s_bar, 0, 2 * sizeof(unsigned int), m->st));
+  cudaError_t e = launch_step(sa, m->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(host, d, sizeof(unsigned long long) * 3 * nb * g, cudaMemcpyDeviceToHost, m->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->st);
+  cudaFree(d);
+  if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("exb_profile_persistent: ") + cudaGetErrorString(e));
+  *nbar = nb;
+  *grid = g;
+  return check_device_errors(m);   // the step wrote position seq_len (not advanced): harmless
 }
 
 int exb_device_errors(exb_model* m, int* bits) {

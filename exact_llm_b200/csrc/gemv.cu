@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "exb_internal.h"
 #include "rowdev.cuh"
+#include "gemvdev.cuh"
 
 namespace exb {
 
@@ -31,133 +32,6 @@ constexpr int NCW = 16;                         // warps per CTA
 constexpr int GEMV_THREADS = 32 * NCW;          // 2 CTAs per SM (64 registers per thread)
 constexpr int PREFETCH_BYTES = 64 * 1024;       // per-CTA L2 prefetch before the PDL wait
 constexpr int DYN_SMEM_MAX = 200 * 1024;        // dynamic shared memory budget of one CTA
-
-EXB_DEV int4 ldg_stream(const int4* p) {
-  int4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-// 16 int16 activations (xa: 0..7, xb: 8..15, packed in pairs) times 16 int8 weights; two
-// independent dp2a chains halve the dependent latency
-EXB_DEV int dot16(const int4 w, const int4 xa, const int4 xb) {
-  int s = 0, t = 0;
-  s = __dp2a_lo(xa.x, w.x, s); t = __dp2a_lo(xb.x, w.z, t);
-  s = __dp2a_hi(xa.y, w.x, s); t = __dp2a_hi(xb.y, w.z, t);
-  s = __dp2a_lo(xa.z, w.y, s); t = __dp2a_lo(xb.z, w.w, t);
-  s = __dp2a_hi(xa.w, w.y, s); t = __dp2a_hi(xb.w, w.w, t);
-  return s + t;
-}
-
-EXB_DEV unsigned long long mod_p(int64_t v, unsigned long long P) {
-  int64_t m = v % (int64_t)P;
-  return (unsigned long long)(m < 0 ? m + (int64_t)P : m);
-}
-
-// requant of one accumulator (group: shr(tot, 28-s); per-channel with the drop rule proven
-// inactive for every input: shr(acc * M, 28 - s))
-EXB_DEV int64_t requant1(const LinW& L, int n, int64_t tot, int s) {
-  int64_t y;
-  if (L.Mg) y = shr64(tot, 28 - s);
-  else y = shr64((int64_t)((uint64_t)tot * (uint64_t)L.Mc[n]), 28 - s);
-  if (L.b) y = (int64_t)((uint64_t)y + (uint64_t)L.b[n]);
-  return y;
-}
-
-// Per-(epilogue lane, activation row) accumulators, kept in shared memory to spare registers.
-struct EpiState {
-  unsigned long long frl[3][2];   // Freivalds left-hand side residue sums (segment, prime)
-  uint64_t omax;                  // max |output| (SwiGLU)
-  int64_t best_v;                 // greedy argmax value / index
-  int best_n;
-};
-
-// Epilogue of one output unit (1 column, or a gate/up pair) for activation row r.
-template <int RPU>
-EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, int sh, EpiState& E) {
-  uint64_t& omax = E.omax;
-  unsigned long long (&frl)[3][2] = E.frl;
-  int64_t& best_v = E.best_v;
-  int& best_n = E.best_n;
-  if (RPU == 2) {
-    // SwiGLU pair: fused row 2u = gate u, 2u + 1 = up u (exact_llm.py:179)
-    const int64_t yg = requant1(a.L, 2 * ug, t2[0], sh);
-    const int64_t yu = requant1(a.L, 2 * ug + 1, t2[RPU - 1], sh);
-    const int64_t hv = shr64((int64_t)((uint64_t)isilu_dev(a.silu_t, yg) * (uint64_t)yu), 16);
-    a.out[(size_t)r * a.ldo + ug] = hv;
-    const uint64_t ah = uabs64(hv);
-    omax = ah > omax ? ah : omax;
-    if (a.raw) a.raw[(size_t)r * a.ldr + ug] = t2[0];
-    if (a.raw2) a.raw2[(size_t)r * a.ldr + ug] = t2[RPU - 1];
-    if (a.fr_nseg) {
-      const int I = a.L.N / 2;
-#pragma unroll
-      for (int pi = 0; pi < 2; ++pi) {
-        frl[0][pi] += mod_p(t2[0], fr_prime(pi)) * (unsigned long long)a.fr_r[0][pi * I + ug] % fr_prime(pi);
-        frl[1][pi] += mod_p(t2[RPU - 1], fr_prime(pi)) * (unsigned long long)a.fr_r[1][pi * I + ug] % fr_prime(pi);
-      }
-    }
-    return;
-  }
-  const int n = ug;
-  const int64_t t = t2[0];
-  if (a.raw) a.raw[(size_t)r * a.ldr + n] = t;
-  if (a.fr_nseg) {
-    const int sg = (a.fr_nseg > 2 && n >= a.fr_seg_start[2]) ? 2 : (a.fr_nseg > 1 && n >= a.fr_seg_start[1]) ? 1 : 0;
-    const int ncols = (sg + 1 < a.fr_nseg ? a.fr_seg_start[sg + 1] : a.L.N) - a.fr_seg_start[sg];
-    const int loc = n - a.fr_seg_start[sg];
-#pragma unroll
-    for (int pi = 0; pi < 2; ++pi) {
-      const unsigned long long v = mod_p(t, fr_prime(pi)) * (unsigned long long)a.fr_r[sg][pi * ncols + loc] % fr_prime(pi);
-      if (sg == 0) frl[0][pi] += v; else if (sg == 1) frl[1][pi] += v; else frl[2][pi] += v;
-    }
-  }
-  if (a.epi == EPI_RAW) return;
-  const int64_t y = requant1(a.L, n, t, sh);
-  if (a.epi == EPI_RESID) {
-    int64_t* o = a.out + (size_t)r * a.ldo + n;
-    *o = (int64_t)((uint64_t)*o + (uint64_t)y);
-  } else if (a.out) {
-    a.out[(size_t)r * a.ldo + n] = y;
-  }
-  if (a.epi == EPI_HEAD && (y > best_v || (y == best_v && n < best_n))) {
-    best_v = y;
-    best_n = n;
-  }
-}
-
-// Sum V int64 values over the warp by recursive halving; payload of P int64 per value.
-// On return lane l holds the totals of value (l / (32 / V)).
-template <int V, int P>
-EXB_DEV void warp_reduce_halving(int64_t (&v)[V][P]) {
-  const int lane = threadIdx.x & 31;
-  int cnt = V;
-#pragma unroll
-  for (int step = 16; step >= 1; step >>= 1) {
-    if (cnt > 1) {
-      const int half = cnt >> 1;
-      const bool upper = (lane & step) != 0;
-#pragma unroll
-      for (int i = 0; i < V / 2; ++i) {
-        if (i < half) {
-#pragma unroll
-          for (int p = 0; p < P; ++p) {
-            const int64_t send = upper ? v[i][p] : v[i + half][p];
-            const int64_t keep = upper ? v[i + half][p] : v[i][p];
-            v[i][p] = (int64_t)((uint64_t)keep + (uint64_t)__shfl_xor_sync(0xffffffffu, send, step));
-          }
-        }
-      }
-      cnt = half;
-    } else {
-#pragma unroll
-      for (int p = 0; p < P; ++p)
-        v[0][p] = (int64_t)((uint64_t)v[0][p] + (uint64_t)__shfl_xor_sync(0xffffffffu, v[0][p], step));
-    }
-  }
-}
 
 template <int R, int RPU, bool GROUP, int RB>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
@@ -210,7 +84,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     // xq, s = qrow(irms(x, g)) for every row, computed by this CTA (exact_llm.py:100-106, 41-46)
     int64_t* ys = reinterpret_cast<int64_t*>(smem_raw + (((size_t)R * K * 2 + 127) & ~(size_t)127));
     for (int r = 0; r < R; ++r)
-      row_norm_q<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, xs + (size_t)r * K, &sh_s[r], ys, rred);
+      row_norm_q_any<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, xs + (size_t)r * K, &sh_s[r], ys, rred);
   } else {
     // xq = clip(shr(x, s)) with s from the producer's published row max (exact_llm.py:41-46)
     for (int r = 0; r < R; ++r) {
@@ -396,7 +270,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
       rope_cache_rows<GEMV_THREADS>(a.rope);
     } else if (a.tail == TAIL_NORM) {
       for (int r = 0; r < R; ++r)
-        row_norm_q<GEMV_THREADS>(a.tail_x + (size_t)r * a.tail_ldx, a.tail_gain, a.tail_K,
+        row_norm_q_any<GEMV_THREADS>(a.tail_x + (size_t)r * a.tail_ldx, a.tail_gain, a.tail_K,
                                  a.tail_xq + (size_t)r * a.tail_ldq, a.tail_xs + r, ys, rred);
     } else {
       for (int r = 0; r < R; ++r) {

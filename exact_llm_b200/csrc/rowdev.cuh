@@ -16,42 +16,190 @@ namespace exb {
 
 EXB_DEV int64_t ld_cg(const int64_t* p) { return (int64_t)__ldcg(reinterpret_cast<const long long*>(p)); }
 
-// One row already staged in shared memory (`ys`, D int64; overwritten): irms + qrow.
-// `m` is this thread's partial max |x| over the elements it staged; `gs` holds the gains (D int64)
-// when the caller staged them too, else nullptr (gains are then read from global memory).
+// Two-barrier block reductions for the latency-bound row operations: warp shuffles, one slot per
+// warp in `buf` (NT/32 entries), one barrier, then every thread folds the slots itself.  A caller
+// alternates two buffers between consecutive reductions (the barrier of reduction i+1 orders
+// every read of reduction i's buffer before reduction i+2 writes it).
+template <int NT>
+EXB_DEV uint64_t block_max_fast(uint64_t v, uint64_t* buf) {
+  v = warp_max_u64(v);
+  if ((threadIdx.x & 31) == 0) buf[threadIdx.x >> 5] = v;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  return warp_max_u64(lane < NT / 32 ? buf[lane] : 0);
+}
+template <int NT>
+EXB_DEV uint64_t block_sum_fast(uint64_t v, uint64_t* buf) {
+  v = warp_sum_u64(v);
+  if ((threadIdx.x & 31) == 0) buf[threadIdx.x >> 5] = v;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  return warp_sum_u64(lane < NT / 32 ? buf[lane] : 0);
+}
+
+// floor(a / b) for b > 0 when the quotient is known to be far below 2^50: one estimate with a
+// precomputed reciprocal, then at most two exact integer corrections each way; any other case
+// (never met for the operands below) takes the general exact routine.
+EXB_DEV int64_t floordiv_small_q(int64_t a, int64_t b, double inv) {
+  int64_t q = __double2ll_rz(__ll2double_rn(a) * inv);
+  int64_t r = (int64_t)((uint64_t)a - (uint64_t)q * (uint64_t)b);
+  if (r < 0) { q -= 1; r += b; }
+  if (r < 0) { q -= 1; r += b; }
+  if (r >= b) { q += 1; r -= b; }
+  if (r >= b) { q += 1; r -= b; }
+  if (r < 0 || r >= b) q = floordiv_recip(a, b, inv);
+  return q;
+}
+
+// Row-constant divisor of irms: den = rt << k (exact_llm.py:105).  y = (x << 16) // den with
+// numpy int64 semantics.  Fast path (|x| < 2^47, so x << 16 does not wrap, and rt << k < 2^62):
+// floor division nests, y = ((x << 16) >> k) // rt with |(x << 16) >> k| < 2^41 and rt < 2^25,
+// computed with a 64-bit reciprocal (high half of a 64 x 64 product) and one exact correction.
+struct NormDiv {
+  int64_t den, rt;
+  uint64_t m;            // ~2^64 / rt, within 2^12 below the exact value
+  double inv;            // 1 / den for the general path
+  int k;
+  bool fast;
+};
+EXB_DEV NormDiv make_norm_div(int64_t rt, int k) {
+  NormDiv d;
+  d.rt = rt; d.k = k;
+  d.den = (int64_t)((uint64_t)rt << k);
+  d.inv = __drcp_rn((double)d.den);
+  d.fast = (bitlen64((uint64_t)rt) + k) <= 62;
+  const double e = 18446744073709551616.0 / (double)rt;             // 2^64 / rt
+  d.m = e >= 18446744073709549568.0 ? ~0ull : (uint64_t)e;           // rt = 1: saturate
+  d.m = d.m > 4096 ? d.m - 4096 : 0;                                 // never above the exact value
+  return d;
+}
+EXB_DEV int64_t norm_div(int64_t x, const NormDiv& d) {
+  const uint64_t ax = uabs64(x);
+  if (d.fast && ax < (1ull << 47)) {
+    const int64_t n = ((int64_t)((uint64_t)x << 16)) >> d.k;         // floor((x << 16) / 2^k)
+    const uint64_t an = uabs64(n);
+    uint64_t q = __umul64hi(an, d.m);                                // floor(an / rt) - {0, 1, 2}
+    uint64_t r = an - q * (uint64_t)d.rt;
+    if (r >= (uint64_t)d.rt) { q += 1; r -= (uint64_t)d.rt; }
+    if (r >= (uint64_t)d.rt) { q += 1; r -= (uint64_t)d.rt; }
+    if (r >= (uint64_t)d.rt) { q += 1; r -= (uint64_t)d.rt; }
+    return n >= 0 ? (int64_t)q : -(int64_t)q - (r != 0 ? 1 : 0);
+  }
+  return floordiv_recip((int64_t)((uint64_t)x << 16), d.den, d.inv);
+}
+
+// One row already staged in shared memory (`ys`, D int64; overwritten): irms + qrow
+// (exact_llm.py:100-106 then :41-46).  `m` is this thread's partial max |x| over the elements
+// it staged; `gs` holds the gains (D int64) when the caller staged them too, else nullptr (gains
+// are then read from global memory).  `red` holds 2 * NT/32 uint64.
+//   k   = max(bitlen(max|x|) - 24, 0);  ms = sum(shr(x, k)^2) // D + 1;  r = max(isqrt(ms), 1)
+//   y_i = (x_i << 16) // (r << k);      a_i = shr(y_i * g_i, 16);        xq, s = qrow(a)
+// |y_i| <= 2^16 sqrt(D) (2^(k+24) * 2^16 at k = 0), so every quotient is far below 2^50.
 template <int NT>
 EXB_DEV void row_norm_q_staged(const int64_t* __restrict__ g, int D, int16_t* __restrict__ xq,
                                int32_t* __restrict__ xs_out, int64_t* ys, uint64_t* red, uint64_t m,
                                const int64_t* gs = nullptr) {
-  m = block_max_u64<NT>(m, red);
+  uint64_t* rA = red;
+  uint64_t* rB = red + NT / 32;
+  m = block_max_fast<NT>(m, rA);
   int k = bitlen64(m) - 24;
   k = k > 0 ? k : 0;
   uint64_t ss = 0;
+#pragma unroll 4
   for (int i = threadIdx.x; i < D; i += NT) {
     const int64_t v = shr64(ys[i], k);
     ss += (uint64_t)v * (uint64_t)v;
   }
-  const int64_t sum = block_sum_i64<NT>((int64_t)ss, red);
-  const int64_t ms = floordiv64(sum, D) + 1;
+  const uint64_t sum = block_sum_fast<NT>(ss, rB);      // < D * 2^48: non-negative as int64
+  // ms = sum // D + 1 with a double estimate and exact corrections
+  const double invD = 1.0 / (double)D;
+  int64_t q = __double2ll_rz(__ll2double_rn((int64_t)sum) * invD);
+  int64_t rem = (int64_t)sum - q * (int64_t)D;
+  while (rem < 0) { q -= 1; rem += D; }
+  while (rem >= D) { q += 1; rem -= D; }
+  const int64_t ms = q + 1;
   int64_t rt = isqrt_ref(ms);
   rt = rt > 1 ? rt : 1;
   const int64_t den = (int64_t)((uint64_t)rt << k);
-  const double inv = 1.0 / (double)den;
+  const double inv = __drcp_rn((double)den);
   uint64_t m2 = 0;
+#pragma unroll 4
   for (int i = threadIdx.x; i < D; i += NT) {
-    const int64_t y = floordiv_recip((int64_t)((uint64_t)ys[i] << 16), den, inv);
+    const int64_t y = floordiv_small_q((int64_t)((uint64_t)ys[i] << 16), den, inv);
     const int64_t gi = gs ? gs[i] : __ldg(g + i);
     const int64_t a = shr64((int64_t)((uint64_t)y * (uint64_t)gi), 16);
     ys[i] = a;
     const uint64_t u = uabs64(a);
     m2 = u > m2 ? u : m2;
   }
-  m2 = block_max_u64<NT>(m2, red);
+  m2 = block_max_fast<NT>(m2, rA);
   const int s = qrow_shift(m2);
+#pragma unroll 4
   for (int i = threadIdx.x; i < D; i += NT) xq[i] = qrow_value(ys[i], s);
   if (threadIdx.x == 0) *xs_out = s;
   __syncthreads();
 }
+
+// One row: irms + qrow with the row held in registers: EPT elements per thread (D <= NT * EPT),
+// element i = threadIdx.x + j * NT in slot j.  Every per-element step is an independent chain the
+// compiler interleaves across the EPT slots; nothing is staged in shared memory.  `red` holds
+// 2 * NT/32 uint64.  Same arithmetic as row_norm_q_staged (exact_llm.py:100-106 then :41-46).
+template <int NT, int EPT>
+EXB_DEV void row_norm_q_regs(const int64_t* __restrict__ xr, const int64_t* __restrict__ g, int D,
+                             int16_t* __restrict__ xq, int32_t* __restrict__ xs_out, uint64_t* red) {
+  uint64_t* rA = red;
+  uint64_t* rB = red + NT / 32;
+  int64_t v[EPT], gv[EPT];
+  uint64_t m = 0;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int i = threadIdx.x + j * NT;
+    v[j] = i < D ? ld_cg(xr + i) : 0;
+    gv[j] = i < D ? __ldg(g + i) : 0;
+  }
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) { const uint64_t u = uabs64(v[j]); m = u > m ? u : m; }
+  m = block_max_fast<NT>(m, rA);
+  int k = bitlen64(m) - 24;
+  k = k > 0 ? k : 0;
+  uint64_t ss = 0;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int64_t t = shr_nn(v[j], k);                 // 0 for the padding slots; 0 <= k <= 39
+    ss += (uint64_t)t * (uint64_t)t;
+  }
+  const uint64_t sum = block_sum_fast<NT>(ss, rB);
+  const double invD = 1.0 / (double)D;
+  int64_t q = __double2ll_rz(__ll2double_rn((int64_t)sum) * invD);
+  int64_t rem = (int64_t)sum - q * (int64_t)D;
+  while (rem < 0) { q -= 1; rem += D; }
+  while (rem >= D) { q += 1; rem -= D; }
+  int64_t rt = isqrt_ref(q + 1);
+  rt = rt > 1 ? rt : 1;
+  const NormDiv nd = make_norm_div(rt, k);
+  uint64_t m2 = 0;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int64_t y = norm_div(v[j], nd);
+    v[j] = shr_nn((int64_t)((uint64_t)y * (uint64_t)gv[j]), 16);
+    const uint64_t u = uabs64(v[j]);
+    m2 = u > m2 ? u : m2;
+  }
+  m2 = block_max_fast<NT>(m2, rA);
+  const int s = qrow_shift(m2);
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int i = threadIdx.x + j * NT;
+    if (i < D) xq[i] = qrow_value(v[j], s);
+  }
+  if (threadIdx.x == 0) *xs_out = s;
+  __syncthreads();
+}
+
+// irms + qrow of one row: registers when D <= 12 NT, else staged in shared memory (`ys`, 2*D int64)
+template <int NT>
+EXB_DEV void row_norm_q_any(const int64_t* __restrict__ xr, const int64_t* __restrict__ g, int D,
+                            int16_t* __restrict__ xq, int32_t* __restrict__ xs_out, int64_t* ys, uint64_t* red);
 
 // One row: irms + qrow.  `ys` = 2*D int64 of shared memory (row, then gains), loaded with all
 // requests in flight (16-byte loads); `red` = 33 uint64 of shared memory.  D is even.
@@ -74,6 +222,15 @@ EXB_DEV void row_norm_q(const int64_t* __restrict__ xr, const int64_t* __restric
   }
   __syncthreads();
   row_norm_q_staged<NT>(g, D, xq, xs_out, ys, red, m, gs);
+}
+
+template <int NT>
+EXB_DEV void row_norm_q_any(const int64_t* __restrict__ xr, const int64_t* __restrict__ g, int D,
+                            int16_t* __restrict__ xq, int32_t* __restrict__ xs_out, int64_t* ys, uint64_t* red) {
+  if (D <= 4 * NT) row_norm_q_regs<NT, 4>(xr, g, D, xq, xs_out, red);
+  else if (D <= 8 * NT) row_norm_q_regs<NT, 8>(xr, g, D, xq, xs_out, red);
+  else if (D <= 12 * NT) row_norm_q_regs<NT, 12>(xr, g, D, xq, xs_out, red);
+  else row_norm_q<NT>(xr, g, D, xq, xs_out, ys, red);
 }
 
 // One row: qrow.  Values are staged in shared memory (`ys`, K int64) so the row is read once.

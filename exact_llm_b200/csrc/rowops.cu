@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restric
   pdl_wait();
   pdl_launch_dependents();
   const int r = blockIdx.x;
-  row_norm_q<ROW_THREADS>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, ys, red);
+  row_norm_q_any<ROW_THREADS>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, ys, red);
 }
 
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,

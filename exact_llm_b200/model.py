@@ -166,6 +166,11 @@ class ExactModel:
         tokens = [first] + [int(t) for t in toks[0, :-1]]
         return lg, [rows[s, 0] for s in range(steps)], tokens
 
+    def set_option(self, name, value):
+        """Engine option (results never change): "step" (persistent decode kernel on/off),
+        "pf_kb" (its per-warp L2 prefetch distance in KiB)."""
+        check(lib.exb_set_option(self.h, name.encode(), int(value)))
+
     # ------------------------------------------------------------------ trace + Freivalds
     def trace_enable(self, on=True):
         check(lib.exb_trace_enable(self.h, int(on)))

@@ -142,6 +142,13 @@ int exb_freivalds_read_keys(exb_model* m, int32_t* d_host, int64_t n);   /* 2 x 
 int exb_freivalds_enable(exb_model* m, int on);
 int exb_freivalds_status(exb_model* m, int64_t* checks, int64_t* failures);
 
+/* Engine options (no counterpart in the reference; they change speed, never results):
+ *   "step"    1: decode steps of <= 2 rows without trace/Freivalds capture run as one persistent
+ *             kernel (grid barriers between phases); 0 (default): one kernel per operation
+ *   "pf_kb"   per-CTA L2 prefetch of the next weight slices where HBM would idle, KiB (default 64; 0 = off)
+ * Cached step graphs are dropped. */
+int exb_set_option(exb_model* m, const char* name, int64_t value);
+
 /* device error word: bit 1 |V| >= 2^31 (V cache range), 2 wait timeout, 4 Freivalds, 8 bounds */
 int exb_device_errors(exb_model* m, int* bits);
 
@@ -155,6 +162,13 @@ int exb_bench_linear(exb_model* m, int layer, int which, int R, int reps, float*
  * launch overlap) with a CUDA event after every launch; ms_out[i] = duration of launch i.  The step
  * writes the KV cache at each sequence's current length without advancing it. */
 int exb_profile_step(exb_model* m, int B, float* ms_out, int max_n, int* n_out);
+
+/* Profiling the persistent decode-step kernel: one step for sequences 0..B-1 (B <= 2, not
+ * advanced), with a global-timer stamp (ns) when each CTA arrives at and leaves each grid barrier:
+ * host[(2k) * grid + c] = arrival of CTA c at barrier k, host[(2k + 1) * grid + c] = release,
+ * host[(2 nbar + k) * grid + c] = end of the prologue of the GEMV phase after barrier k - 1 (0 if none).
+ * Barriers: 0 after the embedding, then 8 per layer (q|k|v, attention x3, o, gate|up, qrow(h), down). */
+int exb_profile_persistent(exb_model* m, int B, uint64_t* host, int64_t n, int* nbar, int* grid);
 
 /* raw pointers for benchmarks / interop */
 void* exb_model_stream(exb_model* m);

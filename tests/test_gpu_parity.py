@@ -200,6 +200,30 @@ def test_synthetic_models_vs_reference(golden, cuda_ok, key):
     assert [eo.h16(r) for r in rows] == g["rows"]
 
 
+@pytest.mark.parametrize("B", [1, 2])
+def test_persistent_step_matches_per_kernel_path(cuda_ok, B):
+    """The persistent decode-step kernel and the one-kernel-per-operation path give the same
+    logits and tokens (7B layer shapes, 2 layers, B sequences decoded together)."""
+    from exact_llm_b200 import ExactModel, configs
+    c = configs.arch("qwen2.5-7b", NL=2)
+    m = ExactModel.synthetic(c, 77, max_batch=2, max_seq=96)
+    rng = np.random.default_rng(5)
+    prompts = rng.integers(0, c["V"], (B, 21)).astype(np.int32)
+    out = {}
+    for step in (1, 0):
+        m.set_option("step", step)
+        for b in range(B):
+            m.new_cache(b)
+        ids = prompts.T.reshape(-1)
+        seqs = np.tile(np.arange(B, dtype=np.int32), prompts.shape[1])
+        _, nxt = m.forward_rows(ids, seqs, want_logits=False)
+        first = nxt[-B:].astype(np.int32)
+        toks, rows = m.generate(first, 12, want_logits=True)
+        out[step] = (np.array(toks), np.array(rows))
+    assert np.array_equal(out[1][0], out[0][0])
+    assert np.array_equal(out[1][1], out[0][1])
+
+
 def test_freivalds_keys_and_self_check(golden, cuda_ok):
     """Device keys equal the reference keys (rng seeded 2026); honest steps pass every check;
     a corrupted weight is caught (experiments/gpu_engine_trace_verify_kaggle.py:803-872)."""
