@@ -462,9 +462,12 @@ int exb_gemv(const int16_t* x16, const int8_t* wT, const int64_t* Mg, int K, int
 static size_t xq_bytes(int R, int K) { return ((size_t)R * K * sizeof(int16_t) + 255) / 256 * 256; }
 static size_t xs_bytes(int R) { return ((size_t)R * sizeof(int32_t) + 255) / 256 * 256; }
 
+static size_t scale_bytes(int K, int N) { return ((size_t)N * (size_t)(((K / 128) + 3) & ~3) * 4 + 255) / 256 * 256; }
+
 size_t exb_linear_g128_scratch_bytes(int R, int K, int N) {
-  const size_t ldm = (size_t)(((K / 128) + 3) & ~3);
-  return xq_bytes(R, K) + xs_bytes(R) + (size_t)N * ldm * 4;
+  size_t b = xq_bytes(R, K) + xs_bytes(R) + scale_bytes(K, N);
+  if (R >= TC_MIN_ROWS) b += gemm_tc_digit_bytes(R, K);       // int8 digit planes for the tensor cores
+  return b;
 }
 
 static int linear_common(const int64_t* x, int R, int K, const LinW& L, int64_t* y, int64_t* raw, void* scratch,
@@ -472,6 +475,13 @@ static int linear_common(const int64_t* x, int R, int K, const LinW& L, int64_t*
   int16_t* xq = (int16_t*)scratch;
   int32_t* xs = (int32_t*)((char*)scratch + xq_bytes(R, K));
   CK(launch_quant(x, K, R, K, xq, K, xs, st, false));
+  if (!channel && R >= TC_MIN_ROWS && gemm_tc_supported(L, EPI_STORE)) {
+    // tcgen05 path: digit planes behind the (re-pitched) scales in the scratch buffer
+    void* digits = (char*)scratch + xq_bytes(R, K) + xs_bytes(R) + scale_bytes(K, L.N);
+    CK(launch_digits(xq, K, R, K, digits, st));
+    CK(launch_gemm_tc(digits, R, L, xs, EPI_STORE, y, L.N, raw, nullptr, L.N, nullptr, nullptr, st));
+    return EXB_OK;
+  }
   for (int r0 = 0; r0 < R; r0 += RMAX) {
     const int rr = R - r0 < RMAX ? R - r0 : RMAX;
     GemvArgs g;

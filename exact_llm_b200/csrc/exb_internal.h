@@ -147,6 +147,16 @@ cudaError_t launch_fr_keys(const int8_t* w, const int32_t* Mg, int ldm, int N, i
 cudaError_t launch_fr_check(const unsigned long long* acc, int nchecks, int* fail_count, int* err,
                             cudaStream_t st, bool pdl);
 
+// ---------------------------------------------------------------- tcgen05 group-128 GEMM (many rows)
+constexpr int TC_MIN_ROWS = 16;        // activation rows from which the tensor-core path is used
+size_t gemm_tc_digit_bytes(int T, int K);
+// int8 digit planes (lo = xq & 255, hi = xq >> 8) of T int16 rows, padded to the tile height
+cudaError_t launch_digits(const int16_t* xq, int ldx, int T, int K, void* digits, cudaStream_t st);
+bool gemm_tc_supported(const LinW& L, int epi);
+// tot / requant epilogue of a group-128 linear over T activation rows given as digit planes
+cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32_t* xs, int epi, int64_t* out, int ldo,
+                           int64_t* raw, int64_t* raw2, int ldr, const int32_t* silu_t, int* err, cudaStream_t st);
+
 // ---------------------------------------------------------------- persistent decode step
 // One layer's linears and norm gains, as the persistent step kernel reads them (device array).
 struct StepLayer {

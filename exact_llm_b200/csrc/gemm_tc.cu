@@ -1,0 +1,360 @@
+// K3: exact group-128 linear on tcgen05 tensor cores, for many activation rows (prefill chunks,
+// batched decode, the reference linear operator at M >= 16).
+//
+//   tot[t, n] = sum_g M[n, g] * sum_{k in g} xq[t, k] * W[n, k]        (int64, exact)
+//   (experiments/speed_fair_kaggle.py:722-725 of novain-shibu/exact-llm; SPEC.md:18)
+//
+// int16 activations do not fit an int8 MMA, so each row is split into two int8 digit planes,
+// xq = 256 * hi + lo with lo = xq & 255 (unsigned) and hi = xq >> 8 (signed).  Per 128-wide group
+// the tensor core accumulates two int32 sums (kind::i8, A = W signed, B = lo unsigned / hi
+// signed); |sum| <= 128 * 255 * 127 < 2^31, so both are exact, and acc_g = 256 * hi + lo is the
+// reference's exact group sum (it fits int32: 128 * 32767 * 127 < 2^31).  The epilogue warps then
+// form tot += acc_g * M[n, g] in int64 registers, one TMEM lane (= one output row n) per thread.
+//
+// Roles ("swap AB": the weights are the MMA's M side, the activation rows its N side):
+//   warp 0  TMA producer: per group a 128 x 128-byte weight tile and two 64 x 128-byte digit
+//           tiles (128-byte swizzle) into a 4-stage shared-memory ring
+//   warp 1  TMEM allocation and the MMA issuer (one elected thread): 8 MMAs per group (2 digits
+//           x 4 K-steps of 32) into a double-buffered TMEM accumulator
+//   warps 2-5  epilogue: tcgen05.ld of both digit accumulators, int64 fold with the group scale,
+//           and at the end requant / bias / residual / SwiGLU (exact_llm.py:41-46, 176-179)
+// Every wait is bounded: a stuck barrier sets the error word, the roles stop, TMEM is freed.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "exb_internal.h"
+#include "gemvdev.cuh"
+
+namespace exb {
+
+constexpr int TC_BM = 128;                              // output rows per tile (MMA M)
+constexpr int TC_BN = 64;                               // activation rows per tile (MMA N)
+constexpr int TC_STAGES = 4;
+constexpr int TC_A_BYTES = TC_BM * 128;                 // one group of 128 weight rows
+constexpr int TC_B_BYTES = TC_BN * 128;                 // one group of 64 activation rows, one digit
+constexpr int TC_STAGE_BYTES = TC_A_BYTES + 2 * TC_B_BYTES;
+constexpr int TC_THREADS = 192;
+constexpr int TC_TMEM_COLS = 256;                       // 2 buffers x 2 digits x 64 columns
+constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024;   // + alignment slack
+constexpr uint32_t TC_WAIT_LIMIT = 1u << 24;
+
+struct TcArgs {
+  int N = 0, K = 0, T = 0;
+  int ldm = 0;
+  const int32_t* Mg = nullptr;        // (N, ldm) group scales; nullptr: unscaled sums (per-channel linear)
+  const int32_t* xs = nullptr;        // (T) activation row shifts
+  const int64_t* bias = nullptr;
+  int epi = EPI_RAW;                  // EPI_RAW, EPI_STORE, EPI_RESID, EPI_SWIGLU
+  int64_t* out = nullptr; int ldo = 0;
+  int64_t* raw = nullptr; int ldr = 0;
+  int64_t* raw2 = nullptr;            // SwiGLU: raw sums of the up rows
+  const int32_t* silu_t = nullptr;
+  int* err = nullptr;
+};
+
+// ---------------------------------------------------------------- PTX wrappers
+EXB_DEV bool tc_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < TC_WAIT_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+EXB_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+EXB_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+EXB_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+EXB_DEV void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+EXB_DEV void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+      : "memory");
+}
+// 16 consecutive 32-bit TMEM columns of this thread's lane
+EXB_DEV void tmem_ld16(uint32_t taddr, int32_t (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = (int32_t)r[i];
+}
+EXB_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major operand in the 128-byte swizzled layout written by
+// TMA (rows of 128 bytes, 8-row core groups 1024 bytes apart), advanced by 32 bytes per K-step.
+EXB_DEV uint64_t tc_desc(const void* tile, int kstep) {
+  const uint32_t addr = smem_u32(tile) + 32u * (uint32_t)kstep;
+  return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+// Instruction descriptor: int32 accumulate, A = signed int8 (weights), B = unsigned (low digit)
+// or signed (high digit) int8, both K-major, M = 128, N = 64.
+__host__ __device__ constexpr uint32_t tc_idesc(bool b_signed) {
+  return (2u << 4) | (1u << 7) | ((b_signed ? 1u : 0u) << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
+         ((uint32_t)(TC_BM >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- the kernel
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmLo,
+              const __grid_constant__ CUtensorMap tmHi, const TcArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint64_t full[TC_STAGES], empty[TC_STAGES], accf[2], acce[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh, issued_sh, consumed_sh;
+  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tm = blockIdx.x, tn = blockIdx.y;
+  const int G = a.K >> 7;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 128); }
+    abort_sh = 0; issued_sh = 0; consumed_sh = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                 "r"(TC_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    // ---- TMA producer
+    if (lane == 0) {
+      for (int g = 0; g < G; ++g) {
+        const int s = g % TC_STAGES;
+        if (g >= TC_STAGES && !tc_wait(&empty[s], ((g / TC_STAGES) - 1) & 1)) {
+          abort_sh = 1;
+          set_err(a.err, ERR_WAIT_TIMEOUT);
+          break;
+        }
+        if (*(volatile int*)&abort_sh) break;
+        unsigned char* st = smem + (size_t)s * TC_STAGE_BYTES;
+        mbar_expect_tx(&full[s], TC_STAGE_BYTES);
+        tma_load_2d(st, &tmA, g * 128, tm * TC_BM, &full[s]);
+        tma_load_2d(st + TC_A_BYTES, &tmLo, g * 128, tn * TC_BN, &full[s]);
+        tma_load_2d(st + TC_A_BYTES + TC_B_BYTES, &tmHi, g * 128, tn * TC_BN, &full[s]);
+        *(volatile int*)&issued_sh = g + 1;
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      const uint32_t id_lo = tc_idesc(false), id_hi = tc_idesc(true);
+      for (int g = 0; g < G; ++g) {
+        const int s = g % TC_STAGES, b = g & 1;
+        if (!tc_wait(&full[s], (g / TC_STAGES) & 1) || !tc_wait(&acce[b], ((g >> 1) & 1) ^ 1)) {
+          abort_sh = 1;
+          set_err(a.err, ERR_WAIT_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const unsigned char* st = smem + (size_t)s * TC_STAGE_BYTES;
+        const uint32_t d_lo = tmem + (uint32_t)(b * 2 * TC_BN), d_hi = d_lo + TC_BN;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) tc_mma_i8(d_lo, tc_desc(st, k), tc_desc(st + TC_A_BYTES, k), id_lo, k > 0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_i8(d_hi, tc_desc(st, k), tc_desc(st + TC_A_BYTES + TC_B_BYTES, k), id_hi, k > 0);
+        tc_commit(&empty[s]);           // the stage is free once these MMAs have read it
+        tc_commit(&accf[b]);            // the group's accumulators are complete
+        *(volatile int*)&consumed_sh = g + 1;
+      }
+    }
+  } else {
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31; thread = output row n
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int n = tm * TC_BM + row;
+    int64_t tot[TC_BN];
+#pragma unroll
+    for (int j = 0; j < TC_BN; ++j) tot[j] = 0;
+    const int32_t* mrow = a.Mg ? a.Mg + (size_t)n * a.ldm : nullptr;
+    int32_t mnext = mrow ? __ldg(mrow) : 1;
+    bool ok = true;
+    for (int g = 0; g < G; ++g) {
+      const int b = g & 1;
+      const int32_t mv = mnext;
+      if (mrow && g + 1 < G) mnext = __ldg(mrow + g + 1);
+      // warp-uniform outcome: the TMEM loads below are .sync.aligned over the whole warp
+      if (!__all_sync(0xffffffffu, tc_wait(&accf[b], (g >> 1) & 1))) {
+        ok = false;
+        set_err(a.err, ERR_WAIT_TIMEOUT);
+        abort_sh = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t_lo = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * TC_BN);
+#pragma unroll
+      for (int c = 0; c < TC_BN / 16; ++c) {
+        int32_t lo[16], hi[16];
+        tmem_ld16(t_lo + c * 16, lo);
+        tmem_ld16(t_lo + TC_BN + c * 16, hi);
+        tmem_wait_ld();
+        if (c == TC_BN / 16 - 1) {
+          tc_fence_before();
+          mbar_arrive(&acce[b]);        // buffer b may be overwritten by the next-but-one group
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int32_t accg = hi[i] * 256 + lo[i];        // exact group sum (|.| < 2^30)
+          tot[c * 16 + i] = (int64_t)((uint64_t)tot[c * 16 + i] + (uint64_t)((int64_t)accg * mv));
+        }
+      }
+    }
+    if (ok) {
+      // final epilogue per (activation row t, output row n): coalesced over n for each t
+#pragma unroll
+      for (int j = 0; j < TC_BN; ++j) {
+        const int t = tn * TC_BN + j;
+        const bool live = t < a.T;
+        const int64_t v = tot[j];
+        if (a.epi == EPI_SWIGLU) {
+          // rows 2u (gate) and 2u + 1 (up) sit in adjacent lanes
+          const int sh = live ? a.xs[t] : 0;
+          int64_t y = shr64(v, 28 - sh);
+          const int64_t other = __shfl_xor_sync(0xffffffffu, y, 1);
+          const int64_t vother = __shfl_xor_sync(0xffffffffu, v, 1);
+          if (live && !(n & 1)) {
+            const int u = n >> 1;
+            const int64_t hv = shr64((int64_t)((uint64_t)isilu_dev(a.silu_t, y) * (uint64_t)other), 16);
+            a.out[(size_t)t * a.ldo + u] = hv;
+            if (a.raw) a.raw[(size_t)t * a.ldr + u] = v;
+            if (a.raw2) a.raw2[(size_t)t * a.ldr + u] = vother;
+          }
+          continue;
+        }
+        if (!live) continue;
+        if (a.raw) a.raw[(size_t)t * a.ldr + n] = v;
+        if (a.epi == EPI_RAW) continue;
+        int64_t y = shr64(v, 28 - a.xs[t]);
+        if (a.bias) y = (int64_t)((uint64_t)y + (uint64_t)a.bias[n]);
+        int64_t* o = a.out + (size_t)t * a.ldo + n;
+        if (a.epi == EPI_RESID) *o = (int64_t)((uint64_t)*o + (uint64_t)y);
+        else *o = y;
+      }
+    }
+  }
+  // drain: on an aborted run wait (bounded) for the weight/digit copies that were issued but never
+  // consumed and for the last MMA group, so nothing writes shared memory or TMEM after the exit
+  __syncthreads();
+  if (abort_sh && threadIdx.x == 32) {
+    for (int g = consumed_sh; g < issued_sh; ++g) (void)tc_wait(&full[g % TC_STAGES], (g / TC_STAGES) & 1);
+    if (consumed_sh > 0) {
+      const int g = consumed_sh - 1;
+      (void)tc_wait(&accf[g & 1], (g >> 1) & 1);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+}
+
+// ---------------------------------------------------------------- digit planes
+// lo = xq & 255 (as uint8), hi = xq >> 8 (int8); rows t >= T are zero (padding to a tile)
+__global__ void k_digits(const int16_t* __restrict__ xq, int ldx, int T, int K, int Tpad, uint8_t* __restrict__ lo,
+                         int8_t* __restrict__ hi) {
+  const long long n = (long long)Tpad * K / 2;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long e = 2 * i;
+    const int t = (int)(e / K), k = (int)(e - (long long)t * K);
+    short2 v = make_short2(0, 0);
+    if (t < T) v = *reinterpret_cast<const short2*>(xq + (size_t)t * ldx + k);
+    reinterpret_cast<uchar2*>(lo)[i] = make_uchar2((uint8_t)(v.x & 255), (uint8_t)(v.y & 255));
+    reinterpret_cast<char2*>(hi)[i] = make_char2((int8_t)(v.x >> 8), (int8_t)(v.y >> 8));
+  }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// rows x cols bytes, row pitch `pitch` bytes, box of box_rows x 128 bytes, 128-byte swizzle
+static bool make_map(CUtensorMap* m, const void* base, int rows, int cols, size_t pitch, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)pitch};
+  const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t gemm_tc_digit_bytes(int T, int K) {
+  const size_t Tpad = (size_t)(T + TC_BN - 1) / TC_BN * TC_BN;
+  return 2 * Tpad * (size_t)K;
+}
+
+cudaError_t launch_digits(const int16_t* xq, int ldx, int T, int K, void* digits, cudaStream_t st) {
+  const int Tpad = (T + TC_BN - 1) / TC_BN * TC_BN;
+  uint8_t* lo = static_cast<uint8_t*>(digits);
+  int8_t* hi = reinterpret_cast<int8_t*>(lo + (size_t)Tpad * K);
+  const long long n = (long long)Tpad * K / 2;
+  const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+  k_digits<<<blocks, 256, 0, st>>>(xq, ldx, T, K, Tpad, lo, hi);
+  return cudaGetLastError();
+}
+
+bool gemm_tc_supported(const LinW& L, int epi) {
+  return L.w && L.K % 128 == 0 && L.N % TC_BM == 0 && ((uintptr_t)L.w & 15) == 0 &&
+         (epi == EPI_RAW || epi == EPI_STORE || epi == EPI_RESID || epi == EPI_SWIGLU) && encode_fn() != nullptr;
+}
+
+cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32_t* xs, int epi, int64_t* out, int ldo,
+                           int64_t* raw, int64_t* raw2, int ldr, const int32_t* silu_t, int* err, cudaStream_t st) {
+  if (!gemm_tc_supported(L, epi) || T <= 0) return cudaErrorInvalidValue;
+  const int Tpad = (T + TC_BN - 1) / TC_BN * TC_BN;
+  const uint8_t* lo = static_cast<const uint8_t*>(digits);
+  const uint8_t* hi = lo + (size_t)Tpad * L.K;
+  CUtensorMap mA, mLo, mHi;
+  if (!make_map(&mA, L.w, L.N, L.K, (size_t)L.K, TC_BM) || !make_map(&mLo, lo, Tpad, L.K, (size_t)L.K, TC_BN) ||
+      !make_map(&mHi, hi, Tpad, L.K, (size_t)L.K, TC_BN))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  TcArgs a;
+  a.N = L.N; a.K = L.K; a.T = T; a.ldm = L.ldm; a.Mg = L.Mg; a.xs = xs; a.bias = L.b; a.epi = epi;
+  a.out = out; a.ldo = ldo; a.raw = raw; a.ldr = ldr; a.raw2 = raw2; a.silu_t = silu_t; a.err = err;
+  dim3 grid(L.N / TC_BM, Tpad / TC_BN);
+  k_gemm_tc<<<grid, TC_THREADS, TC_SMEM, st>>>(mA, mLo, mHi, a);
+  return cudaGetLastError();
+}
+
+}  // namespace exb
