@@ -103,8 +103,17 @@ struct exb_model {
   int64_t fr_checks = 0;
   std::map<uint64_t, cudaGraphExec_t> graphs;
   int32_t *h_ids = nullptr, *h_seq = nullptr, *h_pos = nullptr;           // pinned staging
+  // tensor-core prefill: buffers for chunks of up to pch rows (allocated on first use)
+  int pch = 0;
+  char* p_arena = nullptr;
+  int32_t* p_rows = nullptr; int32_t* p_hrows = nullptr;            // device ids|seq|pos, pinned staging
+  int64_t *p_x = nullptr, *p_qkv = nullptr, *p_ao = nullptr, *p_hb = nullptr, *p_raw = nullptr;
+  int16_t *p_xq = nullptr, *p_qq = nullptr;
+  int32_t *p_xs = nullptr, *p_qs = nullptr, *p_next = nullptr;
+  void* p_dig = nullptr;
   // persistent decode-step kernel (step.cu): per-layer descriptors and accumulators
   bool step_on = false;
+  bool tc_on = true;                    // multi-row chunks on the tensor-core GEMM
   int pf_bytes = 64 * 1024;
   StepLayer* step_layers = nullptr;
   int64_t* s_att = nullptr; long long* s_gmax = nullptr; unsigned long long* s_gsum = nullptr;
@@ -582,6 +591,8 @@ void exb_model_destroy(exb_model* m) {
   cudaFree(m->rarena);
   cudaFree(m->gen_tokens);
   cudaFree(m->emb_q16);
+  cudaFree(m->p_arena);
+  if (m->p_hrows) cudaFreeHost(m->p_hrows);
   if (m->h_ids) cudaFreeHost(m->h_ids);
   if (m->st) cudaStreamDestroy(m->st);
   delete m;
@@ -787,6 +798,91 @@ int exb_seq_len(exb_model* m, int seq) {
   return m->seq_len[seq];
 }
 
+// ------------------------------------------------------------------------------------------ prefill
+// Chunks of many rows (prompt tokens, batched rows) run every linear on the tcgen05 GEMM
+// (gemm_tc.cu) instead of the CUDA-core GEMV: the same kernels for norm, RoPE/cache, attention
+// and qrow, the same integer results.  Rows keep their order; rows of one sequence in one chunk
+// see each other through the KV cache (written before the attention launch).
+static constexpr int PCH = 256;            // rows per tensor-core chunk
+
+static int prefill_alloc(exb_model* m) {
+  if (m->pch) return EXB_OK;
+  const exb_config& c = m->c;
+  const int P = PCH, Hd = c.H * c.hd;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off = (off + bytes + 255) & ~size_t(255); return o; };
+  const size_t o_rows = take(sizeof(int32_t) * 3 * P), o_x = take(8ull * P * c.D), o_qkv = take(8ull * P * m->Nqkv),
+               o_ao = take(8ull * P * Hd), o_hb = take(8ull * P * c.I), o_raw = take(8ull * P * c.V),
+               o_xq = take(2ull * P * m->KMAX), o_qq = take(2ull * P * Hd), o_xs = take(4ull * P),
+               o_qs = take(4ull * P * c.H), o_next = take(4ull * P), o_dig = take(gemm_tc_digit_bytes(P, m->KMAX));
+  CK(cudaMalloc(&m->p_arena, off));
+  CK(cudaMallocHost(&m->p_hrows, sizeof(int32_t) * 3 * P));
+  char* b = m->p_arena;
+  m->p_rows = (int32_t*)(b + o_rows); m->p_x = (int64_t*)(b + o_x); m->p_qkv = (int64_t*)(b + o_qkv);
+  m->p_ao = (int64_t*)(b + o_ao); m->p_hb = (int64_t*)(b + o_hb); m->p_raw = (int64_t*)(b + o_raw);
+  m->p_xq = (int16_t*)(b + o_xq); m->p_qq = (int16_t*)(b + o_qq); m->p_xs = (int32_t*)(b + o_xs);
+  m->p_qs = (int32_t*)(b + o_qs); m->p_next = (int32_t*)(b + o_next); m->p_dig = b + o_dig;
+  m->pch = P;
+  return EXB_OK;
+}
+
+// one chunk of R rows (R <= PCH): host ids / seq / pos already in m->p_hrows
+static int prefill_chunk(exb_model* m, int R, int64_t* logits_host, int32_t* next_host) {
+  const exb_config& c = m->c;
+  cudaStream_t st = m->st;
+  const int D = c.D, Hd = c.H * c.hd, I = c.I;
+  CK(cudaMemcpyAsync(m->p_rows, m->p_hrows, sizeof(int32_t) * 3 * PCH, cudaMemcpyHostToDevice, st));
+  const int32_t* ids = m->p_rows;
+  const int32_t* seq = m->p_rows + PCH;
+  const int32_t* pos = m->p_rows + 2 * PCH;
+  if (m->emb_q16) CK(launch_embed64(m->emb_q16, ids, R, D, m->p_x, st, false));
+  else CK(launch_embed(m->emb, c.emb_shift, ids, R, D, m->p_x, st, false));
+  AttnArgs aa;
+  aa.qkv = m->p_qkv; aa.ldqkv = m->Nqkv; aa.row_seq = seq; aa.row_pos = pos;
+  aa.cos_t = m->cos_t; aa.sin_t = m->sin_t; aa.qq = m->p_qq; aa.qs = m->p_qs; aa.exp_t = m->exp_t;
+  aa.out = m->p_ao; aa.ldo = Hd; aa.R = R; aa.H = c.H; aa.KV = c.KV; aa.hd = c.hd; aa.Smax = c.max_seq;
+  aa.Tmax = c.rope_len; aa.err = m->err;
+  aa.inv = (int64_t)std::nearbyint(65536.0 / std::sqrt((double)c.hd));
+  auto lin = [&](const int16_t* xq, int K, const LinW& L, int epi, int64_t* out, int ldo) -> cudaError_t {
+    cudaError_t e = launch_digits(xq, K, R, K, m->p_dig, st);
+    if (e != cudaSuccess) return e;
+    return launch_gemm_tc(m->p_dig, R, L, m->p_xs, epi, out, ldo, epi == EPI_RAW ? out : nullptr, nullptr, ldo,
+                          m->silu_t, m->err, st);
+  };
+  for (int i = 0; i < c.NL; ++i) {
+    LayerDev& Ld = m->L[i];
+    const size_t kvoff = m->kv_layer_elems * i;
+    aa.kc = m->kc + kvoff; aa.vc = m->vc + kvoff;
+    aa.ks = m->ks + (size_t)c.max_batch * c.KV * c.max_seq * i;
+    CK(launch_norm_q(m->p_x, D, Ld.g1, R, D, m->p_xq, D, m->p_xs, st, false));
+    CK(lin(m->p_xq, D, Ld.qkv, EPI_STORE, m->p_qkv, m->Nqkv));
+    CK(launch_rope_cache(aa, st, false));
+    CK(launch_attn_decode(aa, st, false));
+    CK(launch_quant(m->p_ao, Hd, R, Hd, m->p_xq, Hd, m->p_xs, st, false));
+    CK(lin(m->p_xq, Hd, Ld.o, EPI_RESID, m->p_x, D));
+    CK(launch_norm_q(m->p_x, D, Ld.g2, R, D, m->p_xq, D, m->p_xs, st, false));
+    CK(lin(m->p_xq, D, Ld.gu, EPI_SWIGLU, m->p_hb, I));
+    CK(launch_quant(m->p_hb, I, R, I, m->p_xq, I, m->p_xs, st, false));
+    CK(lin(m->p_xq, I, Ld.down, EPI_RESID, m->p_x, D));
+  }
+  CK(launch_norm_q(m->p_x, D, m->gf, R, D, m->p_xq, D, m->p_xs, st, false));
+  // head: unscaled per-group sums on the tensor cores, then the per-channel requant + argmax per row
+  CK(lin(m->p_xq, D, m->head, EPI_RAW, m->p_raw, c.V));
+  int64_t* lg = logits_host ? m->p_raw : nullptr;             // requant in place (row by row, read before write)
+  CK(launch_head_rows(m->p_raw, c.V, R, m->head, m->p_xs, lg, c.V, m->p_next, st));
+  if (logits_host) CK(cudaMemcpyAsync(logits_host, m->p_raw, sizeof(int64_t) * R * c.V, cudaMemcpyDeviceToHost, st));
+  if (next_host) CK(cudaMemcpyAsync(next_host, m->p_next, sizeof(int32_t) * R, cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  return EXB_OK;
+}
+
+static bool prefill_tc_ok(exb_model* m) {
+  const exb_config& c = m->c;
+  return m->tc_on && m->group && !m->trace_on && !m->fr_on && c.H * c.hd % 128 == 0 && gemm_tc_supported(m->L[0].qkv, EPI_STORE) &&
+         gemm_tc_supported(m->L[0].gu, EPI_SWIGLU) && gemm_tc_supported(m->L[0].down, EPI_RESID) &&
+         gemm_tc_supported(m->L[0].o, EPI_RESID) && gemm_tc_supported(m->head, EPI_RAW) && m->head.nodrop;
+}
+
 int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, int64_t* logits, int32_t* next) {
   if (!m || !m->finalized) FAIL(EXB_EINVAL, "model not finalized");
   if (n <= 0 || !ids || !seqs) FAIL(EXB_EINVAL, "bad rows");
@@ -801,7 +897,21 @@ int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, in
   }
   if (m->trace_on) { m->trace_host.assign((size_t)n * m->trace_row, 0); m->trace_rows = n; }
   CK(cudaMemsetAsync(m->err, 0, sizeof(int), m->st));
-  for (int r0 = 0; r0 < n; r0 += RMAX) {
+  int r_tc = 0;                                              // rows done by tensor-core chunks
+  if (n >= TC_MIN_ROWS && prefill_tc_ok(m)) {
+    int rc = prefill_alloc(m);
+    if (rc) return rc;
+    while (n - r_tc >= TC_MIN_ROWS) {
+      const int R = std::min(PCH, n - r_tc);
+      for (int r = 0; r < R; ++r) {
+        m->p_hrows[r] = ids[r_tc + r]; m->p_hrows[PCH + r] = seqs[r_tc + r]; m->p_hrows[2 * PCH + r] = pos[r_tc + r];
+      }
+      rc = prefill_chunk(m, R, logits ? logits + (size_t)r_tc * c.V : nullptr, next ? next + r_tc : nullptr);
+      if (rc) return rc;
+      r_tc += R;
+    }
+  }
+  for (int r0 = r_tc; r0 < n; r0 += RMAX) {
     const int R = std::min(RMAX, n - r0);
     for (int r = 0; r < R; ++r) { m->h_ids[r] = ids[r0 + r]; m->h_seq[r] = seqs[r0 + r]; m->h_pos[r] = pos[r0 + r]; }
     CK(cudaMemcpyAsync(m->row_ids, m->h_ids, sizeof(int32_t) * RMAX * 3, cudaMemcpyHostToDevice, m->st));
@@ -955,6 +1065,7 @@ int exb_set_option(exb_model* m, const char* name, int64_t value) {
   if (!m || !name) FAIL(EXB_EINVAL, "null argument");
   const std::string n(name);
   if (n == "step") m->step_on = value != 0;
+  else if (n == "tc") m->tc_on = value != 0;
   else if (n == "pf_kb") {
     if (value < 0 || value > 1024) FAIL(EXB_EINVAL, "pf_kb: 0..1024");
     m->pf_bytes = (int)value * 1024;

@@ -135,6 +135,10 @@ cudaError_t launch_quant_known(const int64_t* x, int ldx, int R, int K, const un
 cudaError_t launch_requant_channel(const int64_t* acc, int ld, int R, const LinW& L, int64_t* out, int ldo,
                                    const int32_t* xs, int epi, cudaStream_t st, bool pdl);
 
+// per-channel head over many rows: requant of raw sums, optional logits, greedy next token per row
+cudaError_t launch_head_rows(const int64_t* acc, int ld, int R, const LinW& L, const int32_t* xs, int64_t* logits,
+                             int ldl, int32_t* next, cudaStream_t st);
+
 cudaError_t launch_rope_cache(const AttnArgs& a, cudaStream_t st, bool pdl);
 // attention; when xq_out is set, the last CTA also writes qrow(out) (shift from amax_out)
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);

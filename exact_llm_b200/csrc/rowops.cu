@@ -210,6 +210,51 @@ cudaError_t launch_requant_channel(const int64_t* acc, int ld, int R, const LinW
   return launch_simple((const void*)k_requant_ch, dim3(R), dim3(ROW_THREADS), 0, st, pdl, args);
 }
 
+// ---------------------------------------------------------------- head rows: requant + greedy argmax
+// One CTA per activation row: y = QLin requant of the raw per-channel sums (drop rule of
+// exact_llm.py:89-96), optional logits, next token = first index of the maximum (exact_llm.py:267).
+__global__ void __launch_bounds__(ROW_THREADS) k_head_rows(const int64_t* __restrict__ acc, int ld, int N,
+                                                           const int64_t* __restrict__ M, int mbits,
+                                                           const int32_t* __restrict__ xs, int64_t* __restrict__ logits,
+                                                           int ldl, int32_t* __restrict__ next) {
+  __shared__ uint64_t red[33];
+  __shared__ int64_t bv_s[ROW_THREADS / 32];
+  __shared__ int bn_s[ROW_THREADS / 32];
+  const int r = blockIdx.x;
+  const int64_t* ar = acc + (size_t)r * ld;
+  uint64_t m = 0;
+  for (int i = threadIdx.x; i < N; i += ROW_THREADS) { const uint64_t v = uabs64(ar[i]); m = v > m ? v : m; }
+  m = block_max_u64<ROW_THREADS>(m, red);
+  int drop = bitlen64(m) + mbits - 62;
+  drop = drop > 0 ? drop : 0;
+  const int s = xs[r];
+  int64_t bv = INT64_MIN;
+  int bn = 0x7fffffff;
+  for (int i = threadIdx.x; i < N; i += ROW_THREADS) {
+    const int64_t y = shr64((int64_t)((uint64_t)shr64(ar[i], drop) * (uint64_t)M[i]), 28 - s - drop);
+    if (logits) logits[(size_t)r * ldl + i] = y;
+    if (y > bv) { bv = y; bn = i; }              // i increases: the first maximum is kept
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const int64_t ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int on = __shfl_xor_sync(0xffffffffu, bn, o);
+    if (ov > bv || (ov == bv && on < bn)) { bv = ov; bn = on; }
+  }
+  if ((threadIdx.x & 31) == 0) { bv_s[threadIdx.x >> 5] = bv; bn_s[threadIdx.x >> 5] = bn; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < ROW_THREADS / 32; ++w)
+      if (bv_s[w] > bv || (bv_s[w] == bv && bn_s[w] < bn)) { bv = bv_s[w]; bn = bn_s[w]; }
+    next[r] = bn;
+  }
+}
+
+cudaError_t launch_head_rows(const int64_t* acc, int ld, int R, const LinW& L, const int32_t* xs, int64_t* logits,
+                             int ldl, int32_t* next, cudaStream_t st) {
+  k_head_rows<<<R, ROW_THREADS, 0, st>>>(acc, ld, L.N, L.Mc, L.mbits, xs, logits, ldl, next);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------- Freivalds comparison
 // acc layout: (nchecks, 4) = lhs_p1, lhs_p2, rhs_p1, rhs_p2 (each an unreduced sum of residues)
 __global__ void k_fr_check(const unsigned long long* __restrict__ acc, int n, int* fail, int* err) {

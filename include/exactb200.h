@@ -145,6 +145,8 @@ int exb_freivalds_status(exb_model* m, int64_t* checks, int64_t* failures);
 /* Engine options (no counterpart in the reference; they change speed, never results):
  *   "step"    1: decode steps of <= 2 rows without trace/Freivalds capture run as one persistent
  *             kernel (grid barriers between phases); 0 (default): one kernel per operation
+ *   "tc"      1 (default): forward calls of >= 16 rows run their linears on the tcgen05 tensor-core
+ *             GEMM in chunks of 256 rows; 0: 4-row CUDA-core GEMV passes
  *   "pf_kb"   per-CTA L2 prefetch of the next weight slices where HBM would idle, KiB (default 64; 0 = off)
  * Cached step graphs are dropped. */
 int exb_set_option(exb_model* m, const char* name, int64_t value);

@@ -224,6 +224,25 @@ def test_persistent_step_matches_per_kernel_path(cuda_ok, B):
     assert np.array_equal(out[1][1], out[0][1])
 
 
+@pytest.mark.parametrize("T", [16, 75, 300])
+def test_tensor_core_prefill_matches_gemv_path(cuda_ok, T):
+    """Prefill of T rows on the tcgen05 GEMM (chunks of up to 256 rows, ragged tails, rows of two
+    sequences interleaved) gives the same logits and next tokens as the 4-row CUDA-core GEMV path."""
+    from exact_llm_b200 import ExactModel, configs
+    c = configs.arch("qwen2.5-7b", NL=2)
+    m = ExactModel.synthetic(c, 91, max_batch=2, max_seq=T + 8)
+    rng = np.random.default_rng(T)
+    ids = rng.integers(0, c["V"], T).astype(np.int32)
+    seqs = (np.arange(T) % 2).astype(np.int32)
+    out = {}
+    for tc in (1, 0):
+        m.set_option("tc", tc)
+        m.new_cache(0); m.new_cache(1)
+        out[tc] = m.forward_rows(ids, seqs, want_logits=True)
+    assert np.array_equal(out[1][1], out[0][1])
+    assert np.array_equal(out[1][0], out[0][0])
+
+
 def test_freivalds_keys_and_self_check(golden, cuda_ok):
     """Device keys equal the reference keys (rng seeded 2026); honest steps pass every check;
     a corrupted weight is caught (experiments/gpu_engine_trace_verify_kaggle.py:803-872)."""
