@@ -56,6 +56,7 @@ SIGNATURES = {
     "exb_freivalds_enable": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "exb_freivalds_status": (ctypes.c_int, [ctypes.c_void_p, c_i64p, c_i64p]),
     "exb_set_option": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int64]),
+    "exb_moe_selections": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, c_i32p, ctypes.c_int64]),
     "exb_device_errors": (ctypes.c_int, [ctypes.c_void_p, c_i32p]),
     "exb_bench_linear": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)]),

@@ -7,6 +7,7 @@
 // read from device memory, as in GraphDecoder), on-device greedy feedback, trace capture written
 // directly by the GEMV epilogues, and the Freivalds self-check accumulated inside the GEMVs.
 #include <algorithm>
+#include <cctype>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -40,6 +41,8 @@ void exb::set_last_error(const std::string& msg) { g_err = msg; }
 
 static constexpr int RMAX = 4;          // activation rows per GEMV pass (CUDA-core decode path)
 static constexpr int STEP_ROWS = 2;     // rows the persistent step kernel takes (batch <= 2)
+static constexpr int MOE_ROWS = 256;    // rows per MoE block call (the tensor-core chunk size)
+static constexpr int SEL_CAP = 4096;    // rows of router selections kept for inspection
 static constexpr int EXP_LEN_H = 256 * 40 + 2, SILU_LEN_H = 32 * 256 + 2;
 
 static int bitlen_host(uint64_t v) { int b = 0; while (v) { ++b; v >>= 1; } return b; }
@@ -61,6 +64,10 @@ struct LayerDev {
   int64_t* g2 = nullptr;
   LinW qkv, o, gu, down;
   int li[7];                            // q, k, v, o, gate, up, down -> index into lins
+  // MoE layers (config 4): router, shared-expert gate, experts and the shared expert (index NE)
+  LinW router, sgate;
+  std::vector<LinW> exgu, exd;          // NE + 1 entries
+  ExpertW* ex_dev = nullptr;            // device table (NE + 1)
 };
 
 struct exb_model {
@@ -103,6 +110,13 @@ struct exb_model {
   int64_t fr_checks = 0;
   std::map<uint64_t, cudaGraphExec_t> graphs;
   int32_t *h_ids = nullptr, *h_seq = nullptr, *h_pos = nullptr;           // pinned staging
+  // MoE runtime (rows up to MOE_ROWS per call of the block)
+  int moe_imax = 0;
+  int32_t *moe_sel = nullptr, *moe_off = nullptr, *moe_slot_row = nullptr, *moe_slot_exp = nullptr, *moe_slot_of = nullptr;
+  int32_t *moe_hs = nullptr, *moe_hist = nullptr;   // hist: (NL, SEL_CAP, TOPK) router selections of the last call
+  int64_t *moe_prob = nullptr, *moe_sgv = nullptr, *moe_raw_gu = nullptr, *moe_raw_d = nullptr;
+  int16_t* moe_hq = nullptr;
+  int64_t sel_rows = 0;                              // rows recorded in moe_hist by the last forward call
   // tensor-core prefill: buffers for chunks of up to pch rows (allocated on first use)
   int pch = 0;
   char* p_arena = nullptr;
@@ -155,8 +169,20 @@ static void plan_weights(exb_model* m) {
     Ld.g2 = walloc<int64_t>(m, D);
     mk(Ld.qkv, m->Nqkv, D, true);
     mk(Ld.o, D, Hd, false);
-    mk(Ld.gu, 2 * I, D, false);
-    mk(Ld.down, D, I, false);
+    if (c.n_experts) {
+      mk(Ld.router, c.n_experts, D, false);
+      mk(Ld.sgate, 1, D, false);
+      Ld.exgu.assign(c.n_experts + 1, LinW());
+      Ld.exd.assign(c.n_experts + 1, LinW());
+      for (int e = 0; e <= c.n_experts; ++e) {
+        const int Ie = e < c.n_experts ? c.moe_I : c.shared_I;
+        mk(Ld.exgu[e], 2 * Ie, D, false);
+        mk(Ld.exd[e], D, Ie, false);
+      }
+    } else {
+      mk(Ld.gu, 2 * I, D, false);
+      mk(Ld.down, D, I, false);
+    }
   }
   m->emb = walloc<int8_t>(m, (size_t)c.V * D);
   m->gf = walloc<int64_t>(m, D);
@@ -188,6 +214,22 @@ static void plan_lins(exb_model* m) {
     Ld.li[1] = add(p + "k", &Ld.qkv, kn, c.D, qn, 1);
     Ld.li[2] = add(p + "v", &Ld.qkv, kn, c.D, qn + kn, 1);
     Ld.li[3] = add(p + "o", &Ld.o, c.D, qn, 0, 1);
+    if (c.n_experts) {
+      const int NE = c.n_experts;
+      add(p + "router", &Ld.router, NE, c.D, 0, 1);
+      add(p + "sgate", &Ld.sgate, 1, c.D, 0, 1);
+      add(p + "sg", &Ld.exgu[NE], c.shared_I, c.D, 0, 2);
+      add(p + "su", &Ld.exgu[NE], c.shared_I, c.D, 1, 2);
+      add(p + "sd", &Ld.exd[NE], c.D, c.shared_I, 0, 1);
+      for (int e = 0; e < NE; ++e) {
+        const std::string q = p + "e" + std::to_string(e) + ".";
+        add(q + "g", &Ld.exgu[e], c.moe_I, c.D, 0, 2);
+        add(q + "u", &Ld.exgu[e], c.moe_I, c.D, 1, 2);
+        add(q + "d", &Ld.exd[e], c.D, c.moe_I, 0, 1);
+      }
+      Ld.li[4] = Ld.li[5] = Ld.li[6] = -1;
+      continue;
+    }
     Ld.li[4] = add(p + "gate", &Ld.gu, c.I, c.D, 0, 2);
     Ld.li[5] = add(p + "up", &Ld.gu, c.I, c.D, 1, 2);
     Ld.li[6] = add(p + "down", &Ld.down, c.D, c.I, 0, 1);
@@ -229,6 +271,23 @@ static void plan_runtime(exb_model* m) {
   m->kc = ralloc<int16_t>(m, m->kv_layer_elems * c.NL);
   m->vc = ralloc<int32_t>(m, m->kv_layer_elems * c.NL);
   m->ks = ralloc<int8_t>(m, (size_t)c.max_batch * c.KV * c.max_seq * c.NL);
+  if (c.n_experts) {
+    const int NE = c.n_experts, TK = c.topk, slots = MOE_ROWS * (TK + 1);
+    m->moe_imax = std::max(c.moe_I, c.shared_I);
+    m->moe_sel = ralloc<int32_t>(m, (size_t)MOE_ROWS * TK);
+    m->moe_prob = ralloc<int64_t>(m, (size_t)MOE_ROWS * TK);
+    m->moe_sgv = ralloc<int64_t>(m, MOE_ROWS);
+    m->moe_off = ralloc<int32_t>(m, NE + 2);
+    m->moe_slot_row = ralloc<int32_t>(m, slots);
+    m->moe_slot_exp = ralloc<int32_t>(m, slots);
+    m->moe_slot_of = ralloc<int32_t>(m, (size_t)MOE_ROWS * TK);
+    m->moe_raw_gu = ralloc<int64_t>(m, (size_t)slots * 2 * m->moe_imax);
+    m->moe_hq = ralloc<int16_t>(m, (size_t)slots * m->moe_imax);
+    m->moe_hs = ralloc<int32_t>(m, slots);
+    m->moe_raw_d = ralloc<int64_t>(m, (size_t)slots * c.D);
+    m->moe_hist = ralloc<int32_t>(m, (size_t)c.NL * SEL_CAP * TK);
+    for (int i = 0; i < c.NL; ++i) m->L[i].ex_dev = ralloc<ExpertW>(m, NE + 1);
+  }
   m->step_layers = ralloc<StepLayer>(m, c.NL);
   m->s_att = ralloc<int64_t>(m, (size_t)c.NL * STEP_ROWS * c.H * c.hd);
   m->s_gmax = ralloc<long long>(m, (size_t)c.NL * STEP_ROWS * c.H);
@@ -243,6 +302,28 @@ static void plan_runtime(exb_model* m) {
 // sequence slot and position from device arrays, so the enqueued work is identical for every
 // step and can be captured once into a CUDA graph.
 static std::vector<cudaEvent_t>* g_prof = nullptr;   // profiling: an event after every launch
+
+// MoE block arguments for layer i over R rows (qrow(m) rows xq / xs); selections recorded at row
+// hist_row0 of the layer's history when hist_row0 >= 0
+static MoeArgs moe_args(exb_model* m, int i, int R, const int16_t* xq, int ldq, const int32_t* xs, int hist_row0) {
+  const exb_config& c = m->c;
+  LayerDev& Ld = m->L[i];
+  MoeArgs a;
+  a.R = R; a.D = c.D; a.NE = c.n_experts; a.TOPK = c.topk; a.IMAX = m->moe_imax;
+  a.xq = xq; a.ldq = ldq; a.xs = xs;
+  a.w_router = Ld.router.w; a.M_router = Ld.router.Mc; a.mbits_router = Ld.router.mbits;
+  a.w_sgate = Ld.sgate.w; a.M_sgate = Ld.sgate.Mc; a.mbits_sgate = Ld.sgate.mbits;
+  a.ex = Ld.ex_dev;
+  a.exp_t = m->exp_t; a.silu_t = m->silu_t; a.sig_t = m->sig_t;
+  a.sel = m->moe_sel; a.prob = m->moe_prob; a.sgv = m->moe_sgv;
+  a.sel_hist = (hist_row0 >= 0 && hist_row0 + R <= SEL_CAP) ? m->moe_hist + ((size_t)i * SEL_CAP + hist_row0) * c.topk
+                                                              : nullptr;
+  a.off = m->moe_off; a.slot_row = m->moe_slot_row; a.slot_exp = m->moe_slot_exp; a.slot_of = m->moe_slot_of;
+  a.raw_gu = m->moe_raw_gu; a.ld_gu = 2 * m->moe_imax; a.hq = m->moe_hq; a.ld_h = m->moe_imax; a.hs = m->moe_hs;
+  a.raw_d = m->moe_raw_d;
+  return a;
+}
+static int g_hist_row0 = -1;                             // selection-history row of the step being enqueued
 
 // Arguments of the persistent step kernel, when it can run this step: group-128 model, R <= 2
 // rows, no trace or Freivalds capture (those stay on the per-kernel path), int8 embedding rows.
@@ -363,6 +444,10 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       RUN(launch_gemv(g, st, pdl));
     }
     RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    if (c.n_experts) {
+      RUN(launch_moe(moe_args(m, i, R, m->xq, m->KMAX, m->xs, g_hist_row0), m->x, c.D, st));
+      continue;
+    }
     {
       GemvArgs g; base(g, Ld.gu);
       g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.amax_out = m->amax_h;
@@ -412,6 +497,17 @@ __global__ void k_advance(int B, int32_t* ids, int32_t* pos, const int32_t* next
 // --- graph cache: key = (R, row-array base, logits, advance, trace, freivalds)
 static int run_step(exb_model* m, int R, const int32_t* ids, const int32_t* seq, const int32_t* pos, bool want_logits,
                     int advanceB) {
+  if (m->c.n_experts && g_hist_row0 >= 0) {
+    // direct launches: the MoE history row of this chunk is not a graph constant
+    cudaError_t e = enqueue_step(m, R, ids, seq, pos, want_logits, m->st);
+    if (e == cudaSuccess && advanceB > 0) {
+      k_advance<<<1, 32, 0, m->st>>>(advanceB, const_cast<int32_t*>(ids), const_cast<int32_t*>(pos), m->next_tok,
+                                     m->gen_step, m->gen_tokens, m->gen_cap);
+      e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("step: ") + cudaGetErrorString(e));
+    return EXB_OK;
+  }
   const uint64_t key = ((uint64_t)R) | ((uint64_t)(want_logits ? 1 : 0) << 8) | ((uint64_t)(advanceB) << 9) |
                        ((uint64_t)(m->trace_on ? 1 : 0) << 20) | ((uint64_t)(m->fr_on ? 1 : 0) << 21) |
                        ((uint64_t)((const char*)ids - (const char*)m->rarena) << 24);
@@ -544,7 +640,10 @@ int exb_model_create(const exb_config* cfg, exb_model** out) {
   if (c.D <= 0 || c.H <= 0 || c.KV <= 0 || c.hd <= 0 || c.I <= 0 || c.V <= 0 || c.NL <= 0) FAIL(EXB_EINVAL, "bad dims");
   if (c.H % c.KV || c.H / c.KV > 8) FAIL(EXB_EINVAL, "H must be a multiple of KV with at most 8 query heads per KV head");
   if (c.hd % 16 || c.hd > 128) FAIL(EXB_EINVAL, "head_dim must be a multiple of 16 and <= 128");
-  if (c.n_experts) FAIL(EXB_EINVAL, "MoE models are not supported by this build");
+  if (c.n_experts && (c.lin_kind == 0 || c.n_experts > MOE_MAX_EXPERTS || c.topk < 1 || c.topk > MOE_MAX_TOPK ||
+                      c.topk > c.n_experts || c.moe_I <= 0 || c.shared_I <= 0 || c.moe_I % 16 || c.shared_I % 16))
+    FAIL(EXB_EINVAL, "MoE: per-channel linears, 1 <= topk <= min(8, n_experts), n_experts <= 128, "
+                     "expert and shared widths multiples of 16");
   if (c.max_batch <= 0 || c.max_seq <= 0 || c.rope_len < c.max_seq) FAIL(EXB_EINVAL, "bad capacities");
   const int gk = c.lin_kind == 0 ? 128 : 16;
   if (c.D % gk || (c.H * c.hd) % gk || c.I % gk) FAIL(EXB_EINVAL, "D, H*hd and I must be multiples of 128 (group) or 16 (channel)");
@@ -554,6 +653,7 @@ int exb_model_create(const exb_config* cfg, exb_model** out) {
   m->Nqkv = (c.H + 2 * c.KV) * c.hd;
   m->KMAX = std::max(std::max(c.D, c.H * c.hd), c.I);
   m->NMAX = std::max(std::max(m->Nqkv, 2 * c.I), c.V);
+  if (c.n_experts) m->NMAX = std::max(m->NMAX, 2 * std::max(c.moe_I, c.shared_I));
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -710,12 +810,23 @@ int exb_model_generate(exb_model* m, uint64_t seed) {
   for (auto& l : m->lins) maxn = std::max(maxn, (size_t)l.N * l.K);
   void* tmp = nullptr;
   CK(cudaMallocAsync(&tmp, maxn * 8, m->st));
-  static const std::map<std::string, int> LS = {{"q", 2}, {"k", 5}, {"v", 8}, {"o", 11}, {"gate", 14}, {"up", 17}, {"down", 20}};
+  static const std::map<std::string, int> LS = {{"q", 2}, {"k", 5}, {"v", 8}, {"o", 11}, {"gate", 14}, {"up", 17},
+                                                 {"down", 20}, {"router", 23}, {"sgate", 26}, {"sg", 29}, {"su", 32},
+                                                 {"sd", 35}};
   for (auto& L : m->lins) {
     if (L.name == "head") continue;
     const int li = atoi(L.name.c_str() + 1);
     const std::string nm = L.name.substr(L.name.find('.') + 1);
-    const uint64_t s0 = layer_stream(li, LS.at(nm));
+    uint64_t s0;
+    if (nm[0] == 'e' && nm.size() > 1 && isdigit((unsigned char)nm[1])) {
+      // expert e, linear j in (g, u, d): stream (1 << 24) + layer * 4096 + e * 16 + j * 4
+      const int e = atoi(nm.c_str() + 1);
+      const char part = nm[nm.find('.') + 1];
+      const int j = part == 'g' ? 0 : part == 'u' ? 1 : 2;
+      s0 = (1ull << 24) + (uint64_t)li * 4096 + (uint64_t)e * 16 + (uint64_t)j * 4;
+    } else {
+      s0 = layer_stream(li, LS.at(nm));
+    }
     LinW& F = *L.fused;
     CK(gen_tensor(GEN_WEIGHT, seed, s0, (int64_t)L.N * L.K, L.K, tmp, m->st));
     CK(cudaMemcpy2DAsync((char*)F.w + (size_t)L.row0 * L.K, (size_t)L.K * L.row_step, tmp, L.K, L.K, L.N,
@@ -772,8 +883,34 @@ int exb_model_finalize(exb_model* m) {
     }
   }
   CK(cudaStreamSynchronize(m->st));
+  auto moe_lin = [&](const std::string& nm) {
+    const std::string t = nm.substr(nm.find('.') + 1);
+    return t == "router" || t == "sgate" || t == "sg" || t == "su" || t == "sd" || (t[0] == 'e' && isdigit((unsigned char)t[1]));
+  };
+  if (c.n_experts) {
+    // the MoE linears apply the drop rule per row on the device: record each logical linear's
+    // bitlen(max M) in the expert tables
+    std::map<std::string, int> mb;
+    for (auto& L : m->lins) mb[L.name] = L.mbits;
+    for (int i = 0; i < c.NL; ++i) {
+      LayerDev& Ld = m->L[i];
+      const std::string p = "L" + std::to_string(i) + ".";
+      Ld.router.mbits = mb[p + "router"];
+      Ld.sgate.mbits = mb[p + "sgate"];
+      std::vector<ExpertW> tab(c.n_experts + 1);
+      for (int e = 0; e <= c.n_experts; ++e) {
+        const bool sh = e == c.n_experts;
+        const std::string q = sh ? p : p + "e" + std::to_string(e) + ".";
+        ExpertW& X = tab[e];
+        X.w_gu = Ld.exgu[e].w; X.M_gu = Ld.exgu[e].Mc; X.w_d = Ld.exd[e].w; X.M_d = Ld.exd[e].Mc;
+        X.I = sh ? c.shared_I : c.moe_I;
+        X.mb_g = mb[q + (sh ? "sg" : "g")]; X.mb_u = mb[q + (sh ? "su" : "u")]; X.mb_d = mb[q + (sh ? "sd" : "d")];
+      }
+      CK(cudaMemcpy(Ld.ex_dev, tab.data(), sizeof(ExpertW) * tab.size(), cudaMemcpyHostToDevice));
+    }
+  }
   for (auto& L : m->lins)
-    if (L.fused->Mc && !L.fused->nodrop)
+    if (L.fused->Mc && !L.fused->nodrop && !moe_lin(L.name))
       FAIL(EXB_EINVAL, "per-channel linear " + L.name + " may trigger the overflow drop rule; the fused decode path "
                        "requires bitlen(K*32767*127) + bitlen(max M) <= 62");
   std::vector<StepLayer> sl(c.NL);
@@ -846,8 +983,13 @@ static int prefill_chunk(exb_model* m, int R, int64_t* logits_host, int32_t* nex
   auto lin = [&](const int16_t* xq, int K, const LinW& L, int epi, int64_t* out, int ldo) -> cudaError_t {
     cudaError_t e = launch_digits(xq, K, R, K, m->p_dig, st);
     if (e != cudaSuccess) return e;
-    return launch_gemm_tc(m->p_dig, R, L, m->p_xs, epi, out, ldo, epi == EPI_RAW ? out : nullptr, nullptr, ldo,
-                          m->silu_t, m->err, st);
+    if (L.Mg || epi == EPI_RAW)
+      return launch_gemm_tc(m->p_dig, R, L, m->p_xs, epi, out, ldo, epi == EPI_RAW ? out : nullptr, nullptr, ldo,
+                            m->silu_t, m->err, st);
+    // per-channel linear: raw sums on the tensor cores, then the QLin requant (exact_llm.py:89-96)
+    e = launch_gemm_tc(m->p_dig, R, L, m->p_xs, EPI_RAW, m->p_raw, L.N, m->p_raw, nullptr, L.N, nullptr, m->err, st);
+    if (e != cudaSuccess) return e;
+    return launch_requant_channel(m->p_raw, L.N, R, L, out, ldo, m->p_xs, epi, st, false);
   };
   for (int i = 0; i < c.NL; ++i) {
     LayerDev& Ld = m->L[i];
@@ -861,6 +1003,10 @@ static int prefill_chunk(exb_model* m, int R, int64_t* logits_host, int32_t* nex
     CK(launch_quant(m->p_ao, Hd, R, Hd, m->p_xq, Hd, m->p_xs, st, false));
     CK(lin(m->p_xq, Hd, Ld.o, EPI_RESID, m->p_x, D));
     CK(launch_norm_q(m->p_x, D, Ld.g2, R, D, m->p_xq, D, m->p_xs, st, false));
+    if (c.n_experts) {
+      CK(launch_moe(moe_args(m, i, R, m->p_xq, D, m->p_xs, g_hist_row0), m->p_x, D, st));
+      continue;
+    }
     CK(lin(m->p_xq, D, Ld.gu, EPI_SWIGLU, m->p_hb, I));
     CK(launch_quant(m->p_hb, I, R, I, m->p_xq, I, m->p_xs, st, false));
     CK(lin(m->p_xq, I, Ld.down, EPI_RESID, m->p_x, D));
@@ -878,6 +1024,9 @@ static int prefill_chunk(exb_model* m, int R, int64_t* logits_host, int32_t* nex
 
 static bool prefill_tc_ok(exb_model* m) {
   const exb_config& c = m->c;
+  if (c.n_experts)
+    return m->tc_on && !m->trace_on && !m->fr_on && gemm_tc_supported(m->L[0].qkv, EPI_RAW) &&
+           gemm_tc_supported(m->L[0].o, EPI_RAW) && gemm_tc_supported(m->head, EPI_RAW) && c.D % 16 == 0;
   return m->tc_on && m->group && !m->trace_on && !m->fr_on && c.H * c.hd % 128 == 0 && gemm_tc_supported(m->L[0].qkv, EPI_STORE) &&
          gemm_tc_supported(m->L[0].gu, EPI_SWIGLU) && gemm_tc_supported(m->L[0].down, EPI_RESID) &&
          gemm_tc_supported(m->L[0].o, EPI_RESID) && gemm_tc_supported(m->head, EPI_RAW) && m->head.nodrop;
@@ -897,6 +1046,7 @@ int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, in
   }
   if (m->trace_on) { m->trace_host.assign((size_t)n * m->trace_row, 0); m->trace_rows = n; }
   CK(cudaMemsetAsync(m->err, 0, sizeof(int), m->st));
+  m->sel_rows = c.n_experts ? std::min(n, SEL_CAP) : 0;
   int r_tc = 0;                                              // rows done by tensor-core chunks
   if (n >= TC_MIN_ROWS && prefill_tc_ok(m)) {
     int rc = prefill_alloc(m);
@@ -906,7 +1056,9 @@ int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, in
       for (int r = 0; r < R; ++r) {
         m->p_hrows[r] = ids[r_tc + r]; m->p_hrows[PCH + r] = seqs[r_tc + r]; m->p_hrows[2 * PCH + r] = pos[r_tc + r];
       }
+      g_hist_row0 = c.n_experts ? r_tc : -1;
       rc = prefill_chunk(m, R, logits ? logits + (size_t)r_tc * c.V : nullptr, next ? next + r_tc : nullptr);
+      g_hist_row0 = -1;
       if (rc) return rc;
       r_tc += R;
     }
@@ -915,7 +1067,9 @@ int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, in
     const int R = std::min(RMAX, n - r0);
     for (int r = 0; r < R; ++r) { m->h_ids[r] = ids[r0 + r]; m->h_seq[r] = seqs[r0 + r]; m->h_pos[r] = pos[r0 + r]; }
     CK(cudaMemcpyAsync(m->row_ids, m->h_ids, sizeof(int32_t) * RMAX * 3, cudaMemcpyHostToDevice, m->st));
+    g_hist_row0 = c.n_experts ? r0 : -1;
     int rc = run_step(m, R, m->row_ids, m->row_seq, m->row_pos, logits != nullptr, 0);
+    g_hist_row0 = -1;
     if (rc) return rc;
     if (logits) CK(cudaMemcpyAsync(logits + (size_t)r0 * c.V, m->logits, sizeof(int64_t) * R * c.V, cudaMemcpyDeviceToHost, m->st));
     if (next) CK(cudaMemcpyAsync(next + r0, m->next_tok, sizeof(int32_t) * R, cudaMemcpyDeviceToHost, m->st));
@@ -990,6 +1144,7 @@ int exb_generate_device(exb_model* m, int B, const int32_t* ids_dev, int steps, 
 
 int exb_trace_enable(exb_model* m, int on) {
   if (!m) FAIL(EXB_EINVAL, "null model");
+  if (on && m->c.n_experts) FAIL(EXB_EINVAL, "trace capture covers the dense models (the reference traces them only)");
   m->trace_on = on != 0;
   return EXB_OK;
 }
@@ -1103,6 +1258,15 @@ int exb_profile_persistent(exb_model* m, int B, uint64_t* host, int64_t n, int* 
   *nbar = nb;
   *grid = g;
   return check_device_errors(m);   // the step wrote position seq_len (not advanced): harmless
+}
+
+int exb_moe_selections(exb_model* m, int layer, int32_t* host, int64_t n) {
+  if (!m || !host || !m->c.n_experts || layer < 0 || layer >= m->c.NL) FAIL(EXB_EINVAL, "exb_moe_selections: bad arguments");
+  const int64_t need = m->sel_rows * m->c.topk;
+  if (n != need) FAIL(EXB_EINVAL, "exb_moe_selections: expected " + std::to_string(need) + " values");
+  CK(cudaStreamSynchronize(m->st));
+  CK(cudaMemcpy(host, m->moe_hist + (size_t)layer * SEL_CAP * m->c.topk, sizeof(int32_t) * need, cudaMemcpyDeviceToHost));
+  return EXB_OK;
 }
 
 int exb_device_errors(exb_model* m, int* bits) {

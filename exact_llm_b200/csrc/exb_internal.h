@@ -151,6 +151,41 @@ cudaError_t launch_fr_keys(const int8_t* w, const int32_t* Mg, int ldm, int N, i
 cudaError_t launch_fr_check(const unsigned long long* acc, int nchecks, int* fail_count, int* err,
                             cudaStream_t st, bool pdl);
 
+// ---------------------------------------------------------------- mixture of experts (moe.cu)
+constexpr int MOE_MAX_EXPERTS = 128;
+constexpr int MOE_MAX_TOPK = 8;
+
+// One expert's per-channel SwiGLU MLP: gate|up rows interleaved (2j gate j, 2j+1 up j), (2I, D)
+// int8 + int64 scales; down (D, I) + scales; bitlen of each logical linear's largest scale.
+struct ExpertW {
+  const int8_t* w_gu = nullptr;
+  const int64_t* M_gu = nullptr;
+  const int8_t* w_d = nullptr;
+  const int64_t* M_d = nullptr;
+  int I = 0;
+  int mb_g = 0, mb_u = 0, mb_d = 0;
+};
+
+struct MoeArgs {
+  int R = 0, D = 0, NE = 0, TOPK = 0, IMAX = 0;
+  const int16_t* xq = nullptr; int ldq = 0; const int32_t* xs = nullptr;   // qrow(irms(x, g2)) rows
+  const int8_t* w_router = nullptr; const int64_t* M_router = nullptr; int mbits_router = 0;
+  const int8_t* w_sgate = nullptr; const int64_t* M_sgate = nullptr; int mbits_sgate = 0;
+  const ExpertW* ex = nullptr;                 // NE + 1 entries; entry NE is the shared expert
+  const int32_t* exp_t = nullptr; const int32_t* silu_t = nullptr; const int32_t* sig_t = nullptr;
+  int32_t* sel = nullptr; int64_t* prob = nullptr; int64_t* sgv = nullptr;
+  int32_t* sel_hist = nullptr;                 // optional copy of the selections (R, TOPK)
+  int32_t* off = nullptr;                      // (NE + 2) slot offsets
+  int32_t* slot_row = nullptr; int32_t* slot_exp = nullptr;   // (R * (TOPK + 1))
+  int32_t* slot_of = nullptr;                  // (R * TOPK)
+  int64_t* raw_gu = nullptr; int ld_gu = 0;    // (slots, 2 IMAX)
+  int16_t* hq = nullptr; int ld_h = 0;         // (slots, IMAX)
+  int32_t* hs = nullptr;                       // (slots)
+  int64_t* raw_d = nullptr;                    // (slots, D)
+};
+// x[r] += MoE(m) for the R rows whose qrow(m) is in xq / xs
+cudaError_t launch_moe(const MoeArgs& a, int64_t* x, int ldx, cudaStream_t st);
+
 // ---------------------------------------------------------------- tcgen05 group-128 GEMM (many rows)
 constexpr int TC_MIN_ROWS = 16;        // activation rows from which the tensor-core path is used
 size_t gemm_tc_digit_bytes(int T, int K);

@@ -329,6 +329,7 @@ cudaError_t launch_digits(const int16_t* xq, int ldx, int T, int K, void* digits
 }
 
 bool gemm_tc_supported(const LinW& L, int epi) {
+  if (!L.Mg && epi != EPI_RAW) return false;      // per-channel linears: raw sums, requant elsewhere
   return L.w && L.K % 128 == 0 && L.N % TC_BM == 0 && ((uintptr_t)L.w & 15) == 0 &&
          (epi == EPI_RAW || epi == EPI_STORE || epi == EPI_RESID || epi == EPI_SWIGLU) && encode_fn() != nullptr;
 }

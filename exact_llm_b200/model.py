@@ -166,6 +166,14 @@ class ExactModel:
         tokens = [first] + [int(t) for t in toks[0, :-1]]
         return lg, [rows[s, 0] for s in range(steps)], tokens
 
+    def moe_selections(self, layer):
+        """Router top-k experts of every row of the last forward call at `layer`: int32 (rows, topk)."""
+        k = int(self.c["TOPK"])
+        n = min(int(self._rows), 4096)                   # rows of the last forward call
+        buf = np.empty((n, k), np.int32)
+        check(lib.exb_moe_selections(self.h, int(layer), ptr(buf, ctypes.c_int32), n * k))
+        return buf
+
     def set_option(self, name, value):
         """Engine option (results never change): "step" (persistent decode kernel on/off),
         "pf_kb" (its per-warp L2 prefetch distance in KiB)."""

@@ -151,6 +151,11 @@ int exb_freivalds_status(exb_model* m, int64_t* checks, int64_t* failures);
  * Cached step graphs are dropped. */
 int exb_set_option(exb_model* m, const char* name, int64_t value);
 
+/* MoE models: the router's top-k experts (ties to the lower index) of every row of the last
+ * exb_forward call for one layer, as (rows, topk) int32 (rows <= 4096).  Mirrors the reference's
+ * per-layer `sel` (experiments/moe_exact_kaggle.py:454-467). */
+int exb_moe_selections(exb_model* m, int layer, int32_t* host, int64_t n);
+
 /* device error word: bit 1 |V| >= 2^31 (V cache range), 2 wait timeout, 4 Freivalds, 8 bounds */
 int exb_device_errors(exb_model* m, int* bits);
 

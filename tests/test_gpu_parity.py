@@ -243,6 +243,40 @@ def test_tensor_core_prefill_matches_gemv_path(cuda_ok, T):
     assert np.array_equal(out[1][0], out[0][0])
 
 
+@pytest.mark.parametrize("key", ["tiny-moe", "qwen1.5-moe-L1"])
+def test_moe_models_vs_reference(golden, cuda_ok, key):
+    """BASELINE config 4 layer shape (Qwen1.5-MoE: 60 experts, top-4, shared expert) and a tiny MoE:
+    prefill logits, router selections per layer and token, greedy steps, against the reference
+    MoEInt run on the same integers (experiments/moe_exact_kaggle.py:419-482)."""
+    from exact_llm_b200 import ExactModel
+    g = golden["moe"][key]
+    c = dict(g["config"])
+    m = ExactModel.synthetic(c, g["seed"], max_batch=1, max_seq=len(g["prompt"]) + len(g["tokens"]) + 8)
+    lg = m(g["prompt"])
+    assert eo.h16(lg) == g["prefill"]
+    for layer, want in g["sel"].items():
+        assert m.moe_selections(int(layer)).tolist() == want, layer
+    pre, rows, toks = m.greedy(g["prompt"], len(g["tokens"]))
+    assert toks == g["tokens"]
+    assert [eo.h16(r) for r in rows] == g["rows"]
+
+
+def test_moe_tensor_core_prefill_matches_gemv_path(golden, cuda_ok):
+    """MoE prefill of 40 rows on the tcgen05 GEMM (per-channel raw sums + QLin requant) equals the
+    4-row GEMV path: logits, next tokens and the router selections."""
+    from exact_llm_b200 import ExactModel
+    c = dict(golden["moe"]["qwen1.5-moe-L1"]["config"])
+    m = ExactModel.synthetic(c, 17, max_batch=1, max_seq=64)
+    ids = np.random.default_rng(4).integers(0, c["V"], 40).astype(np.int32)
+    out = {}
+    for tc in (1, 0):
+        m.set_option("tc", tc)
+        lg = m(ids)
+        out[tc] = (lg, m.moe_selections(0))
+    assert np.array_equal(out[1][1], out[0][1])
+    assert np.array_equal(out[1][0], out[0][0])
+
+
 def test_freivalds_keys_and_self_check(golden, cuda_ok):
     """Device keys equal the reference keys (rng seeded 2026); honest steps pass every check;
     a corrupted weight is caught (experiments/gpu_engine_trace_verify_kaggle.py:803-872)."""
