@@ -26,6 +26,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (7B-arch, bs1) as % HBM roofline; prefill int8 TOPS; bit-exact"
 PROMPT = 512
+GU_TRAFFIC = 140.154112e6 + 3.357952e6      # bytes per launch of the 7B gate|up GEMV (one ncu capture)
 
 
 def peaks():
@@ -34,6 +35,57 @@ def peaks():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     return 6650.0, 1590.0, "fallback"
+
+
+def int8_peak_tops():
+    """Dense int8 tensor-core throughput of this GPU measured with the library GEMM (torch._int_mm,
+    cuBLASLt, 8192^3, best of 10 after warm-up): the denominator of the prefill utilisation."""
+    import torch
+    a = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device="cuda")
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = None
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None or ms < best else best
+    del a, b
+    return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
+
+
+def gemm_tc_tops(K, N, T, reps=10):
+    """The exact linear operator at T rows (qrow + digit planes + tcgen05 GEMM + epilogue) on one
+    7B gate|up-shaped layer: effective int16 x int8 TOPS (2 T N K per call) and milliseconds."""
+    import ctypes
+    import torch
+    from exact_llm_b200 import _lib as L
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    w = torch.empty(N * K, dtype=torch.int8, device="cuda")
+    M = torch.empty(N * (K // 128), dtype=torch.int32, device="cuda")
+    L.check(L.lib.exb_gen_tensor(0, 5, 11, N * K, K, L.ptr(w), st))
+    L.check(L.lib.exb_gen_tensor(1, 5, 12, N * (K // 128), K, L.ptr(M), st))
+    x = torch.randint(-(1 << 22), 1 << 22, (T, K), dtype=torch.int64, device="cuda")
+    y = torch.empty((T, N), dtype=torch.int64, device="cuda")
+    sc = torch.empty(L.lib.exb_linear_g128_scratch_bytes(T, K, N), dtype=torch.uint8, device="cuda")
+
+    def f():
+        L.check(L.lib.exb_linear_g128(L.ptr(x), T, K, L.ptr(w), L.ptr(M), None, N, L.ptr(y), None, L.ptr(sc), st))
+    for _ in range(3):
+        f()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        f()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    return 2.0 * T * N * K / (ms * 1e-3) / 1e12, ms
 
 
 # ------------------------------------------------------------------ clocks
@@ -156,6 +208,12 @@ def run_reference(a, rank, world):
 
 
 # ------------------------------------------------------------------ our arm
+def lin_flops_fn(c):
+    """2 x MACs of every linear and the head for one token (int16 x int8 products)."""
+    return 2 * (c["NL"] * ((c["H"] + 2 * c["KV"]) * c["hd"] * c["D"] + c["D"] * c["H"] * c["hd"] + 3 * c["I"] * c["D"])
+                + c["V"] * c["D"])
+
+
 def step_bytes(c, B, S):
     """Algorithmic HBM bytes of one decode step (all B rows): int8 weights + group scales + head
     (int8 + int64 per-channel scales) + KV cache read (K int16 + shift, V int32) at S positions."""
@@ -189,15 +247,19 @@ def run_ours(a, rank, world, local_rank):
     stream = torch.cuda.ExternalStream(m.stream)
     rng = np.random.default_rng(100 + rank)
     prompts = rng.integers(0, c["V"], (B, PROMPT)).astype(np.int32)
-    # prefill (untimed): rows of all sequences, position-major so every chunk holds B sequences
+    # prefill (outside the decode timing): rows of all sequences, position-major so every chunk
+    # holds B sequences; CUDA events on the model stream around the whole forward call
     barrier()
-    t0 = time.perf_counter()
     ids = prompts.T.reshape(-1)
     seqs = np.tile(np.arange(B, dtype=np.int32), PROMPT)
     for b in range(B):
         m.new_cache(b)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
     _, nxt = m.forward_rows(ids, seqs, want_logits=False)
-    prefill_s = time.perf_counter() - t0
+    p1.record(stream)
+    torch.cuda.synchronize()
+    prefill_s = p0.elapsed_time(p1) / 1e3
     first = nxt[-B:].astype(np.int32)
     ids_dev = torch.from_numpy(first).cuda()
     tok_dev = torch.empty((max(W, K), B), dtype=torch.int32, device="cuda")
@@ -234,7 +296,15 @@ def run_ours(a, rank, world, local_rank):
     import ctypes
     avg = ctypes.c_float()
     nbytes = ctypes.c_double()
-    check(lib.exb_bench_linear(m.h, 0, 2, B, 50, ctypes.byref(avg), ctypes.byref(nbytes)))
+    if B <= 4:
+        check(lib.exb_bench_linear(m.h, 0, 2, B, 50, ctypes.byref(avg), ctypes.byref(nbytes)))
+        kern_name = "k_gemv<R,2,group> (fused gate|up, SwiGLU epilogue), layer 0"
+    else:
+        # wider batches run every linear on the tcgen05 GEMM: time the gate|up-shaped linear at B rows
+        _, gms = gemm_tc_tops(c["D"], 2 * c["I"], B)
+        avg.value = gms
+        nbytes.value = 2 * c["I"] * c["D"] * (1 + 4 / 128) + B * c["D"] * 8 + B * 2 * c["I"] * 8
+        kern_name = f"tcgen05 group-128 GEMM, gate|up shape, {B} rows (qrow + digits + GEMM)"
     hbm, _, src = peaks()
     kern_gbs = nbytes.value / (avg.value * 1e-3) / 1e9
     S_mid = PROMPT + W + K // 2
@@ -246,8 +316,18 @@ def run_ours(a, rank, world, local_rank):
             dist.destroy_process_group()
         return
     value = world * B * K / (ms * 1e-3)
-    lin_flops = 2 * (c["NL"] * ((c["H"] + 2 * c["KV"]) * c["hd"] * c["D"] + c["D"] * c["H"] * c["hd"]
-                                + 3 * c["I"] * c["D"]) + c["V"] * c["D"])
+    # prefill: the whole forward (every op) and the tcgen05 linear alone at the 7B gate|up shape
+    prefill = {"tokens": PROMPT * B, "seconds": prefill_s, "tok_s": PROMPT * B / prefill_s,
+               "effective_tops": lin_flops_fn(c) * PROMPT * B / prefill_s / 1e12,
+               "path": "linears on the tcgen05 int8 GEMM (int16 activations as 2 int8 digits), 256-row chunks"}
+    if PROMPT * B >= 16 and not a.no_gemm:
+        tops, gms = gemm_tc_tops(c["D"], 2 * c["I"], 2048)
+        peak8 = int8_peak_tops()
+        prefill["gemm"] = {"shape": f"T=2048 K={c['D']} N={2 * c['I']} (gate|up)", "ms": gms, "effective_tops": tops,
+                           "tensor_pipe_tops": 2 * tops, "int8_peak_tops": peak8,
+                           "peak_source": "measured: torch._int_mm (cuBLASLt) 8192^3 int8, best of 10",
+                           "frac": 2 * tops / peak8}
+
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -258,17 +338,18 @@ def run_ours(a, rank, world, local_rank):
                    "l2": "no flush: 7.3 GB of weights stream from HBM every step (L2 126 MB)"},
         "decode_hbm": {"bytes_per_step": sb, "achieved_gbs": step_gbs, "peak_gbs": hbm, "frac": step_gbs / hbm,
                        "peak_source": src},
-        "roofline": {"bound": "hbm", "kernel": "k_gemv<R,2,group> (fused gate|up, SwiGLU epilogue), layer 0",
+        "roofline": {"bound": "hbm", "kernel": kern_name,
                      "achieved": kern_gbs, "peak": hbm, "unit": "GB/s", "frac": kern_gbs / hbm,
-                     "traffic": None, "avg_launch_ms": avg.value, "algorithmic_bytes": nbytes.value,
+                     "traffic": GU_TRAFFIC if a.model == "qwen2.5-7b" and B == 1 else None,   # R=1 capture
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this kernel, "
+                                       "profiles/gemv_gate_up_7b_r1.md",
+                     "avg_launch_ms": avg.value, "algorithmic_bytes": nbytes.value,
                      "peak_source": src},
-        "prefill": {"tokens": PROMPT * B, "seconds": prefill_s, "tok_s": PROMPT * B / prefill_s,
-                    "effective_tops": lin_flops * PROMPT * B / prefill_s / 1e12,
-                    "path": "CUDA-core GEMV in 4-row chunks (tensor-core GEMM not yet wired)"},
+        "prefill": prefill,
         "e2e": {"value": world * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * 3 * 4,
                 "d2h_bytes_per_step": 4 * B,
                 "path": "exb_forward(host ids) -> host next-token, one call per step"},
-        "gpu_launches": K * (1 + 10 * c["NL"] + 3),
+        "gpu_launches": K * (1 + 10 * c["NL"] + 3) if B <= 4 else None,
         "clocks": clk.summary(),
     }
     if world == 1 and not a.no_cpu:
@@ -288,6 +369,7 @@ def main():
     ap.add_argument("--model", default="qwen2.5-7b")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the tensor-core GEMM / int8 peak measurement")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens before decode (profiling uses a short one)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures only)")
     a = ap.parse_args()

@@ -1096,11 +1096,44 @@ static int ensure_gen(exb_model* m, int B, int steps) {
   return EXB_OK;
 }
 
+// Greedy decode of B > 4 sequences: every step is one tensor-core chunk of B rows (row b = the
+// last token of sequence b at its next position), next tokens fed back through the host.
+static int generate_wide(exb_model* m, int B, const int32_t* ids_dev_or_null, const int32_t* ids_host, int steps,
+                         int32_t* tokens_host, int64_t* logits_host, int32_t* tokens_dev) {
+  const exb_config& c = m->c;
+  if (B > PCH || !prefill_tc_ok(m)) FAIL(EXB_EINVAL, "generate: B > 4 needs the tensor-core path and B <= 256");
+  int rc = prefill_alloc(m);
+  if (rc) return rc;
+  std::vector<int32_t> cur(B), nxt(B), toks((size_t)B * steps);
+  if (ids_dev_or_null) CK(cudaMemcpy(cur.data(), ids_dev_or_null, 4 * (size_t)B, cudaMemcpyDeviceToHost));
+  else memcpy(cur.data(), ids_host, 4 * (size_t)B);
+  for (int b = 0; b < B; ++b)
+    if (cur[b] < 0 || cur[b] >= c.V) FAIL(EXB_EINVAL, "token id out of range");
+  CK(cudaMemsetAsync(m->err, 0, sizeof(int), m->st));
+  for (int s = 0; s < steps; ++s) {
+    for (int b = 0; b < B; ++b) {
+      m->p_hrows[b] = cur[b]; m->p_hrows[PCH + b] = b; m->p_hrows[2 * PCH + b] = m->seq_len[b] + s;
+    }
+    rc = prefill_chunk(m, B, logits_host ? logits_host + (size_t)s * B * c.V : nullptr, nxt.data());
+    if (rc) return rc;
+    for (int b = 0; b < B; ++b) toks[(size_t)s * B + b] = nxt[b];
+    cur = nxt;
+  }
+  for (int b = 0; b < B; ++b) m->seq_len[b] += steps;
+  if (tokens_host) memcpy(tokens_host, toks.data(), 4 * toks.size());
+  if (tokens_dev) CK(cudaMemcpy(tokens_dev, toks.data(), 4 * toks.size(), cudaMemcpyHostToDevice));
+  return check_device_errors(m);
+}
+
 static int generate_common(exb_model* m, int B, const int32_t* ids_dev_or_null, const int32_t* ids_host, int steps,
                            int32_t* tokens_host, int64_t* logits_host, int32_t* tokens_dev) {
   if (!m || !m->finalized) FAIL(EXB_EINVAL, "model not finalized");
   const exb_config& c = m->c;
-  if (B <= 0 || B > RMAX || B > c.max_batch) FAIL(EXB_EINVAL, "generate: 1 <= B <= 4 in this build");
+  if (B <= 0 || B > c.max_batch) FAIL(EXB_EINVAL, "generate: 1 <= B <= max_batch");
+  if (steps > 0)
+    for (int b = 0; b < B; ++b)
+      if (m->seq_len[b] + steps > c.max_seq) FAIL(EXB_EINVAL, "generate: max_seq exceeded");
+  if (B > RMAX && steps > 0) return generate_wide(m, B, ids_dev_or_null, ids_host, steps, tokens_host, logits_host, tokens_dev);
   if (steps <= 0) return EXB_OK;
   for (int b = 0; b < B; ++b)
     if (m->seq_len[b] + steps > c.max_seq) FAIL(EXB_EINVAL, "generate: max_seq exceeded");

@@ -277,6 +277,28 @@ def test_moe_tensor_core_prefill_matches_gemv_path(golden, cuda_ok):
     assert np.array_equal(out[1][0], out[0][0])
 
 
+def test_wide_batch_generate_matches_single_sequences(golden, cuda_ok):
+    """Batch-16 greedy decode (every step one tensor-core chunk of 16 rows, BASELINE config 3's bs16)
+    produces, for every sequence, the tokens and logits of decoding that sequence alone."""
+    from exact_llm_b200 import ExactModel, configs
+    c = configs.arch("qwen2.5-7b", NL=1)
+    B, P, S = 16, 12, 5
+    m = ExactModel.synthetic(c, 23, max_batch=B, max_seq=P + S + 4)
+    prompts = np.random.default_rng(8).integers(0, c["V"], (B, P)).astype(np.int32)
+    ids = prompts.T.reshape(-1)
+    seqs = np.tile(np.arange(B, dtype=np.int32), P)
+    for b in range(B):
+        m.new_cache(b)
+    _, nxt = m.forward_rows(ids, seqs, want_logits=False)
+    toks, rows = m.generate(nxt[-B:], S, want_logits=True)
+    for b in (0, 7, 15):
+        m1 = ExactModel.synthetic(c, 23, max_batch=1, max_seq=P + S + 4)
+        pre, rows1, toks1 = m1.greedy(prompts[b], S)
+        assert [int(nxt[-B + b])] + list(toks[b, :-1]) == toks1, b
+        for s in range(S):
+            assert np.array_equal(rows[s, b], rows1[s]), (b, s)
+
+
 def test_freivalds_keys_and_self_check(golden, cuda_ok):
     """Device keys equal the reference keys (rng seeded 2026); honest steps pass every check;
     a corrupted weight is caught (experiments/gpu_engine_trace_verify_kaggle.py:803-872)."""
