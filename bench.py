@@ -349,7 +349,10 @@ def run_ours(a, rank, world, local_rank):
         "e2e": {"value": world * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * 3 * 4,
                 "d2h_bytes_per_step": 4 * B,
                 "path": "exb_forward(host ids) -> host next-token, one call per step"},
-        "gpu_launches": K * (1 + 10 * c["NL"] + 3) if B <= 4 else None,
+        # per step: B <= 4 one CUDA graph (embed, 10 kernels per layer, final norm, head, token feedback);
+        # wider batches one tensor-core chunk (embed, 14 per layer: norms, digit planes, GEMMs, rope,
+        # attention, qrow; final norm, digits, head GEMM, head rows)
+        "gpu_launches": K * (1 + 10 * c["NL"] + 3) if B <= 4 else K * (1 + 14 * c["NL"] + 4),
         "clocks": clk.summary(),
     }
     if world == 1 and not a.no_cpu:
