@@ -57,6 +57,10 @@ SIGNATURES = {
     "exb_freivalds_status": (ctypes.c_int, [ctypes.c_void_p, c_i64p, c_i64p]),
     "exb_set_option": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int64]),
     "exb_moe_selections": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, c_i32p, ctypes.c_int64]),
+    "exb_tp_plan": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, c_i32p]),
+    "exb_tp_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
+    "exb_model_create_tp": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p,
+                                           ctypes.POINTER(ctypes.c_void_p)]),
     "exb_device_errors": (ctypes.c_int, [ctypes.c_void_p, c_i32p]),
     "exb_bench_linear": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)]),

@@ -11,6 +11,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include"), "-I", SRC]
+LIBS = ["-lnccl"]                     # tensor-parallel collectives (NCCL over NVLink)
 
 
 def sources():
@@ -29,7 +30,7 @@ def needs_build():
 def build(force=False, verbose=False, extra=()):
     if not force and not needs_build():
         return LIB
-    cmd = [NVCC] + ARCH + FLAGS + list(extra) + ["-o", LIB + ".tmp"] + sources()
+    cmd = [NVCC] + ARCH + FLAGS + list(extra) + ["-o", LIB + ".tmp"] + sources() + LIBS
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

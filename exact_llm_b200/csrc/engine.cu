@@ -16,6 +16,8 @@
 #include <string>
 #include <vector>
 
+#include <nccl.h>
+
 #include "exactb200.h"
 #include "common.cuh"
 #include "exb_internal.h"
@@ -50,6 +52,8 @@ static int bitlen_host(uint64_t v) { int b = 0; while (v) { ++b; v >>= 1; } retu
 struct LinInfo {                        // one logical linear (reference naming) inside a fused matrix
   std::string name;
   int N = 0, K = 0;
+  int Ng = 0, Kg = 0;                   // global shape (tensor parallel: this rank holds a slice)
+  int r_lo = 0, c_lo = 0;               // global row / column of the slice's first element
   int row0 = 0, row_step = 1;           // its rows in the fused matrix
   LinW* fused = nullptr;                // owning fused matrix
   int trace_off = 0;
@@ -110,6 +114,15 @@ struct exb_model {
   int64_t fr_checks = 0;
   std::map<uint64_t, cudaGraphExec_t> graphs;
   int32_t *h_ids = nullptr, *h_seq = nullptr, *h_pos = nullptr;           // pinned staging
+  // tensor parallel (tp > 1): this rank's slice of the model; cg = the global architecture
+  exb_config cg{};
+  int tp = 1, tp_rank = 0;
+  int qh0 = 0, qh1 = 0, kh0 = 0, kh1 = 0, ig0 = 0, ig1 = 0, v0 = 0, v1 = 0, vmax = 0;
+  ncclComm_t comm = nullptr;
+  int64_t* tp_tot = nullptr;                // (RMAX, D) partial sums of o / down
+  int64_t* tp_hval = nullptr;               // (RMAX) shard best logit
+  int64_t* tp_hmax = nullptr;               // (RMAX) all-reduced best logit
+  int64_t* tp_gather = nullptr;             // (RMAX, tp, vmax) gathered logits
   // MoE runtime (rows up to MOE_ROWS per call of the block)
   int moe_imax = 0;
   int32_t *moe_sel = nullptr, *moe_off = nullptr, *moe_slot_row = nullptr, *moe_slot_exp = nullptr, *moe_slot_of = nullptr;
@@ -184,10 +197,10 @@ static void plan_weights(exb_model* m) {
       mk(Ld.down, D, I, false);
     }
   }
-  m->emb = walloc<int8_t>(m, (size_t)c.V * D);
+  m->emb = walloc<int8_t>(m, (size_t)m->cg.V * D);            // every rank embeds every token
   m->gf = walloc<int64_t>(m, D);
   m->head.N = c.V; m->head.K = D;
-  m->head.w = c.tie ? m->emb : walloc<int8_t>(m, (size_t)c.V * D);
+  m->head.w = c.tie ? (m->emb ? m->emb + (size_t)m->v0 * D : nullptr) : walloc<int8_t>(m, (size_t)c.V * D);
   m->head.Mc = walloc<int64_t>(m, c.V);
   m->exp_t = walloc<int32_t>(m, EXP_LEN_H);
   m->silu_t = walloc<int32_t>(m, SILU_LEN_H);
@@ -202,6 +215,7 @@ static void plan_lins(exb_model* m) {
   int off = 0;
   auto add = [&](const std::string& nm, LinW* f, int N, int K, int row0, int step) {
     LinInfo li; li.name = nm; li.N = N; li.K = K; li.row0 = row0; li.row_step = step; li.fused = f;
+    li.Ng = N; li.Kg = K;
     li.trace_off = off; off += N;
     m->lins.push_back(li);
     return (int)m->lins.size() - 1;
@@ -236,6 +250,19 @@ static void plan_lins(exb_model* m) {
   }
   add("head", &m->head, c.V, c.D, 0, 1);
   m->n_lin = (int)m->lins.size();
+  if (m->tp > 1) {
+    // global shapes and slice offsets of this rank (column-split q/k/v, gate/up, head; row-split o, down)
+    const exb_config& g = m->cg;
+    for (auto& L : m->lins) {
+      const std::string t = L.name.substr(L.name.find('.') + 1);
+      if (L.name == "head") { L.Ng = g.V; L.r_lo = m->v0; continue; }
+      if (t == "q") { L.Ng = g.H * g.hd; L.r_lo = m->qh0 * g.hd; }
+      else if (t == "k" || t == "v") { L.Ng = g.KV * g.hd; L.r_lo = m->kh0 * g.hd; }
+      else if (t == "o") { L.Kg = g.H * g.hd; L.c_lo = m->qh0 * g.hd; }
+      else if (t == "gate" || t == "up") { L.Ng = g.I; L.r_lo = m->ig0 * 128; }
+      else if (t == "down") { L.Kg = g.I; L.c_lo = m->ig0 * 128; }
+    }
+  }
   m->trace_row = off;
 }
 
@@ -255,7 +282,7 @@ static void plan_runtime(exb_model* m) {
   m->qs = ralloc<int32_t>(m, (size_t)RMAX * c.H);
   m->ao = ralloc<int64_t>(m, (size_t)RMAX * c.H * c.hd);
   m->hb = ralloc<int64_t>(m, (size_t)RMAX * c.I);
-  m->logits = ralloc<int64_t>(m, (size_t)RMAX * c.V);
+  m->logits = ralloc<int64_t>(m, (size_t)RMAX * std::max(c.V, m->vmax));
   m->rawb = ralloc<int64_t>(m, (size_t)RMAX * m->NMAX);
   m->next_tok = ralloc<int32_t>(m, RMAX);
   m->amax_o = ralloc<unsigned long long>(m, RMAX);
@@ -288,6 +315,12 @@ static void plan_runtime(exb_model* m) {
     m->moe_hist = ralloc<int32_t>(m, (size_t)c.NL * SEL_CAP * TK);
     for (int i = 0; i < c.NL; ++i) m->L[i].ex_dev = ralloc<ExpertW>(m, NE + 1);
   }
+  if (m->tp > 1) {
+    m->tp_tot = ralloc<int64_t>(m, (size_t)RMAX * c.D);
+    m->tp_hval = ralloc<int64_t>(m, RMAX);
+    m->tp_hmax = ralloc<int64_t>(m, RMAX);
+    m->tp_gather = ralloc<int64_t>(m, (size_t)RMAX * m->tp * m->vmax);
+  }
   m->step_layers = ralloc<StepLayer>(m, c.NL);
   m->s_att = ralloc<int64_t>(m, (size_t)c.NL * STEP_ROWS * c.H * c.hd);
   m->s_gmax = ralloc<long long>(m, (size_t)c.NL * STEP_ROWS * c.H);
@@ -302,6 +335,12 @@ static void plan_runtime(exb_model* m) {
 // sequence slot and position from device arrays, so the enqueued work is identical for every
 // step and can be captured once into a CUDA graph.
 static std::vector<cudaEvent_t>* g_prof = nullptr;   // profiling: an event after every launch
+
+// NCCL all-reduce on the model stream (captured into the step graph like any kernel)
+static cudaError_t tp_allreduce(exb_model* m, const void* src, void* dst, size_t n, ncclDataType_t t, ncclRedOp_t op,
+                                cudaStream_t st) {
+  return ncclAllReduce(src, dst, n, t, op, m->comm, st) == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+}
 
 // MoE block arguments for layer i over R rows (qrow(m) rows xq / xs); selections recorded at row
 // hist_row0 of the layer's history when hist_row0 >= 0
@@ -330,7 +369,8 @@ static int g_hist_row0 = -1;                             // selection-history ro
 static bool step_args(exb_model* m, int R, const int32_t* ids, const int32_t* seq, const int32_t* pos,
                       bool want_logits, StepArgs& a) {
   const exb_config& c = m->c;
-  if (!m->step_on || !m->group || m->trace_on || m->fr_on || m->emb_q16 || R < 1 || R > STEP_ROWS) return false;
+  if (!m->step_on || !m->group || m->trace_on || m->fr_on || m->emb_q16 || R < 1 || R > STEP_ROWS || m->tp > 1)
+    return false;
   a.layers = m->step_layers; a.NL = c.NL; a.R = R; a.D = c.D; a.H = c.H; a.KV = c.KV; a.hd = c.hd; a.I = c.I;
   a.V = c.V; a.Nqkv = m->Nqkv; a.Smax = c.max_seq; a.Tmax = c.rope_len; a.max_batch = c.max_batch;
   a.emb = m->emb; a.emb_shift = c.emb_shift; a.gf = m->gf; a.head = m->head;
@@ -357,6 +397,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
                                 bool want_logits, cudaStream_t st) {
   const exb_config& c = m->c;
   const bool pdl = m->pdl && !g_prof;
+  const bool tp = m->tp > 1;
   cudaError_t e;
 #define RUN(x)                                                    \
   do {                                                            \
@@ -435,13 +476,20 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     }
     RUN(launch_rope_cache(aa, st, pdl));
     RUN(launch_attn_decode(aa, st, pdl));
-    RUN(launch_quant_known(m->ao, Hd, R, Hd, m->amax_o, m->xq, m->KMAX, m->xs, st, pdl));
+    // tensor parallel: the qrow of o's input needs the max over every rank's heads
+    if (tp) RUN(tp_allreduce(m, m->amax_o, m->amax_o, R, ncclUint64, ncclMax, st));
+    RUN(launch_quant_known(m->ao, Hd, R, Hd, m->amax_o, m->xq, m->KMAX, m->xs, st, pdl && !tp));
     {
       GemvArgs g; base(g, Ld.o);
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[3]);
       g.zero = m->amax_h; g.nzero = RMAX;
+      if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own heads
       set_fr(g, {Ld.li[3]});
       RUN(launch_gemv(g, st, pdl));
+    }
+    if (tp) {
+      RUN(tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st));
+      RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.o.b, m->x, c.D, st));
     }
     RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     if (c.n_experts) {
@@ -455,12 +503,18 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       set_fr(g, {Ld.li[4], Ld.li[5]});
       RUN(launch_gemv(g, st, pdl));
     }
-    RUN(launch_quant_known(m->hb, c.I, R, c.I, m->amax_h, m->xq, m->KMAX, m->xs, st, pdl));
+    if (tp) RUN(tp_allreduce(m, m->amax_h, m->amax_h, R, ncclUint64, ncclMax, st));
+    RUN(launch_quant_known(m->hb, c.I, R, c.I, m->amax_h, m->xq, m->KMAX, m->xs, st, pdl && !tp));
     {
       GemvArgs g; base(g, Ld.down);
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[6]);
+      if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own groups
       set_fr(g, {Ld.li[6]});
       RUN(launch_gemv(g, st, pdl));
+    }
+    if (tp) {
+      RUN(tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st));
+      RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.down.b, m->x, c.D, st));
     }
   }
   RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
@@ -468,11 +522,18 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     GemvArgs g;
     g.L = m->head; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
     g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX;
-    g.epi = EPI_HEAD; g.out = want_logits ? m->logits : nullptr; g.ldo = c.V;
+    g.epi = EPI_HEAD; g.out = want_logits ? m->logits : nullptr; g.ldo = tp ? m->vmax : c.V;
     g.raw = trace_ptr(m->n_lin - 1);
     g.head_part = m->head_part; g.head_ticket = m->head_ticket; g.next_tok = m->next_tok; g.grid = m->head_grid;
+    if (tp) g.head_val = m->tp_hval;
     set_fr(g, {m->n_lin - 1});
     RUN(launch_gemv(g, st, pdl));
+  }
+  if (tp) {
+    // greedy over the vocabulary slices: the largest value, then the lowest index holding it
+    RUN(tp_allreduce(m, m->tp_hval, m->tp_hmax, R, ncclInt64, ncclMax, st));
+    RUN(launch_tp_pick(m->tp_hval, m->tp_hmax, m->next_tok, m->v0, R, st));
+    RUN(tp_allreduce(m, m->next_tok, m->next_tok, R, ncclInt32, ncclMin, st));
   }
   if (m->fr_on) RUN(launch_fr_check(m->fr_acc, m->n_lin * RMAX, m->fr_fail, m->err, st, false));
   // note: fr_acc rows beyond R stay zero and compare equal
@@ -634,9 +695,88 @@ int exb_linear_channel(const int64_t* x, int R, int K, const int8_t* w_NK, const
   return linear_common(x, R, K, L, y, acc_out, scratch, (cudaStream_t)stream, true);
 }
 
-int exb_model_create(const exb_config* cfg, exb_model** out) {
+// Tensor-parallel shard of rank `rank` of `size` (SURVEY-style partition of the reference layer):
+// q heads split inside each KV group when size is a multiple of KV (7B TP8: 4/3 heads per rank
+// pair, one KV head each), whole KV groups per rank when KV is a multiple of size; I split by
+// 128-groups (first ranks one more); vocabulary in equal slices (the last one shorter).
+// out = {qh0, qh1, kh0, kh1, ig0, ig1, v0, v1, vmax}.
+static bool tp_plan(const exb_config& c, int rank, int size, int* o, std::string& why) {
+  if (size < 1 || rank < 0 || rank >= size) { why = "tensor parallel: 0 <= rank < size"; return false; }
+  if (size == 1) {
+    const int vals[9] = {0, c.H, 0, c.KV, 0, (c.I + 127) / 128, 0, c.V, c.V};
+    for (int i = 0; i < 9; ++i) o[i] = vals[i];
+    return true;
+  }
+  if (c.lin_kind != 0 || c.n_experts) { why = "tensor parallel covers the dense group-128 models"; return false; }
+  if (c.KV <= 0 || c.H % c.KV) { why = "H must be a multiple of KV"; return false; }
+  const int rep = c.H / c.KV;
+  int qh0, qh1, kh0, kh1;
+  if (size % c.KV == 0) {
+    const int mm = size / c.KV, g = rank / mm, j = rank % mm;
+    if (mm > rep) { why = "more ranks per KV group than query heads"; return false; }
+    const int base = rep / mm, extra = rep % mm;
+    qh0 = g * rep + j * base + std::min(j, extra);
+    qh1 = qh0 + base + (j < extra ? 1 : 0);
+    kh0 = g; kh1 = g + 1;
+  } else if (c.KV % size == 0) {
+    const int per = c.KV / size;
+    kh0 = rank * per; kh1 = kh0 + per;
+    qh0 = kh0 * rep; qh1 = kh1 * rep;
+  } else {
+    why = "tensor parallel size must divide KV or be a multiple of it";
+    return false;
+  }
+  if (((qh1 - qh0) * c.hd) % 128) { why = "query heads per rank x head_dim must be a multiple of 128"; return false; }
+  if (c.I % 128 || c.I / 128 < size) { why = "I must hold at least one 128-group per rank"; return false; }
+  const int G = c.I / 128, gb = G / size, ge = G % size;
+  const int ig0 = rank * gb + std::min(rank, ge), ig1 = ig0 + gb + (rank < ge ? 1 : 0);
+  const int vmax = (c.V + size - 1) / size, v0 = rank * vmax, v1 = std::min(c.V, v0 + vmax);
+  if (v1 <= v0) { why = "vocabulary smaller than the rank count"; return false; }
+  const int vals[9] = {qh0, qh1, kh0, kh1, ig0, ig1, v0, v1, vmax};
+  for (int i = 0; i < 9; ++i) o[i] = vals[i];
+  return true;
+}
+
+static int create_impl(const exb_config* cfg, int rank, int size, const uint8_t* uid, exb_model** out);
+
+int exb_model_create(const exb_config* cfg, exb_model** out) { return create_impl(cfg, 0, 1, nullptr, out); }
+
+int exb_model_create_tp(const exb_config* cfg, int rank, int size, const uint8_t* unique_id, exb_model** out) {
+  if (size > 1 && !unique_id) FAIL(EXB_EINVAL, "exb_model_create_tp: unique id required");
+  return create_impl(cfg, rank, size, unique_id, out);
+}
+
+int exb_tp_plan(const exb_config* cfg, int rank, int size, int32_t* out9) {
+  if (!cfg || !out9) FAIL(EXB_EINVAL, "null argument");
+  std::string why;
+  int o[9];
+  if (!tp_plan(*cfg, rank, size, o, why)) FAIL(EXB_EINVAL, why);
+  for (int i = 0; i < 9; ++i) out9[i] = o[i];
+  return EXB_OK;
+}
+
+int exb_tp_unique_id(uint8_t* out128) {
+  if (!out128) FAIL(EXB_EINVAL, "null argument");
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) FAIL(EXB_ECUDA, "ncclGetUniqueId failed");
+  static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id is 128 bytes");
+  memcpy(out128, &id, 128);
+  return EXB_OK;
+}
+
+static int create_impl(const exb_config* cfg, int rank, int size, const uint8_t* uid, exb_model** out) {
   if (!cfg || !out) FAIL(EXB_EINVAL, "null argument");
-  const exb_config& c = *cfg;
+  int plan[9];
+  {
+    std::string why;
+    if (!tp_plan(*cfg, rank, size, plan, why)) FAIL(EXB_EINVAL, why);
+  }
+  // this rank's architecture: its heads, MLP groups and vocabulary slice
+  exb_config cl = *cfg;
+  if (size > 1) {
+    cl.H = plan[1] - plan[0]; cl.KV = plan[3] - plan[2]; cl.I = (plan[5] - plan[4]) * 128; cl.V = plan[7] - plan[6];
+  }
+  const exb_config& c = cl;
   if (c.D <= 0 || c.H <= 0 || c.KV <= 0 || c.hd <= 0 || c.I <= 0 || c.V <= 0 || c.NL <= 0) FAIL(EXB_EINVAL, "bad dims");
   if (c.H % c.KV || c.H / c.KV > 8) FAIL(EXB_EINVAL, "H must be a multiple of KV with at most 8 query heads per KV head");
   if (c.hd % 16 || c.hd > 128) FAIL(EXB_EINVAL, "head_dim must be a multiple of 16 and <= 128");
@@ -649,6 +789,10 @@ int exb_model_create(const exb_config* cfg, exb_model** out) {
   if (c.D % gk || (c.H * c.hd) % gk || c.I % gk) FAIL(EXB_EINVAL, "D, H*hd and I must be multiples of 128 (group) or 16 (channel)");
   exb_model* m = new exb_model();
   m->c = c;
+  m->cg = *cfg;
+  m->tp = size; m->tp_rank = rank;
+  m->qh0 = plan[0]; m->qh1 = plan[1]; m->kh0 = plan[2]; m->kh1 = plan[3];
+  m->ig0 = plan[4]; m->ig1 = plan[5]; m->v0 = plan[6]; m->v1 = plan[7]; m->vmax = plan[8];
   m->group = c.lin_kind == 0;
   m->Nqkv = (c.H + 2 * c.KV) * c.hd;
   m->KMAX = std::max(std::max(c.D, c.H * c.hd), c.I);
@@ -679,6 +823,15 @@ int exb_model_create(const exb_config* cfg, exb_model** out) {
   cudaMallocHost(&m->h_ids, sizeof(int32_t) * RMAX * 3);
   m->h_seq = m->h_ids + RMAX; m->h_pos = m->h_ids + 2 * RMAX;
   m->seq_len.assign(c.max_batch, 0);
+  if (size > 1) {
+    ncclUniqueId id;
+    memcpy(&id, uid, sizeof id);
+    // collective: every rank of the group calls this concurrently
+    if (ncclCommInitRank(&m->comm, size, id, rank) != ncclSuccess) {
+      exb_model_destroy(m);
+      FAIL(EXB_ECUDA, "ncclCommInitRank failed");
+    }
+  }
   *out = m;
   return EXB_OK;
 }
@@ -691,6 +844,7 @@ void exb_model_destroy(exb_model* m) {
   cudaFree(m->rarena);
   cudaFree(m->gen_tokens);
   cudaFree(m->emb_q16);
+  if (m->comm) ncclCommDestroy(m->comm);
   cudaFree(m->p_arena);
   if (m->p_hrows) cudaFreeHost(m->p_hrows);
   if (m->h_ids) cudaFreeHost(m->h_ids);
@@ -738,17 +892,68 @@ static LinInfo* find_lin(exb_model* m, const std::string& nm) {
   return nullptr;
 }
 
+// Tensor parallel: cut this rank's window out of a global (rows x cols) row-major host tensor of
+// `esz`-byte elements (rows [r0, r0 + nr), columns [c0, c0 + nc)).
+static std::vector<char> host_window(const void* src, size_t cols, size_t esz, size_t r0, size_t nr, size_t c0, size_t nc) {
+  std::vector<char> out(nr * nc * esz);
+  for (size_t r = 0; r < nr; ++r)
+    memcpy(out.data() + r * nc * esz, (const char*)src + ((r0 + r) * cols + c0) * esz, nc * esz);
+  return out;
+}
+
+static int set_tensor_local(exb_model* m, const std::string& name, const void* host, size_t bytes);
+
 int exb_model_set_tensor(exb_model* m, const char* name_c, const void* host, size_t bytes) {
   if (!m || !name_c || !host) FAIL(EXB_EINVAL, "null argument");
-  const exb_config& c = m->c;
   const std::string name(name_c);
+  if (m->tp == 1) return set_tensor_local(m, name, host, bytes);
+  // global tensors in, this rank's slices stored
+  const exb_config& g = m->cg;
+  if (name == "head.w") {
+    if (bytes != (size_t)g.V * g.D) FAIL(EXB_EINVAL, "head.w: wrong size");
+    auto w = host_window(host, g.D, 1, m->v0, m->v1 - m->v0, 0, g.D);
+    return set_tensor_local(m, name, w.data(), w.size());
+  }
+  if (name == "head.M") {
+    if (bytes != (size_t)g.V * 8) FAIL(EXB_EINVAL, "head.M: wrong size");
+    auto w = host_window(host, 1, 8, m->v0, m->v1 - m->v0, 0, 1);
+    return set_tensor_local(m, name, w.data(), w.size());
+  }
+  const size_t d1 = name.find('.'), d2 = name.find('.', d1 + 1);
+  if (name[0] == 'L' && d2 != std::string::npos) {
+    LinInfo* L = find_lin(m, name.substr(0, d2));
+    if (L && (L->Ng != L->N || L->Kg != L->K)) {
+      const std::string part = name.substr(d2 + 1);
+      if (part == "w") {
+        if (bytes != (size_t)L->Ng * L->Kg) FAIL(EXB_EINVAL, name + ": wrong size (global shape)");
+        auto w = host_window(host, L->Kg, 1, L->r_lo, L->N, L->c_lo, L->K);
+        return set_tensor_local(m, name, w.data(), w.size());
+      }
+      if (part == "M") {
+        const int Gg = L->Kg / 128;
+        if (bytes != (size_t)L->Ng * Gg * 4) FAIL(EXB_EINVAL, name + ": wrong size (global shape, int32 N x K/128)");
+        auto w = host_window(host, Gg, 4, L->r_lo, L->N, L->c_lo / 128, L->K / 128);
+        return set_tensor_local(m, name, w.data(), w.size());
+      }
+      if (part == "b") {
+        if (bytes != (size_t)L->Ng * 8) FAIL(EXB_EINVAL, name + ": wrong size (global shape)");
+        auto w = host_window(host, 1, 8, L->r_lo, L->N, 0, 1);
+        return set_tensor_local(m, name, w.data(), w.size());
+      }
+    }
+  }
+  return set_tensor_local(m, name, host, bytes);
+}
+
+static int set_tensor_local(exb_model* m, const std::string& name, const void* host, size_t bytes) {
+  const exb_config& c = m->c;
   auto need = [&](size_t n) -> bool { return bytes == n; };
   if (name == "emb_q16") {
-    if (!need((size_t)c.V * c.D * 8)) FAIL(EXB_EINVAL, "emb_q16: wrong size");
+    if (!need((size_t)m->cg.V * c.D * 8)) FAIL(EXB_EINVAL, "emb_q16: wrong size");
     if (!m->emb_q16) CK(cudaMalloc(&m->emb_q16, bytes));
     CK(cudaMemcpyAsync(m->emb_q16, host, bytes, cudaMemcpyHostToDevice, m->st));
   } else if (name == "emb") {
-    if (!need((size_t)c.V * c.D)) FAIL(EXB_EINVAL, "emb: wrong size");
+    if (!need((size_t)m->cg.V * c.D)) FAIL(EXB_EINVAL, "emb: wrong size");
     CK(cudaMemcpyAsync(m->emb, host, bytes, cudaMemcpyHostToDevice, m->st));
   } else if (name == "gf") {
     if (!need((size_t)c.D * 8)) FAIL(EXB_EINVAL, "gf: wrong size");
@@ -806,10 +1011,19 @@ static uint64_t layer_stream(int li, int off) { return (uint64_t)li * 64 + off; 
 int exb_model_generate(exb_model* m, uint64_t seed) {
   if (!m) FAIL(EXB_EINVAL, "null model");
   const exb_config& c = m->c;
-  size_t maxn = (size_t)c.V * c.D;
-  for (auto& l : m->lins) maxn = std::max(maxn, (size_t)l.N * l.K);
+  size_t maxn = (size_t)m->cg.V * c.D;
+  for (auto& l : m->lins) maxn = std::max(maxn, (size_t)l.Ng * l.Kg);
   void* tmp = nullptr;
+  void* win = nullptr;                       // tensor parallel: this rank's window of a global tensor
   CK(cudaMallocAsync(&tmp, maxn * 8, m->st));
+  if (m->tp > 1) CK(cudaMallocAsync(&win, maxn * 8, m->st));
+  // global (rows x cols) device tensor of esz-byte elements -> its [r0, +nr) x [c0, +nc) window
+  auto window = [&](const void* src, size_t cols, size_t esz, size_t r0, size_t nr, size_t c0, size_t nc) -> const void* {
+    if (m->tp == 1) return src;
+    cudaMemcpy2DAsync(win, nc * esz, (const char*)src + (r0 * cols + c0) * esz, cols * esz, nc * esz, nr,
+                      cudaMemcpyDeviceToDevice, m->st);
+    return win;
+  };
   static const std::map<std::string, int> LS = {{"q", 2}, {"k", 5}, {"v", 8}, {"o", 11}, {"gate", 14}, {"up", 17},
                                                  {"down", 20}, {"router", 23}, {"sgate", 26}, {"sg", 29}, {"su", 32},
                                                  {"sd", 35}};
@@ -828,23 +1042,27 @@ int exb_model_generate(exb_model* m, uint64_t seed) {
       s0 = layer_stream(li, LS.at(nm));
     }
     LinW& F = *L.fused;
-    CK(gen_tensor(GEN_WEIGHT, seed, s0, (int64_t)L.N * L.K, L.K, tmp, m->st));
-    CK(cudaMemcpy2DAsync((char*)F.w + (size_t)L.row0 * L.K, (size_t)L.K * L.row_step, tmp, L.K, L.K, L.N,
+    CK(gen_tensor(GEN_WEIGHT, seed, s0, (int64_t)L.Ng * L.Kg, L.Kg, tmp, m->st));
+    const void* src = window(tmp, L.Kg, 1, L.r_lo, L.N, L.c_lo, L.K);
+    CK(cudaMemcpy2DAsync((char*)F.w + (size_t)L.row0 * L.K, (size_t)L.K * L.row_step, src, L.K, L.K, L.N,
                          cudaMemcpyDeviceToDevice, m->st));
     if (m->group) {
-      const int G = L.K / 128;
-      CK(gen_tensor(GEN_SCALE32, seed, s0 + 1, (int64_t)L.N * G, L.K, tmp, m->st));
-      int rc = put_rows(m, (void*)F.Mg, (size_t)F.ldm * 4, L.row0, L.row_step, tmp, L.N, (size_t)G * 4,
+      const int G = L.K / 128, Gg = L.Kg / 128;
+      CK(gen_tensor(GEN_SCALE32, seed, s0 + 1, (int64_t)L.Ng * Gg, L.Kg, tmp, m->st));
+      src = window(tmp, Gg, 4, L.r_lo, L.N, L.c_lo / 128, G);
+      int rc = put_rows(m, (void*)F.Mg, (size_t)F.ldm * 4, L.row0, L.row_step, src, L.N, (size_t)G * 4,
                         cudaMemcpyDeviceToDevice);
       if (rc) return rc;
     } else {
-      CK(gen_tensor(GEN_SCALE64, seed, s0 + 1, L.N, L.K, tmp, m->st));
-      CK(cudaMemcpy2DAsync((char*)F.Mc + (size_t)L.row0 * 8, (size_t)8 * L.row_step, tmp, 8, 8, L.N,
+      CK(gen_tensor(GEN_SCALE64, seed, s0 + 1, L.Ng, L.Kg, tmp, m->st));
+      src = window(tmp, 1, 8, L.r_lo, L.N, 0, 1);
+      CK(cudaMemcpy2DAsync((char*)F.Mc + (size_t)L.row0 * 8, (size_t)8 * L.row_step, src, 8, 8, L.N,
                            cudaMemcpyDeviceToDevice, m->st));
     }
     if (F.b) {
-      CK(gen_tensor(GEN_BIAS, seed, s0 + 2, L.N, 0, tmp, m->st));
-      CK(cudaMemcpy2DAsync((char*)F.b + (size_t)L.row0 * 8, (size_t)8 * L.row_step, tmp, 8, 8, L.N,
+      CK(gen_tensor(GEN_BIAS, seed, s0 + 2, L.Ng, 0, tmp, m->st));
+      src = window(tmp, 1, 8, L.r_lo, L.N, 0, 1);
+      CK(cudaMemcpy2DAsync((char*)F.b + (size_t)L.row0 * 8, (size_t)8 * L.row_step, src, 8, 8, L.N,
                            cudaMemcpyDeviceToDevice, m->st));
     }
   }
@@ -853,10 +1071,18 @@ int exb_model_generate(exb_model* m, uint64_t seed) {
     CK(gen_tensor(GEN_GAIN, seed, layer_stream(i, 1), c.D, 0, m->L[i].g2, m->st));
   }
   const uint64_t S_EMB = 1ull << 20;
-  CK(gen_tensor(GEN_WEIGHT, seed, S_EMB, (int64_t)c.V * c.D, c.D, m->emb, m->st));
+  const int Vg = m->cg.V, Vl = m->v1 - m->v0;
+  CK(gen_tensor(GEN_WEIGHT, seed, S_EMB, (int64_t)Vg * c.D, c.D, m->emb, m->st));
   CK(gen_tensor(GEN_GAIN, seed, S_EMB + 1, c.D, 0, m->gf, m->st));
-  if (!c.tie) CK(gen_tensor(GEN_WEIGHT, seed, S_EMB + 2, (int64_t)c.V * c.D, c.D, (void*)m->head.w, m->st));
-  CK(gen_tensor(GEN_SCALE64, seed, S_EMB + 3, c.V, c.D, (void*)m->head.Mc, m->st));
+  if (!c.tie) {
+    CK(gen_tensor(GEN_WEIGHT, seed, S_EMB + 2, (int64_t)Vg * c.D, c.D, tmp, m->st));
+    CK(cudaMemcpyAsync((void*)m->head.w, (const char*)tmp + (size_t)m->v0 * c.D, (size_t)Vl * c.D,
+                       cudaMemcpyDeviceToDevice, m->st));
+  }
+  CK(gen_tensor(GEN_SCALE64, seed, S_EMB + 3, Vg, c.D, tmp, m->st));
+  CK(cudaMemcpyAsync((void*)m->head.Mc, (const char*)tmp + (size_t)m->v0 * 8, (size_t)Vl * 8, cudaMemcpyDeviceToDevice,
+                     m->st));
+  if (win) CK(cudaFreeAsync(win, m->st));
   CK(cudaFreeAsync(tmp, m->st));
   CK(cudaStreamSynchronize(m->st));
   return EXB_OK;
@@ -1024,12 +1250,35 @@ static int prefill_chunk(exb_model* m, int R, int64_t* logits_host, int32_t* nex
 
 static bool prefill_tc_ok(exb_model* m) {
   const exb_config& c = m->c;
+  if (m->tp > 1) return false;                 // tensor-parallel ranks run 4-row steps with in-graph collectives
   if (c.n_experts)
     return m->tc_on && !m->trace_on && !m->fr_on && gemm_tc_supported(m->L[0].qkv, EPI_RAW) &&
            gemm_tc_supported(m->L[0].o, EPI_RAW) && gemm_tc_supported(m->head, EPI_RAW) && c.D % 16 == 0;
   return m->tc_on && m->group && !m->trace_on && !m->fr_on && c.H * c.hd % 128 == 0 && gemm_tc_supported(m->L[0].qkv, EPI_STORE) &&
          gemm_tc_supported(m->L[0].gu, EPI_SWIGLU) && gemm_tc_supported(m->L[0].down, EPI_RESID) &&
          gemm_tc_supported(m->L[0].o, EPI_RESID) && gemm_tc_supported(m->head, EPI_RAW) && m->head.nodrop;
+}
+
+// logits of the R rows of the last step into host rows of the global vocabulary (tensor parallel:
+// every rank's slice gathered with NCCL, then laid out in vocabulary order)
+static int copy_logits(exb_model* m, int R, int64_t* host) {
+  const int Vg = m->cg.V;
+  if (m->tp == 1) {
+    CK(cudaMemcpyAsync(host, m->logits, sizeof(int64_t) * R * Vg, cudaMemcpyDeviceToHost, m->st));
+    return EXB_OK;
+  }
+  const size_t blk = (size_t)R * m->vmax;
+  if (ncclAllGather(m->logits, m->tp_gather, blk, ncclInt64, m->comm, m->st) != ncclSuccess)
+    FAIL(EXB_ECUDA, "ncclAllGather (logits) failed");
+  std::vector<int64_t> g(blk * m->tp);
+  CK(cudaMemcpyAsync(g.data(), m->tp_gather, sizeof(int64_t) * g.size(), cudaMemcpyDeviceToHost, m->st));
+  CK(cudaStreamSynchronize(m->st));
+  for (int k = 0; k < m->tp; ++k) {
+    const int v0 = k * m->vmax, len = std::min(m->vmax, Vg - v0);
+    for (int r = 0; r < R && len > 0; ++r)
+      memcpy(host + (size_t)r * Vg + v0, g.data() + (size_t)k * blk + (size_t)r * m->vmax, sizeof(int64_t) * len);
+  }
+  return EXB_OK;
 }
 
 int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, int64_t* logits, int32_t* next) {
@@ -1040,7 +1289,7 @@ int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, in
   std::vector<int> len = m->seq_len;
   for (int i = 0; i < n; ++i) {
     if (seqs[i] < 0 || seqs[i] >= c.max_batch) FAIL(EXB_EINVAL, "bad sequence slot");
-    if (ids[i] < 0 || ids[i] >= c.V) FAIL(EXB_EINVAL, "token id out of range");
+    if (ids[i] < 0 || ids[i] >= m->cg.V) FAIL(EXB_EINVAL, "token id out of range");
     pos[i] = len[seqs[i]]++;
     if (pos[i] >= c.max_seq) FAIL(EXB_EINVAL, "sequence longer than max_seq");
   }
@@ -1071,7 +1320,10 @@ int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, in
     int rc = run_step(m, R, m->row_ids, m->row_seq, m->row_pos, logits != nullptr, 0);
     g_hist_row0 = -1;
     if (rc) return rc;
-    if (logits) CK(cudaMemcpyAsync(logits + (size_t)r0 * c.V, m->logits, sizeof(int64_t) * R * c.V, cudaMemcpyDeviceToHost, m->st));
+    if (logits) {
+      rc = copy_logits(m, R, logits + (size_t)r0 * m->cg.V);
+      if (rc) return rc;
+    }
     if (next) CK(cudaMemcpyAsync(next + r0, m->next_tok, sizeof(int32_t) * R, cudaMemcpyDeviceToHost, m->st));
     if (m->trace_on)
       CK(cudaMemcpyAsync(m->trace_host.data() + (size_t)r0 * m->trace_row, m->trace, sizeof(int64_t) * R * m->trace_row,
@@ -1108,7 +1360,7 @@ static int generate_wide(exb_model* m, int B, const int32_t* ids_dev_or_null, co
   if (ids_dev_or_null) CK(cudaMemcpy(cur.data(), ids_dev_or_null, 4 * (size_t)B, cudaMemcpyDeviceToHost));
   else memcpy(cur.data(), ids_host, 4 * (size_t)B);
   for (int b = 0; b < B; ++b)
-    if (cur[b] < 0 || cur[b] >= c.V) FAIL(EXB_EINVAL, "token id out of range");
+    if (cur[b] < 0 || cur[b] >= m->cg.V) FAIL(EXB_EINVAL, "token id out of range");
   CK(cudaMemsetAsync(m->err, 0, sizeof(int), m->st));
   for (int s = 0; s < steps; ++s) {
     for (int b = 0; b < B; ++b) {
@@ -1152,7 +1404,10 @@ static int generate_common(exb_model* m, int B, const int32_t* ids_dev_or_null, 
     rc = run_step(m, B, m->gen_ids, m->gen_seq, m->gen_pos, logits_host != nullptr, B);
     if (rc) return rc;
     if (logits_host)
-      CK(cudaMemcpyAsync(logits_host + (size_t)s * B * c.V, m->logits, sizeof(int64_t) * B * c.V, cudaMemcpyDeviceToHost, m->st));
+    {
+      rc = copy_logits(m, B, logits_host + (size_t)s * B * m->cg.V);
+      if (rc) return rc;
+    }
     if (m->trace_on)
       CK(cudaMemcpyAsync(m->trace_host.data() + (size_t)s * B * m->trace_row, m->trace, sizeof(int64_t) * B * m->trace_row,
                          cudaMemcpyDeviceToHost, m->st));
@@ -1178,6 +1433,7 @@ int exb_generate_device(exb_model* m, int B, const int32_t* ids_dev, int steps, 
 int exb_trace_enable(exb_model* m, int on) {
   if (!m) FAIL(EXB_EINVAL, "null model");
   if (on && m->c.n_experts) FAIL(EXB_EINVAL, "trace capture covers the dense models (the reference traces them only)");
+  if (on && m->tp > 1) FAIL(EXB_EINVAL, "trace capture runs on single-GPU models");
   m->trace_on = on != 0;
   return EXB_OK;
 }
@@ -1233,6 +1489,7 @@ int exb_freivalds_read_keys(exb_model* m, int32_t* d_host, int64_t n) {
 
 int exb_freivalds_enable(exb_model* m, int on) {
   if (!m) FAIL(EXB_EINVAL, "null model");
+  if (on && m->tp > 1) FAIL(EXB_EINVAL, "the Freivalds self-check runs on single-GPU models");
   if (on && (m->lins.empty() || !m->lins[0].fr_r)) FAIL(EXB_EINVAL, "set keys first");
   m->fr_on = on != 0;
   if (on) { CK(cudaMemset(m->fr_fail, 0, sizeof(int))); m->fr_checks = 0; }

@@ -112,6 +112,7 @@ struct GemvArgs {
   unsigned long long* head_part = nullptr;      // (grid, R, 2) partial (value, index)
   unsigned int* head_ticket = nullptr;          // last-CTA counter
   int32_t* next_tok = nullptr;                  // (R)
+  int64_t* head_val = nullptr;                  // (R) best value next to next_tok (tensor parallel)
   int* err = nullptr;
   int grid = 0;
 };
@@ -120,6 +121,13 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl);
 int gemv_grid(int N, bool swiglu);
 cudaError_t launch_gemv_op(const int16_t* x16, const int8_t* wT, const int64_t* Mg, int K, int N, int64_t* out,
                            cudaStream_t st);
+
+// tensor parallel helpers (rowops.cu)
+// x[r, n] += shr(tot[r, n], 28 - xs[r]) (+ b[n]): the residual update after an all-reduced partial sum
+cudaError_t launch_tp_resid(const int64_t* tot, int R, int N, const int32_t* xs, const int64_t* b, int64_t* x, int ldx,
+                            cudaStream_t st);
+// next[r] = v0 + idx[r] when val[r] equals the all-reduced maximum gmax[r], else INT32_MAX (min-reduced next)
+cudaError_t launch_tp_pick(const int64_t* val, const int64_t* gmax, int32_t* idx, int v0, int R, cudaStream_t st);
 
 // per-row kernels
 cudaError_t launch_embed(const int8_t* emb, int emb_shift, const int32_t* ids, int R, int D, int64_t* x,

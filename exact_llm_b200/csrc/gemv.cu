@@ -260,6 +260,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
         if (v > bv || (v == bv && n < bn)) { bv = v; bn = n; }
       }
       a.next_tok[r] = bn;
+      if (a.head_val) a.head_val[r] = bv;                  // tensor parallel: the shard's best value
     }
   }
   // ---- last CTA: build the next GEMV's int16 input rows from this kernel's complete output;

@@ -255,6 +255,34 @@ cudaError_t launch_head_rows(const int64_t* acc, int ld, int R, const LinW& L, c
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- tensor parallel helpers
+__global__ void k_tp_resid(const int64_t* __restrict__ tot, int N, const int32_t* __restrict__ xs,
+                           const int64_t* __restrict__ b, int64_t* __restrict__ x, int ldx) {
+  const int r = blockIdx.y;
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  int64_t y = shr64(tot[(size_t)r * N + n], 28 - xs[r]);
+  if (b) y = (int64_t)((uint64_t)y + (uint64_t)b[n]);
+  int64_t* o = x + (size_t)r * ldx + n;
+  *o = (int64_t)((uint64_t)*o + (uint64_t)y);
+}
+
+cudaError_t launch_tp_resid(const int64_t* tot, int R, int N, const int32_t* xs, const int64_t* b, int64_t* x, int ldx,
+                            cudaStream_t st) {
+  k_tp_resid<<<dim3((N + 255) / 256, R), 256, 0, st>>>(tot, N, xs, b, x, ldx);
+  return cudaGetLastError();
+}
+
+__global__ void k_tp_pick(const int64_t* val, const int64_t* gmax, int32_t* idx, int v0, int R) {
+  const int r = threadIdx.x;
+  if (r < R) idx[r] = val[r] == gmax[r] ? v0 + idx[r] : 0x7fffffff;
+}
+
+cudaError_t launch_tp_pick(const int64_t* val, const int64_t* gmax, int32_t* idx, int v0, int R, cudaStream_t st) {
+  k_tp_pick<<<1, 32, 0, st>>>(val, gmax, idx, v0, R);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------- Freivalds comparison
 // acc layout: (nchecks, 4) = lhs_p1, lhs_p2, rhs_p1, rhs_p2 (each an unreduced sum of residues)
 __global__ void k_fr_check(const unsigned long long* __restrict__ acc, int n, int* fail, int* err) {

@@ -40,7 +40,10 @@ class ExactModel:
     ``lin`` ("group" for group-128 GQLin layers, "channel" for per-channel QLin layers).
     """
 
-    def __init__(self, c, max_batch=1, max_seq=None, rope_len=None, emb_shift=9, tie=None):
+    def __init__(self, c, max_batch=1, max_seq=None, rope_len=None, emb_shift=9, tie=None, tp=None):
+        """``tp`` = (rank, size, unique_id) builds this rank's tensor-parallel slice (one process per
+        GPU; every rank constructs its model at the same time; ``unique_id`` = the 128 bytes of
+        ``ExactModel.tp_unique_id()`` made on rank 0 and shared by the caller)."""
         self.c = dict(c)
         self.max_batch = int(max_batch)
         self.max_seq = int(max_seq or c.get("T", 4096))
@@ -51,7 +54,12 @@ class ExactModel:
                      topk=int(c.get("TOPK", 0)), moe_I=int(c.get("MI", 0)), shared_I=int(c.get("SI", 0)),
                      max_batch=self.max_batch, max_seq=self.max_seq, rope_len=self.rope_len, emb_shift=emb_shift)
         h = ctypes.c_void_p()
-        check(lib.exb_model_create(ctypes.byref(cfg), ctypes.byref(h)))
+        self.tp = tp
+        if tp is not None and int(tp[1]) > 1:
+            rank, size, uid = int(tp[0]), int(tp[1]), bytes(tp[2])
+            check(lib.exb_model_create_tp(ctypes.byref(cfg), rank, size, uid, ctypes.byref(h)))
+        else:
+            check(lib.exb_model_create(ctypes.byref(cfg), ctypes.byref(h)))
         self.h = h
         cos, sin = tables.rope_tables(self.rope_len, c["hd"], c["theta"])
         half = c["hd"] // 2
@@ -59,6 +67,24 @@ class ExactModel:
                                                        cos[:, :half], sin[:, :half])]
         check(lib.exb_model_set_tables(self.h, *[ptr(t, ctypes.c_int64) for t in self._tab]))
         self._finalized = False
+
+    @staticmethod
+    def tp_unique_id():
+        """NCCL unique id (128 bytes) for a tensor-parallel group; make it on rank 0."""
+        buf = ctypes.create_string_buffer(128)
+        check(lib.exb_tp_unique_id(buf))
+        return buf.raw
+
+    @staticmethod
+    def tp_plan(c, rank, size):
+        """This rank's slice: dict(qh0, qh1, kh0, kh1, ig0, ig1, v0, v1, vmax) (host computation)."""
+        cfg = Config(D=c["D"], H=c["H"], KV=c["KV"], hd=c["hd"], I=c["I"], V=c["V"], NL=c["NL"],
+                     tie=int(c.get("tie", False)), lin_kind=0 if c.get("lin", "group") == "group" else 1,
+                     n_experts=int(c.get("NE", 0)), topk=int(c.get("TOPK", 0)), moe_I=int(c.get("MI", 0)),
+                     shared_I=int(c.get("SI", 0)), max_batch=1, max_seq=1, rope_len=1, emb_shift=9)
+        out = (ctypes.c_int32 * 9)()
+        check(lib.exb_tp_plan(ctypes.byref(cfg), int(rank), int(size), out))
+        return dict(zip(("qh0", "qh1", "kh0", "kh1", "ig0", "ig1", "v0", "v1", "vmax"), list(out)))
 
     # ------------------------------------------------------------------ construction
     @classmethod

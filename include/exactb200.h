@@ -142,6 +142,22 @@ int exb_freivalds_read_keys(exb_model* m, int32_t* d_host, int64_t n);   /* 2 x 
 int exb_freivalds_enable(exb_model* m, int on);
 int exb_freivalds_status(exb_model* m, int64_t* checks, int64_t* failures);
 
+/* Tensor parallelism over NVLink (one process per GPU, NCCL).  The partition follows the
+ * reference layer: q/k/v column-split by heads (when the rank count is a multiple of KV, each KV
+ * group's query heads split inside a pair of ranks, e.g. 7B TP8 = 4/3 heads), o row-split by the
+ * same heads, gate/up column-split and down row-split by 128-groups of I, the head split over the
+ * vocabulary.  Per layer four in-graph all-reduces keep the result bit-identical to one GPU:
+ * MAX of the attention-output row max (o's qrow), SUM of o's int64 partial sums, MAX of max|h|
+ * (down's qrow), SUM of down's partial sums; the greedy token is MAX of the slice maxima, then
+ * MIN of the indices holding it.  Integer sums are order-independent, so any NCCL algorithm is
+ * exact.  Dense group-128 models; tensors are set and generated in GLOBAL shapes.
+ *   exb_tp_plan      this rank's slice: {qh0, qh1, kh0, kh1, ig0, ig1, v0, v1, vmax} (no GPU needed)
+ *   exb_tp_unique_id the NCCL unique id rank 0 creates and every rank passes to create_tp
+ *   exb_model_create_tp  collective: every rank calls it at the same time */
+int exb_tp_plan(const exb_config* cfg, int rank, int size, int32_t* out9);
+int exb_tp_unique_id(uint8_t* out128);
+int exb_model_create_tp(const exb_config* cfg, int rank, int size, const uint8_t* unique_id, exb_model** out);
+
 /* Engine options (no counterpart in the reference; they change speed, never results):
  *   "step"    1: decode steps of <= 2 rows without trace/Freivalds capture run as one persistent
  *             kernel (grid barriers between phases); 0 (default): one kernel per operation
