@@ -243,7 +243,16 @@ def run_ours(a, rank, world, local_rank):
     c = configs.arch(a.model, **({"NL": a.layers} if a.layers else {}))
     B, K, W = a.batch, a.steps, a.warmup
     max_seq = PROMPT + W + 2 * K + 16
-    m = ExactModel.synthetic(c, 1234, max_batch=B, max_seq=max_seq)
+    tp = a.tp and world > 1
+    if tp:
+        # one model split over the ranks (tensor parallel): NCCL id from rank 0
+        uid = [ExactModel.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        m = ExactModel(c, max_batch=B, max_seq=max_seq, tp=(rank, world, uid[0]))
+        check(lib.exb_model_generate(m.h, 1234))
+        m.finalize()
+    else:
+        m = ExactModel.synthetic(c, 1234, max_batch=B, max_seq=max_seq)
     stream = torch.cuda.ExternalStream(m.stream)
     rng = np.random.default_rng(100 + rank)
     prompts = rng.integers(0, c["V"], (B, PROMPT)).astype(np.int32)
@@ -312,10 +321,11 @@ def run_ours(a, rank, world, local_rank):
     step_ms = ms / K
     step_gbs = sb / (step_ms * 1e-3) / 1e9
     if rank != 0:
+        m.close()                      # step graphs (NCCL inside under --tp) go before the process group
         if dist:
             dist.destroy_process_group()
         return
-    value = world * B * K / (ms * 1e-3)
+    value = (1 if tp else world) * B * K / (ms * 1e-3)
     # prefill: the whole forward (every op) and the tcgen05 linear alone at the 7B gate|up shape
     prefill = {"tokens": PROMPT * B, "seconds": prefill_s, "tok_s": PROMPT * B / prefill_s,
                "effective_tops": lin_flops_fn(c) * PROMPT * B / prefill_s / 1e12,
@@ -330,11 +340,12 @@ def run_ours(a, rank, world, local_rank):
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": "int8 x int16 -> int64", "data": "synthetic",
         "config": {"workload": f"{a.model}-arch greedy decode, batch {B}, after a {PROMPT}-token uniform prompt",
                    "batch": B, "prompt": PROMPT, "decode_steps": K, "layers": c["NL"],
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"tensor parallel x{world} (NCCL, in-graph all-reduces)" if tp else
+                                   f"replicas x{world}" if world > 1 else "single GPU"),
                    "l2": "no flush: 7.3 GB of weights stream from HBM every step (L2 126 MB)"},
         "decode_hbm": {"bytes_per_step": sb, "achieved_gbs": step_gbs, "peak_gbs": hbm, "frac": step_gbs / hbm,
                        "peak_source": src},
@@ -346,7 +357,7 @@ def run_ours(a, rank, world, local_rank):
                      "avg_launch_ms": avg.value, "algorithmic_bytes": nbytes.value,
                      "peak_source": src},
         "prefill": prefill,
-        "e2e": {"value": world * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * 3 * 4,
+        "e2e": {"value": (1 if tp else world) * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * 3 * 4,
                 "d2h_bytes_per_step": 4 * B,
                 "path": "exb_forward(host ids) -> host next-token, one call per step"},
         # per step: B <= 4 one CUDA graph (embed, 10 kernels per layer, final norm, head, token feedback);
@@ -359,6 +370,7 @@ def run_ours(a, rank, world, local_rank):
         v, s = cpu_decode_sample(c, PROMPT + 1)
         line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cpu_cores(), "kind": "port", "sample": s}
     print(json.dumps(line), flush=True)
+    m.close()
     if dist:
         dist.destroy_process_group()
 
@@ -373,6 +385,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-gemm", action="store_true", help="skip the tensor-core GEMM / int8 peak measurement")
+    ap.add_argument("--tp", action="store_true", help="with --gpus N under torchrun: one model split over the N GPUs")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens before decode (profiling uses a short one)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures only)")
     a = ap.parse_args()

@@ -11,7 +11,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include"), "-I", SRC]
-LIBS = ["-lnccl"]                     # tensor-parallel collectives (NCCL over NVLink)
+LIBS = ["-ldl"]                       # NCCL (tensor parallelism) is opened at run time
 
 
 def sources():

@@ -16,6 +16,7 @@
 #include <string>
 #include <vector>
 
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include "exactb200.h"
@@ -336,10 +337,39 @@ static void plan_runtime(exb_model* m) {
 // step and can be captured once into a CUDA graph.
 static std::vector<cudaEvent_t>* g_prof = nullptr;   // profiling: an event after every launch
 
+// NCCL is resolved at run time, on the first tensor-parallel call, so that a process which loads
+// this library before torch still gets torch's own NCCL: the copy already in the process is used
+// when there is one (torch imports it), else the system libnccl.so.2.
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+};
+static const NcclApi* nccl() {
+  static NcclApi api;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h) {
+      api.get_unique_id = (decltype(api.get_unique_id))dlsym(h, "ncclGetUniqueId");
+      api.comm_init_rank = (decltype(api.comm_init_rank))dlsym(h, "ncclCommInitRank");
+      api.comm_destroy = (decltype(api.comm_destroy))dlsym(h, "ncclCommDestroy");
+      api.all_reduce = (decltype(api.all_reduce))dlsym(h, "ncclAllReduce");
+      api.all_gather = (decltype(api.all_gather))dlsym(h, "ncclAllGather");
+    }
+  }
+  return (api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_reduce && api.all_gather) ? &api
+                                                                                                          : nullptr;
+}
+
 // NCCL all-reduce on the model stream (captured into the step graph like any kernel)
 static cudaError_t tp_allreduce(exb_model* m, const void* src, void* dst, size_t n, ncclDataType_t t, ncclRedOp_t op,
                                 cudaStream_t st) {
-  return ncclAllReduce(src, dst, n, t, op, m->comm, st) == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+  return nccl()->all_reduce(src, dst, n, t, op, m->comm, st) == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
 }
 
 // MoE block arguments for layer i over R rows (qrow(m) rows xq / xs); selections recorded at row
@@ -757,8 +787,9 @@ int exb_tp_plan(const exb_config* cfg, int rank, int size, int32_t* out9) {
 
 int exb_tp_unique_id(uint8_t* out128) {
   if (!out128) FAIL(EXB_EINVAL, "null argument");
+  if (!nccl()) FAIL(EXB_ECUDA, "libnccl.so.2 not found (tensor parallelism needs NCCL)");
   ncclUniqueId id;
-  if (ncclGetUniqueId(&id) != ncclSuccess) FAIL(EXB_ECUDA, "ncclGetUniqueId failed");
+  if (nccl()->get_unique_id(&id) != ncclSuccess) FAIL(EXB_ECUDA, "ncclGetUniqueId failed");
   static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id is 128 bytes");
   memcpy(out128, &id, 128);
   return EXB_OK;
@@ -827,7 +858,7 @@ static int create_impl(const exb_config* cfg, int rank, int size, const uint8_t*
     ncclUniqueId id;
     memcpy(&id, uid, sizeof id);
     // collective: every rank of the group calls this concurrently
-    if (ncclCommInitRank(&m->comm, size, id, rank) != ncclSuccess) {
+    if (!nccl() || nccl()->comm_init_rank(&m->comm, size, id, rank) != ncclSuccess) {
       exb_model_destroy(m);
       FAIL(EXB_ECUDA, "ncclCommInitRank failed");
     }
@@ -844,7 +875,7 @@ void exb_model_destroy(exb_model* m) {
   cudaFree(m->rarena);
   cudaFree(m->gen_tokens);
   cudaFree(m->emb_q16);
-  if (m->comm) ncclCommDestroy(m->comm);
+  if (m->comm && nccl()) nccl()->comm_destroy(m->comm);
   cudaFree(m->p_arena);
   if (m->p_hrows) cudaFreeHost(m->p_hrows);
   if (m->h_ids) cudaFreeHost(m->h_ids);
@@ -1268,7 +1299,7 @@ static int copy_logits(exb_model* m, int R, int64_t* host) {
     return EXB_OK;
   }
   const size_t blk = (size_t)R * m->vmax;
-  if (ncclAllGather(m->logits, m->tp_gather, blk, ncclInt64, m->comm, m->st) != ncclSuccess)
+  if (nccl()->all_gather(m->logits, m->tp_gather, blk, ncclInt64, m->comm, m->st) != ncclSuccess)
     FAIL(EXB_ECUDA, "ncclAllGather (logits) failed");
   std::vector<int64_t> g(blk * m->tp);
   CK(cudaMemcpyAsync(g.data(), m->tp_gather, sizeof(int64_t) * g.size(), cudaMemcpyDeviceToHost, m->st));

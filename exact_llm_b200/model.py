@@ -56,6 +56,7 @@ class ExactModel:
         h = ctypes.c_void_p()
         self.tp = tp
         if tp is not None and int(tp[1]) > 1:
+            import torch  # noqa: F401  (torch's NCCL, see tp_unique_id)
             rank, size, uid = int(tp[0]), int(tp[1]), bytes(tp[2])
             check(lib.exb_model_create_tp(ctypes.byref(cfg), rank, size, uid, ctypes.byref(h)))
         else:
@@ -71,6 +72,7 @@ class ExactModel:
     @staticmethod
     def tp_unique_id():
         """NCCL unique id (128 bytes) for a tensor-parallel group; make it on rank 0."""
+        import torch  # noqa: F401  (loads torch's NCCL first; the library then uses that copy)
         buf = ctypes.create_string_buffer(128)
         check(lib.exb_tp_unique_id(buf))
         return buf.raw
