@@ -104,6 +104,7 @@ struct exb_model {
   unsigned int* ticket = nullptr;                            // last-CTA election counter
   unsigned long long* head_part = nullptr; unsigned int* head_ticket = nullptr;
   int head_grid = 0;
+  int sms = 148;
   int64_t* trace = nullptr; int64_t trace_row = 0;
   unsigned long long* fr_acc = nullptr;
   int* fr_fail = nullptr; int* err = nullptr;
@@ -142,6 +143,11 @@ struct exb_model {
   // persistent decode-step kernel (step.cu): per-layer descriptors and accumulators
   bool step_on = false;
   bool tc_on = true;                    // multi-row chunks on the tensor-core GEMM
+  bool fuse_in = false;                 // GEMVs build their int16 input rows themselves (norm / qrow prologue)
+  bool tc_decode = false;               // decode-step linears on the tcgen05 GEMM (8-row tiles, split-K)
+  uint8_t* dq = nullptr;                // digit planes of the decode rows (2 x TC_DECODE_ROWS x KMAX)
+  int64_t* tc_tot = nullptr;            // split-K partial sums (TC_DECODE_ROWS x NMAX)
+  unsigned int* tc_tickets = nullptr;   // split-K last-CTA counters (NMAX / 128)
   int pf_bytes = 64 * 1024;
   StepLayer* step_layers = nullptr;
   int64_t* s_att = nullptr; long long* s_gmax = nullptr; unsigned long long* s_gsum = nullptr;
@@ -322,6 +328,9 @@ static void plan_runtime(exb_model* m) {
     m->tp_hmax = ralloc<int64_t>(m, RMAX);
     m->tp_gather = ralloc<int64_t>(m, (size_t)RMAX * m->tp * m->vmax);
   }
+  m->dq = ralloc<uint8_t>(m, (size_t)2 * TC_DECODE_ROWS * m->KMAX);
+  m->tc_tot = ralloc<int64_t>(m, (size_t)TC_DECODE_ROWS * m->NMAX);
+  m->tc_tickets = ralloc<unsigned int>(m, m->NMAX / 128 + 1);
   m->step_layers = ralloc<StepLayer>(m, c.NL);
   m->s_att = ralloc<int64_t>(m, (size_t)c.NL * STEP_ROWS * c.H * c.hd);
   m->s_gmax = ralloc<long long>(m, (size_t)c.NL * STEP_ROWS * c.H);
@@ -428,6 +437,9 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
   const exb_config& c = m->c;
   const bool pdl = m->pdl && !g_prof;
   const bool tp = m->tp > 1;
+  const bool tcd = m->tc_decode && m->group && !m->trace_on && !m->fr_on && !tp && !c.n_experts && R <= TC_DECODE_ROWS &&
+                   gemm_tc_supported(m->L[0].qkv, EPI_STORE) && gemm_tc_supported(m->L[0].o, EPI_RESID) &&
+                   gemm_tc_supported(m->L[0].gu, EPI_SWIGLU) && gemm_tc_supported(m->L[0].down, EPI_RESID);
   cudaError_t e;
 #define RUN(x)                                                    \
   do {                                                            \
@@ -496,9 +508,53 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       g.L = L; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
       g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX;
     };
-    RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    if (tcd) {
+      // tensor-core decode: the row kernels also write the int8 digit planes the GEMM reads; the
+      // narrow matrices split their 128-groups over more CTAs (int64 partial sums, last CTA finishes)
+      auto dec = [&](const LinW& L) {
+        TcDecode d;
+        const int tiles = L.N / 128, G = L.K / 128;
+        d.ksplit = std::max(1, std::min(G, (2 * m->sms + tiles - 1) / tiles));
+        d.tot_buf = m->tc_tot; d.tickets = m->tc_tickets; d.pdl = pdl;
+        return d;
+      };
+      RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, m->dq));
+      {
+        TcDecode d = dec(Ld.qkv);
+        d.zero = m->amax_o; d.nzero = RMAX;
+        RUN(launch_gemm_tc(m->dq, R, Ld.qkv, m->xs, EPI_STORE, m->qkv, m->Nqkv, nullptr, nullptr, 0, nullptr, m->err,
+                           st, &d));
+      }
+      RUN(launch_rope_cache(aa, st, pdl));
+      RUN(launch_attn_decode(aa, st, pdl));
+      RUN(launch_quant_known(m->ao, Hd, R, Hd, m->amax_o, m->xq, m->KMAX, m->xs, st, pdl, m->dq));
+      {
+        TcDecode d = dec(Ld.o);
+        d.zero = m->amax_h; d.nzero = RMAX;
+        RUN(launch_gemm_tc(m->dq, R, Ld.o, m->xs, EPI_RESID, m->x, c.D, nullptr, nullptr, 0, nullptr, m->err, st, &d));
+      }
+      RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, m->dq));
+      {
+        TcDecode d = dec(Ld.gu);
+        d.amax_out = m->amax_h;
+        RUN(launch_gemm_tc(m->dq, R, Ld.gu, m->xs, EPI_SWIGLU, m->hb, c.I, nullptr, nullptr, 0, m->silu_t, m->err, st,
+                           &d));
+      }
+      RUN(launch_quant_known(m->hb, c.I, R, c.I, m->amax_h, m->xq, m->KMAX, m->xs, st, pdl, m->dq));
+      {
+        TcDecode d = dec(Ld.down);
+        RUN(launch_gemm_tc(m->dq, R, Ld.down, m->xs, EPI_RESID, m->x, c.D, nullptr, nullptr, 0, nullptr, m->err, st,
+                           &d));
+      }
+      continue;
+    }
+    // fused inputs: each GEMV CTA computes its int16 rows in its prologue (norm or qrow with the
+    // producer's published max) while its first weight bytes stream into L2
+    const bool fz = m->fuse_in && !m->fr_on;
+    if (!fz) RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     {
       GemvArgs g; base(g, Ld.qkv);
+      if (fz) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g1; }
       g.epi = EPI_STORE; g.out = m->qkv; g.ldo = m->Nqkv; g.raw = trace_ptr(Ld.li[0]);
       g.zero = m->amax_o; g.nzero = RMAX;
       set_fr(g, {Ld.li[0], Ld.li[1], Ld.li[2]});
@@ -508,9 +564,10 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     RUN(launch_attn_decode(aa, st, pdl));
     // tensor parallel: the qrow of o's input needs the max over every rank's heads
     if (tp) RUN(tp_allreduce(m, m->amax_o, m->amax_o, R, ncclUint64, ncclMax, st));
-    RUN(launch_quant_known(m->ao, Hd, R, Hd, m->amax_o, m->xq, m->KMAX, m->xs, st, pdl && !tp));
+    if (!fz) RUN(launch_quant_known(m->ao, Hd, R, Hd, m->amax_o, m->xq, m->KMAX, m->xs, st, pdl && !tp));
     {
       GemvArgs g; base(g, Ld.o);
+      if (fz) { g.xin = XIN_QUANT; g.x64 = m->ao; g.ldx64 = Hd; g.amax_in = m->amax_o; }
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[3]);
       g.zero = m->amax_h; g.nzero = RMAX;
       if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own heads
@@ -521,22 +578,24 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       RUN(tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st));
       RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.o.b, m->x, c.D, st));
     }
-    RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    if (!fz || c.n_experts) RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     if (c.n_experts) {
       RUN(launch_moe(moe_args(m, i, R, m->xq, m->KMAX, m->xs, g_hist_row0), m->x, c.D, st));
       continue;
     }
     {
       GemvArgs g; base(g, Ld.gu);
+      if (fz) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g2; }
       g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.amax_out = m->amax_h;
       g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]);
       set_fr(g, {Ld.li[4], Ld.li[5]});
       RUN(launch_gemv(g, st, pdl));
     }
     if (tp) RUN(tp_allreduce(m, m->amax_h, m->amax_h, R, ncclUint64, ncclMax, st));
-    RUN(launch_quant_known(m->hb, c.I, R, c.I, m->amax_h, m->xq, m->KMAX, m->xs, st, pdl && !tp));
+    if (!fz) RUN(launch_quant_known(m->hb, c.I, R, c.I, m->amax_h, m->xq, m->KMAX, m->xs, st, pdl && !tp));
     {
       GemvArgs g; base(g, Ld.down);
+      if (fz) { g.xin = XIN_QUANT; g.x64 = m->hb; g.ldx64 = c.I; g.amax_in = m->amax_h; }
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[6]);
       if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own groups
       set_fr(g, {Ld.li[6]});
@@ -547,11 +606,13 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.down.b, m->x, c.D, st));
     }
   }
-  RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+  const bool fzh = m->fuse_in && !m->fr_on;
+  if (!fzh) RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
   {
     GemvArgs g;
     g.L = m->head; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
     g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX;
+    if (fzh) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = m->gf; }
     g.epi = EPI_HEAD; g.out = want_logits ? m->logits : nullptr; g.ldo = tp ? m->vmax : c.V;
     g.raw = trace_ptr(m->n_lin - 1);
     g.head_part = m->head_part; g.head_ticket = m->head_ticket; g.next_tok = m->next_tok; g.grid = m->head_grid;
@@ -833,6 +894,7 @@ static int create_impl(const exb_config* cfg, int rank, int size, const uint8_t*
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   m->head_grid = std::min(2 * sms, (c.V + 3) / 4);   // the GEMV runs two CTAs per SM
+  m->sms = sms;
   plan_weights(m);
   m->wbytes = m->woff;
   plan_lins(m);
@@ -1177,6 +1239,8 @@ int exb_model_finalize(exb_model* m) {
   }
   CK(cudaMemcpy(m->step_layers, sl.data(), sizeof(StepLayer) * c.NL, cudaMemcpyHostToDevice));
   if (const char* v = getenv("EXB_STEP")) m->step_on = atoi(v) != 0;
+  if (const char* v = getenv("EXB_FUSE")) m->fuse_in = atoi(v) != 0;
+  if (const char* v = getenv("EXB_TCD")) m->tc_decode = atoi(v) != 0;
   if (const char* v = getenv("EXB_PF_KB")) m->pf_bytes = std::max(0, atoi(v)) * 1024;
   m->finalized = true;
   return EXB_OK;
@@ -1542,6 +1606,8 @@ int exb_set_option(exb_model* m, const char* name, int64_t value) {
   const std::string n(name);
   if (n == "step") m->step_on = value != 0;
   else if (n == "tc") m->tc_on = value != 0;
+  else if (n == "fuse") m->fuse_in = value != 0;
+  else if (n == "tcd") m->tc_decode = value != 0;
   else if (n == "pf_kb") {
     if (value < 0 || value > 1024) FAIL(EXB_EINVAL, "pf_kb: 0..1024");
     m->pf_bytes = (int)value * 1024;

@@ -134,12 +134,13 @@ cudaError_t launch_embed(const int8_t* emb, int emb_shift, const int32_t* ids, i
                          cudaStream_t st, bool pdl);
 cudaError_t launch_embed64(const int64_t* emb_q16, const int32_t* ids, int R, int D, int64_t* x, cudaStream_t st,
                            bool pdl);
+// dig (optional): int8 digit planes of the rows for the tensor-core decode GEMM (TC_DECODE_ROWS-row planes)
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
-                          int32_t* xs, cudaStream_t st, bool pdl);
+                          int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig = nullptr);
 cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, int ldq, int32_t* xs,
                          cudaStream_t st, bool pdl);
 cudaError_t launch_quant_known(const int64_t* x, int ldx, int R, int K, const unsigned long long* amax, int16_t* xq,
-                               int ldq, int32_t* xs, cudaStream_t st, bool pdl);
+                               int ldq, int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig = nullptr);
 cudaError_t launch_requant_channel(const int64_t* acc, int ld, int R, const LinW& L, int64_t* out, int ldo,
                                    const int32_t* xs, int epi, cudaStream_t st, bool pdl);
 
@@ -200,9 +201,23 @@ size_t gemm_tc_digit_bytes(int T, int K);
 // int8 digit planes (lo = xq & 255, hi = xq >> 8) of T int16 rows, padded to the tile height
 cudaError_t launch_digits(const int16_t* xq, int ldx, int T, int K, void* digits, cudaStream_t st);
 bool gemm_tc_supported(const LinW& L, int epi);
+// Decode steps (T <= TC_DECODE_ROWS rows, digit planes of exactly TC_DECODE_ROWS rows): 8-row
+// activation tiles, optional split over the 128-groups (int64 partial sums in tot_buf, the last
+// CTA of each 128-row tile finishes it; tot_buf and tickets are zero between uses), SwiGLU row
+// max published to amax_out, words cleared for a later producer, programmatic dependent launch.
+constexpr int TC_DECODE_ROWS = 8;
+struct TcDecode {
+  int ksplit = 1;
+  int64_t* tot_buf = nullptr;           // (TC_DECODE_ROWS, N) int64
+  unsigned int* tickets = nullptr;      // (N / 128)
+  unsigned long long* amax_out = nullptr;
+  unsigned long long* zero = nullptr; int nzero = 0;
+  bool pdl = false;
+};
 // tot / requant epilogue of a group-128 linear over T activation rows given as digit planes
 cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32_t* xs, int epi, int64_t* out, int ldo,
-                           int64_t* raw, int64_t* raw2, int ldr, const int32_t* silu_t, int* err, cudaStream_t st);
+                           int64_t* raw, int64_t* raw2, int ldr, const int32_t* silu_t, int* err, cudaStream_t st,
+                           const TcDecode* dec = nullptr);
 
 // ---------------------------------------------------------------- persistent decode step
 // One layer's linears and norm gains, as the persistent step kernel reads them (device array).

@@ -28,15 +28,23 @@
 namespace exb {
 
 constexpr int TC_BM = 128;                              // output rows per tile (MMA M)
-constexpr int TC_BN = 64;                               // activation rows per tile (MMA N)
+constexpr int TC_PAD = 128;                             // activation rows are padded to this
 constexpr int TC_STAGES = 4;
 constexpr int TC_A_BYTES = TC_BM * 128;                 // one group of 128 weight rows
-constexpr int TC_B_BYTES = TC_BN * 128;                 // one group of 64 activation rows, one digit
-constexpr int TC_STAGE_BYTES = TC_A_BYTES + 2 * TC_B_BYTES;
-constexpr int TC_THREADS = 192;
-constexpr int TC_TMEM_COLS = 256;                       // 2 buffers x 2 digits x 64 columns
-constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024;   // + alignment slack
 constexpr uint32_t TC_WAIT_LIMIT = 1u << 24;
+
+// Tile geometry for BN activation rows per tile (MMA N = 8, 64 or 128).  Every epilogue thread owns
+// one output row (TMEM lane) and CW activation columns; BN = 128 takes 8 epilogue warps.
+template <int BN>
+struct TcGeo {
+  static constexpr int B_BYTES = BN * 128;              // one group of BN activation rows, one digit
+  static constexpr int STAGE_BYTES = TC_A_BYTES + 2 * B_BYTES;
+  static constexpr int EPI_WARPS = BN >= 64 ? 4 * (BN / 64) : 4;
+  static constexpr int CW = BN >= 64 ? 64 : BN;         // columns per epilogue thread
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int TMEM_COLS = 4 * BN < 32 ? 32 : 4 * BN;   // 2 buffers x 2 digits x BN
+  static constexpr int SMEM = TC_STAGES * STAGE_BYTES + 1024;   // + alignment slack
+};
 
 struct TcArgs {
   int N = 0, K = 0, T = 0;
@@ -50,6 +58,12 @@ struct TcArgs {
   int64_t* raw2 = nullptr;            // SwiGLU: raw sums of the up rows
   const int32_t* silu_t = nullptr;
   int* err = nullptr;
+  // decode extras
+  int ksplit = 1;                     // CTAs sharing one 128-row tile over the 128-groups
+  int64_t* tot_buf = nullptr;         // (T, N) int64 partial sums (zero between uses)
+  unsigned int* tickets = nullptr;    // (N / 128) last-CTA counters (zero between uses)
+  unsigned long long* amax_out = nullptr;   // SwiGLU: per-row max |h| (atomicMax)
+  unsigned long long* zero = nullptr; int nzero = 0;   // cleared by CTA (0, 0) for a later producer
 };
 
 // ---------------------------------------------------------------- PTX wrappers
@@ -77,16 +91,14 @@ EXB_DEV void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
       : "memory");
 }
-// 16 consecutive 32-bit TMEM columns of this thread's lane
-EXB_DEV void tmem_ld16(uint32_t taddr, int32_t (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+// 8 consecutive 32-bit TMEM columns of this thread's lane
+EXB_DEV void tmem_ld8(uint32_t taddr, int32_t* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = (int32_t)r[i];
+  for (int i = 0; i < 8; ++i) v[i] = (int32_t)r[i];
 }
 EXB_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -98,34 +110,81 @@ EXB_DEV uint64_t tc_desc(const void* tile, int kstep) {
          (2ull << 61);
 }
 // Instruction descriptor: int32 accumulate, A = signed int8 (weights), B = unsigned (low digit)
-// or signed (high digit) int8, both K-major, M = 128, N = 64.
+// or signed (high digit) int8, both K-major, M = 128, N = BN.
+template <int BN>
 __host__ __device__ constexpr uint32_t tc_idesc(bool b_signed) {
-  return (2u << 4) | (1u << 7) | ((b_signed ? 1u : 0u) << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
+  return (2u << 4) | (1u << 7) | ((b_signed ? 1u : 0u) << 10) | ((uint32_t)(BN >> 3) << 17) |
          ((uint32_t)(TC_BM >> 4) << 24);
 }
 
+// final epilogue of one (activation row t, output row n) total; SwiGLU pairs sit in adjacent lanes
+// (every lane of the warp calls this with the same t)
+EXB_DEV void tc_finish(const TcArgs& a, int t, int n, int64_t v, bool live, uint64_t& hmax) {
+  if (a.epi == EPI_SWIGLU) {
+    const int sh = live ? a.xs[t] : 0;
+    const int64_t y = shr64(v, 28 - sh);
+    const int64_t other = __shfl_xor_sync(0xffffffffu, y, 1);
+    const int64_t vother = __shfl_xor_sync(0xffffffffu, v, 1);
+    if (live && !(n & 1)) {
+      const int u = n >> 1;
+      const int64_t hv = shr64((int64_t)((uint64_t)isilu_dev(a.silu_t, y) * (uint64_t)other), 16);
+      a.out[(size_t)t * a.ldo + u] = hv;
+      const uint64_t ah = uabs64(hv);
+      hmax = ah > hmax ? ah : hmax;
+      if (a.raw) a.raw[(size_t)t * a.ldr + u] = v;
+      if (a.raw2) a.raw2[(size_t)t * a.ldr + u] = vother;
+    }
+    return;
+  }
+  if (!live) return;
+  if (a.raw) a.raw[(size_t)t * a.ldr + n] = v;
+  if (a.epi == EPI_RAW) return;
+  int64_t y = shr64(v, 28 - a.xs[t]);
+  if (a.bias) y = (int64_t)((uint64_t)y + (uint64_t)a.bias[n]);
+  int64_t* o = a.out + (size_t)t * a.ldo + n;
+  if (a.epi == EPI_RESID) *o = (int64_t)((uint64_t)__ldcg(reinterpret_cast<const long long*>(o)) + (uint64_t)y);
+  else *o = y;
+}
+
+// per-row max |h| of a SwiGLU tile column: warp maximum, one atomic per warp
+EXB_DEV void tc_publish_hmax(const TcArgs& a, int t, uint64_t v) {
+  v = warp_max_u64(v);
+  if ((threadIdx.x & 31) == 0 && v && t < a.T) atomicMax(a.amax_out + t, (unsigned long long)v);
+}
+
 // ---------------------------------------------------------------- the kernel
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <int BN>
+__global__ void __launch_bounds__(TcGeo<BN>::THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmLo,
               const __grid_constant__ CUtensorMap tmHi, const TcArgs a) {
+  using Geo = TcGeo<BN>;
+  constexpr int B_BYTES = Geo::B_BYTES;
+  constexpr int STAGE_BYTES = Geo::STAGE_BYTES;
+  constexpr int TMEM_COLS = Geo::TMEM_COLS;
+  constexpr int NEPI = 32 * Geo::EPI_WARPS;               // epilogue threads
+  constexpr int CW = Geo::CW;
   extern __shared__ unsigned char smem_raw[];
   __shared__ uint64_t full[TC_STAGES], empty[TC_STAGES], accf[2], acce[2];
   __shared__ uint32_t tmem_base_sh;
-  __shared__ int abort_sh, issued_sh, consumed_sh;
+  __shared__ int abort_sh, issued_sh, consumed_sh, last_sh;
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tm = blockIdx.x, tn = blockIdx.y;
+  const int tm = blockIdx.x;
+  const int tn = a.ksplit > 1 ? 0 : (int)blockIdx.y;      // split-K: grid.y indexes K ranges
+  const int ks = a.ksplit > 1 ? (int)blockIdx.y : 0;
   const int G = a.K >> 7;
+  const int g0 = (int)((long long)G * ks / a.ksplit), g1 = (int)((long long)G * (ks + 1) / a.ksplit);
+  const int ng = g1 - g0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 128); }
-    abort_sh = 0; issued_sh = 0; consumed_sh = 0;
+    for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], NEPI); }
+    abort_sh = 0; issued_sh = 0; consumed_sh = 0; last_sh = 0;
     mbar_fence_init();
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
-                 "r"(TC_TMEM_COLS)
+                 "r"(TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -135,119 +194,153 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t tmem = tmem_base_sh;
 
   if (warp == 0) {
-    // ---- TMA producer
+    // ---- TMA producer: the weight tiles of the first stages do not depend on the previous
+    // kernel and go out before the programmatic-dependent-launch wait; activation digits after it
     if (lane == 0) {
-      for (int g = 0; g < G; ++g) {
-        const int s = g % TC_STAGES;
-        if (g >= TC_STAGES && !tc_wait(&empty[s], ((g / TC_STAGES) - 1) & 1)) {
+      const int pre = ng < TC_STAGES ? ng : TC_STAGES;
+      for (int i = 0; i < pre; ++i) {
+        unsigned char* st = smem + (size_t)i * STAGE_BYTES;
+        mbar_expect_tx(&full[i], STAGE_BYTES);
+        tma_load_2d(st, &tmA, (g0 + i) * 128, tm * TC_BM, &full[i]);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        unsigned char* st = smem + (size_t)i * STAGE_BYTES;
+        tma_load_2d(st + TC_A_BYTES, &tmLo, (g0 + i) * 128, tn * BN, &full[i]);
+        tma_load_2d(st + TC_A_BYTES + B_BYTES, &tmHi, (g0 + i) * 128, tn * BN, &full[i]);
+      }
+      *(volatile int*)&issued_sh = pre;
+      for (int i = pre; i < ng; ++i) {
+        const int s = i % TC_STAGES;
+        if (!tc_wait(&empty[s], ((i / TC_STAGES) - 1) & 1)) {
           abort_sh = 1;
           set_err(a.err, ERR_WAIT_TIMEOUT);
           break;
         }
         if (*(volatile int*)&abort_sh) break;
-        unsigned char* st = smem + (size_t)s * TC_STAGE_BYTES;
-        mbar_expect_tx(&full[s], TC_STAGE_BYTES);
-        tma_load_2d(st, &tmA, g * 128, tm * TC_BM, &full[s]);
-        tma_load_2d(st + TC_A_BYTES, &tmLo, g * 128, tn * TC_BN, &full[s]);
-        tma_load_2d(st + TC_A_BYTES + TC_B_BYTES, &tmHi, g * 128, tn * TC_BN, &full[s]);
-        *(volatile int*)&issued_sh = g + 1;
+        unsigned char* st = smem + (size_t)s * STAGE_BYTES;
+        mbar_expect_tx(&full[s], STAGE_BYTES);
+        tma_load_2d(st, &tmA, (g0 + i) * 128, tm * TC_BM, &full[s]);
+        tma_load_2d(st + TC_A_BYTES, &tmLo, (g0 + i) * 128, tn * BN, &full[s]);
+        tma_load_2d(st + TC_A_BYTES + B_BYTES, &tmHi, (g0 + i) * 128, tn * BN, &full[s]);
+        *(volatile int*)&issued_sh = i + 1;
       }
     }
   } else if (warp == 1) {
     // ---- MMA issuer
     if (lane == 0) {
-      const uint32_t id_lo = tc_idesc(false), id_hi = tc_idesc(true);
-      for (int g = 0; g < G; ++g) {
-        const int s = g % TC_STAGES, b = g & 1;
-        if (!tc_wait(&full[s], (g / TC_STAGES) & 1) || !tc_wait(&acce[b], ((g >> 1) & 1) ^ 1)) {
+      const uint32_t id_lo = tc_idesc<BN>(false), id_hi = tc_idesc<BN>(true);
+      for (int i = 0; i < ng; ++i) {
+        const int s = i % TC_STAGES, b = i & 1;
+        if (!tc_wait(&full[s], (i / TC_STAGES) & 1) || !tc_wait(&acce[b], ((i >> 1) & 1) ^ 1)) {
           abort_sh = 1;
           set_err(a.err, ERR_WAIT_TIMEOUT);
           break;
         }
         tc_fence_after();
-        const unsigned char* st = smem + (size_t)s * TC_STAGE_BYTES;
-        const uint32_t d_lo = tmem + (uint32_t)(b * 2 * TC_BN), d_hi = d_lo + TC_BN;
+        const unsigned char* st = smem + (size_t)s * STAGE_BYTES;
+        const uint32_t d_lo = tmem + (uint32_t)(b * 2 * BN), d_hi = d_lo + BN;
 #pragma unroll
         for (int k = 0; k < 4; ++k) tc_mma_i8(d_lo, tc_desc(st, k), tc_desc(st + TC_A_BYTES, k), id_lo, k > 0);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc_mma_i8(d_hi, tc_desc(st, k), tc_desc(st + TC_A_BYTES + TC_B_BYTES, k), id_hi, k > 0);
+          tc_mma_i8(d_hi, tc_desc(st, k), tc_desc(st + TC_A_BYTES + B_BYTES, k), id_hi, k > 0);
         tc_commit(&empty[s]);           // the stage is free once these MMAs have read it
         tc_commit(&accf[b]);            // the group's accumulators are complete
-        *(volatile int*)&consumed_sh = g + 1;
+        *(volatile int*)&consumed_sh = i + 1;
       }
     }
   } else {
-    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31; thread = output row n
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (thread = output row n) and the
+    // CW accumulator columns [hc * CW, hc * CW + CW) of each digit
+    pdl_wait();
+    if (a.zero && blockIdx.x == 0 && blockIdx.y == 0)
+      for (int i = (int)threadIdx.x - 64; i < a.nzero; i += NEPI) a.zero[i] = 0;
     const int q = warp & 3;
+    const int hc = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     const int n = tm * TC_BM + row;
-    int64_t tot[TC_BN];
+    int64_t tot[CW];
 #pragma unroll
-    for (int j = 0; j < TC_BN; ++j) tot[j] = 0;
+    for (int j = 0; j < CW; ++j) tot[j] = 0;
     const int32_t* mrow = a.Mg ? a.Mg + (size_t)n * a.ldm : nullptr;
-    int32_t mnext = mrow ? __ldg(mrow) : 1;
+    int32_t mnext = (mrow && ng > 0) ? __ldg(mrow + g0) : 1;
     bool ok = true;
-    for (int g = 0; g < G; ++g) {
-      const int b = g & 1;
+    for (int i = 0; i < ng; ++i) {
+      const int b = i & 1;
       const int32_t mv = mnext;
-      if (mrow && g + 1 < G) mnext = __ldg(mrow + g + 1);
+      if (mrow && i + 1 < ng) mnext = __ldg(mrow + g0 + i + 1);
       // warp-uniform outcome: the TMEM loads below are .sync.aligned over the whole warp
-      if (!__all_sync(0xffffffffu, tc_wait(&accf[b], (g >> 1) & 1))) {
+      if (!__all_sync(0xffffffffu, tc_wait(&accf[b], (i >> 1) & 1))) {
         ok = false;
         set_err(a.err, ERR_WAIT_TIMEOUT);
         abort_sh = 1;
         break;
       }
       tc_fence_after();
-      const uint32_t t_lo = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * TC_BN);
+      const uint32_t t_lo = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * BN + hc * CW);
 #pragma unroll
-      for (int c = 0; c < TC_BN / 16; ++c) {
-        int32_t lo[16], hi[16];
-        tmem_ld16(t_lo + c * 16, lo);
-        tmem_ld16(t_lo + TC_BN + c * 16, hi);
+      for (int c = 0; c < CW / 8; ++c) {
+        int32_t lo[8], hi[8];
+        tmem_ld8(t_lo + c * 8, lo);
+        tmem_ld8(t_lo + BN + c * 8, hi);
         tmem_wait_ld();
-        if (c == TC_BN / 16 - 1) {
+        if (c == CW / 8 - 1) {
           tc_fence_before();
           mbar_arrive(&acce[b]);        // buffer b may be overwritten by the next-but-one group
         }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int32_t accg = hi[i] * 256 + lo[i];        // exact group sum (|.| < 2^30)
-          tot[c * 16 + i] = (int64_t)((uint64_t)tot[c * 16 + i] + (uint64_t)((int64_t)accg * mv));
+        for (int e = 0; e < 8; ++e) {
+          const int32_t accg = hi[e] * 256 + lo[e];        // exact group sum (|.| < 2^30)
+          tot[c * 8 + e] = (int64_t)((uint64_t)tot[c * 8 + e] + (uint64_t)((int64_t)accg * mv));
         }
       }
     }
-    if (ok) {
-      // final epilogue per (activation row t, output row n): coalesced over n for each t
+    pdl_launch_dependents();
+    // every epilogue thread reaches this point (finished or timed out): one decision for all
+    named_sync(1, NEPI);
+    ok = ok && !*(volatile int*)&abort_sh;
+    ok = __all_sync(0xffffffffu, ok);
+    named_sync(1, NEPI);
+    if (ok && a.ksplit == 1) {
 #pragma unroll
-      for (int j = 0; j < TC_BN; ++j) {
-        const int t = tn * TC_BN + j;
-        const bool live = t < a.T;
-        const int64_t v = tot[j];
-        if (a.epi == EPI_SWIGLU) {
-          // rows 2u (gate) and 2u + 1 (up) sit in adjacent lanes
-          const int sh = live ? a.xs[t] : 0;
-          int64_t y = shr64(v, 28 - sh);
-          const int64_t other = __shfl_xor_sync(0xffffffffu, y, 1);
-          const int64_t vother = __shfl_xor_sync(0xffffffffu, v, 1);
-          if (live && !(n & 1)) {
-            const int u = n >> 1;
-            const int64_t hv = shr64((int64_t)((uint64_t)isilu_dev(a.silu_t, y) * (uint64_t)other), 16);
-            a.out[(size_t)t * a.ldo + u] = hv;
-            if (a.raw) a.raw[(size_t)t * a.ldr + u] = v;
-            if (a.raw2) a.raw2[(size_t)t * a.ldr + u] = vother;
+      for (int j = 0; j < CW; ++j) {
+        const int t = tn * BN + hc * CW + j;
+        uint64_t hm = 0;
+        tc_finish(a, t, n, tot[j], t < a.T, hm);
+        if (a.amax_out) tc_publish_hmax(a, t, hm);
+      }
+    } else if (ok) {
+      // split-K: add this CTA's partial sums, the last CTA of the tile finishes it
+#pragma unroll
+      for (int j = 0; j < CW; ++j) {
+        const int t = hc * CW + j;
+        if (t < a.T) atomicAdd(reinterpret_cast<unsigned long long*>(a.tot_buf + (size_t)t * a.N + n),
+                               (unsigned long long)tot[j]);
+      }
+      __threadfence();
+      named_sync(1, NEPI);
+      if (threadIdx.x == 64) {
+        const unsigned prev = atomicAdd(a.tickets + tm, 1u);
+        last_sh = prev == (unsigned)(a.ksplit - 1);
+        if (last_sh) a.tickets[tm] = 0;
+      }
+      named_sync(1, NEPI);
+      if (last_sh) {
+        __threadfence();
+#pragma unroll
+        for (int j = 0; j < CW; ++j) {
+          const int t = hc * CW + j;
+          int64_t v = 0;
+          if (t < a.T) {
+            int64_t* p = a.tot_buf + (size_t)t * a.N + n;
+            v = (int64_t)__ldcg(reinterpret_cast<const long long*>(p));
+            *p = 0;                     // ready for the next use
           }
-          continue;
+          uint64_t hm = 0;
+          tc_finish(a, t, n, v, t < a.T, hm);
+          if (a.amax_out) tc_publish_hmax(a, t, hm);
         }
-        if (!live) continue;
-        if (a.raw) a.raw[(size_t)t * a.ldr + n] = v;
-        if (a.epi == EPI_RAW) continue;
-        int64_t y = shr64(v, 28 - a.xs[t]);
-        if (a.bias) y = (int64_t)((uint64_t)y + (uint64_t)a.bias[n]);
-        int64_t* o = a.out + (size_t)t * a.ldo + n;
-        if (a.epi == EPI_RESID) *o = (int64_t)((uint64_t)*o + (uint64_t)y);
-        else *o = y;
       }
     }
   }
@@ -265,7 +358,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
 }
 
 // ---------------------------------------------------------------- digit planes
@@ -314,12 +407,12 @@ static bool make_map(CUtensorMap* m, const void* base, int rows, int cols, size_
 }
 
 size_t gemm_tc_digit_bytes(int T, int K) {
-  const size_t Tpad = (size_t)(T + TC_BN - 1) / TC_BN * TC_BN;
+  const size_t Tpad = (size_t)(T + TC_PAD - 1) / TC_PAD * TC_PAD;
   return 2 * Tpad * (size_t)K;
 }
 
 cudaError_t launch_digits(const int16_t* xq, int ldx, int T, int K, void* digits, cudaStream_t st) {
-  const int Tpad = (T + TC_BN - 1) / TC_BN * TC_BN;
+  const int Tpad = (T + TC_PAD - 1) / TC_PAD * TC_PAD;
   uint8_t* lo = static_cast<uint8_t*>(digits);
   int8_t* hi = reinterpret_cast<int8_t*>(lo + (size_t)Tpad * K);
   const long long n = (long long)Tpad * K / 2;
@@ -334,28 +427,55 @@ bool gemm_tc_supported(const LinW& L, int epi) {
          (epi == EPI_RAW || epi == EPI_STORE || epi == EPI_RESID || epi == EPI_SWIGLU) && encode_fn() != nullptr;
 }
 
-cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32_t* xs, int epi, int64_t* out, int ldo,
-                           int64_t* raw, int64_t* raw2, int ldr, const int32_t* silu_t, int* err, cudaStream_t st) {
-  if (!gemm_tc_supported(L, epi) || T <= 0) return cudaErrorInvalidValue;
-  const int Tpad = (T + TC_BN - 1) / TC_BN * TC_BN;
-  const uint8_t* lo = static_cast<const uint8_t*>(digits);
-  const uint8_t* hi = lo + (size_t)Tpad * L.K;
-  CUtensorMap mA, mLo, mHi;
-  if (!make_map(&mA, L.w, L.N, L.K, (size_t)L.K, TC_BM) || !make_map(&mLo, lo, Tpad, L.K, (size_t)L.K, TC_BN) ||
-      !make_map(&mHi, hi, Tpad, L.K, (size_t)L.K, TC_BN))
-    return cudaErrorInvalidValue;
-  static bool attr = false;
+template <int BN>
+static cudaError_t tc_launch(dim3 grid, const CUtensorMap& mA, const CUtensorMap& mLo, const CUtensorMap& mHi,
+                             const TcArgs& a, bool pdl, cudaStream_t st) {
+  static bool attr = false;                 // raised once to the full budget, never lowered
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcGeo<BN>::SMEM);
     if (e != cudaSuccess) return e;
     attr = true;
   }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(TcGeo<BN>::THREADS);
+  cfg.dynamicSmemBytes = TcGeo<BN>::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_gemm_tc<BN>, mA, mLo, mHi, a);
+}
+
+cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32_t* xs, int epi, int64_t* out, int ldo,
+                           int64_t* raw, int64_t* raw2, int ldr, const int32_t* silu_t, int* err, cudaStream_t st,
+                           const TcDecode* dec) {
+  if (!gemm_tc_supported(L, epi) || T <= 0) return cudaErrorInvalidValue;
+  // activation-row tile: 8 for decode steps (digit planes of TC_DECODE_ROWS rows), else 64 / 128
+  const int BN = dec ? 8 : (T > 64 ? 128 : 64);
+  const int Tpad = dec ? TC_DECODE_ROWS : (T + TC_PAD - 1) / TC_PAD * TC_PAD;
+  if (dec && (T > TC_DECODE_ROWS || dec->ksplit < 1 || (dec->ksplit > 1 && (!dec->tot_buf || !dec->tickets))))
+    return cudaErrorInvalidValue;
+  const uint8_t* lo = static_cast<const uint8_t*>(digits);
+  const uint8_t* hi = lo + (size_t)Tpad * L.K;
+  CUtensorMap mA, mLo, mHi;
+  if (!make_map(&mA, L.w, L.N, L.K, (size_t)L.K, TC_BM) || !make_map(&mLo, lo, Tpad, L.K, (size_t)L.K, BN) ||
+      !make_map(&mHi, hi, Tpad, L.K, (size_t)L.K, BN))
+    return cudaErrorInvalidValue;
   TcArgs a;
   a.N = L.N; a.K = L.K; a.T = T; a.ldm = L.ldm; a.Mg = L.Mg; a.xs = xs; a.bias = L.b; a.epi = epi;
   a.out = out; a.ldo = ldo; a.raw = raw; a.ldr = ldr; a.raw2 = raw2; a.silu_t = silu_t; a.err = err;
-  dim3 grid(L.N / TC_BM, Tpad / TC_BN);
-  k_gemm_tc<<<grid, TC_THREADS, TC_SMEM, st>>>(mA, mLo, mHi, a);
-  return cudaGetLastError();
+  if (dec) {
+    const int G = L.K / 128;
+    a.ksplit = dec->ksplit < G ? dec->ksplit : G;
+    a.tot_buf = dec->tot_buf; a.tickets = dec->tickets; a.amax_out = dec->amax_out;
+    a.zero = dec->zero; a.nzero = dec->nzero;
+    return tc_launch<8>(dim3(L.N / TC_BM, a.ksplit), mA, mLo, mHi, a, dec->pdl, st);
+  }
+  if (BN == 128) return tc_launch<128>(dim3(L.N / TC_BM, Tpad / 128), mA, mLo, mHi, a, false, st);
+  return tc_launch<64>(dim3(L.N / TC_BM, (T + 63) / 64), mA, mLo, mHi, a, false, st);
 }
 
 }  // namespace exb

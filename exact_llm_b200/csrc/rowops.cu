@@ -97,19 +97,29 @@ cudaError_t launch_embed_norm(const int8_t* emb, const int64_t* emb_q16, int emb
 }
 
 // ---------------------------------------------------------------- irms + qrow, qrow (one CTA per row)
+// int8 digit planes (lo = xq & 255, hi = xq >> 8) of row r for the tensor-core GEMM: planes of
+// TC_DECODE_ROWS rows of K bytes, the hi plane right after the lo plane
+EXB_DEV void put_digits(uint8_t* dig, int K, int r, int i, int16_t v) {
+  dig[(size_t)r * K + i] = (uint8_t)(v & 255);
+  dig[(size_t)(TC_DECODE_ROWS + r) * K + i] = (uint8_t)(int8_t)(v >> 8);
+}
+
 __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restrict__ x, int ldx,
                                                         const int64_t* __restrict__ g, int D,
-                                                        int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs) {
+                                                        int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs,
+                                                        uint8_t* __restrict__ dig) {
   extern __shared__ int64_t ys[];
   __shared__ uint64_t red[33];
   pdl_wait();
   pdl_launch_dependents();
   const int r = blockIdx.x;
   row_norm_q_any<ROW_THREADS>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, ys, red);
+  if (dig)   // the row was written by this CTA (visible after the function's final barrier)
+    for (int i = threadIdx.x; i < D; i += ROW_THREADS) put_digits(dig, D, r, i, xq[(size_t)r * ldq + i]);
 }
 
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
-                          int32_t* xs, cudaStream_t st, bool pdl) {
+                          int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig) {
   const size_t smem = (size_t)D * 16;
   static bool attr_set = false;   // raised once to the full budget, never lowered
   if (!attr_set) {
@@ -117,7 +127,7 @@ cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, in
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  void* args[] = {(void*)&x, (void*)&ldx, (void*)&g, (void*)&D, (void*)&xq, (void*)&ldq, (void*)&xs};
+  void* args[] = {(void*)&x, (void*)&ldx, (void*)&g, (void*)&D, (void*)&xq, (void*)&ldq, (void*)&xs, (void*)&dig};
   return launch_simple((const void*)k_norm_q, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
 }
 
@@ -150,7 +160,8 @@ cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, i
 // slice of a row, so a long row (e.g. the 18944-wide MLP activation) is converted in parallel.
 __global__ void __launch_bounds__(256) k_quant_known(const int64_t* __restrict__ x, int ldx, int K,
                                                      const unsigned long long* __restrict__ amax,
-                                                     int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs) {
+                                                     int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs,
+                                                     uint8_t* __restrict__ dig) {
   pdl_wait();
   pdl_launch_dependents();
   const int r = blockIdx.y;
@@ -161,16 +172,18 @@ __global__ void __launch_bounds__(256) k_quant_known(const int64_t* __restrict__
   short2* q2 = reinterpret_cast<short2*>(xq + (size_t)r * ldq);
   for (int i = (k0 >> 1) + threadIdx.x; i < (k1 >> 1); i += 256) {
     const longlong2 v = __ldcg(x2 + i);
-    q2[i] = make_short2(qrow_value(v.x, s), qrow_value(v.y, s));
+    const short2 q = make_short2(qrow_value(v.x, s), qrow_value(v.y, s));
+    q2[i] = q;
+    if (dig) { put_digits(dig, K, r, 2 * i, q.x); put_digits(dig, K, r, 2 * i + 1, q.y); }
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) xs[r] = s;
 }
 
 cudaError_t launch_quant_known(const int64_t* x, int ldx, int R, int K, const unsigned long long* amax, int16_t* xq,
-                               int ldq, int32_t* xs, cudaStream_t st, bool pdl) {
+                               int ldq, int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig) {
   if ((K & 1) || (ldx & 1) || (ldq & 1)) return cudaErrorInvalidValue;
   int slices = (K + 2047) / 2048;
-  void* args[] = {(void*)&x, (void*)&ldx, (void*)&K, (void*)&amax, (void*)&xq, (void*)&ldq, (void*)&xs};
+  void* args[] = {(void*)&x, (void*)&ldx, (void*)&K, (void*)&amax, (void*)&xq, (void*)&ldq, (void*)&xs, (void*)&dig};
   return launch_simple((const void*)k_quant_known, dim3(slices, R), dim3(256), 0, st, pdl, args);
 }
 

@@ -224,6 +224,41 @@ def test_persistent_step_matches_per_kernel_path(cuda_ok, B):
     assert np.array_equal(out[1][1], out[0][1])
 
 
+def test_fused_gemv_inputs_match_separate_kernels(cuda_ok):
+    """GEMVs that build their int16 input rows in their prologue (norm + qrow, or qrow from the
+    producer's published max) give the same logits and tokens as the separate row kernels."""
+    from exact_llm_b200 import ExactModel, configs
+    c = configs.arch("qwen2.5-7b", NL=2)
+    m = ExactModel.synthetic(c, 55, max_batch=1, max_seq=64)
+    prompt = np.random.default_rng(9).integers(0, c["V"], 7).astype(np.int32)
+    out = {}
+    for fz in (1, 0):
+        m.set_option("fuse", fz)
+        out[fz] = m.greedy(prompt, 6)
+    assert np.array_equal(out[1][0], out[0][0])
+    assert out[1][2] == out[0][2]
+    assert all(np.array_equal(a, b) for a, b in zip(out[1][1], out[0][1]))
+
+
+@pytest.mark.parametrize("B", [1, 3])
+def test_tensor_core_decode_matches_gemv(cuda_ok, B):
+    """Decode steps with the tcgen05 GEMM (8-row tiles, split over the 128-groups, digit planes
+    written by the row kernels) give the logits and tokens of the CUDA-core GEMV path."""
+    from exact_llm_b200 import ExactModel, configs
+    c = configs.arch("qwen2.5-7b", NL=2)
+    m = ExactModel.synthetic(c, 63, max_batch=B, max_seq=48)
+    prompts = np.random.default_rng(B).integers(0, c["V"], (B, 9)).astype(np.int32)
+    out = {}
+    for tcd in (1, 0):
+        m.set_option("tcd", tcd)
+        for b in range(B):
+            m.new_cache(b)
+        _, nxt = m.forward_rows(prompts.T.reshape(-1), np.tile(np.arange(B, dtype=np.int32), 9), want_logits=False)
+        out[tcd] = m.generate(nxt[-B:], 6, want_logits=True)
+    assert np.array_equal(out[1][0], out[0][0])
+    assert np.array_equal(out[1][1], out[0][1])
+
+
 @pytest.mark.parametrize("T", [16, 75, 300])
 def test_tensor_core_prefill_matches_gemv_path(cuda_ok, T):
     """Prefill of T rows on the tcgen05 GEMM (chunks of up to 256 rows, ragged tails, rows of two
