@@ -388,8 +388,17 @@ def main():
     ap.add_argument("--tp", action="store_true", help="with --gpus N under torchrun: one model split over the N GPUs")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens before decode (profiling uses a short one)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures only)")
+    ap.add_argument("--linear", type=int, default=0, metavar="T",
+                    help="only the exact linear op at T rows on the 7B gate|up shape (profiling)")
     a = ap.parse_args()
     globals()["PROMPT"] = a.prompt
+    if a.linear:
+        import torch
+        torch.cuda.set_device(0)
+        tops, ms = gemm_tc_tops(3584, 37888, a.linear, reps=max(1, a.steps))
+        print(json.dumps({"linear": {"T": a.linear, "K": 3584, "N": 37888, "ms": round(ms, 4),
+                                     "effective_tops": round(tops, 1)}}))
+        return
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

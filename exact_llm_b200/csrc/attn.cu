@@ -34,6 +34,7 @@ __global__ void __launch_bounds__(256) k_rope_cache(const AttnArgs a) {
   pdl_wait();
   pdl_launch_dependents();
   rope_cache_rows<256>(a, blockIdx.x * 8, gridDim.x * 8);
+  tl_exit();
 }
 
 cudaError_t launch_rope_cache(const AttnArgs& a, cudaStream_t st, bool pdl) {
@@ -227,6 +228,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
       if (tid == 0) a.xs_out[rr] = s;
     }
   }
+  tl_exit();
 }
 
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
@@ -249,6 +251,322 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CL, a.KV, a.R);
+  cfg.blockDim = dim3(ATT_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, a, SCmax);
+}
+
+
+// ---------------------------------------------------------------- fused RoPE + cache write + decode attention
+// One 8-CTA cluster per (row, query head); CTA c of the cluster takes a contiguous slice of the
+// key positions.  The rows cached by earlier steps never depend on the kernel before this one, so
+// each CTA stages its first tile of K/V rows (and the row's cos/sin) in shared memory BEFORE the
+// dependent-launch wait; after it, the CTA ropes and quantises its query head (exact_llm.py:157-160,
+// 41-46) and computes the rows of this step (positions of the chunk's rows of the same sequence)
+// directly from q|k|v, never reading them back from the cache.  The cluster of the first query
+// head of a KV group writes the row of its own position to the cache (one writer per KV row).
+// The three exact softmax phases exchange maxima, sums and partial p.v through distributed shared
+// memory (every peer value loaded at once); all sums are integer sums, so the split changes no bit.
+constexpr int ATR_TILE = 128;       // key/value positions staged in shared memory at a time
+
+EXB_DEV int64_t rope_value(const int64_t* row, int d, int half, int64_t c, int64_t s) {
+  const int64_t x = ld_cg(row + d);
+  const int64_t rot = d < half ? (int64_t)(0ull - (uint64_t)ld_cg(row + d + half)) : ld_cg(row + d - half);
+  return shr64((int64_t)((uint64_t)x * (uint64_t)c + (uint64_t)rot * (uint64_t)s), 16);
+}
+
+template <int HD>
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn_rope(const AttnArgs a, int SCmax) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  constexpr int TP = HD + 8;                 // padded K row (int16): 8 consecutive rows hit distinct banks
+  constexpr int HALF = HD / 2;
+  constexpr int NW = ATT_THREADS / 32;
+  __shared__ uint64_t red[NW];
+  __shared__ int64_t lmax_s, lsum_s, gmax_s, gsum_s;
+  __shared__ int qs_s;
+  __shared__ int64_t gath[HD];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int c = (int)cluster.block_rank();
+  const int h = blockIdx.y, r = blockIdx.z;
+  const int rep = a.H / a.KV, j = h / rep;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  int16_t* qq_s = reinterpret_cast<int16_t*>(sm);                            // HD
+  int32_t* cs_s = reinterpret_cast<int32_t*>(sm + 256);                      // HALF cos | HALF sin
+  int64_t* sc = reinterpret_cast<int64_t*>(sm + 768);                        // SCmax
+  int64_t* pout = sc + SCmax;                                                 // HD
+  int64_t* pv = pout + HD;                                                    // ATT_THREADS
+  int* ksh = reinterpret_cast<int*>(pv + ATT_THREADS);                        // ATR_TILE
+  int16_t* ktile = reinterpret_cast<int16_t*>(ksh + ATR_TILE);                // ATR_TILE x TP
+  int32_t* vtile = reinterpret_cast<int32_t*>(ktile + (size_t)ATR_TILE * TP); // ATR_TILE x HD
+
+  // ---- before the wait: positions, this row's cos/sin, the first tile of cached rows
+  const int pos = a.row_pos[r], seq = a.row_seq[r];
+  const bool ok = pos >= 0 && pos < a.Smax && pos < a.Tmax;
+  const int S = ok ? pos + 1 : 0;
+  const int chunk = (S + CL - 1) / CL;
+  const int t0 = min(S, c * chunk);
+  const int t1 = min(S, t0 + chunk);
+  const int n = t1 - t0;
+  const size_t cbase = ((size_t)seq * a.KV + j) * a.Smax;
+  if (ok)
+    for (int i = tid; i < HALF; i += ATT_THREADS) {
+      cs_s[i] = a.cos_t[(size_t)pos * HALF + i];
+      cs_s[HALF + i] = a.sin_t[(size_t)pos * HALF + i];
+    }
+  auto stage_k = [&](int tb, int nt) {
+    for (int e = tid; e < nt * (HD / 8); e += ATT_THREADS) {
+      const int t = e / (HD / 8), c4 = e - t * (HD / 8);
+      *reinterpret_cast<int4*>(ktile + (size_t)t * TP + c4 * 8) =
+          reinterpret_cast<const int4*>(a.kc + (cbase + t0 + tb + t) * HD)[c4];
+    }
+    for (int t = tid; t < nt; t += ATT_THREADS) ksh[t] = a.ks[cbase + t0 + tb + t];
+  };
+  auto stage_v = [&](int tb, int nt) {
+    for (int e = tid; e < nt * (HD / 4); e += ATT_THREADS)
+      reinterpret_cast<int4*>(vtile)[e] = reinterpret_cast<const int4*>(a.vc + (cbase + t0 + tb) * HD)[e];
+  };
+  const int nt0 = min(ATR_TILE, n);
+  stage_k(0, nt0);
+  stage_v(0, nt0);
+
+  pdl_wait();
+  pdl_launch_dependents();
+  if (!ok && c == 0 && tid == 0) set_err(a.err, ERR_BOUNDS);
+  __syncthreads();                                       // cos/sin staged by other threads
+
+  // ---- this head's query row: RoPE, then qrow over the head (one shift per (row, head))
+  int64_t qv = 0;
+  if (ok && tid < HD)
+    qv = rope_value(a.qkv + (size_t)r * a.ldqkv + (size_t)h * HD, tid, HALF, cs_s[tid % HALF], cs_s[HALF + tid % HALF]);
+  {
+    const uint64_t m = warp_max_u64(uabs64(qv));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    uint64_t mm = 0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) mm = red[w] > mm ? red[w] : mm;
+    const int s = qrow_shift(mm);
+    if (tid < HD) qq_s[tid] = qrow_value(qv, s);
+    if (tid == 0) qs_s = s;
+  }
+
+  // ---- rows of this step that fall in [t0 + tb, t0 + tb + nt): computed from q|k|v (one warp
+  // per row of the chunk); the (first head of the group, own row) cluster writes them to the cache
+  auto patch = [&](int tb, int nt, bool do_k, bool do_v) {
+    if (warp < a.R) {
+      const int r2 = warp;
+      const int p2 = a.row_pos[r2];
+      if (ok && a.row_seq[r2] == seq && p2 >= t0 + tb && p2 < t0 + tb + nt && p2 < a.Tmax) {
+        const int t = p2 - t0 - tb;
+        const bool writer = (h == j * rep) && r2 == r;
+        const size_t cidx = cbase + p2;
+        if (do_k) {
+          const int64_t* krow = a.qkv + (size_t)r2 * a.ldqkv + (size_t)(a.H + j) * HD;
+          int64_t kv[4];
+          uint64_t m = 0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int d = lane + 32 * q;
+            kv[q] = 0;
+            if (d < HD) {
+              kv[q] = rope_value(krow, d, HALF, a.cos_t[(size_t)p2 * HALF + d % HALF], a.sin_t[(size_t)p2 * HALF + d % HALF]);
+              const uint64_t u = uabs64(kv[q]);
+              m = u > m ? u : m;
+            }
+          }
+          for (int o = 16; o > 0; o >>= 1) { const uint64_t w = __shfl_xor_sync(0xffffffffu, m, o); m = w > m ? w : m; }
+          const int sh = qrow_shift(m);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int d = lane + 32 * q;
+            if (d < HD) {
+              const int16_t v16 = qrow_value(kv[q], sh);
+              ktile[(size_t)t * TP + d] = v16;
+              if (writer) a.kc[cidx * HD + d] = v16;
+            }
+          }
+          if (lane == 0) {
+            ksh[t] = sh;
+            if (writer) a.ks[cidx] = (int8_t)sh;
+          }
+        }
+        if (do_v) {
+          const int64_t* vrow = a.qkv + (size_t)r2 * a.ldqkv + (size_t)(a.H + a.KV + j) * HD;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int d = lane + 32 * q;
+            if (d < HD) {
+              const int64_t v = ld_cg(vrow + d);
+              if (v > INT32_MAX || v < INT32_MIN) set_err(a.err, ERR_V_RANGE);
+              vtile[(size_t)t * HD + d] = (int32_t)v;
+              if (writer) a.vc[cidx * HD + d] = (int32_t)v;
+            }
+          }
+        }
+      }
+    }
+  };
+  patch(0, nt0, true, true);
+  __syncthreads();
+
+  // ---- phase 1: scores (two threads per key row, half a head each), local max
+  const int qs = qs_s;
+  for (int tb = 0; tb < n; tb += ATR_TILE) {
+    const int nt = min(ATR_TILE, n - tb);
+    if (tb > 0) {
+      __syncthreads();
+      stage_k(tb, nt);
+      patch(tb, nt, true, false);
+      __syncthreads();
+    }
+    for (int p0 = 0; p0 < 2 * ATR_TILE; p0 += ATT_THREADS) {
+      const int p = p0 + tid, t = p >> 1, hf = p & 1;
+      int64_t acc = 0;
+      if (t < nt) {
+        const int16_t* kr = ktile + (size_t)t * TP + hf * HALF;
+        const int16_t* qr = qq_s + hf * HALF;
+#pragma unroll
+        for (int d = 0; d < HALF; d += 8) {
+          const int4 x = *reinterpret_cast<const int4*>(qr + d);
+          const int4 y = *reinterpret_cast<const int4*>(kr + d);
+          const int xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            acc += (int)(short)(xs[q] & 0xffff) * (int)(short)(ys[q] & 0xffff) + (xs[q] >> 16) * (ys[q] >> 16);
+        }
+      }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      if (t < nt && hf == 0)
+        sc[tb + t] = shr64((int64_t)((uint64_t)acc * (uint64_t)a.inv), 32 - qs - ksh[t]);
+    }
+  }
+  __syncthreads();
+  {
+    int64_t m = INT64_MIN;
+    for (int t = tid; t < n; t += ATT_THREADS) m = sc[t] > m ? sc[t] : m;
+    for (int o = 16; o > 0; o >>= 1) { const int64_t w = __shfl_xor_sync(0xffffffffu, m, o); m = w > m ? w : m; }
+    if (lane == 0) red[warp] = (uint64_t)m;
+    __syncthreads();
+    if (tid == 0) {
+      int64_t mm = INT64_MIN;
+      for (int w = 0; w < NW; ++w) mm = (int64_t)red[w] > mm ? (int64_t)red[w] : mm;
+      lmax_s = mm;
+    }
+  }
+  cluster.sync();
+  if (warp == 0) {
+    int64_t g = lane < CL ? *cluster.map_shared_rank(&lmax_s, lane) : INT64_MIN;
+    for (int o = 16; o > 0; o >>= 1) { const int64_t w = __shfl_xor_sync(0xffffffffu, g, o); g = w > g ? w : g; }
+    if (lane == 0) gmax_s = g;
+  }
+  __syncthreads();
+  // ---- phase 2: e = exp table at (max - score), local sum
+  {
+    const int64_t g = gmax_s;
+    int64_t s = 0;
+    for (int t = tid; t < n; t += ATT_THREADS) {
+      const int64_t e = exp_lookup(a.exp_t, g - sc[t]);
+      sc[t] = e;
+      s += e;
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) red[warp] = (uint64_t)s;
+    __syncthreads();
+    if (tid == 0) {
+      int64_t ss = 0;
+      for (int w = 0; w < NW; ++w) ss += (int64_t)red[w];
+      lsum_s = ss;
+    }
+  }
+  cluster.sync();
+  if (warp == 0) {
+    int64_t g = lane < CL ? *cluster.map_shared_rank(&lsum_s, lane) : 0;
+    for (int o = 16; o > 0; o >>= 1) g += __shfl_xor_sync(0xffffffffu, g, o);
+    if (lane == 0) gsum_s = g;
+  }
+  __syncthreads();
+  // ---- phase 3: p = (e << 20) // sum(e), partial p.v over this CTA's positions
+  {
+    const uint64_t g = (uint64_t)gsum_s;
+    for (int t = tid; t < n; t += ATT_THREADS) sc[t] = (int64_t)(((uint64_t)sc[t] << 20) / g);
+  }
+  {
+    constexpr int NP = ATT_THREADS / HD;
+    const int d = tid % HD, part = tid / HD;
+    int64_t acc = 0;
+    for (int tb = 0; tb < n; tb += ATR_TILE) {
+      const int nt = min(ATR_TILE, n - tb);
+      __syncthreads();
+      if (tb > 0) {
+        stage_v(tb, nt);
+        patch(tb, nt, false, true);
+        __syncthreads();
+      }
+#pragma unroll 4
+      for (int t = part; t < nt; t += NP) acc += sc[tb + t] * (int64_t)vtile[(size_t)t * HD + d];
+    }
+    pv[tid] = acc;
+    __syncthreads();
+    if (tid < HD) {
+      int64_t s = 0;
+#pragma unroll
+      for (int q = 0; q < NP; ++q) s += pv[q * HD + tid];
+      pout[tid] = s;
+    }
+  }
+  cluster.sync();
+  // ---- combine: CTA c finalises HD / CL output dims, each from the CL partials loaded at once
+  {
+    constexpr int PER = HD / CL;
+    if (tid < HD) {
+      const int dd = c * PER + tid / CL, peer = tid % CL;
+      gath[tid] = cluster.map_shared_rank(pout, peer)[dd];
+    }
+    __syncthreads();
+    uint64_t om = 0;
+    if (tid < PER) {
+      int64_t s = 0;
+#pragma unroll
+      for (int q = 0; q < CL; ++q) s += gath[tid * CL + q];
+      const int64_t o = shr64(s, 20);
+      if (ok) a.out[(size_t)r * a.ldo + (size_t)h * HD + c * PER + tid] = o;
+      om = uabs64(o);
+    }
+    if (warp == 0 && a.amax_out) {
+      om = warp_max_u64(om);
+      if (lane == 0 && om && ok) atomicMax(a.amax_out + r, (unsigned long long)om);
+    }
+  }
+  cluster.sync();                                        // peers' shared memory stays alive until read
+  tl_exit();
+}
+
+cudaError_t launch_attn_rope(const AttnArgs& a, cudaStream_t st, bool pdl) {
+  const int rep = a.KV > 0 ? a.H / a.KV : 0;
+  if (rep < 1 || a.H % a.KV || a.R < 1 || a.R > ATT_THREADS / 32) return cudaErrorInvalidValue;
+  if (a.hd != 128 && a.hd != 64 && a.hd != 32 && a.hd != 16) return cudaErrorInvalidValue;
+  const int SCmax = (((a.Smax + CL - 1) / CL) + 1) & ~1;   // even: keeps the arrays after sc 16-byte aligned
+  const size_t smem = 768 + (size_t)SCmax * 8 + (size_t)a.hd * 8 + (size_t)ATT_THREADS * 8 + (size_t)ATR_TILE * 4 +
+                      (size_t)ATR_TILE * (a.hd + 8) * 2 + (size_t)ATR_TILE * a.hd * 4;
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  void (*kern)(const AttnArgs, int) = a.hd == 128 ? k_attn_rope<128> : a.hd == 64 ? k_attn_rope<64>
+                                    : a.hd == 32 ? k_attn_rope<32> : k_attn_rope<16>;
+  static bool attr_set[4] = {false, false, false, false};
+  const int ti = a.hd == 128 ? 0 : a.hd == 64 ? 1 : a.hd == 32 ? 2 : 3;
+  if (!attr_set[ti]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set[ti] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CL, a.H, a.R);
   cfg.blockDim = dim3(ATT_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;

@@ -168,7 +168,61 @@ EXB_DEV int64_t block_sum_i64(int64_t v, uint64_t* red) {
 // ---------------------------------------------------------------- programmatic dependent launch
 // Kernels launched with the PDL attribute may start while the previous kernel drains; they
 // must call pdl_wait() before touching data the previous kernel produced.
+#ifndef EXB_TIMELINE
 EXB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+EXB_DEV void tl_exit() {}
+EXB_DEV void tl_start() {}
+#else
+// Timeline build (compiled with -DEXB_TIMELINE; never the shipped library): each kernel of a
+// step stamps %globaltimer into slot `seq` of a device buffer -- earliest CTA arrival at the
+// dependency wait, earliest CTA past it, latest CTA exit -- and the last CTA to exit advances
+// `seq`.  A kernel's successors wait for its completion, so slot n is the n-th kernel.
+constexpr int TL_SLOTS = 4096;
+struct TlBuf {
+  unsigned long long seq, cnt, pad[2];
+  unsigned long long t[TL_SLOTS][4];      // enter (min), waited (min), exit (max), CTAs
+};
+static __device__ TlBuf* g_tlb = nullptr;
+EXB_DEV unsigned long long tl_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+EXB_DEV unsigned long long tl_seq() {
+  return *reinterpret_cast<volatile unsigned long long*>(&g_tlb->seq) % TL_SLOTS;
+}
+EXB_DEV void tl_mark(unsigned long long t0) {
+  if (g_tlb && threadIdx.x == 0 && threadIdx.y == 0) {
+    const unsigned long long q = tl_seq();
+    atomicMin(&g_tlb->t[q][0], t0);
+    atomicMin(&g_tlb->t[q][1], tl_now());
+  }
+}
+EXB_DEV void pdl_wait() {
+  const unsigned long long t0 = tl_now();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  tl_mark(t0);
+}
+EXB_DEV void tl_start() { tl_mark(tl_now()); }     // kernels launched without a dependency wait
+EXB_DEV void tl_exit() {
+  __syncthreads();
+  if (g_tlb && threadIdx.x == 0 && threadIdx.y == 0) {
+    const unsigned long long q = tl_seq();
+    atomicMax(&g_tlb->t[q][2], tl_now());
+    atomicAdd(&g_tlb->t[q][3], 1ull);
+    __threadfence();
+    const unsigned long long nb = (unsigned long long)gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(&g_tlb->cnt, 1ull) + 1 == nb) {
+      atomicExch(&g_tlb->cnt, 0ull);
+      __threadfence();
+      atomicAdd(&g_tlb->seq, 1ull);
+    }
+  }
+}
+int tl_register(int (*install)(void*));
+static int tl_install(void* p) { return cudaMemcpyToSymbol(g_tlb, &p, sizeof(p)) == cudaSuccess ? 0 : -1; }
+static const int tl_registered = tl_register(&tl_install);
+#endif
 EXB_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 EXB_DEV void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   // fire-and-forget L2 prefetch of a 16-byte aligned range (no completion to wait for)

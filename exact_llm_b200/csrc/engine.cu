@@ -143,7 +143,9 @@ struct exb_model {
   // persistent decode-step kernel (step.cu): per-layer descriptors and accumulators
   bool step_on = false;
   bool tc_on = true;                    // multi-row chunks on the tensor-core GEMM
-  bool fuse_in = false;                 // GEMVs build their int16 input rows themselves (norm / qrow prologue)
+  int fuse_in = 1;                      // GEMVs build their int16 input rows: 1 = qrow prologue (o, down),
+                                        // 2 = also the norm (q|k|v, gate|up, head), 0 = separate kernels
+  bool attn_fused = true;               // decode: RoPE + cache write inside the attention kernel
   bool tc_decode = false;               // decode-step linears on the tcgen05 GEMM (8-row tiles, split-K)
   uint8_t* dq = nullptr;                // digit planes of the decode rows (2 x TC_DECODE_ROWS x KMAX)
   int64_t* tc_tot = nullptr;            // split-K partial sums (TC_DECODE_ROWS x NMAX)
@@ -525,8 +527,12 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
         RUN(launch_gemm_tc(m->dq, R, Ld.qkv, m->xs, EPI_STORE, m->qkv, m->Nqkv, nullptr, nullptr, 0, nullptr, m->err,
                            st, &d));
       }
-      RUN(launch_rope_cache(aa, st, pdl));
-      RUN(launch_attn_decode(aa, st, pdl));
+      if (m->attn_fused) {
+        RUN(launch_attn_rope(aa, st, pdl));
+      } else {
+        RUN(launch_rope_cache(aa, st, pdl));
+        RUN(launch_attn_decode(aa, st, pdl));
+      }
       RUN(launch_quant_known(m->ao, Hd, R, Hd, m->amax_o, m->xq, m->KMAX, m->xs, st, pdl, m->dq));
       {
         TcDecode d = dec(Ld.o);
@@ -548,20 +554,26 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       }
       continue;
     }
-    // fused inputs: each GEMV CTA computes its int16 rows in its prologue (norm or qrow with the
-    // producer's published max) while its first weight bytes stream into L2
-    const bool fz = m->fuse_in && !m->fr_on;
-    if (!fz) RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    // fused inputs: each GEMV CTA computes its int16 rows in its prologue (qrow with the
+    // producer's published max at level 1, also the norm at level 2) while its first weight bytes
+    // stream into L2
+    const bool fz = m->fuse_in >= 1 && !m->fr_on;          // o and down: qrow in the prologue
+    const bool fzn = m->fuse_in >= 2 && !m->fr_on;         // q|k|v and gate|up: norm in the prologue
+    if (!fzn) RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     {
       GemvArgs g; base(g, Ld.qkv);
-      if (fz) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g1; }
+      if (fzn) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g1; }
       g.epi = EPI_STORE; g.out = m->qkv; g.ldo = m->Nqkv; g.raw = trace_ptr(Ld.li[0]);
       g.zero = m->amax_o; g.nzero = RMAX;
       set_fr(g, {Ld.li[0], Ld.li[1], Ld.li[2]});
       RUN(launch_gemv(g, st, pdl));
     }
-    RUN(launch_rope_cache(aa, st, pdl));
-    RUN(launch_attn_decode(aa, st, pdl));
+    if (m->attn_fused) {
+      RUN(launch_attn_rope(aa, st, pdl));
+    } else {
+      RUN(launch_rope_cache(aa, st, pdl));
+      RUN(launch_attn_decode(aa, st, pdl));
+    }
     // tensor parallel: the qrow of o's input needs the max over every rank's heads
     if (tp) RUN(tp_allreduce(m, m->amax_o, m->amax_o, R, ncclUint64, ncclMax, st));
     if (!fz) RUN(launch_quant_known(m->ao, Hd, R, Hd, m->amax_o, m->xq, m->KMAX, m->xs, st, pdl && !tp));
@@ -578,14 +590,14 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       RUN(tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st));
       RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.o.b, m->x, c.D, st));
     }
-    if (!fz || c.n_experts) RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    if (!fzn || c.n_experts) RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     if (c.n_experts) {
       RUN(launch_moe(moe_args(m, i, R, m->xq, m->KMAX, m->xs, g_hist_row0), m->x, c.D, st));
       continue;
     }
     {
       GemvArgs g; base(g, Ld.gu);
-      if (fz) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g2; }
+      if (fzn) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g2; }
       g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.amax_out = m->amax_h;
       g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]);
       set_fr(g, {Ld.li[4], Ld.li[5]});
@@ -606,7 +618,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.down.b, m->x, c.D, st));
     }
   }
-  const bool fzh = m->fuse_in && !m->fr_on;
+  const bool fzh = m->fuse_in >= 2 && !m->fr_on;
   if (!fzh) RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
   {
     GemvArgs g;
@@ -634,6 +646,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
 
 __global__ void k_advance(int B, int32_t* ids, int32_t* pos, const int32_t* next, int32_t* step, int32_t* tokens,
                           int cap) {
+  tl_start();
   const int r = threadIdx.x;
   const int s = *step;
   __syncthreads();
@@ -644,6 +657,7 @@ __global__ void k_advance(int B, int32_t* ids, int32_t* pos, const int32_t* next
   }
   __syncthreads();
   if (r == 0) *step = s + 1;
+  tl_exit();
 }
 
 // --- graph cache: key = (R, row-array base, logits, advance, trace, freivalds)
@@ -699,6 +713,19 @@ static int check_device_errors(exb_model* m) {
 }
 
 // ------------------------------------------------------------------------------------------ C ABI
+#ifdef EXB_TIMELINE
+namespace exb {
+std::vector<int (*)(void*)>& tl_installers() {
+  static std::vector<int (*)(void*)> v;
+  return v;
+}
+int tl_register(int (*install)(void*)) {
+  tl_installers().push_back(install);
+  return 0;
+}
+}  // namespace exb
+#endif
+
 extern "C" {
 
 const char* exb_last_error(void) { return g_err.c_str(); }
@@ -1239,7 +1266,7 @@ int exb_model_finalize(exb_model* m) {
   }
   CK(cudaMemcpy(m->step_layers, sl.data(), sizeof(StepLayer) * c.NL, cudaMemcpyHostToDevice));
   if (const char* v = getenv("EXB_STEP")) m->step_on = atoi(v) != 0;
-  if (const char* v = getenv("EXB_FUSE")) m->fuse_in = atoi(v) != 0;
+  if (const char* v = getenv("EXB_FUSE")) m->fuse_in = atoi(v);
   if (const char* v = getenv("EXB_TCD")) m->tc_decode = atoi(v) != 0;
   if (const char* v = getenv("EXB_PF_KB")) m->pf_bytes = std::max(0, atoi(v)) * 1024;
   m->finalized = true;
@@ -1606,7 +1633,8 @@ int exb_set_option(exb_model* m, const char* name, int64_t value) {
   const std::string n(name);
   if (n == "step") m->step_on = value != 0;
   else if (n == "tc") m->tc_on = value != 0;
-  else if (n == "fuse") m->fuse_in = value != 0;
+  else if (n == "fuse") m->fuse_in = (int)value;
+  else if (n == "attn") m->attn_fused = value != 0;
   else if (n == "tcd") m->tc_decode = value != 0;
   else if (n == "pf_kb") {
     if (value < 0 || value > 1024) FAIL(EXB_EINVAL, "pf_kb: 0..1024");
@@ -1655,6 +1683,29 @@ int exb_moe_selections(exb_model* m, int layer, int32_t* host, int64_t n) {
   CK(cudaMemcpy(host, m->moe_hist + (size_t)layer * SEL_CAP * m->c.topk, sizeof(int32_t) * need, cudaMemcpyDeviceToHost));
   return EXB_OK;
 }
+
+#ifdef EXB_TIMELINE
+// Timeline build only: op 0 installs a zeroed stamp buffer in every translation unit, op 1
+// resets it, op 2 copies n x 4 stamps (enter, waited, exit, CTAs) to `host`.
+int exb_timeline(int op, uint64_t* host, int n) {
+  static TlBuf* buf = nullptr;
+  if (op == 0 && !buf) {
+    if (cudaMalloc(&buf, sizeof(TlBuf)) != cudaSuccess) FAIL(EXB_ECUDA, "timeline alloc");
+    for (auto fn : tl_installers())
+      if (fn(buf)) FAIL(EXB_ECUDA, "timeline install");
+  }
+  if (!buf) FAIL(EXB_EINVAL, "timeline not installed");
+  if (op <= 1) {
+    std::vector<unsigned long long> h(sizeof(TlBuf) / 8, 0);
+    for (int i = 0; i < TL_SLOTS; ++i) h[4 + 4 * i] = h[5 + 4 * i] = ~0ull;
+    CK(cudaMemcpy(buf, h.data(), sizeof(TlBuf), cudaMemcpyHostToDevice));
+    return EXB_OK;
+  }
+  if (n > TL_SLOTS) n = TL_SLOTS;
+  CK(cudaMemcpy(host, reinterpret_cast<char*>(buf) + 32, (size_t)n * 32, cudaMemcpyDeviceToHost));
+  return EXB_OK;
+}
+#endif
 
 int exb_device_errors(exb_model* m, int* bits) {
   if (!m || !bits) FAIL(EXB_EINVAL, "null argument");

@@ -359,6 +359,7 @@ __global__ void __launch_bounds__(TcGeo<BN>::THREADS, 1)
   tc_fence_after();
   if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  tl_exit();
 }
 
 // ---------------------------------------------------------------- digit planes
@@ -374,6 +375,7 @@ __global__ void k_digits(const int16_t* __restrict__ xq, int ldx, int T, int K, 
     reinterpret_cast<uchar2*>(lo)[i] = make_uchar2((uint8_t)(v.x & 255), (uint8_t)(v.y & 255));
     reinterpret_cast<char2*>(hi)[i] = make_char2((int8_t)(v.x >> 8), (int8_t)(v.y >> 8));
   }
+  tl_exit();
 }
 
 // ---------------------------------------------------------------- host side

@@ -282,6 +282,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
       }
     }
   }
+  tl_exit();
 }
 
 template <int R, int RPU, bool GROUP, int RB>

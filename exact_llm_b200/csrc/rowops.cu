@@ -34,6 +34,7 @@ __global__ void k_embed(const int8_t* __restrict__ emb, int shift, const int32_t
   const int8_t* e = emb + (size_t)ids[r] * D;
   for (int i = threadIdx.x; i < D; i += blockDim.x) x[(size_t)r * D + i] = (int64_t)e[i] << shift;
   pdl_launch_dependents();
+  tl_exit();
 }
 
 cudaError_t launch_embed(const int8_t* emb, int emb_shift, const int32_t* ids, int R, int D, int64_t* x,
@@ -49,6 +50,7 @@ __global__ void k_embed64(const int64_t* __restrict__ emb, const int32_t* __rest
   const int64_t* e = emb + (size_t)ids[r] * D;
   for (int i = threadIdx.x; i < D; i += blockDim.x) x[(size_t)r * D + i] = e[i];
   pdl_launch_dependents();
+  tl_exit();
 }
 
 cudaError_t launch_embed64(const int64_t* emb, const int32_t* ids, int R, int D, int64_t* x, cudaStream_t st,
@@ -79,6 +81,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_embed_norm(const int8_t* __rest
     m = a > m ? a : m;
   }
   row_norm_q_staged<ROW_THREADS>(g, D, xq + (size_t)r * ldq, xs + r, ys, red, m);
+  tl_exit();
 }
 
 cudaError_t launch_embed_norm(const int8_t* emb, const int64_t* emb_q16, int emb_shift, const int32_t* ids, int R,
@@ -116,6 +119,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restric
   row_norm_q_any<ROW_THREADS>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, ys, red);
   if (dig)   // the row was written by this CTA (visible after the function's final barrier)
     for (int i = threadIdx.x; i < D; i += ROW_THREADS) put_digits(dig, D, r, i, xq[(size_t)r * ldq + i]);
+  tl_exit();
 }
 
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
@@ -139,6 +143,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_quant(const int64_t* __restrict
   pdl_launch_dependents();
   const int r = blockIdx.x;
   row_quant<ROW_THREADS>(x + (size_t)r * ldx, K, xq + (size_t)r * ldq, xs + r, ys, red);
+  tl_exit();
 }
 
 cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, int ldq, int32_t* xs,
@@ -177,6 +182,7 @@ __global__ void __launch_bounds__(256) k_quant_known(const int64_t* __restrict__
     if (dig) { put_digits(dig, K, r, 2 * i, q.x); put_digits(dig, K, r, 2 * i + 1, q.y); }
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) xs[r] = s;
+  tl_exit();
 }
 
 cudaError_t launch_quant_known(const int64_t* x, int ldx, int R, int K, const unsigned long long* amax, int16_t* xq,
@@ -211,6 +217,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_requant_ch(const int64_t* __res
     *o = resid ? (int64_t)((uint64_t)*o + (uint64_t)y) : y;
   }
   pdl_launch_dependents();
+  tl_exit();
 }
 
 cudaError_t launch_requant_channel(const int64_t* acc, int ld, int R, const LinW& L, int64_t* out, int ldo,
@@ -260,6 +267,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_head_rows(const int64_t* __rest
       if (bv_s[w] > bv || (bv_s[w] == bv && bn_s[w] < bn)) { bv = bv_s[w]; bn = bn_s[w]; }
     next[r] = bn;
   }
+  tl_exit();
 }
 
 cudaError_t launch_head_rows(const int64_t* acc, int ld, int R, const LinW& L, const int32_t* xs, int64_t* logits,
