@@ -172,6 +172,7 @@ EXB_DEV int64_t block_sum_i64(int64_t v, uint64_t* red) {
 EXB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 EXB_DEV void tl_exit() {}
 EXB_DEV void tl_start() {}
+EXB_DEV void tl_point(int) {}
 #else
 // Timeline build (compiled with -DEXB_TIMELINE; never the shipped library): each kernel of a
 // step stamps %globaltimer into slot `seq` of a device buffer -- earliest CTA arrival at the
@@ -180,9 +181,13 @@ EXB_DEV void tl_start() {}
 constexpr int TL_SLOTS = 4096;
 struct TlBuf {
   unsigned long long seq, cnt, pad[2];
-  unsigned long long t[TL_SLOTS][4];      // enter (min), waited (min), exit (max), CTAs
+  unsigned long long t[TL_SLOTS][8];      // enter (min), waited (min), exit (max), CTAs, enter (max),
+                                          // waited (max), exit (min), spare
+  unsigned long long pt[TL_SLOTS][16];    // in-kernel points: 0-7 min over CTAs, 8-15 max
 };
 static __device__ TlBuf* g_tlb = nullptr;
+static __shared__ unsigned long long tl_slot;    // this kernel's slot, read once at the wait
+static __shared__ TlBuf* tl_buf;                 // g_tlb, read once at the wait
 EXB_DEV unsigned long long tl_now() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -192,10 +197,15 @@ EXB_DEV unsigned long long tl_seq() {
   return *reinterpret_cast<volatile unsigned long long*>(&g_tlb->seq) % TL_SLOTS;
 }
 EXB_DEV void tl_mark(unsigned long long t0) {
+  if (threadIdx.x == 0 && threadIdx.y == 0) tl_buf = g_tlb;
   if (g_tlb && threadIdx.x == 0 && threadIdx.y == 0) {
     const unsigned long long q = tl_seq();
+    tl_slot = q;
+    const unsigned long long t1 = tl_now();
     atomicMin(&g_tlb->t[q][0], t0);
-    atomicMin(&g_tlb->t[q][1], tl_now());
+    atomicMin(&g_tlb->t[q][1], t1);
+    atomicMax(&g_tlb->t[q][4], t0);
+    atomicMax(&g_tlb->t[q][5], t1);
   }
 }
 EXB_DEV void pdl_wait() {
@@ -204,11 +214,23 @@ EXB_DEV void pdl_wait() {
   tl_mark(t0);
 }
 EXB_DEV void tl_start() { tl_mark(tl_now()); }     // kernels launched without a dependency wait
+EXB_DEV void tl_point(int i) {                       // thread 0 of each CTA passed point i (0..7)
+  if (threadIdx.x == 0 && threadIdx.y == 0) {
+    const unsigned long long t = tl_now();
+    TlBuf* b = tl_buf;
+    if (!b) return;
+    const unsigned long long q = tl_slot % TL_SLOTS;
+    atomicMin(&b->pt[q][i], t);
+    atomicMax(&b->pt[q][8 + i], t);
+  }
+}
 EXB_DEV void tl_exit() {
   __syncthreads();
   if (g_tlb && threadIdx.x == 0 && threadIdx.y == 0) {
+    const unsigned long long te = tl_now();      // stamp first: the slot read below has latency
     const unsigned long long q = tl_seq();
-    atomicMax(&g_tlb->t[q][2], tl_now());
+    atomicMax(&g_tlb->t[q][2], te);
+    atomicMin(&g_tlb->t[q][6], te);
     atomicAdd(&g_tlb->t[q][3], 1ull);
     __threadfence();
     const unsigned long long nb = (unsigned long long)gridDim.x * gridDim.y * gridDim.z;
@@ -273,5 +295,15 @@ EXB_DEV void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes, uint64_t*
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// lane-private asynchronous copies global -> shared (completion tracked per thread in groups)
+EXB_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+EXB_DEV void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+EXB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+EXB_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 EXB_DEV void named_sync(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
 }  // namespace exb

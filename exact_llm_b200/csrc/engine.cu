@@ -1686,7 +1686,7 @@ int exb_moe_selections(exb_model* m, int layer, int32_t* host, int64_t n) {
 
 #ifdef EXB_TIMELINE
 // Timeline build only: op 0 installs a zeroed stamp buffer in every translation unit, op 1
-// resets it, op 2 copies n x 4 stamps (enter, waited, exit, CTAs) to `host`.
+// resets it, op 2 copies n x 8 stamps (see TlBuf) to `host`.
 int exb_timeline(int op, uint64_t* host, int n) {
   static TlBuf* buf = nullptr;
   if (op == 0 && !buf) {
@@ -1697,12 +1697,17 @@ int exb_timeline(int op, uint64_t* host, int n) {
   if (!buf) FAIL(EXB_EINVAL, "timeline not installed");
   if (op <= 1) {
     std::vector<unsigned long long> h(sizeof(TlBuf) / 8, 0);
-    for (int i = 0; i < TL_SLOTS; ++i) h[4 + 4 * i] = h[5 + 4 * i] = ~0ull;
+    for (int i = 0; i < TL_SLOTS; ++i) h[4 + 8 * i] = h[5 + 8 * i] = h[10 + 8 * i] = ~0ull;
+    for (int i = 0; i < TL_SLOTS; ++i)
+      for (int f = 0; f < 8; ++f) h[4 + 8 * TL_SLOTS + 16 * i + f] = ~0ull;
     CK(cudaMemcpy(buf, h.data(), sizeof(TlBuf), cudaMemcpyHostToDevice));
     return EXB_OK;
   }
   if (n > TL_SLOTS) n = TL_SLOTS;
-  CK(cudaMemcpy(host, reinterpret_cast<char*>(buf) + 32, (size_t)n * 32, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(host, reinterpret_cast<char*>(buf) + 32, (size_t)n * 64, cudaMemcpyDeviceToHost));
+  if (op == 3)   // in-kernel points follow the stamps in `host`
+    CK(cudaMemcpy(host + (size_t)n * 8, reinterpret_cast<char*>(buf) + 32 + (size_t)TL_SLOTS * 64, (size_t)n * 128,
+                  cudaMemcpyDeviceToHost));
   return EXB_OK;
 }
 #endif

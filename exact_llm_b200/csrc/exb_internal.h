@@ -82,6 +82,9 @@ struct GemvArgs {
   const int64_t* gain = nullptr;                // XIN_NORM gains
   const unsigned long long* amax_in = nullptr;  // XIN_QUANT per-row max |x|
   int rb = 0;                                   // columns per warp block (0: chosen by the launcher)
+  int pre = -1;                                 // first load batch copied to shared memory before the
+                                                // PDL wait: -1 where two CTAs per SM still fit, 0 never
+  int pre_off = 0;                              // set by the launcher: byte offset of that area
   unsigned long long* amax_out = nullptr;       // epilogue: per-row max |output| (atomicMax)
   unsigned long long* zero = nullptr; int nzero = 0;   // CTA 0 clears these words (for a later producer)
   int tail = TAIL_NONE;

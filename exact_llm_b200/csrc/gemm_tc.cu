@@ -59,6 +59,8 @@ struct TcArgs {
   const int32_t* silu_t = nullptr;
   int* err = nullptr;
   // decode extras
+  int act_fast = 0;                   // grid.x indexes activation tiles (CTAs resident together
+                                      // share a weight tile, read from HBM once), grid.y weight tiles
   int ksplit = 1;                     // CTAs sharing one 128-row tile over the 128-groups
   int64_t* tot_buf = nullptr;         // (T, N) int64 partial sums (zero between uses)
   unsigned int* tickets = nullptr;    // (N / 128) last-CTA counters (zero between uses)
@@ -169,8 +171,9 @@ __global__ void __launch_bounds__(TcGeo<BN>::THREADS, 1)
   __shared__ int abort_sh, issued_sh, consumed_sh, last_sh;
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tm = blockIdx.x;
-  const int tn = a.ksplit > 1 ? 0 : (int)blockIdx.y;      // split-K: grid.y indexes K ranges
+  const bool af = a.act_fast && a.ksplit <= 1;
+  const int tm = af ? (int)blockIdx.y : (int)blockIdx.x;
+  const int tn = a.ksplit > 1 ? 0 : (af ? (int)blockIdx.x : (int)blockIdx.y);   // split-K: grid.y = K ranges
   const int ks = a.ksplit > 1 ? (int)blockIdx.y : 0;
   const int G = a.K >> 7;
   const int g0 = (int)((long long)G * ks / a.ksplit), g1 = (int)((long long)G * (ks + 1) / a.ksplit);
@@ -476,8 +479,11 @@ cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32
     a.zero = dec->zero; a.nzero = dec->nzero;
     return tc_launch<8>(dim3(L.N / TC_BM, a.ksplit), mA, mLo, mHi, a, dec->pdl, st);
   }
-  if (BN == 128) return tc_launch<128>(dim3(L.N / TC_BM, Tpad / 128), mA, mLo, mHi, a, false, st);
-  return tc_launch<64>(dim3(L.N / TC_BM, (T + 63) / 64), mA, mLo, mHi, a, false, st);
+  // activation tiles fastest: the CTAs resident together cover a few weight tiles x every
+  // activation tile, so each weight byte comes from HBM once and the activations stay in L2
+  a.act_fast = 1;
+  if (BN == 128) return tc_launch<128>(dim3(Tpad / 128, L.N / TC_BM), mA, mLo, mHi, a, false, st);
+  return tc_launch<64>(dim3((T + 63) / 64, L.N / TC_BM), mA, mLo, mHi, a, false, st);
 }
 
 }  // namespace exb

@@ -32,6 +32,7 @@ constexpr int NCW = 16;                         // warps per CTA
 constexpr int GEMV_THREADS = 32 * NCW;          // 2 CTAs per SM (64 registers per thread)
 constexpr int PREFETCH_BYTES = 64 * 1024;       // per-CTA L2 prefetch before the PDL wait
 constexpr int DYN_SMEM_MAX = 200 * 1024;        // dynamic shared memory budget of one CTA
+constexpr int PRE_SMEM_MAX = 104 * 1024;        // with the pre-wait area: two CTAs still fit one SM
 
 template <int R, int RPU, bool GROUP, int RB>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
@@ -59,6 +60,46 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     bytes = bytes > PREFETCH_BYTES ? PREFETCH_BYTES : bytes;
     for (size_t off = 0; off < bytes; off += 16384)
       prefetch_l2_bulk(w0 + off, (uint32_t)(bytes - off < 16384 ? bytes - off : 16384));
+  }
+
+  // The group scales, per-channel multipliers and biases of this CTA's columns are weights too:
+  // one 128-byte line per thread into L2 before the wait, so the epilogue never waits on HBM.
+  if (uhi > ulo) {
+    const int n0 = ulo * RPU, n1 = uhi * RPU;
+    int t = threadIdx.x;
+    auto pf_lines = [&](const void* p0, const void* p1) {
+      const uintptr_t a0 = reinterpret_cast<uintptr_t>(p0) & ~(uintptr_t)127;
+      const int nl = (int)((reinterpret_cast<uintptr_t>(p1) - a0 + 127) >> 7);
+      if (t >= 0 && t < nl) asm volatile("prefetch.global.L2 [%0];" ::"l"(a0 + ((uintptr_t)t << 7)));
+      t -= nl;
+    };
+    if (GROUP) pf_lines(a.L.Mg + (size_t)n0 * ldm, a.L.Mg + (size_t)n1 * ldm);
+    if (a.L.Mc) pf_lines(a.L.Mc + n0, a.L.Mc + n1);
+    if (a.L.b) pf_lines(a.L.b + n0, a.L.b + n1);
+  }
+
+  // Weights never depend on the previous kernel either: each warp's first load batch (its first
+  // column's first CPL chunks per lane) is copied to a lane-private shared-memory area before the
+  // wait, its group scales held in registers, so the first round of HBM latency overlaps the
+  // previous kernel instead of following it.
+  const int nblk = (uhi - ulo + RB - 1) / RB;
+  const bool pre = a.pre_off > 0 && warp < nblk;
+  int4* pre_s = reinterpret_cast<int4*>(smem_raw + a.pre_off) + (size_t)warp * CPL * 32;
+  int32_t* pre_m = reinterpret_cast<int32_t*>(reinterpret_cast<int4*>(smem_raw + a.pre_off) + (size_t)NCW * CPL * 32) +
+                   (size_t)warp * CPL * 32;
+  if (pre) {
+    const int n = (ulo + warp * RB) * RPU;
+    const int4* wrow = reinterpret_cast<const int4*>(a.L.w + (size_t)n * K);
+    const int32_t* mrow = GROUP ? a.L.Mg + (size_t)n * ldm : nullptr;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      const int ch = lane + 32 * i;
+      if (ch < C) {
+        cp_async16(pre_s + i * 32 + lane, wrow + ch);
+        if (GROUP) cp_async4(pre_m + i * 32 + lane, mrow + (ch >> 3));
+      }
+    }
+    cp_async_commit();
   }
 
   if (lane < RB)
@@ -94,12 +135,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     }
   }
   __syncthreads();
+  tl_point(0);
   pdl_launch_dependents();
   int sh[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) sh[r] = sh_s[r];
 
-  const int nblk = (uhi - ulo + RB - 1) / RB;
   for (int blk = warp; blk < nblk; blk += NCW) {
     const int u0 = ulo + blk * RB;
     int64_t acc[RB][PAY];
@@ -119,15 +160,26 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
           for (int c0 = 0; c0 < C; c0 += 32 * CPL) {
             int4 wv[CPL];
             int32_t mv[CPL];
+            if (b == 0 && q == 0 && pre && c0 == 0 && blk == warp) {
+              cp_async_wait<0>();                      // this lane's own copies
+              tl_point(3);
 #pragma unroll
-            for (int i = 0; i < CPL; ++i) {
-              const int ch = c0 + lane + 32 * i;
-              if (ch < C) {
-                wv[i] = ldg_stream(wrow + ch);
-                mv[i] = GROUP ? __ldg(mrow + (ch >> 3)) : 1;
-              } else {
-                wv[i] = make_int4(0, 0, 0, 0);
-                mv[i] = 0;
+              for (int i = 0; i < CPL; ++i) {
+                const int ch = lane + 32 * i;
+                wv[i] = ch < C ? pre_s[i * 32 + lane] : make_int4(0, 0, 0, 0);
+                mv[i] = ch < C ? (GROUP ? pre_m[i * 32 + lane] : 1) : 0;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < CPL; ++i) {
+                const int ch = c0 + lane + 32 * i;
+                if (ch < C) {
+                  wv[i] = ldg_stream(wrow + ch);
+                  mv[i] = GROUP ? __ldg(mrow + (ch >> 3)) : 1;
+                } else {
+                  wv[i] = make_int4(0, 0, 0, 0);
+                  mv[i] = 0;
+                }
               }
             }
 #pragma unroll
@@ -148,7 +200,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
         }
       }
     }
+    if (blk == warp) tl_point(4);
     warp_reduce_halving<RB, PAY>(acc);
+    if (blk == warp) tl_point(5);
     // lane b * (32 / RB) holds the totals of column block entry b: run its epilogue
     if ((lane & (32 / RB - 1)) == 0) {
       const int b = lane / (32 / RB);
@@ -163,8 +217,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
         }
       }
     }
+    if (blk == warp) tl_point(6);
   }
   __syncwarp();
+  tl_point(1);
   // fold this warp's epilogue states (one per column-block entry) into lane-0 values
   uint64_t omax[R];
   int64_t best_v[R];
@@ -186,6 +242,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     }
   }
   __syncthreads();
+  tl_point(2);
 
   // ---- per-row max |output| for the consumer's qrow (SwiGLU output)
   if (a.amax_out) {
@@ -360,6 +417,17 @@ cudaError_t launch_gemv(const GemvArgs& a0, cudaStream_t st, bool pdl) {
   if (a.xin == XIN_NORM) smem += (size_t)a.L.K * 16;                                       // row + gains
   if (a.tail == TAIL_NORM && smem < (size_t)a.tail_K * 16) smem = (size_t)a.tail_K * 16;   // tail stages row + gains
   if (smem > DYN_SMEM_MAX) return cudaErrorInvalidValue;
+  a.pre_off = 0;
+  if (a.pre != 0) {
+    // the pre-wait area: NCW warps x CPL chunks x 32 lanes x 16 bytes, when two CTAs per SM fit
+    const size_t off = (smem + 127) & ~(size_t)127;
+    const int rb_eff = a.R == 1 ? a.rb : (a.R == 2 ? 2 : 1);     // the RB launch_r instantiates
+    const size_t bytes = (size_t)NCW * (rb_eff == 1 ? 8 : 4) * 32 * 20;   // 16-byte chunk + its scale
+    if (off + bytes <= PRE_SMEM_MAX) {
+      a.pre_off = (int)off;
+      smem = off + bytes;
+    }
+  }
   if (RPU == 2) return group ? launch_r<2, true>(a, smem, st, pdl) : launch_r<2, false>(a, smem, st, pdl);
   return group ? launch_r<1, true>(a, smem, st, pdl) : launch_r<1, false>(a, smem, st, pdl);
 }

@@ -53,14 +53,6 @@ constexpr int ATT_TT = 32;                     // key/value positions staged per
 #endif
 constexpr int STEP_RING = EXB_STEP_RING;       // cp.async ring depth per lane (16-byte chunks in flight)
 
-// lane-private asynchronous copies global -> shared (completion tracked per thread in groups)
-EXB_DEV void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-EXB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-EXB_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 EXB_DEV unsigned ld_acquire_u32(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
