@@ -26,7 +26,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (7B-arch, bs1) as % HBM roofline; prefill int8 TOPS; bit-exact"
 PROMPT = 512
-GU_TRAFFIC = 140.154112e6 + 3.357952e6      # bytes per launch of the 7B gate|up GEMV (one ncu capture)
+GU_TRAFFIC = 140.154624e6 + 6.384128e6      # bytes per launch of the 7B gate|up GEMV (one ncu capture)
 
 
 def peaks():
@@ -353,7 +353,7 @@ def run_ours(a, rank, world, local_rank):
                      "achieved": kern_gbs, "peak": hbm, "unit": "GB/s", "frac": kern_gbs / hbm,
                      "traffic": GU_TRAFFIC if a.model == "qwen2.5-7b" and B == 1 else None,   # R=1 capture
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this kernel, "
-                                       "profiles/gemv_gate_up_7b_r1.md",
+                                       "profiles/gemv_gate_up_7b_bs1.md",
                      "avg_launch_ms": avg.value, "algorithmic_bytes": nbytes.value,
                      "peak_source": src},
         "prefill": prefill,
