@@ -51,6 +51,10 @@ SIGNATURES = {
     "exb_trace_enable": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "exb_trace_row_len": (ctypes.c_int64, [ctypes.c_void_p]),
     "exb_trace_read": (ctypes.c_int, [ctypes.c_void_p, c_i64p, ctypes.c_int64]),
+    "exb_commit_begin": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
+    "exb_commit_root": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_int64]),
+    "exb_commit_end": (ctypes.c_int, [ctypes.c_void_p]),
     "exb_freivalds_set_keys": (ctypes.c_int, [ctypes.c_void_p, c_i32p, ctypes.c_int64]),
     "exb_freivalds_read_keys": (ctypes.c_int, [ctypes.c_void_p, c_i32p, ctypes.c_int64]),
     "exb_freivalds_enable": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),

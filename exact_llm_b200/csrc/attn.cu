@@ -390,6 +390,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
               const int16_t v16 = qrow_value(kv[q], sh);
               ktile[(size_t)t * TP + d] = v16;
               if (writer) a.kc[cidx * HD + d] = v16;
+              if (writer && a.kr_out) a.kr_out[(size_t)r2 * a.ldkr + (size_t)j * HD + d] = kv[q];   // roped K
             }
           }
           if (lane == 0) {
@@ -407,6 +408,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
               if (v > INT32_MAX || v < INT32_MIN) set_err(a.err, ERR_V_RANGE);
               vtile[(size_t)t * HD + d] = (int32_t)v;
               if (writer) a.vc[cidx * HD + d] = (int32_t)v;
+              if (writer && a.kr_out) a.kr_out[(size_t)r2 * a.ldkr + (size_t)(a.KV + j) * HD + d] = v;
             }
           }
         }

@@ -106,6 +106,14 @@ struct exb_model {
   int head_grid = 0;
   int sms = 148;
   int64_t* trace = nullptr; int64_t trace_row = 0;
+  // Merkle trace commitment: per-row capture of X (NL+1 rows of D) and the roped K | V of every
+  // layer (2 KV hd), appended with the trace row to a device log indexed by position
+  bool commit_on = false; int commit_seq = 0; int commit_cap = 0;
+  int64_t cap_row = 0;
+  int64_t* cap = nullptr;               // (RMAX, cap_row), arena
+  int* commit_npos = nullptr;           // device: 1 + the largest logged position, arena
+  int64_t* commit_log = nullptr;        // (commit_cap, trace_row + cap_row), allocated by exb_commit_begin
+  int64_t* commit_lin = nullptr;        // device: accumulator offsets | lengths in the trace row
   unsigned long long* fr_acc = nullptr;
   int* fr_fail = nullptr; int* err = nullptr;
   int16_t* kc = nullptr; int8_t* ks = nullptr; int32_t* vc = nullptr;
@@ -300,6 +308,9 @@ static void plan_runtime(exb_model* m) {
   m->head_part = ralloc<unsigned long long>(m, (size_t)m->head_grid * RMAX * 2);
   m->head_ticket = ralloc<unsigned int>(m, 1);
   m->trace = ralloc<int64_t>(m, (size_t)RMAX * m->trace_row);
+  m->cap_row = (int64_t)(c.NL + 1) * c.D + (int64_t)c.NL * 2 * c.KV * c.hd;
+  m->cap = ralloc<int64_t>(m, (size_t)RMAX * m->cap_row);
+  m->commit_npos = ralloc<int>(m, 1);
   m->fr_acc = ralloc<unsigned long long>(m, (size_t)m->n_lin * RMAX * 4);
   m->fr_fail = ralloc<int>(m, 1);
   m->err = ralloc<int>(m, 1);
@@ -439,6 +450,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
   const exb_config& c = m->c;
   const bool pdl = m->pdl && !g_prof;
   const bool tp = m->tp > 1;
+  const bool cm = m->commit_on;        // trace commitment capture (implies trace capture)
   const bool tcd = m->tc_decode && m->group && !m->trace_on && !m->fr_on && !tp && !c.n_experts && R <= TC_DECODE_ROWS &&
                    gemm_tc_supported(m->L[0].qkv, EPI_STORE) && gemm_tc_supported(m->L[0].o, EPI_RESID) &&
                    gemm_tc_supported(m->L[0].gu, EPI_SWIGLU) && gemm_tc_supported(m->L[0].down, EPI_RESID);
@@ -558,8 +570,10 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     // producer's published max at level 1, also the norm at level 2) while its first weight bytes
     // stream into L2
     const bool fz = m->fuse_in >= 1 && !m->fr_on;          // o and down: qrow in the prologue
-    const bool fzn = m->fuse_in >= 2 && !m->fr_on;         // q|k|v and gate|up: norm in the prologue
-    if (!fzn) RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    const bool fzn = m->fuse_in >= 2 && !m->fr_on && !cm;  // q|k|v and gate|up: norm in the prologue
+    if (!fzn)
+      RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, nullptr,
+                        cm ? m->cap + (size_t)i * c.D : nullptr, m->cap_row));
     {
       GemvArgs g; base(g, Ld.qkv);
       if (fzn) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g1; }
@@ -568,7 +582,9 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       set_fr(g, {Ld.li[0], Ld.li[1], Ld.li[2]});
       RUN(launch_gemv(g, st, pdl));
     }
-    if (m->attn_fused) {
+    if (m->attn_fused || cm) {
+      aa.kr_out = cm ? m->cap + (size_t)(c.NL + 1) * c.D + (size_t)i * 2 * c.KV * c.hd : nullptr;
+      aa.ldkr = m->cap_row;
       RUN(launch_attn_rope(aa, st, pdl));
     } else {
       RUN(launch_rope_cache(aa, st, pdl));
@@ -618,8 +634,10 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.down.b, m->x, c.D, st));
     }
   }
-  const bool fzh = m->fuse_in >= 2 && !m->fr_on;
-  if (!fzh) RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+  const bool fzh = m->fuse_in >= 2 && !m->fr_on && !cm;
+  if (!fzh)
+    RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, nullptr,
+                      cm ? m->cap + (size_t)c.NL * c.D : nullptr, m->cap_row));
   {
     GemvArgs g;
     g.L = m->head; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
@@ -640,6 +658,9 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
   }
   if (m->fr_on) RUN(launch_fr_check(m->fr_acc, m->n_lin * RMAX, m->fr_fail, m->err, st, false));
   // note: fr_acc rows beyond R stay zero and compare equal
+  if (cm)
+    RUN(launch_commit_log(R, seq, pos, m->commit_seq, m->trace, m->trace_row, m->cap, m->cap_row, m->commit_log,
+                          m->commit_cap, m->commit_npos, m->err, st));
 #undef RUN
   return cudaSuccess;
 }
@@ -676,6 +697,7 @@ static int run_step(exb_model* m, int R, const int32_t* ids, const int32_t* seq,
   }
   const uint64_t key = ((uint64_t)R) | ((uint64_t)(want_logits ? 1 : 0) << 8) | ((uint64_t)(advanceB) << 9) |
                        ((uint64_t)(m->trace_on ? 1 : 0) << 20) | ((uint64_t)(m->fr_on ? 1 : 0) << 21) |
+                       ((uint64_t)(m->commit_on ? 1 : 0) << 22) |
                        ((uint64_t)((const char*)ids - (const char*)m->rarena) << 24);
   auto it = m->graphs.find(key);
   if (it == m->graphs.end()) {
@@ -962,6 +984,8 @@ void exb_model_destroy(exb_model* m) {
   if (m->st) cudaStreamSynchronize(m->st);
   cudaFree(m->warena);
   cudaFree(m->rarena);
+  cudaFree(m->commit_log);
+  cudaFree(m->commit_lin);
   cudaFree(m->gen_tokens);
   cudaFree(m->emb_q16);
   if (m->comm && nccl()) nccl()->comm_destroy(m->comm);
@@ -1560,6 +1584,85 @@ int exb_trace_enable(exb_model* m, int on) {
   return EXB_OK;
 }
 int64_t exb_trace_row_len(exb_model* m) { return m ? m->trace_row : -1; }
+// ---- Merkle trace commitment
+int exb_commit_begin(exb_model* m, int seq, int capacity) {
+  if (!m || !m->finalized) FAIL(EXB_EINVAL, "exb_commit_begin: model not finalized");
+  if (m->c.n_experts) FAIL(EXB_EINVAL, "exb_commit_begin: the commitment covers the dense models");
+  if (m->tp > 1) FAIL(EXB_EINVAL, "exb_commit_begin: single-GPU models only");
+  if (seq < 0 || seq >= m->c.max_batch || capacity < 1 || capacity > m->c.max_seq)
+    FAIL(EXB_EINVAL, "exb_commit_begin: seq in [0, max_batch), capacity in [1, max_seq]");
+  const size_t row = (size_t)(m->trace_row + m->cap_row);
+  CK(cudaStreamSynchronize(m->st));
+  cudaFree(m->commit_log);
+  m->commit_log = nullptr;
+  if (cudaMalloc(&m->commit_log, row * capacity * sizeof(int64_t)) != cudaSuccess) {
+    cudaGetLastError();
+    FAIL(EXB_ECUDA, "exb_commit_begin: no device memory for " + std::to_string(capacity) + " log rows of " +
+                        std::to_string(row * 8) + " bytes");
+  }
+  if (!m->commit_lin) {
+    std::vector<int64_t> h(2 * m->lins.size());
+    for (size_t i = 0; i < m->lins.size(); ++i) {
+      h[i] = m->lins[i].trace_off;
+      h[m->lins.size() + i] = m->lins[i].N;
+    }
+    CK(cudaMalloc(&m->commit_lin, h.size() * sizeof(int64_t)));
+    CK(cudaMemcpy(m->commit_lin, h.data(), h.size() * sizeof(int64_t), cudaMemcpyHostToDevice));
+  }
+  CK(cudaMemsetAsync(m->commit_npos, 0, sizeof(int), m->st));
+  m->commit_on = true;
+  m->trace_on = true;
+  m->commit_seq = seq;
+  m->commit_cap = capacity;
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  m->graphs.clear();
+  return EXB_OK;
+}
+
+int exb_commit_root(exb_model* m, int T, uint8_t* root32, uint8_t* leaves_host, int64_t leaves_bytes) {
+  if (!m || !root32) FAIL(EXB_EINVAL, "null argument");
+  if (!m->commit_on) FAIL(EXB_EINVAL, "exb_commit_root: call exb_commit_begin first");
+  if (T < 1 || T > m->commit_cap) FAIL(EXB_EINVAL, "exb_commit_root: T in [1, capacity]");
+  const exb_config& c = m->c;
+  const int64_t n = commit_leaf_count(c.NL, T);
+  if (leaves_host && leaves_bytes != n * 32)
+    FAIL(EXB_EINVAL, "exb_commit_root: leaves buffer must hold " + std::to_string(n * 32) + " bytes");
+  int npos = 0;
+  CK(cudaMemcpyAsync(&npos, m->commit_npos, sizeof(int), cudaMemcpyDeviceToHost, m->st));
+  CK(cudaStreamSynchronize(m->st));
+  if (npos < T) FAIL(EXB_EINVAL, "exb_commit_root: only positions 0.." + std::to_string(npos - 1) + " were logged");
+  CommitLayout L;
+  L.NL = c.NL; L.D = c.D; L.KV = c.KV; L.hd = c.hd;
+  L.x_off = m->trace_row;
+  L.kr_off = m->trace_row + (int64_t)(c.NL + 1) * c.D;
+  L.lin_off = m->commit_lin;
+  L.lin_len = m->commit_lin + m->lins.size();
+  uint8_t* buf = nullptr;
+  const size_t lv = (size_t)n * 32;
+  CK(cudaMalloc(&buf, 3 * lv));
+  uint8_t* root_dev = nullptr;
+  cudaError_t e = commit_root(m->commit_log, m->trace_row + m->cap_row, T, L, buf, buf + lv, buf + 2 * lv, &root_dev,
+                              m->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(root32, root_dev, 32, cudaMemcpyDeviceToHost, m->st);
+  if (e == cudaSuccess && leaves_host) e = cudaMemcpyAsync(leaves_host, buf, lv, cudaMemcpyDeviceToHost, m->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->st);
+  cudaFree(buf);
+  if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("exb_commit_root: ") + cudaGetErrorString(e));
+  return check_device_errors(m);
+}
+
+int exb_commit_end(exb_model* m) {
+  if (!m) FAIL(EXB_EINVAL, "null model");
+  CK(cudaStreamSynchronize(m->st));
+  cudaFree(m->commit_log);
+  m->commit_log = nullptr;
+  m->commit_on = false;
+  m->commit_cap = 0;
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  m->graphs.clear();
+  return EXB_OK;
+}
+
 int exb_trace_read(exb_model* m, int64_t* host, int64_t n) {
   if (!m || !host) FAIL(EXB_EINVAL, "null argument");
   const int64_t have = (int64_t)m->trace_host.size();

@@ -47,6 +47,7 @@ struct AttnArgs {
   unsigned long long* amax_out = nullptr;       // per-row max |out| (atomicMax), for the next qrow
   unsigned int* ticket = nullptr;
   int16_t* xq_out = nullptr; int ldq = 0; int32_t* xs_out = nullptr;   // last CTA: qrow(out) rows
+  int64_t* kr_out = nullptr; int64_t ldkr = 0;  // trace commitment: roped K | V rows (R, 2 KV hd)
   int* err = nullptr;
 };
 enum Epi {
@@ -138,8 +139,25 @@ cudaError_t launch_embed(const int8_t* emb, int emb_shift, const int32_t* ids, i
 cudaError_t launch_embed64(const int64_t* emb_q16, const int32_t* ids, int R, int D, int64_t* x, cudaStream_t st,
                            bool pdl);
 // dig (optional): int8 digit planes of the rows for the tensor-core decode GEMM (TC_DECODE_ROWS-row planes)
+// xcap (optional): a copy of each input row x (row stride ldcap), for the trace commitment
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
-                          int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig = nullptr);
+                          int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig = nullptr, int64_t* xcap = nullptr,
+                          int64_t ldcap = 0);
+
+// ---- Merkle trace commitment (csrc/commit.cu)
+struct CommitLayout {
+  int NL = 0, D = 0, KV = 0, hd = 0;
+  int64_t x_off = 0;                  // X[0..NL] (D each) within a log row
+  int64_t kr_off = 0;                 // roped K | V of every layer (2 KV hd each)
+  const int64_t* lin_off = nullptr;   // device: (7 NL + 1) accumulator offsets in the trace row
+  const int64_t* lin_len = nullptr;   // device: their lengths
+};
+inline int64_t commit_leaf_count(int NL, int T) { return (int64_t)(5 * NL + 2) * T; }
+cudaError_t launch_commit_log(int R, const int32_t* row_seq, const int32_t* row_pos, int seq, const int64_t* trace,
+                              int64_t trace_row, const int64_t* cap, int64_t cap_row, int64_t* log, int npos_cap,
+                              int* npos, int* err, cudaStream_t st);
+cudaError_t commit_root(const int64_t* log, int64_t row, int T, const CommitLayout& c, uint8_t* leaves,
+                        uint8_t* lv_a, uint8_t* lv_b, uint8_t** root_dev, cudaStream_t st);
 cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, int ldq, int32_t* xs,
                          cudaStream_t st, bool pdl);
 cudaError_t launch_quant_known(const int64_t* x, int ldx, int R, int K, const unsigned long long* amax, int16_t* xq,

@@ -110,7 +110,8 @@ EXB_DEV void put_digits(uint8_t* dig, int K, int r, int i, int16_t v) {
 __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restrict__ x, int ldx,
                                                         const int64_t* __restrict__ g, int D,
                                                         int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs,
-                                                        uint8_t* __restrict__ dig) {
+                                                        uint8_t* __restrict__ dig, int64_t* __restrict__ xcap,
+                                                        int64_t ldcap) {
   extern __shared__ int64_t ys[];
   __shared__ uint64_t red[33];
   pdl_wait();
@@ -119,11 +120,13 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restric
   row_norm_q_any<ROW_THREADS>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, ys, red);
   if (dig)   // the row was written by this CTA (visible after the function's final barrier)
     for (int i = threadIdx.x; i < D; i += ROW_THREADS) put_digits(dig, D, r, i, xq[(size_t)r * ldq + i]);
+  if (xcap)
+    for (int i = threadIdx.x; i < D; i += ROW_THREADS) xcap[(size_t)r * ldcap + i] = ld_cg(x + (size_t)r * ldx + i);
   tl_exit();
 }
 
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
-                          int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig) {
+                          int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig, int64_t* xcap, int64_t ldcap) {
   const size_t smem = (size_t)D * 16;
   static bool attr_set = false;   // raised once to the full budget, never lowered
   if (!attr_set) {
@@ -131,7 +134,8 @@ cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, in
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  void* args[] = {(void*)&x, (void*)&ldx, (void*)&g, (void*)&D, (void*)&xq, (void*)&ldq, (void*)&xs, (void*)&dig};
+  void* args[] = {(void*)&x,  (void*)&ldx, (void*)&g,   (void*)&D,    (void*)&xq,
+                  (void*)&ldq, (void*)&xs,  (void*)&dig, (void*)&xcap, (void*)&ldcap};
   return launch_simple((const void*)k_norm_q, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
 }
 

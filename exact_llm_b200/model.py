@@ -223,6 +223,23 @@ class ExactModel:
         check(lib.exb_trace_read(self.h, ptr(out, ctypes.c_int64), out.size))
         return out.reshape(n, self.trace_row_len)
 
+    def commit_begin(self, seq=0, capacity=None):
+        """Start logging sequence slot ``seq`` for the Merkle trace commitment (turns trace capture on)."""
+        check(lib.exb_commit_begin(self.h, int(seq), int(capacity or self.max_seq)))
+
+    def commit_root(self, T, leaves=False):
+        """Merkle root (32 bytes) over positions 0..T-1 of the committed sequence, computed on the
+        GPU with the reference's leaves and tree (experiments/commit_audit_kaggle.py:567-628); with
+        ``leaves=True`` also the leaf digests, shape ((5 NL + 2) T, 32) uint8."""
+        root = (ctypes.c_uint8 * 32)()
+        n = (5 * self.c["NL"] + 2) * int(T)
+        lv = np.empty((n, 32), np.uint8) if leaves else None
+        check(lib.exb_commit_root(self.h, int(T), root, lv.ctypes.data if leaves else None, n * 32 if leaves else 0))
+        return (bytes(root), lv) if leaves else bytes(root)
+
+    def commit_end(self):
+        check(lib.exb_commit_end(self.h))
+
     def linear_sizes(self):
         c = self.c
         out = []

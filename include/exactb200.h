@@ -133,6 +133,21 @@ int64_t exb_trace_row_len(exb_model* m);
 /* copy the trace of the last forward/decode step's rows (rows x row_len int64) to host */
 int exb_trace_read(exb_model* m, int64_t* host, int64_t n);
 
+/* Merkle trace commitment computed on the GPU (experiments/commit_audit_kaggle.py:567-628, which
+ * hashes on the host): exb_commit_begin turns trace capture on and logs, for every later forward or
+ * decode row of sequence slot `seq` at positions < capacity, its trace row plus the residual
+ * stream entering every layer and the final one (X) and every layer's roped K and V rows.
+ * exb_commit_root hashes the leaves of positions 0..T-1 in the reference order -- Hb(X[L][t]) for
+ * L = 0..NL, then per (L, t) Hb(k acc, v acc), Hb(roped K, V), Hb(q acc), Hb(o, gate, up, down acc),
+ * then Hb(head acc) per t, where Hb = SHA-256 over each int64 array's little-endian bytes each
+ * followed by "|" -- and builds the Merkle tree (leaf nodes SHA-256("L"+leaf), parents
+ * SHA-256("N"+left+right), an odd last node paired with itself); it writes the 32-byte root and,
+ * when leaves_host is given, the (5 NL + 2) T leaf digests (leaves_bytes must equal 32 times that).
+ * Every position 0..T-1 must have been logged.  Dense single-GPU models. */
+int exb_commit_begin(exb_model* m, int seq, int capacity);
+int exb_commit_root(exb_model* m, int T, uint8_t* root32, uint8_t* leaves_host, int64_t leaves_bytes);
+int exb_commit_end(exb_model* m);
+
 /* Freivalds self-check on every linear (experiments/gpu_engine_trace_verify_kaggle.py:803-834):
  * r_host holds, for each linear in trace order, 2 x N values in [0, p) for p = 2^31-1 and
  * 2147483629 (int32).  The device builds d_p = (W*M)^T r_p mod p and, on every later forward,

@@ -409,3 +409,74 @@ def step_digest(flat):
     step = (len(arr) + 3) // 4
     parts = [hashlib.sha256(arr[i * step:(i + 1) * step].tobytes()).digest() for i in range(4)]
     return hashlib.sha256(b"".join(parts)).digest()
+
+
+# ----------------------------------------------------------------------------- Merkle trace commitment
+def commit_trace(model, ids):
+    """One full forward of ``ids`` recording what the trace commitment covers: the residual
+    stream X entering every layer (and the final one), every linear's integer accumulator, the
+    roped K and the V rows of every layer, and the head accumulator.  Restates ``prover_trace``
+    (experiments/commit_audit_kaggle.py:587-613) without its attack hooks; a group-128 linear's
+    accumulator is its ``tot``, as in the reference's trace capture."""
+    c = model.c
+    H, KV, hd = c["H"], c["KV"], c["hd"]
+    T = len(ids)
+    x = model.emb_q16(np.asarray(ids))
+    cos, sin = model.cos[:T], model.sin[:T]
+    X, A, KR = [], [], []
+    for li, L in enumerate(model.layers):
+        X.append(x.copy())
+        tr = []
+        a = irms(x, L["g1"])
+        q = rope(L["q"](a, tr, "q").reshape(T, H, hd).transpose(1, 0, 2), cos, sin)
+        k = rope(L["k"](a, tr, "k").reshape(T, KV, hd).transpose(1, 0, 2), cos, sin)
+        v = L["v"](a, tr, "v").reshape(T, KV, hd).transpose(1, 0, 2)
+        KR.append((k.copy(), v.copy()))
+        out = model._attention(li, q, k, v, None, 0)
+        x = x + L["o"](out.transpose(1, 0, 2).reshape(T, H * hd), tr, "o")
+        m_ = irms(x, L["g2"])
+        g = L["gate"](m_, tr, "gate")
+        u = L["up"](m_, tr, "up")
+        x = x + L["down"](shr(isilu(g) * u, F), tr, "down")
+        A.append({nm: raw for nm, raw, _ in tr})
+    X.append(x.copy())
+    htr = []
+    model.head(irms(x, model.gf), htr, "head")
+    return {"X": X, "A": A, "KR": KR, "head": htr[0][1], "T": T}
+
+
+def hb(*arrs):
+    """Leaf digest: SHA-256 over each array's int64 bytes, each followed by b"|"
+    (experiments/commit_audit_kaggle.py:567-570)."""
+    hh = hashlib.sha256()
+    for a in arrs:
+        hh.update(np.ascontiguousarray(a, dtype=np.int64).tobytes())
+        hh.update(b"|")
+    return hh.digest()
+
+
+def commit_leaves(tr, NL):
+    """Leaf digests in the reference order (experiments/commit_audit_kaggle.py:614-628): X of
+    every (layer 0..NL, position), then per (layer, position) the k|v accumulators, the roped
+    K|V rows, the q accumulator and the o|gate|up|down accumulators, then the head per position."""
+    T = tr["T"]
+    leaves = [hb(tr["X"][L][t]) for L in range(NL + 1) for t in range(T)]
+    for L in range(NL):
+        a = tr["A"][L]
+        for t in range(T):
+            leaves.append(hb(a["k"][t], a["v"][t]))
+            leaves.append(hb(tr["KR"][L][0][:, t, :], tr["KR"][L][1][:, t, :]))
+            leaves.append(hb(a["q"][t]))
+            leaves.append(hb(a["o"][t], a["gate"][t], a["up"][t], a["down"][t]))
+    leaves += [hb(tr["head"][t]) for t in range(T)]
+    return leaves
+
+
+def merkle_root(leaves):
+    """Merkle root: leaf nodes SHA-256(b"L" + leaf), parents SHA-256(b"N" + left + right), an odd
+    last node paired with itself (experiments/commit_audit_kaggle.py:571-575)."""
+    lv = [hashlib.sha256(b"L" + leaf).digest() for leaf in leaves]
+    while len(lv) > 1:
+        lv = [hashlib.sha256(b"N" + lv[i] + (lv[i + 1] if i + 1 < len(lv) else lv[i])).digest()
+              for i in range(0, len(lv), 2)]
+    return lv[0]

@@ -13,6 +13,8 @@ definitions the hot path needs (the scripts' top-level code downloads checkpoint
   * ``keys_group/keys_channel/fr``     experiments/gpu_engine_trace_verify_kaggle.py:802-819, 830-834
   * the tiny preflight model           experiments/_pre_tiny.py:1-15
   * the G1 GEMV known-answer inputs    experiments/speed_fair_kaggle.py:704-708
+  * ``requant/Hb/merkle/prover_trace/leaves_of``  experiments/commit_audit_kaggle.py:442-445,
+                                      567-575, 587-628 (the Merkle trace commitment)
 
 Synthetic integer weights come from ``oracle.synth`` and are handed to the reference's
 classes through ``__new__`` (no float checkpoint is involved).  Nothing here is imported
@@ -244,6 +246,28 @@ def g_models(ex, G):
     _dense_case(ex, G, "tiny-ch", synth.config("tiny-ch"), 2, 10, 6, 4, save_npz=True)
 
 
+def g_commit(ex, G):
+    """Merkle trace commitment of one full forward, computed by the reference's own prover_trace,
+    leaves_of, Hb and merkle (experiments/commit_audit_kaggle.py:442-445, 567-575, 587-628) on the
+    per-channel tiny model over its prompt plus its greedy tokens."""
+    ns = dict(ex.__dict__)
+    ex._exec_lines("experiments/commit_audit_kaggle.py", 442, 445, ns)              # requant
+    ex._exec_lines("experiments/commit_audit_kaggle.py", 567, 575, ns)              # Hb, merkle
+    ex._exec_lines("experiments/commit_audit_kaggle.py", 587, 628, ns)              # prover_trace, leaves_of
+    cfg = synth.config("tiny-ch")
+    om = synth.build_model(cfg, 2)
+    g = G["models"]["tiny-ch"]
+    ids = [int(t) for t in g["prompt"]] + [int(t) for t in g["tokens"]]
+    rm = ref_int_model(ex, om)
+    tr = ns["prover_trace"](rm, ids)
+    index, leaves = ns["leaves_of"](tr, cfg["NL"])
+    levels = ns["merkle"](leaves)
+    G["commit"] = dict(model="tiny-ch", seed=2, ids=ids, n_leaves=len(leaves),
+                       root=levels[-1][0].hex(), leaf0=leaves[0].hex(), leaf_last=leaves[-1].hex(),
+                       leaf_sample={str(i): leaves[i].hex() for i in range(0, len(leaves), max(1, len(leaves) // 9))})
+    print("commit root", levels[-1][0].hex(), len(leaves), flush=True)
+
+
 def g_config1(ex, G):
     """0.5B architecture, 32 prompt ids, 64 greedy steps (reference full recompute)."""
     _dense_case(ex, G, "qwen2.5-0.5b", synth.config("qwen2.5-0.5b"), 5, 32, 64, 5)
@@ -327,7 +351,8 @@ def g_moe(ex, G):
 
 
 BUILDERS = dict(tables=g_tables, gemv_kat=g_gemv_kat, models=g_models, freivalds=g_freivalds,
-                pre_tiny=g_pre_tiny, moe=g_moe, linear=g_linear, config1=g_config1, big=g_big_layers)
+                pre_tiny=g_pre_tiny, moe=g_moe, linear=g_linear, config1=g_config1, big=g_big_layers,
+                commit=g_commit)
 
 
 def main():

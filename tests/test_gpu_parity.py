@@ -359,3 +359,41 @@ def test_freivalds_keys_and_self_check(golden, cuda_ok):
     m(g["prompt"])
     _, fails = m.freivalds_status()
     assert fails > 0
+
+
+def test_commit_root_matches_reference(golden, cuda_ok):
+    """Merkle trace commitment hashed on the GPU: the root of a 16-token forward of the per-channel
+    tiny model equals the root the reference's own prover_trace / leaves_of / merkle computed."""
+    g = golden["commit"]
+    om = synth.build_model(synth.config(g["model"]), g["seed"])
+    m = _engine_from_oracle(om, max_batch=1, max_seq=64)
+    m.new_cache(0)
+    m.commit_begin(0, 32)
+    m.forward(g["ids"], m.new_cache(0))
+    root, leaves = m.commit_root(len(g["ids"]), leaves=True)
+    assert leaves.shape[0] == g["n_leaves"]
+    assert leaves[0].tobytes().hex() == g["leaf0"] and leaves[-1].tobytes().hex() == g["leaf_last"]
+    for i, h in g["leaf_sample"].items():
+        assert leaves[int(i)].tobytes().hex() == h, i
+    assert root.hex() == g["root"]
+    m.commit_end()
+
+
+def test_commit_root_prefill_and_decode_match_oracle(cuda_ok):
+    """Group-128 model: positions logged by a prefill and by greedy decode steps give the root of
+    one full forward over the same tokens (the oracle restatement of the reference's commitment)."""
+    cfg = synth.config("tiny-g128")
+    om = synth.build_model(cfg, 5)
+    m = _engine_from_oracle(om, max_batch=1, max_seq=64)
+    prompt = [int(t) for t in synth.prompt_ids(11, 1, 9, cfg["V"])[0]]
+    m.commit_begin(0, 40)
+    _, _, toks = m.greedy(prompt, 6)
+    ids = prompt + toks
+    root = m.commit_root(len(ids))
+    tr = eo.commit_trace(om, ids)
+    assert root == eo.merkle_root(eo.commit_leaves(tr, cfg["NL"]))
+    # a shorter prefix commits to a different root, and positions never logged are refused
+    assert m.commit_root(len(ids) - 1) == eo.merkle_root(eo.commit_leaves(eo.commit_trace(om, ids[:-1]), cfg["NL"]))
+    with pytest.raises(RuntimeError):
+        m.commit_root(len(ids) + 1)
+    m.commit_end()

@@ -166,3 +166,19 @@ def test_moe_models(golden, key):
         assert np.array_equal(np.concatenate(stats[int(li)]), np.array(sel)), li
     pre, rows, toks = eo.greedy_generate(om, g["prompt"], len(g["tokens"]))
     assert toks == g["tokens"] and [eo.h16(r) for r in rows] == g["rows"]
+
+
+def test_commit_root_matches_reference(golden):
+    """The Merkle trace commitment restated in the oracle (X, accumulators, roped K/V and head
+    leaves, L/N-prefixed SHA-256 tree) reproduces the root the reference's own prover_trace,
+    leaves_of and merkle computed on the same integers."""
+    g = golden["commit"]
+    cfg = synth.config(g["model"])
+    om = synth.build_model(cfg, g["seed"])
+    tr = eo.commit_trace(om, g["ids"])
+    leaves = eo.commit_leaves(tr, cfg["NL"])
+    assert len(leaves) == g["n_leaves"] == (5 * cfg["NL"] + 2) * len(g["ids"])
+    assert leaves[0].hex() == g["leaf0"] and leaves[-1].hex() == g["leaf_last"]
+    for i, h in g["leaf_sample"].items():
+        assert leaves[int(i)].hex() == h
+    assert eo.merkle_root(leaves).hex() == g["root"]
