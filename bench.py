@@ -88,6 +88,51 @@ def gemm_tc_tops(K, N, T, reps=10):
     return 2.0 * T * N * K / (ms * 1e-3) / 1e12, ms
 
 
+def commit_bench(model, T, layers=0):
+    """Merkle trace commitment over T logged positions of the named architecture: the GPU root
+    (leaf SHA-256 + tree, exb_commit_root) timed against hashlib on one host core over leaves of
+    the same byte layout (the reference hashes its trace on the host)."""
+    import hashlib
+    import torch
+    from exact_llm_b200 import ExactModel, configs
+    c = configs.arch(model, **({"NL": layers} if layers else {}))
+    m = ExactModel.synthetic(c, 1234, max_batch=1, max_seq=T + 8)
+    ids = np.random.default_rng(7).integers(0, c["V"], T).astype(np.int32)
+    m.commit_begin(0, T)
+    t0 = time.perf_counter()
+    m.forward(ids, m.new_cache(0), want_logits=False)
+    torch.cuda.synchronize()
+    fwd_s = time.perf_counter() - t0
+    m.commit_root(T)                                         # warm-up (module load)
+    t0 = time.perf_counter()
+    root = m.commit_root(T)
+    gpu_s = time.perf_counter() - t0
+    NL, D, I, V, kv, q = c["NL"], c["D"], c["I"], c["V"], c["KV"] * c["hd"], c["H"] * c["hd"]
+    sizes = [[D]] * ((NL + 1) * T) + [[kv, kv], [kv, kv], [q], [D, I, I, D]] * (NL * T) + [[V]] * T
+    buf = np.random.default_rng(0).integers(-2**40, 2**40, max(V, 2 * I + 2 * D), dtype=np.int64).tobytes()
+    t0 = time.perf_counter()
+    leaves = []
+    for segs in sizes:
+        hh = hashlib.sha256()
+        for n in segs:
+            hh.update(buf[:8 * n])
+            hh.update(b"|")
+        leaves.append(hh.digest())
+    lv = [hashlib.sha256(b"L" + x).digest() for x in leaves]
+    while len(lv) > 1:
+        lv = [hashlib.sha256(b"N" + lv[i] + (lv[i + 1] if i + 1 < len(lv) else lv[i])).digest()
+              for i in range(0, len(lv), 2)]
+    host_s = time.perf_counter() - t0
+    nbytes = sum(8 * n + 1 for segs in sizes for n in segs)
+    m.commit_end()
+    m.close()
+    return {"model": model, "positions": T, "leaves": len(sizes), "hashed_bytes": nbytes,
+            "gpu_ms": round(gpu_s * 1e3, 2), "gpu_gbs": round(nbytes / gpu_s / 1e9, 2),
+            "host_1core_ms": round(host_s * 1e3, 1), "host_1core_gbs": round(nbytes / host_s / 1e9, 2),
+            "speedup": round(host_s / gpu_s, 1), "prefill_with_capture_s": round(fwd_s, 3),
+            "root": root.hex()}
+
+
 # ------------------------------------------------------------------ clocks
 class Clocks:
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
@@ -388,10 +433,15 @@ def main():
     ap.add_argument("--tp", action="store_true", help="with --gpus N under torchrun: one model split over the N GPUs")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens before decode (profiling uses a short one)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures only)")
+    ap.add_argument("--commit", type=int, default=0, metavar="T",
+                    help="only the Merkle trace commitment of T logged 7B positions: GPU vs host hashlib")
     ap.add_argument("--linear", type=int, default=0, metavar="T",
                     help="only the exact linear op at T rows on the 7B gate|up shape (profiling)")
     a = ap.parse_args()
     globals()["PROMPT"] = a.prompt
+    if a.commit:
+        print(json.dumps({"commit": commit_bench(a.model, a.commit, a.layers)}))
+        return
     if a.linear:
         import torch
         torch.cuda.set_device(0)

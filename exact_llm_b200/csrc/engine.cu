@@ -114,6 +114,12 @@ struct exb_model {
   int* commit_npos = nullptr;           // device: 1 + the largest logged position, arena
   int64_t* commit_log = nullptr;        // (commit_cap, trace_row + cap_row), allocated by exb_commit_begin
   int64_t* commit_lin = nullptr;        // device: accumulator offsets | lengths in the trace row
+  // integer sampler (exb_sampling): per-row seed and next sampling position, used by the decode
+  // steps of exb_generate / exb_generate_device instead of the greedy argmax
+  bool samp_on = false, samp_active = false;
+  int64_t samp_tnum = 1 << 16;
+  unsigned long long* samp_seed = nullptr;   // (RMAX), arena
+  int32_t* samp_pos = nullptr;               // (RMAX), arena
   unsigned long long* fr_acc = nullptr;
   int* fr_fail = nullptr; int* err = nullptr;
   int16_t* kc = nullptr; int8_t* ks = nullptr; int32_t* vc = nullptr;
@@ -311,6 +317,8 @@ static void plan_runtime(exb_model* m) {
   m->cap_row = (int64_t)(c.NL + 1) * c.D + (int64_t)c.NL * 2 * c.KV * c.hd;
   m->cap = ralloc<int64_t>(m, (size_t)RMAX * m->cap_row);
   m->commit_npos = ralloc<int>(m, 1);
+  m->samp_seed = ralloc<unsigned long long>(m, RMAX);
+  m->samp_pos = ralloc<int32_t>(m, RMAX);
   m->fr_acc = ralloc<unsigned long long>(m, (size_t)m->n_lin * RMAX * 4);
   m->fr_fail = ralloc<int>(m, 1);
   m->err = ralloc<int>(m, 1);
@@ -421,7 +429,8 @@ static int g_hist_row0 = -1;                             // selection-history ro
 static bool step_args(exb_model* m, int R, const int32_t* ids, const int32_t* seq, const int32_t* pos,
                       bool want_logits, StepArgs& a) {
   const exb_config& c = m->c;
-  if (!m->step_on || !m->group || m->trace_on || m->fr_on || m->emb_q16 || R < 1 || R > STEP_ROWS || m->tp > 1)
+  if (!m->step_on || !m->group || m->trace_on || m->fr_on || m->emb_q16 || R < 1 || R > STEP_ROWS || m->tp > 1 ||
+      m->samp_active)
     return false;
   a.layers = m->step_layers; a.NL = c.NL; a.R = R; a.D = c.D; a.H = c.H; a.KV = c.KV; a.hd = c.hd; a.I = c.I;
   a.V = c.V; a.Nqkv = m->Nqkv; a.Smax = c.max_seq; a.Tmax = c.rope_len; a.max_batch = c.max_batch;
@@ -451,6 +460,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
   const bool pdl = m->pdl && !g_prof;
   const bool tp = m->tp > 1;
   const bool cm = m->commit_on;        // trace commitment capture (implies trace capture)
+  const bool smp = m->samp_active;     // the next tokens come from the integer sampler
   const bool tcd = m->tc_decode && m->group && !m->trace_on && !m->fr_on && !tp && !c.n_experts && R <= TC_DECODE_ROWS &&
                    gemm_tc_supported(m->L[0].qkv, EPI_STORE) && gemm_tc_supported(m->L[0].o, EPI_RESID) &&
                    gemm_tc_supported(m->L[0].gu, EPI_SWIGLU) && gemm_tc_supported(m->L[0].down, EPI_RESID);
@@ -643,7 +653,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     g.L = m->head; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
     g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX;
     if (fzh) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = m->gf; }
-    g.epi = EPI_HEAD; g.out = want_logits ? m->logits : nullptr; g.ldo = tp ? m->vmax : c.V;
+    g.epi = EPI_HEAD; g.out = (want_logits || smp) ? m->logits : nullptr; g.ldo = tp ? m->vmax : c.V;
     g.raw = trace_ptr(m->n_lin - 1);
     g.head_part = m->head_part; g.head_ticket = m->head_ticket; g.next_tok = m->next_tok; g.grid = m->head_grid;
     if (tp) g.head_val = m->tp_hval;
@@ -656,6 +666,9 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     RUN(launch_tp_pick(m->tp_hval, m->tp_hmax, m->next_tok, m->v0, R, st));
     RUN(tp_allreduce(m, m->next_tok, m->next_tok, R, ncclInt32, ncclMin, st));
   }
+  if (smp)   // replaces the head's greedy choice; advances each row's sampling position
+    RUN(launch_sample(R, m->logits, c.V, c.V, m->samp_seed, m->samp_pos, true, m->samp_tnum, m->exp_t, m->next_tok,
+                      st, pdl));
   if (m->fr_on) RUN(launch_fr_check(m->fr_acc, m->n_lin * RMAX, m->fr_fail, m->err, st, false));
   // note: fr_acc rows beyond R stay zero and compare equal
   if (cm)
@@ -697,7 +710,7 @@ static int run_step(exb_model* m, int R, const int32_t* ids, const int32_t* seq,
   }
   const uint64_t key = ((uint64_t)R) | ((uint64_t)(want_logits ? 1 : 0) << 8) | ((uint64_t)(advanceB) << 9) |
                        ((uint64_t)(m->trace_on ? 1 : 0) << 20) | ((uint64_t)(m->fr_on ? 1 : 0) << 21) |
-                       ((uint64_t)(m->commit_on ? 1 : 0) << 22) |
+                       ((uint64_t)(m->commit_on ? 1 : 0) << 22) | ((uint64_t)(m->samp_active ? 1 : 0) << 23) |
                        ((uint64_t)((const char*)ids - (const char*)m->rarena) << 24);
   auto it = m->graphs.find(key);
   if (it == m->graphs.end()) {
@@ -1531,8 +1544,14 @@ static int generate_common(exb_model* m, int B, const int32_t* ids_dev_or_null, 
   if (steps > 0)
     for (int b = 0; b < B; ++b)
       if (m->seq_len[b] + steps > c.max_seq) FAIL(EXB_EINVAL, "generate: max_seq exceeded");
+  if (B > RMAX && steps > 0 && m->samp_on) FAIL(EXB_EINVAL, "generate: sampling runs batches of <= 4 rows");
   if (B > RMAX && steps > 0) return generate_wide(m, B, ids_dev_or_null, ids_host, steps, tokens_host, logits_host, tokens_dev);
   if (steps <= 0) return EXB_OK;
+  struct SampScope {                    // sampling applies to these decode steps only
+    exb_model* m;
+    explicit SampScope(exb_model* mm) : m(mm) { m->samp_active = m->samp_on; }
+    ~SampScope() { m->samp_active = false; }
+  } samp_scope(m);
   for (int b = 0; b < B; ++b)
     if (m->seq_len[b] + steps > c.max_seq) FAIL(EXB_EINVAL, "generate: max_seq exceeded");
   int rc = ensure_gen(m, B, steps);
@@ -1649,6 +1668,55 @@ int exb_commit_root(exb_model* m, int T, uint8_t* root32, uint8_t* leaves_host, 
   cudaFree(buf);
   if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("exb_commit_root: ") + cudaGetErrorString(e));
   return check_device_errors(m);
+}
+
+// ---- integer sampler
+int exb_sampling(exb_model* m, int on, int B, const uint64_t* seeds, const int32_t* positions, int64_t tnum) {
+  if (!m || !m->finalized) FAIL(EXB_EINVAL, "exb_sampling: model not finalized");
+  if (on) {
+    if (m->tp > 1) FAIL(EXB_EINVAL, "exb_sampling: single-GPU models (the logits rows are sharded under TP)");
+    if (B < 1 || B > RMAX || !seeds || !positions) FAIL(EXB_EINVAL, "exb_sampling: 1 <= B <= 4 rows of seeds and positions");
+    if (tnum < 1 || tnum > (1ll << 32)) FAIL(EXB_EINVAL, "exb_sampling: temperature multiplier in [1, 2^32]");
+    for (int b = 0; b < B; ++b)
+      if (positions[b] < 0) FAIL(EXB_EINVAL, "exb_sampling: negative sampling position");
+    CK(cudaMemcpyAsync(m->samp_seed, seeds, 8 * (size_t)B, cudaMemcpyHostToDevice, m->st));
+    CK(cudaMemcpyAsync(m->samp_pos, positions, 4 * (size_t)B, cudaMemcpyHostToDevice, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    m->samp_tnum = tnum;
+  }
+  m->samp_on = on != 0;
+  return EXB_OK;
+}
+
+int exb_sampling_positions(exb_model* m, int32_t* positions, int B) {
+  if (!m || !positions || B < 1 || B > RMAX) FAIL(EXB_EINVAL, "exb_sampling_positions: 1 <= B <= 4");
+  CK(cudaMemcpyAsync(positions, m->samp_pos, 4 * (size_t)B, cudaMemcpyDeviceToHost, m->st));
+  CK(cudaStreamSynchronize(m->st));
+  return EXB_OK;
+}
+
+int exb_sample(exb_model* m, const int64_t* logits, int R, int V, const uint64_t* seeds, const int32_t* positions,
+               int64_t tnum, int32_t* tokens) {
+  if (!m || !m->finalized || !logits || !seeds || !positions || !tokens) FAIL(EXB_EINVAL, "exb_sample: null argument");
+  if (R < 1 || V < 1 || tnum < 1 || tnum > (1ll << 32)) FAIL(EXB_EINVAL, "exb_sample: R >= 1, V >= 1, tnum in [1, 2^32]");
+  for (int r = 0; r < R; ++r)
+    if (positions[r] < 0) FAIL(EXB_EINVAL, "exb_sample: negative sampling position");
+  const size_t lb = (size_t)R * V * 8;
+  char* buf = nullptr;
+  CK(cudaMalloc(&buf, lb + (size_t)R * 16));
+  int64_t* dl = reinterpret_cast<int64_t*>(buf);
+  unsigned long long* ds = reinterpret_cast<unsigned long long*>(buf + lb);
+  int32_t* dp = reinterpret_cast<int32_t*>(buf + lb + (size_t)R * 8);
+  int32_t* dt = dp + R;
+  cudaError_t e = cudaMemcpyAsync(dl, logits, lb, cudaMemcpyHostToDevice, m->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(ds, seeds, (size_t)R * 8, cudaMemcpyHostToDevice, m->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dp, positions, (size_t)R * 4, cudaMemcpyHostToDevice, m->st);
+  if (e == cudaSuccess) e = launch_sample(R, dl, V, V, ds, dp, false, tnum, m->exp_t, dt, m->st, false);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(tokens, dt, (size_t)R * 4, cudaMemcpyDeviceToHost, m->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->st);
+  cudaFree(buf);
+  if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("exb_sample: ") + cudaGetErrorString(e));
+  return EXB_OK;
 }
 
 int exb_commit_end(exb_model* m) {

@@ -153,6 +153,10 @@ struct CommitLayout {
   const int64_t* lin_len = nullptr;   // device: their lengths
 };
 inline int64_t commit_leaf_count(int NL, int T) { return (int64_t)(5 * NL + 2) * T; }
+
+// ---- integer sampler (csrc/sample.cu): token of each row, position pos[r] (advanced when pos_inc)
+cudaError_t launch_sample(int R, const int64_t* logits, int V, int64_t ld, const unsigned long long* seeds, int32_t* pos,
+                          bool pos_inc, int64_t tnum, const int32_t* exp_t, int32_t* tokens, cudaStream_t st, bool pdl);
 cudaError_t launch_commit_log(int R, const int32_t* row_seq, const int32_t* row_pos, int seq, const int64_t* trace,
                               int64_t trace_row, const int64_t* cap, int64_t cap_row, int64_t* log, int npos_cap,
                               int* npos, int* err, cudaStream_t st);

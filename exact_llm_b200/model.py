@@ -13,6 +13,7 @@ All compute runs in libexactb200.so (sm_100a CUDA kernels); this module only mov
 arrays and calls the C ABI.  Outputs are numpy int64 Q16 logits exactly as the reference returns.
 """
 import ctypes
+import hashlib
 
 import numpy as np
 
@@ -239,6 +240,74 @@ class ExactModel:
 
     def commit_end(self):
         check(lib.exb_commit_end(self.h))
+
+    # ------------------------------------------------------------------ integer sampler
+    @staticmethod
+    def temp_num(temp):
+        """Temperature as the integer multiplier the sampler uses (exact_llm.py:249)."""
+        return int(round((1 << 16) / temp))
+
+    def sample(self, logits, seeds, positions, tnum):
+        """Tokens of int64 logits rows (R, V) drawn on the GPU with per-row seeds and positions
+        (exact_llm.py:256-259)."""
+        lg = np.ascontiguousarray(np.atleast_2d(logits), dtype=np.int64)
+        R, V = lg.shape
+        sd = np.ascontiguousarray(np.broadcast_to(np.asarray(seeds, np.uint64), (R,)))
+        ps = np.ascontiguousarray(np.broadcast_to(np.asarray(positions, np.int32), (R,)))
+        out = np.empty(R, np.int32)
+        check(lib.exb_sample(self.h, ptr(lg, ctypes.c_int64), R, V, sd.ctypes.data, ps.ctypes.data, int(tnum),
+                             out.ctypes.data))
+        return out
+
+    def sampling(self, on, seeds=(), positions=(), tnum=1 << 16):
+        """Make the decode steps of generate() sample (row b: seeds[b], from positions[b] on)."""
+        sd = np.ascontiguousarray(np.asarray(seeds, np.uint64))
+        ps = np.ascontiguousarray(np.asarray(positions, np.int32))
+        check(lib.exb_sampling(self.h, int(bool(on)), len(sd), sd.ctypes.data if on else None,
+                               ps.ctypes.data if on else None, int(tnum)))
+
+    @staticmethod
+    def _step_hash(prev, row):
+        # receipt chain link (exact_llm.py:260-261): host SHA-256, sequential per step
+        return hashlib.sha256(prev.encode() + np.ascontiguousarray(row, dtype=np.int64).tobytes()).hexdigest()[:16]
+
+    def generate_sampled(self, prompt, n, seed, temp, slot=0):
+        """Seeded integer sampling of ``n`` tokens after ``prompt`` with the receipt the
+        reference's generate() returns (exact_llm.py:262-268): (receipt, greedy argmax per step)."""
+        tnum = self.temp_num(temp)
+        lg = self.forward(prompt, self.new_cache(slot))
+        rows = [lg[-1]]
+        toks = [int(self.sample(lg[-1:], [seed], [0], tnum)[0])]
+        if n > 1:
+            if slot != 0:
+                raise ValueError("generate_sampled decodes slot 0")
+            self.sampling(True, [seed], [1], tnum)
+            try:
+                produced, lrows = self.generate([toks[0]], n - 1, want_logits=True)
+            finally:
+                self.sampling(False)
+            toks += [int(t) for t in produced[0]]
+            rows += [lrows[s, 0] for s in range(n - 1)]
+        chain = "start"
+        for r in rows:
+            chain = self._step_hash(chain, r)
+        receipt = dict(prompt=[int(t) for t in prompt], seed=seed, temp=temp, tokens=toks, chain=chain)
+        return receipt, [int(np.argmax(r)) for r in rows]
+
+    def verify_receipt(self, receipt, slot=0):
+        """Recompute a receipt with one forward over prompt + tokens: (ok, first bad position or
+        "chain" or None), as the reference's verify() (exact_llm.py:269-276)."""
+        prompt, toks = list(receipt["prompt"]), list(receipt["tokens"])
+        n = len(toks)
+        lg = self.forward(prompt + toks[:-1], self.new_cache(slot))[len(prompt) - 1:]
+        got = self.sample(lg, [receipt["seed"]] * n, np.arange(n), self.temp_num(receipt["temp"]))
+        for t in range(n):
+            if int(got[t]) != toks[t]:
+                return False, t
+        chain = "start"
+        for r in lg:
+            chain = self._step_hash(chain, r)
+        return (True, None) if chain == receipt["chain"] else (False, "chain")
 
     def linear_sizes(self):
         c = self.c

@@ -148,6 +148,23 @@ int exb_commit_begin(exb_model* m, int seq, int capacity);
 int exb_commit_root(exb_model* m, int T, uint8_t* root32, uint8_t* leaves_host, int64_t leaves_bytes);
 int exb_commit_end(exb_model* m);
 
+/* Integer sampler on the GPU (exact_llm.py:243-259): y = shr(logit * tnum, 16) with
+ * tnum = round(2^16 / temperature); Q20 probabilities p = (e << 20) // sum(e) from the exp table at
+ * max(y) - y; token = first index whose running sum of p exceeds (u20 * sum(p)) >> 20, where
+ * u20 = splitmix64(seed, position) >> 44.
+ *   exb_sample        tokens of R host logits rows (R x V int64), per-row seed and position
+ *   exb_sampling      on: the decode steps of exb_generate / exb_generate_device (B <= 4 rows)
+ *                     choose row b's next token with seeds[b] at positions[b], which then advance
+ *                     by one per step (the reference's generate() samples its t-th token at t);
+ *                     off: greedy argmax again.  Single-GPU models.
+ *   exb_sampling_positions  read the rows' next sampling positions
+ * The receipt chain (SHA-256 over each step's 1.2 MB logits row, exact_llm.py:260-268) is a
+ * sequential hash per step and stays on the host (Python shim `generate_sampled`). */
+int exb_sample(exb_model* m, const int64_t* logits, int R, int V, const uint64_t* seeds, const int32_t* positions,
+               int64_t tnum, int32_t* tokens);
+int exb_sampling(exb_model* m, int on, int B, const uint64_t* seeds, const int32_t* positions, int64_t tnum);
+int exb_sampling_positions(exb_model* m, int32_t* positions, int B);
+
 /* Freivalds self-check on every linear (experiments/gpu_engine_trace_verify_kaggle.py:803-834):
  * r_host holds, for each linear in trace order, 2 x N values in [0, p) for p = 2^31-1 and
  * 2147483629 (int32).  The device builds d_p = (W*M)^T r_p mod p and, on every later forward,

@@ -480,3 +480,65 @@ def merkle_root(leaves):
         lv = [hashlib.sha256(b"N" + lv[i] + (lv[i + 1] if i + 1 < len(lv) else lv[i])).digest()
               for i in range(0, len(lv), 2)]
     return lv[0]
+
+
+# ----------------------------------------------------------------------------- integer sampler + receipts
+MASK64 = (1 << 64) - 1
+
+
+def splitmix64(seed, pos):
+    """exact_llm.py:243-247 (Python integers, modulo 2^64)."""
+    z = (seed + (pos + 1) * 0x9E3779B97F4A7C15) & MASK64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & MASK64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & MASK64
+    return z ^ (z >> 31)
+
+
+def u20(seed, pos):
+    """Uniform integer in [0, 2^20) (exact_llm.py:248)."""
+    return splitmix64(seed, pos) >> 44
+
+
+def temp_num(t):
+    """Temperature as an integer multiplier (exact_llm.py:249)."""
+    return int(round((1 << 16) / t))
+
+
+def isoftmax_row(lg):
+    """Q20 probabilities of one Q16 logits row through the exp table (exact_llm.py:250-255)."""
+    T = exp_table()
+    d = lg.max() - lg
+    i = np.minimum(d >> 8, len(T) - 2)
+    fr = d & 255
+    e = T[i] - shr((T[i] - T[i + 1]) * fr, 8)
+    e = np.where(d < (40 << 16), e, 0)
+    return (e << 20) // e.sum()
+
+
+def sample_int(lg_row, seed, pos, tnum):
+    """Token = first index whose cumulative probability exceeds (u20 * total) >> 20
+    (exact_llm.py:256-259)."""
+    p = isoftmax_row(shr(np.asarray(lg_row, np.int64) * tnum, 16))
+    cum = np.cumsum(p)
+    target = (u20(seed, pos) * int(cum[-1])) >> 20
+    return int(np.searchsorted(cum, target, side="right")), p
+
+
+def step_hash(prev, lg_row):
+    """Receipt chain link: SHA-256 over the previous link's ASCII and the logits row's int64 bytes,
+    first 16 hex characters (exact_llm.py:260-261)."""
+    return hashlib.sha256(prev.encode() + np.ascontiguousarray(lg_row, dtype=np.int64).tobytes()).hexdigest()[:16]
+
+
+def sampled_generate(model, prompt_ids, n, seed, temp):
+    """Seeded integer sampling with the receipt hash chain, full recompute per token
+    (exact_llm.py:262-268)."""
+    ids, chain, toks, greedy, tnum = list(prompt_ids), "start", [], [], temp_num(temp)
+    for t in range(n):
+        lg = model(ids)[-1]
+        tok, _ = sample_int(lg, seed, t, tnum)
+        chain = step_hash(chain, lg)
+        toks.append(tok)
+        greedy.append(int(lg.argmax()))
+        ids.append(tok)
+    return dict(prompt=list(prompt_ids), seed=seed, temp=temp, tokens=toks, chain=chain), greedy

@@ -13,6 +13,7 @@ definitions the hot path needs (the scripts' top-level code downloads checkpoint
   * ``keys_group/keys_channel/fr``     experiments/gpu_engine_trace_verify_kaggle.py:802-819, 830-834
   * the tiny preflight model           experiments/_pre_tiny.py:1-15
   * the G1 GEMV known-answer inputs    experiments/speed_fair_kaggle.py:704-708
+  * ``splitmix64/u20/temp_num/isoftmax_row/sample_int/step_hash/generate``  exact_llm.py:243-263
   * ``requant/Hb/merkle/prover_trace/leaves_of``  experiments/commit_audit_kaggle.py:442-445,
                                       567-575, 587-628 (the Merkle trace commitment)
 
@@ -268,6 +269,29 @@ def g_commit(ex, G):
     print("commit root", levels[-1][0].hex(), len(leaves), flush=True)
 
 
+def g_sampler(ex, G):
+    """The reference's integer sampler (exact_llm.py:243-263): sample_int on seeded synthetic
+    logits rows, and generate() -- seeded, temperature-scaled decode with the receipt hash chain --
+    on the group-128 tiny model."""
+    rng = np.random.default_rng(31)
+    rows = []
+    for i, (V, scale, temp, seed, pos) in enumerate([(1000, 4 << 16, 0.8, 12345, 0), (1000, 1 << 16, 1.0, 7, 3),
+                                                     (4099, 12 << 16, 0.6, 2**63 + 5, 17),
+                                                     (151936, 6 << 16, 0.8, 12345, 1), (50, 40 << 16, 1.7, 0, 9)]):
+        lg = rng.integers(-scale, scale, V).astype(np.int64)
+        tnum = ex.temp_num(temp)
+        tok, p = ex.sample_int(lg, seed, pos, tnum)
+        rows.append(dict(V=V, scale=scale, temp=temp, tnum=tnum, seed=seed, pos=pos, rng_index=i,
+                         token=tok, p=h16(p), u20=int(ex.u20(seed, pos))))
+    g = G["models"]["tiny-g128"]
+    om = synth.build_model(synth.config("tiny-g128"), g["seed"])
+    rm = ref_int_model(ex, om)
+    receipt, greedy = ex.generate(rm, g["prompt"], 8, 12345, 0.8)
+    G["sampler"] = dict(rows=rows, rows_seed=31, receipt=receipt, greedy=greedy, model="tiny-g128",
+                        model_seed=g["seed"])
+    print("sampler", receipt["tokens"], receipt["chain"], greedy, flush=True)
+
+
 def g_config1(ex, G):
     """0.5B architecture, 32 prompt ids, 64 greedy steps (reference full recompute)."""
     _dense_case(ex, G, "qwen2.5-0.5b", synth.config("qwen2.5-0.5b"), 5, 32, 64, 5)
@@ -352,7 +376,7 @@ def g_moe(ex, G):
 
 BUILDERS = dict(tables=g_tables, gemv_kat=g_gemv_kat, models=g_models, freivalds=g_freivalds,
                 pre_tiny=g_pre_tiny, moe=g_moe, linear=g_linear, config1=g_config1, big=g_big_layers,
-                commit=g_commit)
+                commit=g_commit, sampler=g_sampler)
 
 
 def main():

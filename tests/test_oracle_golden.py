@@ -182,3 +182,20 @@ def test_commit_root_matches_reference(golden):
     for i, h in g["leaf_sample"].items():
         assert leaves[int(i)].hex() == h
     assert eo.merkle_root(leaves).hex() == g["root"]
+
+
+def test_sampler_matches_reference(golden):
+    """Integer sampler (splitmix64 / u20 / isoftmax_row / sample_int) and the seeded decode with
+    its receipt chain reproduce the reference's own outputs."""
+    g = golden["sampler"]
+    rng = np.random.default_rng(g["rows_seed"])
+    for row in g["rows"]:
+        lg = rng.integers(-row["scale"], row["scale"], row["V"]).astype(np.int64)
+        assert eo.temp_num(row["temp"]) == row["tnum"]
+        assert eo.u20(row["seed"], row["pos"]) == row["u20"]
+        tok, p = eo.sample_int(lg, row["seed"], row["pos"], row["tnum"])
+        assert tok == row["token"] and eo.h16(p) == row["p"]
+    om = synth.build_model(synth.config(g["model"]), g["model_seed"])
+    r = g["receipt"]
+    receipt, greedy = eo.sampled_generate(om, r["prompt"], len(r["tokens"]), r["seed"], r["temp"])
+    assert receipt == r and greedy == g["greedy"]
