@@ -41,7 +41,7 @@ class ExactModel:
     ``lin`` ("group" for group-128 GQLin layers, "channel" for per-channel QLin layers).
     """
 
-    def __init__(self, c, max_batch=1, max_seq=None, rope_len=None, emb_shift=9, tie=None, tp=None):
+    def __init__(self, c, max_batch=1, max_seq=None, rope_len=None, emb_shift=9, tie=None, tp=None, tabs=None):
         """``tp`` = (rank, size, unique_id) builds this rank's tensor-parallel slice (one process per
         GPU; every rank constructs its model at the same time; ``unique_id`` = the 128 bytes of
         ``ExactModel.tp_unique_id()`` made on rank 0 and shared by the caller)."""
@@ -63,10 +63,16 @@ class ExactModel:
         else:
             check(lib.exb_model_create(ctypes.byref(cfg), ctypes.byref(h)))
         self.h = h
-        cos, sin = tables.rope_tables(self.rope_len, c["hd"], c["theta"])
         half = c["hd"] // 2
-        self._tab = [np.ascontiguousarray(t) for t in (tables.exp_table(), tables.silu_table(), tables.sig_table(),
-                                                       cos[:, :half], sin[:, :half])]
+        if tabs is not None:            # shipped tables of a release (never recomputed)
+            if tabs["cos"].shape[0] < self.rope_len:
+                raise ValueError(f"the release's RoPE tables cover {tabs['cos'].shape[0]} positions < {self.rope_len}")
+            self._tab = [np.ascontiguousarray(tabs[k][:self.rope_len] if k in ("cos", "sin") else tabs[k], dtype=np.int64)
+                         for k in ("exp", "silu", "sig", "cos", "sin")]
+        else:
+            cos, sin = tables.rope_tables(self.rope_len, c["hd"], c["theta"])
+            self._tab = [np.ascontiguousarray(t) for t in (tables.exp_table(), tables.silu_table(), tables.sig_table(),
+                                                           cos[:, :half], sin[:, :half])]
         check(lib.exb_model_set_tables(self.h, *[ptr(t, ctypes.c_int64) for t in self._tab]))
         self._finalized = False
 
@@ -104,6 +110,26 @@ class ExactModel:
         m = cls(c, **kw)
         for name, arr in tensors.items():
             m.set_tensor(name, arr)
+        m.finalize()
+        return m
+
+    @classmethod
+    def from_artifact(cls, path, **kw):
+        """Load an exact release (``artifact.write_artifact`` layout): every file's SHA-256 is checked
+        against the manifest, the shipped tables are used as they are."""
+        from .artifact import load_artifact
+        arch, tensors, tabs = load_artifact(path)
+        c = dict(arch)
+        kw.setdefault("rope_len", int(arch["rope_len"]))
+        kw.setdefault("max_seq", int(arch["rope_len"]))
+        kw.setdefault("tie", "head.w" not in tensors and bool(arch.get("tie")))   # a shipped head is used as is
+        m = cls(c, tabs=tabs, **kw)
+        for name, a in tensors.items():
+            if name.endswith(".M") and a.ndim == 2:          # group-128 scales ship as int64, run as int32
+                if a.size and (int(a.max()) >= 1 << 31 or int(a.min()) < -(1 << 31)):
+                    raise ValueError(f"{name}: group scale outside int32")
+                a = np.asarray(a, dtype=np.int32)
+            m.set_tensor(name, a)
         m.finalize()
         return m
 

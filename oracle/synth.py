@@ -184,3 +184,27 @@ def linear_case(seed, K, N, R):
     x = np.random.default_rng(seed).integers(-128, 128, (R, K)).astype(np.int64)
     lin = group_linear(seed, 7, N, K, False)
     return x, lin
+
+
+def float_checkpoint(c, seed):
+    """Seeded float64 stand-in for a Qwen2-family checkpoint in the Hugging Face naming (conversion
+    tests only): weights N(0, 0.05), norm gains 1 + N(0, 0.1), q/k/v biases N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+    D, I, V, qn, kn = c["D"], c["I"], c["V"], c["H"] * c["hd"], c["KV"] * c["hd"]
+    t = {"model.embed_tokens.weight": rng.normal(0, 0.05, (V, D)), "model.norm.weight": 1 + rng.normal(0, 0.1, D)}
+    if not c.get("tie"):
+        t["lm_head.weight"] = rng.normal(0, 0.05, (V, D))
+    for i in range(c["NL"]):
+        p = f"model.layers.{i}."
+        t[p + "input_layernorm.weight"] = 1 + rng.normal(0, 0.1, D)
+        t[p + "post_attention_layernorm.weight"] = 1 + rng.normal(0, 0.1, D)
+        for nm, (o, k) in {"self_attn.q_proj": (qn, D), "self_attn.k_proj": (kn, D), "self_attn.v_proj": (kn, D),
+                           "self_attn.o_proj": (D, qn), "mlp.gate_proj": (I, D), "mlp.up_proj": (I, D),
+                           "mlp.down_proj": (D, I)}.items():
+            t[p + nm + ".weight"] = rng.normal(0, 0.05, (o, k))
+            if nm in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"):
+                t[p + nm + ".bias"] = rng.normal(0, 0.02, o)
+    return t
+
+
+CONVERT_CFG = dict(D=256, H=4, KV=2, hd=64, I=512, V=1000, NL=2, theta=1e4, tie=False, T=64)

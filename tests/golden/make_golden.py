@@ -14,6 +14,7 @@ definitions the hot path needs (the scripts' top-level code downloads checkpoint
   * the tiny preflight model           experiments/_pre_tiny.py:1-15
   * the G1 GEMV known-answer inputs    experiments/speed_fair_kaggle.py:704-708
   * ``splitmix64/u20/temp_num/isoftmax_row/sample_int/step_hash/generate``  exact_llm.py:243-263
+  * ``GQLin`` constructor (float64 group-128 conversion)  experiments/group128_quality_kaggle.py:406-414
   * ``requant/Hb/merkle/prover_trace/leaves_of``  experiments/commit_audit_kaggle.py:442-445,
                                       567-575, 587-628 (the Merkle trace commitment)
 
@@ -292,6 +293,32 @@ def g_sampler(ex, G):
     print("sampler", receipt["tokens"], receipt["chain"], greedy, flush=True)
 
 
+def g_convert(ex, G):
+    """float64 checkpoint -> integer release, by the reference's own QLin / qlin_chunked / GQLin and
+    IntModel (exact_llm.py:83-88, 133-157; experiments/group128_quality_kaggle.py:406-414), on a
+    seeded float stand-in; logits of the converted per-channel model on 16 ids."""
+    c = dict(synth.CONVERT_CFG)
+    f = synth.float_checkpoint(c, 41)
+    ns = dict(ex.__dict__)
+    ns["G"] = 128                                    # group size set at experiments/group128_quality_kaggle.py:405
+    ex._exec_lines("experiments/group128_quality_kaggle.py", 406, 414, ns)           # GQLin constructor
+    GQ = ns["GQLin"]
+    mats = {}
+    for nm in ("model.layers.0.self_attn.q_proj", "model.layers.1.mlp.down_proj", "model.layers.0.mlp.gate_proj"):
+        w = f[nm + ".weight"]
+        b = f.get(nm + ".bias")
+        q = ex.qlin_chunked(w, b, chunk=100)                  # row blocks: identical to one shot
+        g = GQ(w, b)
+        mats[nm] = dict(ch_w=h16(np.ascontiguousarray(q.w.T)), ch_M=h16(q.M), b=None if b is None else h16(q.b),
+                        g_w=h16(np.ascontiguousarray(g.w.T)), g_M=h16(np.ascontiguousarray(g.M.T)))
+    m = ex.IntModel(f.__getitem__, c)
+    ids = [int(t) for t in synth.prompt_ids(5, 1, 16, c["V"])[0]]
+    lg = m(ids)
+    G["convert"] = dict(config=c, seed=41, mats=mats, ids=ids, logits=h16(lg), emb_q16=h16(np.rint(m.emb * ex.ONE)
+                                                                                       .astype(np.int64)))
+    print("convert", h16(lg), flush=True)
+
+
 def g_config1(ex, G):
     """0.5B architecture, 32 prompt ids, 64 greedy steps (reference full recompute)."""
     _dense_case(ex, G, "qwen2.5-0.5b", synth.config("qwen2.5-0.5b"), 5, 32, 64, 5)
@@ -376,7 +403,7 @@ def g_moe(ex, G):
 
 BUILDERS = dict(tables=g_tables, gemv_kat=g_gemv_kat, models=g_models, freivalds=g_freivalds,
                 pre_tiny=g_pre_tiny, moe=g_moe, linear=g_linear, config1=g_config1, big=g_big_layers,
-                commit=g_commit, sampler=g_sampler)
+                commit=g_commit, sampler=g_sampler, convert=g_convert)
 
 
 def main():
