@@ -60,6 +60,10 @@ SIGNATURES = {
     "exb_sampling": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                     ctypes.c_int64]),
     "exb_sampling_positions": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]),
+    "exb_verifier_emb_keys": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "exb_verify_cells": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                        ctypes.c_int64, ctypes.c_void_p]),
     "exb_freivalds_set_keys": (ctypes.c_int, [ctypes.c_void_p, c_i32p, ctypes.c_int64]),
     "exb_freivalds_read_keys": (ctypes.c_int, [ctypes.c_void_p, c_i32p, ctypes.c_int64]),
     "exb_freivalds_enable": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),

@@ -120,6 +120,9 @@ struct exb_model {
   int64_t samp_tnum = 1 << 16;
   unsigned long long* samp_seed = nullptr;   // (RMAX), arena
   int32_t* samp_pos = nullptr;               // (RMAX), arena
+  // weightless verifier: embedding row digests (exb_verifier_emb_keys)
+  int32_t* ver_emb_r = nullptr;              // (2, D)
+  int64_t* ver_emb_de = nullptr;             // (2, V)
   unsigned long long* fr_acc = nullptr;
   int* fr_fail = nullptr; int* err = nullptr;
   int16_t* kc = nullptr; int8_t* ks = nullptr; int32_t* vc = nullptr;
@@ -999,6 +1002,8 @@ void exb_model_destroy(exb_model* m) {
   cudaFree(m->rarena);
   cudaFree(m->commit_log);
   cudaFree(m->commit_lin);
+  cudaFree(m->ver_emb_r);
+  cudaFree(m->ver_emb_de);
   cudaFree(m->gen_tokens);
   cudaFree(m->emb_q16);
   if (m->comm && nccl()) nccl()->comm_destroy(m->comm);
@@ -1667,6 +1672,146 @@ int exb_commit_root(exb_model* m, int T, uint8_t* root32, uint8_t* leaves_host, 
   if (e == cudaSuccess) e = cudaStreamSynchronize(m->st);
   cudaFree(buf);
   if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("exb_commit_root: ") + cudaGetErrorString(e));
+  return check_device_errors(m);
+}
+
+// ---- weightless cell verifier
+int exb_verifier_emb_keys(exb_model* m, const int32_t* r_host) {
+  if (!m || !m->finalized || !r_host) FAIL(EXB_EINVAL, "exb_verifier_emb_keys: null argument / not finalized");
+  if (m->tp > 1) FAIL(EXB_EINVAL, "exb_verifier_emb_keys: single-GPU models");
+  const exb_config& c = m->c;
+  for (int i = 0; i < 2 * c.D; ++i)
+    if (r_host[i] < 0 || (uint32_t)r_host[i] >= (i < c.D ? 2147483647u : 2147483629u))
+      FAIL(EXB_EINVAL, "exb_verifier_emb_keys: r outside [0, p)");
+  if (!m->ver_emb_r) CK(cudaMalloc(&m->ver_emb_r, sizeof(int32_t) * 2 * c.D));
+  if (!m->ver_emb_de) CK(cudaMalloc(&m->ver_emb_de, sizeof(int64_t) * 2 * c.V));
+  CK(cudaMemcpyAsync(m->ver_emb_r, r_host, sizeof(int32_t) * 2 * c.D, cudaMemcpyHostToDevice, m->st));
+  CK(launch_emb_digest(m->emb, c.emb_shift, m->emb_q16, c.V, c.D, m->ver_emb_r, m->ver_emb_de, m->st));
+  CK(cudaStreamSynchronize(m->st));
+  return EXB_OK;
+}
+
+int exb_verify_cells(exb_model* m, int T, const uint8_t* root32, int n_cells, const int32_t* cells, const int32_t* ids,
+                     const int64_t* values, int64_t n_values, const uint8_t* proofs, int64_t proof_bytes,
+                     int32_t* verdicts) {
+  if (!m || !m->finalized || !root32 || !cells || !ids || !values || !proofs || !verdicts)
+    FAIL(EXB_EINVAL, "exb_verify_cells: null argument / not finalized");
+  const exb_config& c = m->c;
+  if (m->tp > 1 || c.n_experts) FAIL(EXB_EINVAL, "exb_verify_cells: dense single-GPU models");
+  if (T < 1 || T > c.rope_len || n_cells < 1) FAIL(EXB_EINVAL, "exb_verify_cells: T in [1, rope_len], n_cells >= 1");
+  for (auto& L : m->lins)
+    if (!L.fr_d) FAIL(EXB_EINVAL, "exb_verify_cells: set the Freivalds keys first (exb_freivalds_set_keys)");
+  if (!m->ver_emb_de) FAIL(EXB_EINVAL, "exb_verify_cells: set the embedding keys first (exb_verifier_emb_keys)");
+  const int NL = c.NL, D = c.D, Hd = c.H * c.hd, KVd = c.KV * c.hd, I = c.I;
+  const int64_t nleaves = commit_leaf_count(NL, T);
+  int depth = 0;
+  for (int64_t n = nleaves; n > 1; n = (n + 1) / 2) ++depth;
+  // leaf records in needed() order (experiments/commit_audit_kaggle.py:647-651)
+  std::vector<VLeafRec> recs;
+  std::vector<int64_t> voff(n_cells);
+  std::vector<int> leaf0(n_cells + 1);
+  int64_t v = 0, pb = 0;
+  auto lid = [&](int kind, int L, int t) -> int64_t {     // 0 X, 1 KV, 2 KR, 3 Q, 4 R, 5 HEAD
+    if (kind == 0) return (int64_t)L * T + t;
+    if (kind == 5) return (int64_t)(NL + 1) * T + 4ll * NL * T + t;
+    return (int64_t)(NL + 1) * T + ((int64_t)L * T + t) * 4 + (kind - 1);
+  };
+  auto add = [&](int kind, int L, int t, std::initializer_list<int64_t> lens) {
+    VLeafRec r;
+    r.voff = v; r.leaf = lid(kind, L, t); r.poff = pb; r.nseg = (int)lens.size();
+    int j = 0;
+    for (int64_t x : lens) { r.len[j++] = x; v += x; }
+    pb += 32ll * depth;
+    recs.push_back(r);
+  };
+  for (int i = 0; i < n_cells; ++i) {
+    const int L = cells[2 * i], t = cells[2 * i + 1];
+    if (L < 0 || L > NL || t < 0 || t >= T) FAIL(EXB_EINVAL, "exb_verify_cells: cell outside (0..NL, 0..T-1)");
+    voff[i] = v;
+    leaf0[i] = (int)recs.size();
+    if (L == NL) {
+      add(0, NL, t, {D});
+      add(5, NL, t, {c.V});
+    } else {
+      add(0, L, t, {D});
+      add(1, L, t, {KVd, KVd});
+      for (int s = 0; s <= t; ++s) add(2, L, s, {KVd, KVd});
+      add(3, L, t, {Hd});
+      add(4, L, t, {D, I, I, D});
+      add(0, L + 1, t, {D});
+    }
+  }
+  leaf0[n_cells] = (int)recs.size();
+  if (v != n_values) FAIL(EXB_EINVAL, "exb_verify_cells: expected " + std::to_string(v) + " opened values");
+  if (pb != proof_bytes) FAIL(EXB_EINVAL, "exb_verify_cells: expected " + std::to_string(pb) + " proof bytes");
+  for (int t = 0; t < T; ++t)
+    if (ids[t] < 0 || ids[t] >= c.V) FAIL(EXB_EINVAL, "exb_verify_cells: token id outside the vocabulary");
+  // device copies
+  std::vector<VLinDev> vl(m->lins.size());
+  for (size_t i = 0; i < m->lins.size(); ++i) {
+    const LinInfo& L = m->lins[i];
+    VLinDev& d = vl[i];
+    d.N = L.N; d.K = L.K; d.group = L.fused->Mg != nullptr; d.row0 = L.row0; d.row_step = L.row_step;
+    d.mbits = L.mbits; d.b = L.fused->b; d.Mc = L.fused->Mc; d.r = L.fr_r; d.d = L.fr_d;
+  }
+  std::vector<const int64_t*> gains(2 * NL);
+  for (int l = 0; l < NL; ++l) { gains[l] = m->L[l].g1; gains[NL + l] = m->L[l].g2; }
+  const int ymax = std::max(std::max(I, Hd), 2 * KVd);
+  const int q16 = std::max(std::max(D, Hd), I);
+  const int64_t scr_len = 2ll * Hd + D + 2ll * ymax + (int64_t)c.H * T;
+  auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+  const size_t b_vl = al(vl.size() * sizeof(VLinDev)), b_g = al(gains.size() * 8), b_ids = al(4ull * T),
+               b_cells = al(8ull * n_cells), b_val = al(8ull * v), b_voff = al(8ull * n_cells),
+               b_l0 = al(4ull * (n_cells + 1)), b_rec = al(recs.size() * sizeof(VLeafRec)), b_pr = al(pb),
+               b_root = al(32), b_ok = al(4 * recs.size() + 4), b_scr = al(8ull * scr_len * n_cells), b_vd = al(4ull * n_cells);
+  char* buf = nullptr;
+  const size_t total = b_vl + b_g + b_ids + b_cells + b_val + b_voff + b_l0 + b_rec + b_pr + b_root + b_ok + b_scr + b_vd;
+  if (cudaMalloc(&buf, total) != cudaSuccess) {
+    cudaGetLastError();
+    FAIL(EXB_ECUDA, "exb_verify_cells: no device memory for " + std::to_string(total) + " bytes");
+  }
+  char* p = buf;
+  auto take = [&](size_t b) { char* q = p; p += b; return q; };
+  VLinDev* d_vl = (VLinDev*)take(b_vl);
+  const int64_t** d_g = (const int64_t**)take(b_g);
+  int32_t* d_ids = (int32_t*)take(b_ids);
+  int32_t* d_cells = (int32_t*)take(b_cells);
+  int64_t* d_val = (int64_t*)take(b_val);
+  int64_t* d_voff = (int64_t*)take(b_voff);
+  int* d_l0 = (int*)take(b_l0);
+  VLeafRec* d_rec = (VLeafRec*)take(b_rec);
+  uint8_t* d_pr = (uint8_t*)take(b_pr);
+  uint8_t* d_root = (uint8_t*)take(b_root);
+  int* d_ok = (int*)take(b_ok);
+  int64_t* d_scr = (int64_t*)take(b_scr);
+  int32_t* d_vd = (int32_t*)take(b_vd);
+  cudaError_t e = cudaSuccess;
+  auto up = [&](void* dst, const void* src, size_t b) {
+    if (e == cudaSuccess && b) e = cudaMemcpyAsync(dst, src, b, cudaMemcpyHostToDevice, m->st);
+  };
+  up(d_vl, vl.data(), vl.size() * sizeof(VLinDev));
+  up(d_g, gains.data(), gains.size() * 8);
+  up(d_ids, ids, 4ull * T);
+  up(d_cells, cells, 8ull * n_cells);
+  up(d_val, values, 8ull * v);
+  up(d_voff, voff.data(), 8ull * n_cells);
+  up(d_l0, leaf0.data(), 4ull * (n_cells + 1));
+  up(d_rec, recs.data(), recs.size() * sizeof(VLeafRec));
+  up(d_pr, proofs, pb);
+  up(d_root, root32, 32);
+  VerifyArgs a;
+  a.NL = NL; a.D = D; a.H = c.H; a.KV = c.KV; a.hd = c.hd; a.I = I; a.V = c.V; a.T = T;
+  a.inv = (int64_t)std::nearbyint(65536.0 / std::sqrt((double)c.hd));
+  a.lins = d_vl; a.g1 = d_g; a.g2 = d_g + NL; a.gf = m->gf;
+  a.cos_t = m->cos_t; a.sin_t = m->sin_t; a.exp_t = m->exp_t; a.silu_t = m->silu_t;
+  a.emb_r = m->ver_emb_r; a.emb_de = m->ver_emb_de; a.ids = d_ids; a.cells = d_cells;
+  a.values = d_val; a.cell_voff = d_voff; a.cell_leaf0 = d_l0; a.leaf_ok = d_ok;
+  a.scratch = d_scr; a.scr_len = scr_len; a.ymax = ymax; a.q16_len = q16; a.verdict = d_vd;
+  if (e == cudaSuccess) e = launch_verify(a, n_cells, (int)recs.size(), d_rec, d_pr, depth, d_root, d_ok, m->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(verdicts, d_vd, 4ull * n_cells, cudaMemcpyDeviceToHost, m->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->st);
+  cudaFree(buf);
+  if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("exb_verify_cells: ") + cudaGetErrorString(e));
   return check_device_errors(m);
 }
 

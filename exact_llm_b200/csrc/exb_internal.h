@@ -154,6 +154,53 @@ struct CommitLayout {
 };
 inline int64_t commit_leaf_count(int NL, int T) { return (int64_t)(5 * NL + 2) * T; }
 
+// ---- weightless cell verifier (csrc/verify.cu)
+struct VLinDev {                      // one logical linear, seen by the verifier (no weights)
+  int N = 0, K = 0, group = 0;
+  int row0 = 0, row_step = 1;         // its rows in the fused matrix (bias / per-channel scale index)
+  int mbits = 0;                      // per channel: bitlen(max M) of the logical linear
+  const int64_t* b = nullptr;         // fused bias or nullptr
+  const int64_t* Mc = nullptr;        // fused per-channel scales (per-channel linears)
+  const int32_t* r = nullptr;         // (2, N) Freivalds r
+  const int32_t* d = nullptr;         // (2, K) Freivalds digests
+};
+struct VLeafRec {                     // one opened leaf of one cell
+  int64_t voff = 0;                   // first value in the opened-values buffer
+  int64_t leaf = 0;                   // index among the committed leaves
+  int64_t poff = 0;                   // first proof byte
+  int nseg = 0;
+  int64_t len[4] = {0, 0, 0, 0};
+};
+enum Verdict {
+  VERDICT_OK = 0, VERDICT_EMB = 2, VERDICT_KV = 3, VERDICT_KR = 4, VERDICT_Q = 5, VERDICT_O = 6,
+  VERDICT_GU = 7, VERDICT_DOWN = 8, VERDICT_RESID = 9, VERDICT_HEAD = 10,
+  VERDICT_MERKLE = 1000,              // + the position of the failing leaf among the cell's leaves
+};
+struct VerifyArgs {
+  int NL = 0, D = 0, H = 0, KV = 0, hd = 0, I = 0, V = 0, T = 0;
+  int64_t inv = 0;
+  const VLinDev* lins = nullptr;      // 7 NL + 1
+  const int64_t* const* g1 = nullptr; // device arrays of NL gain pointers
+  const int64_t* const* g2 = nullptr;
+  const int64_t* gf = nullptr;
+  const int32_t *cos_t = nullptr, *sin_t = nullptr, *exp_t = nullptr, *silu_t = nullptr;
+  const int32_t* emb_r = nullptr;     // (2, D)
+  const int64_t* emb_de = nullptr;    // (2, V)
+  const int32_t* ids = nullptr;       // (T)
+  const int32_t* cells = nullptr;     // (n, 2): layer, position
+  const int64_t* values = nullptr;    // opened values, cell after cell
+  const int64_t* cell_voff = nullptr; // (n)
+  const int* cell_leaf0 = nullptr;    // (n + 1): the cells' leaf records
+  const int* leaf_ok = nullptr;
+  int64_t* scratch = nullptr; int64_t scr_len = 0;
+  int ymax = 0, q16_len = 0;
+  int32_t* verdict = nullptr;
+};
+cudaError_t launch_verify(const VerifyArgs& a, int n_cells, int n_leaves, const VLeafRec* recs, const uint8_t* proofs,
+                          int depth, const uint8_t* root, int* leaf_ok, cudaStream_t st);
+cudaError_t launch_emb_digest(const int8_t* emb, int shift, const int64_t* emb_q16, int V, int D, const int32_t* r,
+                              int64_t* de, cudaStream_t st);
+
 // ---- integer sampler (csrc/sample.cu): token of each row, position pos[r] (advanced when pos_inc)
 cudaError_t launch_sample(int R, const int64_t* logits, int V, int64_t ld, const unsigned long long* seeds, int32_t* pos,
                           bool pos_inc, int64_t tnum, const int32_t* exp_t, int32_t* tokens, cudaStream_t st, bool pdl);

@@ -335,6 +335,64 @@ class ExactModel:
             chain = self._step_hash(chain, r)
         return (True, None) if chain == receipt["chain"] else (False, "chain")
 
+    # ------------------------------------------------------------------ weightless cell verifier
+    def verifier_keys(self, seed=2026):
+        """Draw the verifier's secrets in the reference's make_verifier order
+        (experiments/commit_audit_kaggle.py:461-512): per linear (trace order) r ~ U[0, p) of
+        length N for p = 2^31 - 1 then 2147483629, then the embedding's r of length D per prime;
+        builds the digests on the device."""
+        rng = np.random.default_rng(seed)
+        P = (2147483647, 2147483629)
+        rs = [np.stack([rng.integers(0, p, N, dtype=np.int64) for p in P]) for _, N, _ in self.linear_sizes()]
+        er = np.stack([rng.integers(0, p, self.c["D"], dtype=np.int64) for p in P])
+        self.freivalds_set_keys(rs)
+        e = np.ascontiguousarray(er.astype(np.int32))
+        check(lib.exb_verifier_emb_keys(self.h, e.ctypes.data))
+
+    @staticmethod
+    def cell_leaves(cell, NL):
+        """Names of the leaves a cell opens, in the reference's needed() order."""
+        L, t = cell
+        if L == NL:
+            return [("X", NL, t), ("HEAD", NL, t)]
+        return [("X", L, t), ("KV", L, t)] + [("KR", L, s) for s in range(t + 1)] + \
+               [("Q", L, t), ("R", L, t), ("X", L + 1, t)]
+
+    def verify_cells(self, T, root, cells, opened, ids):
+        """Verify cells of a committed forward on the GPU without the weights: ``opened[cell]`` maps
+        each leaf name of ``cell_leaves(cell)`` to (list of int64 arrays, list of 32-byte Merkle
+        siblings), as the reference's Prover.open returns.  Returns [(ok, reason)] with the
+        reference's reasons (experiments/commit_audit_kaggle.py:659-705)."""
+        NL = self.c["NL"]
+        vals, prfs, names = [], [], []
+        for cell in cells:
+            nm = self.cell_leaves(cell, NL)
+            names.append(nm)
+            for n in nm:
+                v, pr = opened[cell][n]
+                vals += [np.asarray(a, np.int64).reshape(-1) for a in v]
+                prfs += [bytes(b) for b in pr]
+        values = np.ascontiguousarray(np.concatenate(vals))
+        proofs = np.frombuffer(b"".join(prfs), np.uint8).copy()
+        cl = np.ascontiguousarray(np.asarray(cells, np.int32).reshape(-1, 2))
+        idv = np.ascontiguousarray(np.asarray(ids, np.int32))
+        rt = np.frombuffer(bytes(root), np.uint8).copy()
+        out = np.empty(len(cells), np.int32)
+        check(lib.exb_verify_cells(self.h, int(T), rt.ctypes.data, len(cells), cl.ctypes.data, idv.ctypes.data,
+                                   values.ctypes.data, values.size, proofs.ctypes.data, proofs.size, out.ctypes.data))
+        reasons = {2: "embedding@{t}", 3: "kv@{t}", 4: "kr@{t}", 5: "q", 6: "o", 7: "gate/up", 8: "down",
+                   9: "residual", 10: "head"}
+        res = []
+        for (L, t), v, nm in zip(cells, out, names):
+            v = int(v)
+            if v == 0:
+                res.append((True, None))
+            elif v >= 1000:
+                res.append((False, f"merkle {nm[v - 1000]}"))
+            else:
+                res.append((False, reasons[v].format(t=t)))
+        return res
+
     def linear_sizes(self):
         c = self.c
         out = []

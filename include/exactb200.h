@@ -148,6 +148,27 @@ int exb_commit_begin(exb_model* m, int seq, int capacity);
 int exb_commit_root(exb_model* m, int T, uint8_t* root32, uint8_t* leaves_host, int64_t leaves_bytes);
 int exb_commit_end(exb_model* m);
 
+/* Weightless cell verifier on the GPU (experiments/commit_audit_kaggle.py:461-512, 647-705): the
+ * verifier's secrets are the Freivalds keys of every linear (exb_freivalds_set_keys, r per linear
+ * and prime in trace order -- the reference's make_verifier draws them in that order) and a digest
+ * of every embedding row (exb_verifier_emb_keys: r_host = 2 x D values in [0, p)).  It checks
+ * cells (layer L, position t) of a committed forward of T positions (root from exb_commit_root or
+ * any prover) from opened leaves, without using the weights:
+ *   cells    n x 2 int32 (L in 0..NL, t in 0..T-1); ids = the T committed token ids
+ *   values   per cell, in the reference's needed() order, the opened int64 arrays:
+ *            L < NL: X(L,t)[D] | k acc[KV hd] v acc[KV hd] | for s = 0..t: K(L,s)[KV hd] V(L,s)[KV hd]
+ *                    | q acc[H hd] | o acc[D] gate acc[I] up acc[I] down acc[D] | X(L+1,t)[D]
+ *            L = NL: X(NL,t)[D] | head acc[V]
+ *   proofs   per opened leaf, its Merkle path: depth x 32 bytes, depth = number of halvings of
+ *            the (5 NL + 2) T leaves to one root
+ *   verdicts 0 accepted; 1000 + j: leaf j of the cell fails its proof; 2 embedding row, 3 k/v,
+ *            4 committed K/V row, 5 q, 6 o, 7 gate/up, 8 down, 9 next residual row, 10 head
+ *            (the reference's rejection reasons). */
+int exb_verifier_emb_keys(exb_model* m, const int32_t* r_host);
+int exb_verify_cells(exb_model* m, int T, const uint8_t* root32, int n_cells, const int32_t* cells, const int32_t* ids,
+                     const int64_t* values, int64_t n_values, const uint8_t* proofs, int64_t proof_bytes,
+                     int32_t* verdicts);
+
 /* Integer sampler on the GPU (exact_llm.py:243-259): y = shr(logit * tnum, 16) with
  * tnum = round(2^16 / temperature); Q20 probabilities p = (e << 20) // sum(e) from the exp table at
  * max(y) - y; token = first index whose running sum of p exceeds (u20 * sum(p)) >> 20, where

@@ -412,12 +412,14 @@ def step_digest(flat):
 
 
 # ----------------------------------------------------------------------------- Merkle trace commitment
-def commit_trace(model, ids):
+def commit_trace(model, ids, fake=None, cheat_layer=None, cheat_down=None):
     """One full forward of ``ids`` recording what the trace commitment covers: the residual
     stream X entering every layer (and the final one), every linear's integer accumulator, the
     roped K and the V rows of every layer, and the head accumulator.  Restates ``prover_trace``
-    (experiments/commit_audit_kaggle.py:587-613) without its attack hooks; a group-128 linear's
-    accumulator is its ``tot``, as in the reference's trace capture."""
+    (experiments/commit_audit_kaggle.py:587-613); a group-128 linear's accumulator is its ``tot``,
+    as in the reference's trace capture.  Attack hooks as the reference's: ``fake = (layer, fn)``
+    replaces that layer's attention probabilities by ``fn(p)`` (every head), ``cheat_down`` is
+    used as layer ``cheat_layer``'s down projection."""
     c = model.c
     H, KV, hd = c["H"], c["KV"], c["hd"]
     T = len(ids)
@@ -432,12 +434,23 @@ def commit_trace(model, ids):
         k = rope(L["k"](a, tr, "k").reshape(T, KV, hd).transpose(1, 0, 2), cos, sin)
         v = L["v"](a, tr, "v").reshape(T, KV, hd).transpose(1, 0, 2)
         KR.append((k.copy(), v.copy()))
-        out = model._attention(li, q, k, v, None, 0)
+        if fake is not None and fake[0] == li:
+            valid = np.tril(np.ones((T, T), bool))
+            out = np.empty((H, T, hd), np.int64)
+            for hh in range(H):
+                kh = hh // (H // KV)
+                qq, sq = qrow(q[hh])
+                kk, sk = qrow(k[kh])
+                sc = shr(mm_exact(qq, kk.T) * model.INV, (F - sq - sk.T) + 16)
+                out[hh] = shr(np.matmul(fake[1](isoftmax(sc, valid)), v[kh]), 20)
+        else:
+            out = model._attention(li, q, k, v, None, 0)
         x = x + L["o"](out.transpose(1, 0, 2).reshape(T, H * hd), tr, "o")
         m_ = irms(x, L["g2"])
         g = L["gate"](m_, tr, "gate")
         u = L["up"](m_, tr, "up")
-        x = x + L["down"](shr(isilu(g) * u, F), tr, "down")
+        dn = cheat_down if (cheat_down is not None and cheat_layer == li) else L["down"]
+        x = x + dn(shr(isilu(g) * u, F), tr, "down")
         A.append({nm: raw for nm, raw, _ in tr})
     X.append(x.copy())
     htr = []
@@ -542,3 +555,204 @@ def sampled_generate(model, prompt_ids, n, seed, temp):
         greedy.append(int(lg.argmax()))
         ids.append(tok)
     return dict(prompt=list(prompt_ids), seed=seed, temp=temp, tokens=toks, chain=chain), greedy
+
+
+# ----------------------------------------------------------------------------- weightless cell verifier
+def leaf_index(kind, L, t, T, NL):
+    """Position of a named leaf in the leaves_of order (experiments/commit_audit_kaggle.py:614-628)."""
+    if kind == "X":
+        return L * T + t
+    if kind == "HEAD":
+        return (NL + 1) * T + 4 * NL * T + t
+    return (NL + 1) * T + (L * T + t) * 4 + ("KV", "KR", "Q", "R").index(kind)
+
+
+def leaf_values(tr, name):
+    """Opened values of a named leaf (experiments/commit_audit_kaggle.py:632-639)."""
+    kind, L, t = name
+    if kind == "X":
+        return [tr["X"][L][t]]
+    if kind == "HEAD":
+        return [tr["head"][t]]
+    if kind == "KR":
+        return [tr["KR"][L][0][:, t, :], tr["KR"][L][1][:, t, :]]
+    a = tr["A"][L]
+    if kind == "KV":
+        return [a["k"][t], a["v"][t]]
+    if kind == "Q":
+        return [a["q"][t]]
+    return [a["o"][t], a["gate"][t], a["up"][t], a["down"][t]]
+
+
+def merkle_levels(leaves):
+    lv = [hashlib.sha256(b"L" + leaf).digest() for leaf in leaves]
+    levels = [lv]
+    while len(lv) > 1:
+        lv = [hashlib.sha256(b"N" + lv[i] + (lv[i + 1] if i + 1 < len(lv) else lv[i])).digest()
+              for i in range(0, len(lv), 2)]
+        levels.append(lv)
+    return levels
+
+
+def merkle_proof(levels, idx):
+    """Sibling path, the node itself where it has no sibling (experiments/commit_audit_kaggle.py:576-580)."""
+    pr = []
+    for lv in levels[:-1]:
+        sib = idx ^ 1
+        pr.append(lv[sib] if sib < len(lv) else lv[idx])
+        idx >>= 1
+    return pr
+
+
+def merkle_verify(root, leaf, idx, pr):
+    """experiments/commit_audit_kaggle.py:581-585."""
+    h = hashlib.sha256(b"L" + leaf).digest()
+    for sib in pr:
+        h = hashlib.sha256(b"N" + (h + sib if idx % 2 == 0 else sib + h)).digest()
+        idx >>= 1
+    return h == root
+
+
+def needed(cell, NL):
+    """Leaves a cell verification opens (experiments/commit_audit_kaggle.py:647-651)."""
+    L, t = cell
+    if L == NL:
+        return [("X", NL, t), ("HEAD", NL, t)]
+    return [("X", L, t), ("KV", L, t)] + [("KR", L, s) for s in range(t + 1)] + \
+           [("Q", L, t), ("R", L, t), ("X", L + 1, t)]
+
+
+def open_cell(tr, NL, levels, cell, lie=None):
+    """{name: (values, proof)} for a cell; ``lie`` = a name whose first value is altered by one
+    (experiments/commit_audit_kaggle.py:640-646)."""
+    out = {}
+    for n in needed(cell, NL):
+        vals = [np.array(v, np.int64, copy=True) for v in leaf_values(tr, n)]
+        if lie is not None and n == lie:
+            vals[0].reshape(-1)[0] += 1
+        out[n] = (vals, merkle_proof(levels, leaf_index(*n, tr["T"], NL)))
+    return out
+
+
+def verifier_keys(model, seed=2026):
+    """The weightless verifier's secrets in the reference's draw order (make_verifier,
+    experiments/commit_audit_kaggle.py:461-512): per linear (layers' q,k,v,o,gate,up,down, then the
+    head) and prime, r ~ U[0, p) of length N and d = W r mod p (W r over the fused W * M for a
+    group-128 linear, whose accumulator is tot); for the embedding, r of length D and the digest
+    de of every Q16 row."""
+    rng = np.random.default_rng(seed)
+
+    def vlin(lin):
+        keys = []
+        for p in (P1, P2):
+            r = rng.integers(0, p, lin.N, dtype=np.int64)
+            d = np.zeros(lin.K, np.int64)
+            if lin.kind == "group":
+                for g in range(lin.K // GROUP):
+                    ks = slice(g * GROUP, (g + 1) * GROUP)
+                    wm = (lin.w[:, ks].astype(np.int64) * (lin.M[:, g:g + 1] % p)) % p          # (N, 128)
+                    for j in range(0, lin.N, 4096):
+                        d[ks] = (d[ks] + ((wm[j:j + 4096].T % p) * r[j:j + 4096] % p).sum(-1)) % p
+            else:
+                for j in range(0, lin.N, 8192):
+                    d = (d + lin.w[j:j + 8192].astype(np.int64).T @ r[j:j + 8192]) % p
+            keys.append((p, r, d))
+        return keys
+
+    keys = {"layers": [{nm: vlin(L[nm]) for nm in ("q", "k", "v", "o", "gate", "up", "down")} for L in model.layers]}
+    keys["head"] = vlin(model.head)
+    D = model.c["D"]
+    X = model.emb_q16(np.arange(model.c["V"]))
+    keys["emb"] = []
+    for p in (P1, P2):
+        r = rng.integers(0, p, D, dtype=np.int64)
+        keys["emb"].append((p, r, (((X % p) * r) % p).sum(-1) % p))
+    return keys
+
+
+def fr_row(lin, keys, xq_row, acc_row):
+    """Freivalds check of one accumulator row (experiments/commit_audit_kaggle.py:652-656); the
+    size bound applies to per-channel accumulators."""
+    if acc_row.shape != (lin.N,):
+        return False
+    if lin.kind != "group" and int(np.abs(acc_row).max()) > 127 * 32767 * lin.K:
+        return False
+    for p, r, d in keys:
+        if int((((acc_row % p) * r) % p).sum() % p) != int((((xq_row % p) * d) % p).sum() % p):
+            return False
+    return True
+
+
+def _rq(lin, acc_row, s):
+    """experiments/commit_audit_kaggle.py:657-658."""
+    return lin.requant(acc_row[None, :], np.array([[s]], np.int64))[0]
+
+
+def verify_cell(model, keys, root, T, cell, opened, ids):
+    """(ok, reason) of one cell from its opened leaves, without the weights (verify_cell,
+    experiments/commit_audit_kaggle.py:659-705)."""
+    NL = len(model.layers)
+    c = model.c
+    for n in needed(cell, NL):
+        if n not in opened:
+            return False, f"missing {n}"
+        vals, pr = opened[n]
+        if not merkle_verify(root, hb(*vals), leaf_index(*n, T, NL), pr):
+            return False, f"merkle {n}"
+    L, t = cell
+    H, KV, hd = c["H"], c["KV"], c["hd"]
+    if L == NL:
+        x = opened[("X", NL, t)][0][0]
+        hacc = opened[("HEAD", NL, t)][0][0]
+        xq, s = qrow(irms(x[None, :], model.gf), 15)
+        if not fr_row(model.head, keys["head"], xq[0], hacc):
+            return False, "head"
+        return True, None
+    Lw = model.layers[L]
+    K = keys["layers"][L]
+    if L == 0:
+        xr = opened[("X", 0, t)][0][0]
+        for p, r, de in keys["emb"]:
+            if int((((xr % p) * r) % p).sum() % p) != int(de[ids[t]]):
+                return False, f"embedding@{t}"
+    x = opened[("X", L, t)][0][0]
+    kacc, vacc = opened[("KV", L, t)][0]
+    xq, sh = qrow(irms(x[None, :], Lw["g1"]), 15)
+    if not (fr_row(Lw["k"], K["k"], xq[0], kacc) and fr_row(Lw["v"], K["v"], xq[0], vacc)):
+        return False, f"kv@{t}"
+    ko = _rq(Lw["k"], kacc, sh[0, 0]).reshape(KV, hd)
+    vo = _rq(Lw["v"], vacc, sh[0, 0]).reshape(KV, hd)
+    kt = shr(ko * model.cos[t] + rot_half(ko) * model.sin[t], F)
+    krk, krv = opened[("KR", L, t)][0]
+    if not (np.array_equal(krk, kt) and np.array_equal(krv, vo)):
+        return False, f"kr@{t}"
+    Kc = np.stack([opened[("KR", L, s_)][0][0] for s_ in range(t + 1)], 1)
+    Vc = np.stack([opened[("KR", L, s_)][0][1] for s_ in range(t + 1)], 1)
+    qacc = opened[("Q", L, t)][0][0]
+    oacc, gacc, uacc, dacc = opened[("R", L, t)][0]
+    if not fr_row(Lw["q"], K["q"], xq[0], qacc):
+        return False, "q"
+    qo = _rq(Lw["q"], qacc, sh[0, 0]).reshape(H, hd)
+    qo = shr(qo * model.cos[t] + rot_half(qo) * model.sin[t], F)
+    out = np.empty((H, hd), np.int64)
+    valid = np.ones((1, t + 1), bool)
+    for hh in range(H):
+        kh = hh // (H // KV)
+        qq, sq = qrow(qo[hh][None, :])
+        kk, sk = qrow(Kc[kh])
+        sc = shr(mm_exact(qq, kk.T) * model.INV, (F - sq - sk.T) + 16)
+        out[hh] = shr(np.matmul(isoftmax(sc, valid), Vc[kh]), 20)[0]
+    oq, so = qrow(out.reshape(1, H * hd), 15)
+    if not fr_row(Lw["o"], K["o"], oq[0], oacc):
+        return False, "o"
+    x2 = x + _rq(Lw["o"], oacc, so[0, 0])
+    mq, sm = qrow(irms(x2[None, :], Lw["g2"]), 15)
+    if not (fr_row(Lw["gate"], K["gate"], mq[0], gacc) and fr_row(Lw["up"], K["up"], mq[0], uacc)):
+        return False, "gate/up"
+    act = shr(isilu(_rq(Lw["gate"], gacc, sm[0, 0])) * _rq(Lw["up"], uacc, sm[0, 0]), F)
+    dq, sd = qrow(act[None, :], 15)
+    if not fr_row(Lw["down"], K["down"], dq[0], dacc):
+        return False, "down"
+    if not np.array_equal(x2 + _rq(Lw["down"], dacc, sd[0, 0]), opened[("X", L + 1, t)][0][0]):
+        return False, "residual"
+    return True, None

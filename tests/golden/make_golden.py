@@ -17,6 +17,8 @@ definitions the hot path needs (the scripts' top-level code downloads checkpoint
   * ``GQLin`` constructor (float64 group-128 conversion)  experiments/group128_quality_kaggle.py:406-414
   * ``requant/Hb/merkle/prover_trace/leaves_of``  experiments/commit_audit_kaggle.py:442-445,
                                       567-575, 587-628 (the Merkle trace commitment)
+  * ``VLin/VEmb/make_verifier/Prover/needed/verify_cell``  experiments/commit_audit_kaggle.py:460-512,
+                                      629-705 (the weightless cell verifier)
 
 Synthetic integer weights come from ``oracle.synth`` and are handed to the reference's
 classes through ``__new__`` (no float checkpoint is involved).  Nothing here is imported
@@ -319,6 +321,67 @@ def g_convert(ex, G):
     print("convert", h16(lg), flush=True)
 
 
+def g_verify(ex, G):
+    """Weightless cell verification, by the reference's own make_verifier, prover_trace, Prover,
+    needed and verify_cell (experiments/commit_audit_kaggle.py:440-445, 460-512, 567-705) on the
+    per-channel tiny model: every honest cell, lying openings, a cheating down projection at one
+    layer and consistent fake attention at one layer (the reference's audit gates A1, A5, A2, A3)."""
+    ns = dict(ex.__dict__)
+    ns["P1"], ns["P2"] = 2147483647, 2147483629
+    ex._exec_lines("experiments/commit_audit_kaggle.py", 442, 445, ns)              # requant
+    ex._exec_lines("experiments/commit_audit_kaggle.py", 460, 512, ns)              # VER, VLin, VEmb, make_verifier
+    ex._exec_lines("experiments/commit_audit_kaggle.py", 567, 705, ns)              # Hb .. verify_cell
+    cfg = synth.config("tiny-ch")
+    om = synth.build_model(cfg, 2)
+    rm = ref_int_model(ex, om)
+    ids = [int(t) for t in G["commit"]["ids"]]
+    NL, T = cfg["NL"], len(ids)
+    vm, _, _ = ns["make_verifier"](rm)
+    keys = {"head_d": [h16(d) for _, _, d in vm.head.keys], "emb_de": [h16(de) for _, _, de in vm.emb.keys],
+            "L1.down_d": [h16(d) for _, _, d in vm.layers[1]["down"].keys]}
+    out = []
+    pv = ns["Prover"](ns["prover_trace"](rm, ids), NL)
+    for L in range(NL + 1):
+        for t in range(T):
+            ok, why = ns["verify_cell"](vm, cfg, pv.root, pv.index, (L, t), pv.open(ns["needed"]((L, t), NL)), ids)
+            out.append(dict(scenario="honest", cell=[L, t], ok=bool(ok), why=why))
+    rng = np.random.default_rng(11)
+    for _ in range(8):
+        cell = (int(rng.integers(NL + 1)), int(rng.integers(T)))
+        names = ns["needed"](cell, NL)
+        lie = names[int(rng.integers(len(names)))]
+        ok, why = ns["verify_cell"](vm, cfg, pv.root, pv.index, cell, pv.open(names, lie=lie), ids)
+        out.append(dict(scenario="lie", cell=list(cell), lie=[lie[0], lie[1], lie[2]], ok=bool(ok), why=why))
+    dn = rm.layers[1]["down"]                           # cheating down projection: 7-bit weights
+    cheat = ex.QLin.__new__(ex.QLin)
+    cheat.w = np.clip(np.rint(dn.w / 2.0), -63, 63).astype(np.int8)
+    cheat.M = dn.M * 2
+    cheat.Mbits = int(ex.bitlen(np.array([cheat.M.max()]))[0])
+    cheat.b = None
+    ns["CHEAT_DOWN"] = cheat
+    pc = ns["Prover"](ns["prover_trace"](rm, ids, cheat_layer=1), NL)
+    for L in range(NL + 1):
+        for t in (0, 5, 15):
+            ok, why = ns["verify_cell"](vm, cfg, pc.root, pc.index, (L, t), pc.open(ns["needed"]((L, t), NL)), ids)
+            out.append(dict(scenario="cheat", cell=[L, t], ok=bool(ok), why=why))
+
+    def fakefn(p):
+        p = p.copy()
+        for row in range(max(1, p.shape[0] // 2), p.shape[0]):
+            a0, a1 = int(p[row, 0]), int(p[row, row])
+            p[row, 0], p[row, row] = a1, a0
+        return p
+    pf = ns["Prover"](ns["prover_trace"](rm, ids, fake=(1, fakefn)), NL)
+    for t in (2, 7, 8, 12, 15):
+        ok, why = ns["verify_cell"](vm, cfg, pf.root, pf.index, (1, t), pf.open(ns["needed"]((1, t), NL)), ids)
+        out.append(dict(scenario="fake", cell=[1, t], ok=bool(ok), why=why))
+    G["verify"] = dict(model="tiny-ch", seed=2, ids=ids, keys=keys, cells=out,
+                       cheat=dict(layer=1, rule="w = clip(rint(w / 2), -63, 63), M = 2 M"),
+                       fake=dict(layer=1, rule="rows >= T/2 swap p[row, 0] and p[row, row]"))
+    bad = [(o["scenario"], o["cell"], o["why"]) for o in out if not o["ok"]]
+    print("verify", len(out), "cells;", len(bad), "rejected:", bad[:12], flush=True)
+
+
 def g_config1(ex, G):
     """0.5B architecture, 32 prompt ids, 64 greedy steps (reference full recompute)."""
     _dense_case(ex, G, "qwen2.5-0.5b", synth.config("qwen2.5-0.5b"), 5, 32, 64, 5)
@@ -403,7 +466,7 @@ def g_moe(ex, G):
 
 BUILDERS = dict(tables=g_tables, gemv_kat=g_gemv_kat, models=g_models, freivalds=g_freivalds,
                 pre_tiny=g_pre_tiny, moe=g_moe, linear=g_linear, config1=g_config1, big=g_big_layers,
-                commit=g_commit, sampler=g_sampler, convert=g_convert)
+                commit=g_commit, sampler=g_sampler, convert=g_convert, verify=g_verify)
 
 
 def main():

@@ -433,3 +433,57 @@ def test_sampled_generate_matches_reference_receipt(golden, cuda_ok):
     bad["tokens"][3] = (bad["tokens"][3] + 1) % om.c["V"]
     assert m.verify_receipt(bad) == (False, 3)
     assert m.verify_receipt(dict(r, chain="0" * 16)) == (False, "chain")
+
+
+def test_weightless_verifier_gpu_matches_reference(golden, cuda_ok):
+    """Batch cell verification on the GPU (no weights used: Freivalds keys, scales, gains, tables,
+    embedding digests) gives the reference's verdict and reason on every honest, lying, cheating
+    and fake-attention cell of the fixture."""
+    from tests.test_oracle_golden import _verify_scenarios
+    g = golden["verify"]
+    om, ids, NL, trs = _verify_scenarios(g)
+    m = _engine_from_oracle(om, max_batch=1, max_seq=64)
+    m.verifier_keys(2026)
+    keys = eo.verifier_keys(om)
+    for li, d in enumerate(m.freivalds_keys()):     # device digests equal the reference-pinned keys
+        kk = keys["head"] if li == 7 * NL else keys["layers"][li // 7][eo.LIN_NAMES[li % 7]]
+        assert np.array_equal(d, np.stack([x for _, _, x in kk])), li
+    T = len(ids)
+    levels = {k: eo.merkle_levels(eo.commit_leaves(tr, NL)) for k, tr in trs.items()}
+    for sc in ("honest", "cheat", "fake"):
+        cases = [c for c in g["cells"] if c["scenario"] == sc]
+        cells = [tuple(c["cell"]) for c in cases]
+        opened = {cell: eo.open_cell(trs[sc], NL, levels[sc], cell) for cell in cells}
+        got = m.verify_cells(T, levels[sc][-1][0], cells, opened, ids)
+        assert got == [(c["ok"], c["why"]) for c in cases], sc
+    for c in (c for c in g["cells"] if c["scenario"] == "lie"):
+        cell = tuple(c["cell"])
+        op = {cell: eo.open_cell(trs["lie"], NL, levels["lie"], cell, lie=tuple(c["lie"]))}
+        assert m.verify_cells(T, levels["lie"][-1][0], [cell], op, ids) == [(c["ok"], c["why"])], c
+
+
+def test_weightless_verifier_gpu_group_model(cuda_ok):
+    """Group-128 model (accumulators are the scaled group sums): the GPU verifier accepts every
+    honest cell and rejects tampered openings and a forged next residual row, as the oracle does."""
+    cfg = synth.config("tiny-g128")
+    om = synth.build_model(cfg, 3)
+    ids = [int(t) for t in synth.prompt_ids(4, 1, 12, cfg["V"])[0]]
+    NL, T = cfg["NL"], len(ids)
+    tr = eo.commit_trace(om, ids)
+    levels = eo.merkle_levels(eo.commit_leaves(tr, NL))
+    root = levels[-1][0]
+    m = _engine_from_oracle(om, max_batch=1, max_seq=64)
+    m.verifier_keys(7)
+    cells = [(L, t) for L in range(NL + 1) for t in range(T)]
+    opened = {cell: eo.open_cell(tr, NL, levels, cell) for cell in cells}
+    assert all(ok for ok, _ in m.verify_cells(T, root, cells, opened, ids))
+    # a changed accumulator with its leaf re-committed elsewhere still fails its Merkle proof
+    bad = {(1, 5): eo.open_cell(tr, NL, levels, (1, 5), lie=("R", 1, 5))}
+    assert m.verify_cells(T, root, [(1, 5)], bad, ids) == [(False, "merkle ('R', 1, 5)")]
+    # a prover whose whole commitment carries a wrong down accumulator is caught by Freivalds
+    tr2 = eo.commit_trace(om, ids)
+    tr2["A"][0]["down"] = tr2["A"][0]["down"].copy()
+    tr2["A"][0]["down"][7, 3] += 1
+    lv2 = eo.merkle_levels(eo.commit_leaves(tr2, NL))
+    got = m.verify_cells(T, lv2[-1][0], [(0, 7), (0, 6)], {c: eo.open_cell(tr2, NL, lv2, c) for c in [(0, 7), (0, 6)]}, ids)
+    assert got == [(False, "down"), (True, None)]

@@ -199,3 +199,44 @@ def test_sampler_matches_reference(golden):
     r = g["receipt"]
     receipt, greedy = eo.sampled_generate(om, r["prompt"], len(r["tokens"]), r["seed"], r["temp"])
     assert receipt == r and greedy == g["greedy"]
+
+
+def _verify_scenarios(g):
+    """(model, ids, NL, traces by scenario) for the weightless-verifier fixture."""
+    cfg = synth.config(g["model"])
+    om = synth.build_model(cfg, g["seed"])
+    ids = g["ids"]
+    dn = om.layers[g["cheat"]["layer"]]["down"]
+    cheat = eo.ChannelLinear(np.clip(np.rint(dn.w / 2.0), -63, 63).astype(np.int8), dn.M * 2)
+
+    def fakefn(p):
+        p = p.copy()
+        for row in range(max(1, p.shape[0] // 2), p.shape[0]):
+            a0, a1 = int(p[row, 0]), int(p[row, row])
+            p[row, 0], p[row, row] = a1, a0
+        return p
+    trs = {"honest": eo.commit_trace(om, ids),
+           "cheat": eo.commit_trace(om, ids, cheat_layer=g["cheat"]["layer"], cheat_down=cheat),
+           "fake": eo.commit_trace(om, ids, fake=(g["fake"]["layer"], fakefn))}
+    trs["lie"] = trs["honest"]
+    return om, ids, cfg["NL"], trs
+
+
+def test_weightless_verifier_matches_reference(golden):
+    """The verifier restatement (keys, Merkle openings, Freivalds rows, recomputed cell) gives the
+    reference's verdict and reason on every honest, lying, cheating and fake-attention cell."""
+    g = golden["verify"]
+    om, ids, NL, trs = _verify_scenarios(g)
+    keys = eo.verifier_keys(om)
+    assert [eo.h16(d) for _, _, d in keys["head"]] == g["keys"]["head_d"]
+    assert [eo.h16(de) for _, _, de in keys["emb"]] == g["keys"]["emb_de"]
+    assert [eo.h16(d) for _, _, d in keys["layers"][1]["down"]] == g["keys"]["L1.down_d"]
+    T = len(ids)
+    levels = {k: eo.merkle_levels(eo.commit_leaves(tr, NL)) for k, tr in trs.items()}
+    for case in g["cells"]:
+        sc = case["scenario"]
+        cell = tuple(case["cell"])
+        lie = tuple(case["lie"]) if "lie" in case else None
+        opened = eo.open_cell(trs[sc], NL, levels[sc], cell, lie=lie)
+        ok, why = eo.verify_cell(om, keys, levels[sc][-1][0], T, cell, opened, ids)
+        assert (ok, why) == (case["ok"], case["why"]), case
