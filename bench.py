@@ -319,6 +319,7 @@ def run_ours(a, rank, world, local_rank):
     tok_dev = torch.empty((max(W, K), B), dtype=torch.int32, device="cuda")
     check(lib.exb_generate_device(m.h, B, ptr(ids_dev), W, ptr(tok_dev)))       # warm-up (captures graphs)
     torch.cuda.synchronize()
+    step_kernels = lib.exb_step_launches(m.h)       # kernel nodes of the step graph the timed loop replays
     ids_dev = tok_dev[W - 1].clone() if W > 0 else ids_dev
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -405,10 +406,11 @@ def run_ours(a, rank, world, local_rank):
         "e2e": {"value": (1 if tp else world) * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * 3 * 4,
                 "d2h_bytes_per_step": 4 * B,
                 "path": "exb_forward(host ids) -> host next-token, one call per step"},
-        # per step: B <= 4 one CUDA graph (embed, 10 kernels per layer, final norm, head, token feedback);
-        # wider batches one tensor-core chunk (embed, 14 per layer: norms, digit planes, GEMMs, rope,
-        # attention, qrow; final norm, digits, head GEMM, head rows)
-        "gpu_launches": K * (1 + 10 * c["NL"] + 3) if B <= 4 else K * (1 + 14 * c["NL"] + 4),
+        # B <= 4: every step is one CUDA graph whose kernel nodes the engine counts at capture (embed,
+        # 7 per layer, final norm, head, token feedback); wider batches launch one tensor-core chunk
+        # per step (embed, 14 per layer: norms, digit planes, GEMMs, rope, attention, qrow; final
+        # norm, digits, head GEMM, head rows)
+        "gpu_launches": K * step_kernels if B <= 4 else K * (1 + 14 * c["NL"] + 4),
         "clocks": clk.summary(),
     }
     if world == 1 and not a.no_cpu:

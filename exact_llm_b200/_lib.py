@@ -61,6 +61,7 @@ SIGNATURES = {
                                     ctypes.c_int64]),
     "exb_sampling_positions": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]),
     "exb_verifier_emb_keys": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "exb_step_launches": (ctypes.c_int, [ctypes.c_void_p]),
     "exb_verify_cells": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
                                         ctypes.c_int64, ctypes.c_void_p]),

@@ -116,6 +116,7 @@ struct exb_model {
   int64_t* commit_lin = nullptr;        // device: accumulator offsets | lengths in the trace row
   // integer sampler (exb_sampling): per-row seed and next sampling position, used by the decode
   // steps of exb_generate / exb_generate_device instead of the greedy argmax
+  int step_kernels = 0;                 // kernel nodes of the last captured step graph
   bool samp_on = false, samp_active = false;
   int64_t samp_tnum = 1 << 16;
   unsigned long long* samp_seed = nullptr;   // (RMAX), arena
@@ -728,6 +729,19 @@ static int run_step(exb_model* m, int R, const int32_t* ids, const int32_t* seq,
     cudaError_t e2 = cudaStreamEndCapture(m->st, &graph);
     if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("step capture: ") + cudaGetErrorString(e));
     if (e2 != cudaSuccess) FAIL(EXB_ECUDA, std::string("end capture: ") + cudaGetErrorString(e2));
+    {   // kernel launches of this step graph (reported by exb_step_launches)
+      size_t nn = 0;
+      int kernels = 0;
+      if (cudaGraphGetNodes(graph, nullptr, &nn) == cudaSuccess && nn) {
+        std::vector<cudaGraphNode_t> nodes(nn);
+        if (cudaGraphGetNodes(graph, nodes.data(), &nn) == cudaSuccess)
+          for (auto nd : nodes) {
+            cudaGraphNodeType ty;
+            if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++kernels;
+          }
+      }
+      m->step_kernels = kernels;
+    }
     cudaGraphExec_t ge;
     e = cudaGraphInstantiate(&ge, graph, 0);
     cudaGraphDestroy(graph);
@@ -1608,6 +1622,7 @@ int exb_trace_enable(exb_model* m, int on) {
   return EXB_OK;
 }
 int64_t exb_trace_row_len(exb_model* m) { return m ? m->trace_row : -1; }
+int exb_step_launches(exb_model* m) { return m ? m->step_kernels : -1; }
 // ---- Merkle trace commitment
 int exb_commit_begin(exb_model* m, int seq, int capacity) {
   if (!m || !m->finalized) FAIL(EXB_EINVAL, "exb_commit_begin: model not finalized");

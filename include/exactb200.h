@@ -229,6 +229,9 @@ int exb_set_option(exb_model* m, const char* name, int64_t value);
  * per-layer `sel` (experiments/moe_exact_kaggle.py:454-467). */
 int exb_moe_selections(exb_model* m, int layer, int32_t* host, int64_t n);
 
+/* kernel launches in the last captured decode-step graph (the count behind bench.py's gpu_launches) */
+int exb_step_launches(exb_model* m);
+
 /* device error word: bit 1 |V| >= 2^31 (V cache range), 2 wait timeout, 4 Freivalds, 8 bounds */
 int exb_device_errors(exb_model* m, int* bits);
 
