@@ -105,8 +105,7 @@ __global__ void __launch_bounds__(128) k_commit_leaves(const int64_t* __restrict
   Sha256 s;
   sha_init(s);
   for (int j = 0; j < ns; ++j) {
-    const int64_t* p = base + off[j];
-    for (int64_t i = 0; i < len[j]; ++i) sha_i64(s, (uint64_t)__ldg(reinterpret_cast<const long long*>(p + i)));
+    sha_i64_array(s, base + off[j], len[j]);
     sha_byte(s, '|');
   }
   sha_final(s, out + idx * 32);

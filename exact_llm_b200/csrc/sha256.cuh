@@ -96,6 +96,50 @@ EXB_DEV void sha_i64(Sha256& s, uint64_t v) {
   }
 }
 
+// An int64 array's little-endian bytes: bytes up to the next block boundary go through the
+// buffer, then whole 64-byte blocks are assembled straight from memory (aligned 32-bit loads,
+// shifted by the stream's byte offset, byte-swapped to big-endian words) into a register block,
+// then the tail goes through the buffer again.  No load reaches past the array: the extra word of
+// a misaligned block is 4-byte aligned and starts inside the array, whose end is 8-byte aligned.
+EXB_DEV void sha_i64_array(Sha256& s, const int64_t* p, int64_t n) {
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(p);
+  const int64_t nbytes = n * 8;
+  int64_t pos = 0;
+  while (s.nb != 0 && pos < nbytes) {
+    if ((pos & 7) == 0 && s.nb + 8 <= 64 && pos + 8 <= nbytes) {
+      sha_i64(s, (uint64_t)__ldg(reinterpret_cast<const long long*>(src + pos)));
+      pos += 8;
+    } else {
+      sha_byte(s, src[pos]);
+      ++pos;
+    }
+  }
+  if (nbytes - pos >= 64) {
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(src + pos);
+    const int sh = (int)(a0 & 3) * 8;
+    const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(a0 & ~(uintptr_t)3);
+    const int64_t nblk = (nbytes - pos) / 64;
+    uint32_t h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = s.h[i];
+    for (int64_t b = 0; b < nblk; ++b) {
+      uint32_t lw[17];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) lw[i] = __ldg(wsrc + 16 * b + i);
+      lw[16] = sh ? __ldg(wsrc + 16 * b + 16) : 0u;
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = __byte_perm(__funnelshift_r(lw[i], lw[i + 1], sh), 0, 0x0123);
+      sha_compress(h, w);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s.h[i] = h[i];
+    s.total += (uint64_t)nblk * 64;
+    pos += nblk * 64;
+  }
+  for (; pos < nbytes; ++pos) sha_byte(s, src[pos]);
+}
+
 EXB_DEV void sha_final(Sha256& s, uint8_t* out) {
   const uint64_t bits = s.total * 8;
   sha_byte(s, 0x80u);

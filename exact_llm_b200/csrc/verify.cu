@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(128) k_verify_leaves(int n, const VLeafRec* __
   sha_init(s);
   int64_t off = r.voff;
   for (int j = 0; j < r.nseg; ++j) {
-    for (int64_t e = 0; e < r.len[j]; ++e) sha_i64(s, (uint64_t)__ldg(reinterpret_cast<const long long*>(values + off + e)));
+    sha_i64_array(s, values + off, r.len[j]);
     sha_byte(s, '|');
     off += r.len[j];
   }
