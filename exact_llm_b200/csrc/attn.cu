@@ -580,4 +580,226 @@ cudaError_t launch_attn_rope(const AttnArgs& a, cudaStream_t st, bool pdl) {
   return cudaLaunchKernelEx(&cfg, kern, a, SCmax);
 }
 
+
+// ---------------------------------------------------------------- prefill attention (query tiles)
+// A chunk of consecutive positions of ONE sequence: each CTA takes PRT query rows of one head and
+// streams that KV head's cached rows 0..(its last position) in tiles of PKT keys, three times --
+// the row maxima, then the sums of the exp table at (max - score), then p = (e << 20) // sum and
+// p.v -- recomputing the scores each time, so the exact softmax needs no rescaling and every
+// cached K/V byte a CTA reads serves PRT query rows (the per-row kernel reads the whole prefix
+// once per row).  Keys are staged as two byte planes (k = 256 hi + lo, lo unsigned, hi signed) so
+// a score is dp2a sums: per 128 dims |sum q lo| <= 128 * 32767 * 255 < 2^31 and |sum q hi| <= 2^29,
+// then 256 hi + lo in int64 is the exact q.k.  Scores, table and shifts are the decode kernel's
+// (exact_llm.py:170-176).
+constexpr int PRT = 32;             // query rows per CTA
+constexpr int PKT = 64;             // keys per tile
+constexpr int PA_THREADS = 256;
+
+EXB_DEV int dp2a_lo_su(int a, unsigned b, int c) {
+  int d;
+  asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+EXB_DEV int dp2a_hi_su(int a, unsigned b, int c) {
+  int d;
+  asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  constexpr int TQ = HD + 8;                          // padded int16 query rows
+  constexpr int TK = HD + 8;                          // padded byte-plane key rows (bank spread)
+  int16_t* qt = reinterpret_cast<int16_t*>(sm);                                   // PRT x TQ
+  uint8_t* klo = reinterpret_cast<uint8_t*>(qt + PRT * TQ);                       // PKT x TK
+  uint8_t* khi = klo + PKT * TK;                                                  // PKT x TK
+  int32_t* vt = reinterpret_cast<int32_t*>(khi + PKT * TK);                       // PKT x HD
+  int64_t* pt = reinterpret_cast<int64_t*>(vt + PKT * HD);                        // PRT x PKT
+  __shared__ int64_t mx[PRT], ssum[PRT];
+  __shared__ int rpos[PRT], rqs[PRT], kshift[PKT];
+  const int tid = threadIdx.x, h = blockIdx.y;
+  const int r0 = blockIdx.x * PRT;
+  const int nr = min(PRT, a.R - r0);
+  const int rep = a.H / a.KV, j = h / rep;
+  const int seq = a.row_seq[r0];
+  const size_t cbase = ((size_t)seq * a.KV + j) * a.Smax;
+  for (int e = tid; e < PRT * (HD / 8); e += PA_THREADS) {
+    const int r = e / (HD / 8), c8 = e - r * (HD / 8);
+    int4 v = make_int4(0, 0, 0, 0);
+    if (r < nr) v = reinterpret_cast<const int4*>(a.qq + ((size_t)(r0 + r) * a.H + h) * HD)[c8];
+    *reinterpret_cast<int4*>(qt + r * TQ + c8 * 8) = v;
+  }
+  if (tid < PRT) {
+    rpos[tid] = tid < nr ? a.row_pos[r0 + tid] : -1;
+    rqs[tid] = tid < nr ? a.qs[(size_t)(r0 + tid) * a.H + h] : 0;
+    mx[tid] = INT64_MIN;
+    ssum[tid] = 0;
+  }
+  __syncthreads();
+  int pend = 0;
+  for (int r = 0; r < nr; ++r) pend = max(pend, rpos[r] + 1);
+  // this thread's score block: rows 2 rg, 2 rg + 1; keys kg, kg + 16, kg + 32, kg + 48 of the tile
+  const int rg = tid >> 4, kg = tid & 15;
+  auto scores = [&](int t0, int64_t sc[2][4], bool valid[2][4]) {
+    int lo[2][4], hi[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) lo[i][k] = hi[i][k] = 0;
+#pragma unroll 4
+    for (int d = 0; d < HD; d += 8) {
+      int4 q4[2];
+      uint2 kl[4], kh[4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) q4[i] = *reinterpret_cast<const int4*>(qt + (2 * rg + i) * TQ + d);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        kl[k] = *reinterpret_cast<const uint2*>(klo + (kg + 16 * k) * TK + d);
+        kh[k] = *reinterpret_cast<const uint2*>(khi + (kg + 16 * k) * TK + d);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          lo[i][k] = dp2a_lo_su(q4[i].x, kl[k].x, lo[i][k]);
+          lo[i][k] = dp2a_hi_su(q4[i].y, kl[k].x, lo[i][k]);
+          lo[i][k] = dp2a_lo_su(q4[i].z, kl[k].y, lo[i][k]);
+          lo[i][k] = dp2a_hi_su(q4[i].w, kl[k].y, lo[i][k]);
+          hi[i][k] = __dp2a_lo(q4[i].x, (int)kh[k].x, hi[i][k]);
+          hi[i][k] = __dp2a_hi(q4[i].y, (int)kh[k].x, hi[i][k]);
+          hi[i][k] = __dp2a_lo(q4[i].z, (int)kh[k].y, hi[i][k]);
+          hi[i][k] = __dp2a_hi(q4[i].w, (int)kh[k].y, hi[i][k]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int row = 2 * rg + i, key = kg + 16 * k;
+        const int64_t acc = (int64_t)hi[i][k] * 256 + (int64_t)lo[i][k];
+        valid[i][k] = row < nr && t0 + key <= rpos[row];
+        sc[i][k] = valid[i][k] ? shr64((int64_t)((uint64_t)acc * (uint64_t)a.inv), 32 - rqs[row] - kshift[key]) : 0;
+      }
+  };
+  auto load_k = [&](int t0) {
+    const int nk = min(PKT, pend - t0);
+    for (int e = tid; e < PKT * (HD / 8); e += PA_THREADS) {
+      const int t = e / (HD / 8), c8 = e - t * (HD / 8);
+      int4 v = make_int4(0, 0, 0, 0);
+      if (t < nk) v = reinterpret_cast<const int4*>(a.kc + (cbase + t0 + t) * HD)[c8];
+      const int vs[4] = {v.x, v.y, v.z, v.w};
+      uint32_t wl[2] = {0, 0}, wh[2] = {0, 0};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {          // int16 pair -> two lo bytes and two hi bytes
+        const uint32_t x0 = (uint32_t)vs[q] & 0xffffu, x1 = (uint32_t)vs[q] >> 16;
+        const uint32_t b = (uint32_t)(q & 1) * 16;
+        wl[q >> 1] |= ((x0 & 0xffu) | ((x1 & 0xffu) << 8)) << b;
+        wh[q >> 1] |= ((x0 >> 8) | ((x1 >> 8) << 8)) << b;
+      }
+      *reinterpret_cast<uint2*>(klo + t * TK + c8 * 8) = make_uint2(wl[0], wl[1]);
+      *reinterpret_cast<uint2*>(khi + t * TK + c8 * 8) = make_uint2(wh[0], wh[1]);
+    }
+    for (int t = tid; t < PKT; t += PA_THREADS) kshift[t] = t < nk ? a.ks[cbase + t0 + t] : 0;
+  };
+  // pass 1: row maxima
+  for (int t0 = 0; t0 < pend; t0 += PKT) {
+    __syncthreads();
+    load_k(t0);
+    __syncthreads();
+    int64_t sc[2][4];
+    bool valid[2][4];
+    scores(t0, sc, valid);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      int64_t m = INT64_MIN;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) m = valid[i][k] && sc[i][k] > m ? sc[i][k] : m;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) { const int64_t w = __shfl_xor_sync(0xffffffffu, m, o); m = w > m ? w : m; }
+      if (kg == 0 && m > mx[2 * rg + i]) mx[2 * rg + i] = m;
+    }
+  }
+  // pass 2: sums of e
+  for (int t0 = 0; t0 < pend; t0 += PKT) {
+    __syncthreads();
+    load_k(t0);
+    __syncthreads();
+    int64_t sc[2][4];
+    bool valid[2][4];
+    scores(t0, sc, valid);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      int64_t sacc = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) sacc += valid[i][k] ? exp_lookup(a.exp_t, mx[2 * rg + i] - sc[i][k]) : 0;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+      if (kg == 0) ssum[2 * rg + i] += sacc;
+    }
+  }
+  // pass 3: p = (e << 20) // sum, then out += p . v (thread: row tid / 8, dims tid % 8 + 8 i)
+  constexpr int DPT = HD / 8;
+  const int orow = tid >> 3, od = tid & 7;
+  int64_t oacc[DPT];
+#pragma unroll
+  for (int i = 0; i < DPT; ++i) oacc[i] = 0;
+  for (int t0 = 0; t0 < pend; t0 += PKT) {
+    __syncthreads();
+    load_k(t0);
+    const int nk = min(PKT, pend - t0);
+    for (int e = tid; e < PKT * (HD / 4); e += PA_THREADS) {
+      const int t = e / (HD / 4), c4 = e - t * (HD / 4);
+      int4 v = make_int4(0, 0, 0, 0);
+      if (t < nk) v = reinterpret_cast<const int4*>(a.vc + (cbase + t0 + t) * HD)[c4];
+      reinterpret_cast<int4*>(vt)[e] = v;
+    }
+    __syncthreads();
+    int64_t sc[2][4];
+    bool valid[2][4];
+    scores(t0, sc, valid);
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int row = 2 * rg + i;
+        int64_t p = 0;
+        if (valid[i][k])
+          p = (int64_t)(((uint64_t)exp_lookup(a.exp_t, mx[row] - sc[i][k]) << 20) / (uint64_t)ssum[row]);
+        pt[row * PKT + kg + 16 * k] = p;
+      }
+    __syncthreads();
+    for (int t = 0; t < nk; ++t) {
+      const int64_t p = pt[orow * PKT + t];
+      if (p == 0) continue;
+#pragma unroll
+      for (int i = 0; i < DPT; ++i) oacc[i] += p * (int64_t)vt[t * HD + od + 8 * i];
+    }
+  }
+  if (orow < nr)
+#pragma unroll
+    for (int i = 0; i < DPT; ++i)
+      a.out[(size_t)(r0 + orow) * a.ldo + (size_t)h * HD + od + 8 * i] = shr64(oacc[i], 20);
+  tl_exit();
+}
+
+cudaError_t launch_attn_prefill(const AttnArgs& a, cudaStream_t st) {
+  const int rep = a.KV > 0 ? a.H / a.KV : 0;
+  if (rep < 1 || a.H % a.KV || a.R < 1) return cudaErrorInvalidValue;
+  if (a.hd != 128 && a.hd != 64 && a.hd != 32 && a.hd != 16) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)PRT * (a.hd + 8) * 2 + (size_t)PKT * (a.hd + 8) * 2 + (size_t)PKT * a.hd * 4 +
+                      (size_t)PRT * PKT * 8;
+  void (*kern)(const AttnArgs) = a.hd == 128 ? k_attn_prefill<128> : a.hd == 64 ? k_attn_prefill<64>
+                               : a.hd == 32 ? k_attn_prefill<32> : k_attn_prefill<16>;
+  static bool attr_set[4] = {false, false, false, false};
+  const int ti = a.hd == 128 ? 0 : a.hd == 64 ? 1 : a.hd == 32 ? 2 : 3;
+  if (!attr_set[ti]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set[ti] = true;
+  }
+  kern<<<dim3((a.R + PRT - 1) / PRT, a.H), PA_THREADS, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace exb

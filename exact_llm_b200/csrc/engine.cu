@@ -164,6 +164,7 @@ struct exb_model {
   int fuse_in = 1;                      // GEMVs build their int16 input rows: 1 = qrow prologue (o, down),
                                         // 2 = also the norm (q|k|v, gate|up, head), 0 = separate kernels
   bool attn_fused = true;               // decode: RoPE + cache write inside the attention kernel
+  bool attn_prefill = true;             // prefill chunks of one sequence: query-tile attention kernel
   bool tc_decode = false;               // decode-step linears on the tcgen05 GEMM (8-row tiles, split-K)
   uint8_t* dq = nullptr;                // digit planes of the decode rows (2 x TC_DECODE_ROWS x KMAX)
   int64_t* tc_tot = nullptr;            // split-K partial sums (TC_DECODE_ROWS x NMAX)
@@ -1384,6 +1385,10 @@ static int prefill_chunk(exb_model* m, int R, int64_t* logits_host, int32_t* nex
   aa.out = m->p_ao; aa.ldo = Hd; aa.R = R; aa.H = c.H; aa.KV = c.KV; aa.hd = c.hd; aa.Smax = c.max_seq;
   aa.Tmax = c.rope_len; aa.err = m->err;
   aa.inv = (int64_t)std::nearbyint(65536.0 / std::sqrt((double)c.hd));
+  // a chunk of consecutive positions of one sequence takes the query-tile attention kernel
+  bool one_seq = m->attn_prefill;
+  for (int r = 1; r < R && one_seq; ++r)
+    one_seq = m->p_hrows[PCH + r] == m->p_hrows[PCH] && m->p_hrows[2 * PCH + r] == m->p_hrows[2 * PCH] + r;
   auto lin = [&](const int16_t* xq, int K, const LinW& L, int epi, int64_t* out, int ldo) -> cudaError_t {
     cudaError_t e = launch_digits(xq, K, R, K, m->p_dig, st);
     if (e != cudaSuccess) return e;
@@ -1403,7 +1408,8 @@ static int prefill_chunk(exb_model* m, int R, int64_t* logits_host, int32_t* nex
     CK(launch_norm_q(m->p_x, D, Ld.g1, R, D, m->p_xq, D, m->p_xs, st, false));
     CK(lin(m->p_xq, D, Ld.qkv, EPI_STORE, m->p_qkv, m->Nqkv));
     CK(launch_rope_cache(aa, st, false));
-    CK(launch_attn_decode(aa, st, false));
+    if (one_seq) CK(launch_attn_prefill(aa, st));       // query tiles share the cached K/V rows
+    else CK(launch_attn_decode(aa, st, false));
     CK(launch_quant(m->p_ao, Hd, R, Hd, m->p_xq, Hd, m->p_xs, st, false));
     CK(lin(m->p_xq, Hd, Ld.o, EPI_RESID, m->p_x, D));
     CK(launch_norm_q(m->p_x, D, Ld.g2, R, D, m->p_xq, D, m->p_xs, st, false));
@@ -1966,6 +1972,7 @@ int exb_set_option(exb_model* m, const char* name, int64_t value) {
   else if (n == "tc") m->tc_on = value != 0;
   else if (n == "fuse") m->fuse_in = (int)value;
   else if (n == "attn") m->attn_fused = value != 0;
+  else if (n == "pattn") m->attn_prefill = value != 0;
   else if (n == "tcd") m->tc_decode = value != 0;
   else if (n == "pf_kb") {
     if (value < 0 || value > 1024) FAIL(EXB_EINVAL, "pf_kb: 0..1024");

@@ -224,6 +224,8 @@ cudaError_t launch_rope_cache(const AttnArgs& a, cudaStream_t st, bool pdl);
 // attention; when xq_out is set, the last CTA also writes qrow(out) (shift from amax_out)
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_attn_rope(const AttnArgs& a, cudaStream_t st, bool pdl);   // decode rows, R <= 8
+// prefill chunk of consecutive positions of one sequence (q rows and the K/V cache already written)
+cudaError_t launch_attn_prefill(const AttnArgs& a, cudaStream_t st);
 cudaError_t launch_embed_norm(const int8_t* emb, const int64_t* emb_q16, int emb_shift, const int32_t* ids, int R,
                               int D, const int64_t* g, int64_t* x, int16_t* xq, int ldq, int32_t* xs,
                               cudaStream_t st, bool pdl);

@@ -220,6 +220,8 @@ int exb_model_create_tp(const exb_config* cfg, int rank, int size, const uint8_t
  *   "fuse"    decode GEMVs build their own int16 input rows: 1 (default) the qrow of the o and down
  *             inputs; 2 also the RMSNorm of the q|k|v, gate|up and head inputs; 0 separate kernels
  *   "attn"    1 (default): decode RoPE + K/V cache write inside the attention kernel; 0 separate
+ *   "pattn"   1 (default): prefill chunks of one sequence run the query-tile attention kernel;
+ *             0: the per-row kernel
  *   "tcd"     1: decode-step linears on the tcgen05 GEMM (8-row tiles); 0 (default) CUDA-core GEMVs
  * Cached step graphs are dropped. */
 int exb_set_option(exb_model* m, const char* name, int64_t value);

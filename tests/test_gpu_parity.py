@@ -487,3 +487,18 @@ def test_weightless_verifier_gpu_group_model(cuda_ok):
     lv2 = eo.merkle_levels(eo.commit_leaves(tr2, NL))
     got = m.verify_cells(T, lv2[-1][0], [(0, 7), (0, 6)], {c: eo.open_cell(tr2, NL, lv2, c) for c in [(0, 7), (0, 6)]}, ids)
     assert got == [(False, "down"), (True, None)]
+
+
+@pytest.mark.parametrize("T", [37, 300])
+def test_prefill_attention_kernels_agree(cuda_ok, T):
+    """Prefill chunks of one sequence through the query-tile attention kernel give the logits of
+    the per-row kernel bit for bit (7B layer shapes, chunks of 256 rows, a ragged last tile)."""
+    from exact_llm_b200 import ExactModel, configs
+    c = configs.arch("qwen2.5-7b", NL=2)
+    m = ExactModel.synthetic(c, 91, max_batch=1, max_seq=T + 8)
+    ids = np.random.default_rng(T).integers(0, c["V"], T).astype(np.int32)
+    out = {}
+    for pa in (0, 1):
+        m.set_option("pattn", pa)
+        out[pa] = m.forward(ids, m.new_cache(0))
+    assert np.array_equal(out[0], out[1])
