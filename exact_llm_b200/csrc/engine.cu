@@ -584,7 +584,9 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     // fused inputs: each GEMV CTA computes its int16 rows in its prologue (qrow with the
     // producer's published max at level 1, also the norm at level 2) while its first weight bytes
     // stream into L2
-    const bool fz = m->fuse_in >= 1 && !m->fr_on;          // o and down: qrow in the prologue
+    // o and down: qrow in the prologue (not under tensor parallelism: the residual update after the
+    // all-reduce requantises with the row shift the separate qrow kernel publishes in m->xs)
+    const bool fz = m->fuse_in >= 1 && !m->fr_on && !tp;
     const bool fzn = m->fuse_in >= 2 && !m->fr_on && !cm;  // q|k|v and gate|up: norm in the prologue
     if (!fzn)
       RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, nullptr,

@@ -32,11 +32,13 @@ def main():
     check(lib.exb_model_generate(m.h, int(g["seed"])))
     m.finalize()
     pre, rows, toks = m.greedy(g["prompt"], len(g["tokens"]))
-    ok = eo.h16(pre) == g["prefill"] and toks == g["tokens"] and [eo.h16(r) for r in rows] == g["rows"]
+    parts = {"prefill": eo.h16(pre) == g["prefill"], "tokens": toks == g["tokens"],
+             "rows": [eo.h16(r) for r in rows] == g["rows"]}
+    ok = all(parts.values())
     flags = [None] * world
     dist.all_gather_object(flags, bool(ok))
     if rank == 0:
-        print(json.dumps({"key": key, "world": world, "ranks_ok": flags}), flush=True)
+        print(json.dumps({"key": key, "world": world, "ranks_ok": flags, "rank0_parts": parts}), flush=True)
     m.close()
     dist.destroy_process_group()
     sys.exit(0 if all(flags) else 1)
