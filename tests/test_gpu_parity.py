@@ -502,3 +502,23 @@ def test_prefill_attention_kernels_agree(cuda_ok, T):
         m.set_option("pattn", pa)
         out[pa] = m.forward(ids, m.new_cache(0))
     assert np.array_equal(out[0], out[1])
+
+
+def test_long_context_attention_kernels_agree(cuda_ok):
+    """1100-token context (every decode-attention CTA walks several 128-key tiles, the prefill runs
+    five 256-row chunks): the fused decode attention and the query-tile prefill attention give the
+    per-row kernels' logits bit for bit."""
+    from exact_llm_b200 import ExactModel, configs
+    c = configs.arch("qwen2.5-7b", NL=1)
+    T, steps = 1100, 3
+    m = ExactModel.synthetic(c, 17, max_batch=1, max_seq=T + steps + 8)
+    ids = np.random.default_rng(5).integers(0, c["V"], T).astype(np.int32)
+    out = {}
+    for fused in (0, 1):
+        m.set_option("pattn", fused)
+        m.set_option("attn", fused)
+        pre = m.forward(ids, m.new_cache(0))
+        toks, rows = m.generate([int(pre[-1].argmax())], steps, want_logits=True)
+        out[fused] = (pre, np.array(toks), np.array(rows))
+    for a, b in zip(out[0], out[1]):
+        assert np.array_equal(a, b)
