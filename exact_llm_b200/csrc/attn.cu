@@ -615,8 +615,9 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
   uint8_t* klo = reinterpret_cast<uint8_t*>(qt + PRT * TQ);                       // PKT x TK
   uint8_t* khi = klo + PKT * TK;                                                  // PKT x TK
   int32_t* vt = reinterpret_cast<int32_t*>(khi + PKT * TK);                       // PKT x HD
-  int64_t* pt = reinterpret_cast<int64_t*>(vt + PKT * HD);                        // PRT x PKT
+  int32_t* pt = vt + PKT * HD;                                                    // PRT x PKT (p <= 2^20)
   __shared__ int64_t mx[PRT], ssum[PRT];
+  __shared__ double sinv[PRT];
   __shared__ int rpos[PRT], rqs[PRT], kshift[PKT];
   const int tid = threadIdx.x, h = blockIdx.y;
   const int r0 = blockIdx.x * PRT;
@@ -738,7 +739,11 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
       if (kg == 0) ssum[2 * rg + i] += sacc;
     }
   }
-  // pass 3: p = (e << 20) // sum, then out += p . v (thread: row tid / 8, dims tid % 8 + 8 i)
+  // pass 3: p = (e << 20) // sum (exact floor division through a per-row reciprocal and integer
+  // corrections; p <= 2^20), then out += p . v as 32 x 32 -> 64-bit products (thread: row tid / 8,
+  // dims tid % 8 + 8 i)
+  __syncthreads();
+  if (tid < PRT) sinv[tid] = ssum[tid] > 0 ? __drcp_rn((double)ssum[tid]) : 0.0;
   constexpr int DPT = HD / 8;
   const int orow = tid >> 3, od = tid & 7;
   int64_t oacc[DPT];
@@ -763,17 +768,17 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int row = 2 * rg + i;
-        int64_t p = 0;
+        int32_t p = 0;
         if (valid[i][k])
-          p = (int64_t)(((uint64_t)exp_lookup(a.exp_t, mx[row] - sc[i][k]) << 20) / (uint64_t)ssum[row]);
+          p = (int32_t)floordiv_small_q(exp_lookup(a.exp_t, mx[row] - sc[i][k]) << 20, ssum[row], sinv[row]);
         pt[row * PKT + kg + 16 * k] = p;
       }
     __syncthreads();
     for (int t = 0; t < nk; ++t) {
-      const int64_t p = pt[orow * PKT + t];
+      const int32_t p = pt[orow * PKT + t];
       if (p == 0) continue;
 #pragma unroll
-      for (int i = 0; i < DPT; ++i) oacc[i] += p * (int64_t)vt[t * HD + od + 8 * i];
+      for (int i = 0; i < DPT; ++i) oacc[i] += (int64_t)p * (int64_t)vt[t * HD + od + 8 * i];
     }
   }
   if (orow < nr)
@@ -788,7 +793,7 @@ cudaError_t launch_attn_prefill(const AttnArgs& a, cudaStream_t st) {
   if (rep < 1 || a.H % a.KV || a.R < 1) return cudaErrorInvalidValue;
   if (a.hd != 128 && a.hd != 64 && a.hd != 32 && a.hd != 16) return cudaErrorInvalidValue;
   const size_t smem = (size_t)PRT * (a.hd + 8) * 2 + (size_t)PKT * (a.hd + 8) * 2 + (size_t)PKT * a.hd * 4 +
-                      (size_t)PRT * PKT * 8;
+                      (size_t)PRT * PKT * 4;
   void (*kern)(const AttnArgs) = a.hd == 128 ? k_attn_prefill<128> : a.hd == 64 ? k_attn_prefill<64>
                                : a.hd == 32 ? k_attn_prefill<32> : k_attn_prefill<16>;
   static bool attr_set[4] = {false, false, false, false};
