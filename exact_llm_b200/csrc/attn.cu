@@ -273,7 +273,9 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
 // head of a KV group writes the row of its own position to the cache (one writer per KV row).
 // The three exact softmax phases exchange maxima, sums and partial p.v through distributed shared
 // memory (every peer value loaded at once); all sums are integer sums, so the split changes no bit.
-constexpr int ATR_TILE = 128;       // key/value positions staged in shared memory at a time
+// key/value positions staged in shared memory at a time: 128, or 64 where the cache holds more than
+// 2048 positions, so the score array and the tiles stay small enough for every CTA of a 40-head
+// model to be resident at once (one wave)
 
 EXB_DEV int64_t rope_value(const int64_t* row, int d, int half, int64_t c, int64_t s) {
   const int64_t x = ld_cg(row + d);
@@ -281,7 +283,7 @@ EXB_DEV int64_t rope_value(const int64_t* row, int d, int half, int64_t c, int64
   return shr64((int64_t)((uint64_t)x * (uint64_t)c + (uint64_t)rot * (uint64_t)s), 16);
 }
 
-template <int HD>
+template <int HD, int TILE>
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn_rope(const AttnArgs a, int SCmax) {
   extern __shared__ __align__(16) unsigned char sm[];
   constexpr int TP = HD + 8;                 // padded K row (int16): 8 consecutive rows hit distinct banks
@@ -302,9 +304,9 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
   int64_t* sc = reinterpret_cast<int64_t*>(sm + 768);                        // SCmax
   int64_t* pout = sc + SCmax;                                                 // HD
   int64_t* pv = pout + HD;                                                    // ATT_THREADS
-  int* ksh = reinterpret_cast<int*>(pv + ATT_THREADS);                        // ATR_TILE
-  int16_t* ktile = reinterpret_cast<int16_t*>(ksh + ATR_TILE);                // ATR_TILE x TP
-  int32_t* vtile = reinterpret_cast<int32_t*>(ktile + (size_t)ATR_TILE * TP); // ATR_TILE x HD
+  int* ksh = reinterpret_cast<int*>(pv + ATT_THREADS);                        // TILE
+  int16_t* ktile = reinterpret_cast<int16_t*>(ksh + TILE);                // TILE x TP
+  int32_t* vtile = reinterpret_cast<int32_t*>(ktile + (size_t)TILE * TP); // TILE x HD
 
   // ---- before the wait: positions, this row's cos/sin, the first tile of cached rows
   const int pos = a.row_pos[r], seq = a.row_seq[r];
@@ -332,7 +334,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
     for (int e = tid; e < nt * (HD / 4); e += ATT_THREADS)
       reinterpret_cast<int4*>(vtile)[e] = reinterpret_cast<const int4*>(a.vc + (cbase + t0 + tb) * HD)[e];
   };
-  const int nt0 = min(ATR_TILE, n);
+  const int nt0 = min(TILE, n);
   stage_k(0, nt0);
   stage_v(0, nt0);
 
@@ -420,15 +422,15 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
 
   // ---- phase 1: scores (two threads per key row, half a head each), local max
   const int qs = qs_s;
-  for (int tb = 0; tb < n; tb += ATR_TILE) {
-    const int nt = min(ATR_TILE, n - tb);
+  for (int tb = 0; tb < n; tb += TILE) {
+    const int nt = min(TILE, n - tb);
     if (tb > 0) {
       __syncthreads();
       stage_k(tb, nt);
       patch(tb, nt, true, false);
       __syncthreads();
     }
-    for (int p0 = 0; p0 < 2 * ATR_TILE; p0 += ATT_THREADS) {
+    for (int p0 = 0; p0 < 2 * TILE; p0 += ATT_THREADS) {
       const int p = p0 + tid, t = p >> 1, hf = p & 1;
       int64_t acc = 0;
       if (t < nt) {
@@ -503,8 +505,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
     constexpr int NP = ATT_THREADS / HD;
     const int d = tid % HD, part = tid / HD;
     int64_t acc = 0;
-    for (int tb = 0; tb < n; tb += ATR_TILE) {
-      const int nt = min(ATR_TILE, n - tb);
+    for (int tb = 0; tb < n; tb += TILE) {
+      const int nt = min(TILE, n - tb);
       __syncthreads();
       if (tb > 0) {
         stage_v(tb, nt);
@@ -555,13 +557,18 @@ cudaError_t launch_attn_rope(const AttnArgs& a, cudaStream_t st, bool pdl) {
   if (rep < 1 || a.H % a.KV || a.R < 1 || a.R > ATT_THREADS / 32) return cudaErrorInvalidValue;
   if (a.hd != 128 && a.hd != 64 && a.hd != 32 && a.hd != 16) return cudaErrorInvalidValue;
   const int SCmax = (((a.Smax + CL - 1) / CL) + 1) & ~1;   // even: keeps the arrays after sc 16-byte aligned
-  const size_t smem = 768 + (size_t)SCmax * 8 + (size_t)a.hd * 8 + (size_t)ATT_THREADS * 8 + (size_t)ATR_TILE * 4 +
-                      (size_t)ATR_TILE * (a.hd + 8) * 2 + (size_t)ATR_TILE * a.hd * 4;
+  const bool longc = a.Smax > 2048;
+  const size_t tile = longc ? 64 : 128;
+  const size_t smem = 768 + (size_t)SCmax * 8 + (size_t)a.hd * 8 + (size_t)ATT_THREADS * 8 + tile * 4 +
+                      tile * (a.hd + 8) * 2 + tile * a.hd * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  void (*kern)(const AttnArgs, int) = a.hd == 128 ? k_attn_rope<128> : a.hd == 64 ? k_attn_rope<64>
-                                    : a.hd == 32 ? k_attn_rope<32> : k_attn_rope<16>;
-  static bool attr_set[4] = {false, false, false, false};
-  const int ti = a.hd == 128 ? 0 : a.hd == 64 ? 1 : a.hd == 32 ? 2 : 3;
+  void (*kern)(const AttnArgs, int) =
+      longc ? (a.hd == 128 ? k_attn_rope<128, 64> : a.hd == 64 ? k_attn_rope<64, 64>
+               : a.hd == 32 ? k_attn_rope<32, 64> : k_attn_rope<16, 64>)
+            : (a.hd == 128 ? k_attn_rope<128, 128> : a.hd == 64 ? k_attn_rope<64, 128>
+               : a.hd == 32 ? k_attn_rope<32, 128> : k_attn_rope<16, 128>);
+  static bool attr_set[8] = {false, false, false, false, false, false, false, false};
+  const int ti = (a.hd == 128 ? 0 : a.hd == 64 ? 1 : a.hd == 32 ? 2 : 3) + (longc ? 4 : 0);
   if (!attr_set[ti]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
