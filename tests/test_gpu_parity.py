@@ -504,14 +504,16 @@ def test_prefill_attention_kernels_agree(cuda_ok, T):
     assert np.array_equal(out[0], out[1])
 
 
-def test_long_context_attention_kernels_agree(cuda_ok):
-    """1100-token context (every decode-attention CTA walks several 128-key tiles, the prefill runs
-    five 256-row chunks): the fused decode attention and the query-tile prefill attention give the
-    per-row kernels' logits bit for bit."""
+@pytest.mark.parametrize("max_seq", [1111, 2304])
+def test_long_context_attention_kernels_agree(cuda_ok, max_seq):
+    """1100-token context (every decode-attention CTA walks several key tiles -- 128 keys while the
+    cache holds at most 2048 positions, 64 beyond -- and the prefill runs five 256-row chunks): the
+    fused decode attention and the query-tile prefill attention give the per-row kernels' logits
+    bit for bit."""
     from exact_llm_b200 import ExactModel, configs
     c = configs.arch("qwen2.5-7b", NL=1)
     T, steps = 1100, 3
-    m = ExactModel.synthetic(c, 17, max_batch=1, max_seq=T + steps + 8)
+    m = ExactModel.synthetic(c, 17, max_batch=1, max_seq=max_seq)
     ids = np.random.default_rng(5).integers(0, c["V"], T).astype(np.int32)
     out = {}
     for fused in (0, 1):
