@@ -594,34 +594,51 @@ cudaError_t launch_attn_rope(const AttnArgs& a, cudaStream_t st, bool pdl) {
 // the row maxima, then the sums of the exp table at (max - score), then p = (e << 20) // sum and
 // p.v -- recomputing the scores each time, so the exact softmax needs no rescaling and every
 // cached K/V byte a CTA reads serves PRT query rows (the per-row kernel reads the whole prefix
-// once per row).  Keys are staged as two byte planes (k = 256 hi + lo, lo unsigned, hi signed) so
-// a score is dp2a sums: per 128 dims |sum q lo| <= 128 * 32767 * 255 < 2^31 and |sum q hi| <= 2^29,
-// then 256 hi + lo in int64 is the exact q.k.  Scores, table and shifts are the decode kernel's
-// (exact_llm.py:170-176).
+// once per row).  Queries and keys are staged as two byte planes each (x = 256 hi + lo, lo
+// unsigned, hi signed) and a 32 x 64 score tile is int8 tensor-core MMAs (mma.sync m16n8k32, int32
+// accumulators): q.k = 65536 (qh.kh) + 256 (qh.kl + ql.kh) + ql.kl, each plane product over 128
+// dims below 128 * 255 * 255 < 2^31, combined exactly in int64.  Scores, table and shifts are the
+// decode kernel's (exact_llm.py:170-176).
 constexpr int PRT = 32;             // query rows per CTA
 constexpr int PKT = 64;             // keys per tile
 constexpr int PA_THREADS = 256;
 
-EXB_DEV int dp2a_lo_su(int a, unsigned b, int c) {
-  int d;
-  asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
+// 8 int16 -> their 8 low bytes (unsigned digits) and 8 high bytes (signed digits), element order kept
+EXB_DEV void split_planes(const int4 v, uint2& lo, uint2& hi) {
+  lo = make_uint2(__byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x6420), __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x6420));
+  hi = make_uint2(__byte_perm((uint32_t)v.x, (uint32_t)v.y, 0x7531), __byte_perm((uint32_t)v.z, (uint32_t)v.w, 0x7531));
 }
-EXB_DEV int dp2a_hi_su(int a, unsigned b, int c) {
-  int d;
-  asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
+
+EXB_DEV uint32_t ld_s32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// D += A (16 x 32) . B (32 x 8), int8 digits (signed or unsigned per operand), int32 accumulators
+template <bool AS, bool BS>
+EXB_DEV void mma_i8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (!AS && !BS)
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3]) : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else if constexpr (!AS && BS)
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3]) : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else if constexpr (AS && !BS)
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3]) : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3]) : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 template <int HD>
 __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
   extern __shared__ __align__(16) unsigned char sm[];
-  constexpr int TQ = HD + 8;                          // padded int16 query rows
-  constexpr int TK = HD + 8;                          // padded byte-plane key rows (bank spread)
-  int16_t* qt = reinterpret_cast<int16_t*>(sm);                                   // PRT x TQ
-  uint8_t* klo = reinterpret_cast<uint8_t*>(qt + PRT * TQ);                       // PKT x TK
-  uint8_t* khi = klo + PKT * TK;                                                  // PKT x TK
-  int32_t* vt = reinterpret_cast<int32_t*>(khi + PKT * TK);                       // PKT x HD
+  constexpr int PW = HD < 32 ? 32 : HD;               // plane row: whole 32-dim MMA steps (zero tail)
+  constexpr int TB = PW + 16;                          // padded plane row: fragment loads hit 32 banks
+  constexpr int KS = PW / 32;                          // MMA k-steps per score
+  uint8_t* qlo = sm;                                                              // PRT x TB
+  uint8_t* qhi = qlo + PRT * TB;                                                  // PRT x TB
+  uint8_t* klo = qhi + PRT * TB;                                                  // PKT x TB
+  uint8_t* khi = klo + PKT * TB;                                                  // PKT x TB
+  int32_t* vt = reinterpret_cast<int32_t*>(khi + PKT * TB);                       // PKT x HD
   int32_t* pt = vt + PKT * HD;                                                    // PRT x PKT (p <= 2^20)
   __shared__ int64_t mx[PRT], ssum[PRT];
   __shared__ double sinv[PRT];
@@ -632,11 +649,14 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
   const int rep = a.H / a.KV, j = h / rep;
   const int seq = a.row_seq[r0];
   const size_t cbase = ((size_t)seq * a.KV + j) * a.Smax;
-  for (int e = tid; e < PRT * (HD / 8); e += PA_THREADS) {
-    const int r = e / (HD / 8), c8 = e - r * (HD / 8);
+  for (int e = tid; e < PRT * (PW / 8); e += PA_THREADS) {
+    const int r = e / (PW / 8), c8 = e - r * (PW / 8);
     int4 v = make_int4(0, 0, 0, 0);
-    if (r < nr) v = reinterpret_cast<const int4*>(a.qq + ((size_t)(r0 + r) * a.H + h) * HD)[c8];
-    *reinterpret_cast<int4*>(qt + r * TQ + c8 * 8) = v;
+    if (r < nr && c8 < HD / 8) v = reinterpret_cast<const int4*>(a.qq + ((size_t)(r0 + r) * a.H + h) * HD)[c8];
+    uint2 lo, hi;
+    split_planes(v, lo, hi);
+    *reinterpret_cast<uint2*>(qlo + r * TB + c8 * 8) = lo;
+    *reinterpret_cast<uint2*>(qhi + r * TB + c8 * 8) = hi;
   }
   if (tid < PRT) {
     rpos[tid] = tid < nr ? a.row_pos[r0 + tid] : -1;
@@ -647,70 +667,64 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
   __syncthreads();
   int pend = 0;
   for (int r = 0; r < nr; ++r) pend = max(pend, rpos[r] + 1);
-  // this thread's score block: rows 2 rg, 2 rg + 1; keys kg, kg + 16, kg + 32, kg + 48 of the tile
-  const int rg = tid >> 4, kg = tid & 15;
+  // warp tile: rows 16 mt .. +15, keys 16 nq .. +15 (two n8 MMA tiles); this thread's scores are
+  // the accumulator fragment: rows 16 mt + g (+ 8), keys 16 nq + 8 n + 2 tq (+ 1)
+  const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
+  const int mt = warp & 1, nq = warp >> 1;
+  auto srow = [&](int i) { return mt * 16 + g + 8 * i; };
+  auto skey = [&](int k) { return nq * 16 + (k >> 1) * 8 + 2 * tq + (k & 1); };
   auto scores = [&](int t0, int64_t sc[2][4], bool valid[2][4]) {
-    int lo[2][4], hi[2][4];
+    int acc[4][2][4];                                  // plane product (ll, lh, hl, hh) x n tile x fragment
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int p = 0; p < 4; ++p)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) lo[i][k] = hi[i][k] = 0;
-#pragma unroll 4
-    for (int d = 0; d < HD; d += 8) {
-      int4 q4[2];
-      uint2 kl[4], kh[4];
+      for (int n = 0; n < 2; ++n)
 #pragma unroll
-      for (int i = 0; i < 2; ++i) q4[i] = *reinterpret_cast<const int4*>(qt + (2 * rg + i) * TQ + d);
+        for (int f = 0; f < 4; ++f) acc[p][n][f] = 0;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        kl[k] = *reinterpret_cast<const uint2*>(klo + (kg + 16 * k) * TK + d);
-        kh[k] = *reinterpret_cast<const uint2*>(khi + (kg + 16 * k) * TK + d);
+    for (int ks = 0; ks < KS; ++ks) {
+      const int d0 = ks * 32 + 4 * tq;
+      const int ra = (mt * 16 + g) * TB + d0, rb = ra + 8 * TB;
+      const uint32_t al[4] = {ld_s32(qlo + ra), ld_s32(qlo + rb), ld_s32(qlo + ra + 16), ld_s32(qlo + rb + 16)};
+      const uint32_t ah[4] = {ld_s32(qhi + ra), ld_s32(qhi + rb), ld_s32(qhi + ra + 16), ld_s32(qhi + rb + 16)};
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        const int kb = (nq * 16 + n * 8 + g) * TB + d0;
+        const uint32_t bl0 = ld_s32(klo + kb), bl1 = ld_s32(klo + kb + 16);
+        const uint32_t bh0 = ld_s32(khi + kb), bh1 = ld_s32(khi + kb + 16);
+        mma_i8<false, false>(acc[0][n], al, bl0, bl1);
+        mma_i8<false, true>(acc[1][n], al, bh0, bh1);
+        mma_i8<true, false>(acc[2][n], ah, bl0, bl1);
+        mma_i8<true, true>(acc[3][n], ah, bh0, bh1);
       }
-#pragma unroll
-      for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          lo[i][k] = dp2a_lo_su(q4[i].x, kl[k].x, lo[i][k]);
-          lo[i][k] = dp2a_hi_su(q4[i].y, kl[k].x, lo[i][k]);
-          lo[i][k] = dp2a_lo_su(q4[i].z, kl[k].y, lo[i][k]);
-          lo[i][k] = dp2a_hi_su(q4[i].w, kl[k].y, lo[i][k]);
-          hi[i][k] = __dp2a_lo(q4[i].x, (int)kh[k].x, hi[i][k]);
-          hi[i][k] = __dp2a_hi(q4[i].y, (int)kh[k].x, hi[i][k]);
-          hi[i][k] = __dp2a_lo(q4[i].z, (int)kh[k].y, hi[i][k]);
-          hi[i][k] = __dp2a_hi(q4[i].w, (int)kh[k].y, hi[i][k]);
-        }
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const int row = 2 * rg + i, key = kg + 16 * k;
-        const int64_t acc = (int64_t)hi[i][k] * 256 + (int64_t)lo[i][k];
+        const int n = k >> 1, f = 2 * i + (k & 1);
+        const int row = srow(i), key = skey(k);
+        const int64_t qk = (int64_t)acc[3][n][f] * 65536 + ((int64_t)acc[1][n][f] + (int64_t)acc[2][n][f]) * 256 +
+                           (int64_t)acc[0][n][f];
         valid[i][k] = row < nr && t0 + key <= rpos[row];
-        sc[i][k] = valid[i][k] ? shr64((int64_t)((uint64_t)acc * (uint64_t)a.inv), 32 - rqs[row] - kshift[key]) : 0;
+        sc[i][k] = valid[i][k] ? shr64((int64_t)((uint64_t)qk * (uint64_t)a.inv), 32 - rqs[row] - kshift[key]) : 0;
       }
   };
   auto load_k = [&](int t0) {
     const int nk = min(PKT, pend - t0);
-    for (int e = tid; e < PKT * (HD / 8); e += PA_THREADS) {
-      const int t = e / (HD / 8), c8 = e - t * (HD / 8);
+    for (int e = tid; e < PKT * (PW / 8); e += PA_THREADS) {
+      const int t = e / (PW / 8), c8 = e - t * (PW / 8);
       int4 v = make_int4(0, 0, 0, 0);
-      if (t < nk) v = reinterpret_cast<const int4*>(a.kc + (cbase + t0 + t) * HD)[c8];
-      const int vs[4] = {v.x, v.y, v.z, v.w};
-      uint32_t wl[2] = {0, 0}, wh[2] = {0, 0};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {          // int16 pair -> two lo bytes and two hi bytes
-        const uint32_t x0 = (uint32_t)vs[q] & 0xffffu, x1 = (uint32_t)vs[q] >> 16;
-        const uint32_t b = (uint32_t)(q & 1) * 16;
-        wl[q >> 1] |= ((x0 & 0xffu) | ((x1 & 0xffu) << 8)) << b;
-        wh[q >> 1] |= ((x0 >> 8) | ((x1 >> 8) << 8)) << b;
-      }
-      *reinterpret_cast<uint2*>(klo + t * TK + c8 * 8) = make_uint2(wl[0], wl[1]);
-      *reinterpret_cast<uint2*>(khi + t * TK + c8 * 8) = make_uint2(wh[0], wh[1]);
+      if (t < nk && c8 < HD / 8) v = reinterpret_cast<const int4*>(a.kc + (cbase + t0 + t) * HD)[c8];
+      uint2 lo, hi;
+      split_planes(v, lo, hi);
+      *reinterpret_cast<uint2*>(klo + t * TB + c8 * 8) = lo;
+      *reinterpret_cast<uint2*>(khi + t * TB + c8 * 8) = hi;
     }
     for (int t = tid; t < PKT; t += PA_THREADS) kshift[t] = t < nk ? a.ks[cbase + t0 + t] : 0;
   };
-  // pass 1: row maxima
+  // pass 1: row maxima (the four lanes of a row in the warp by shuffles, the four warps of a row
+  // by shared-memory atomics)
   for (int t0 = 0; t0 < pend; t0 += PKT) {
     __syncthreads();
     load_k(t0);
@@ -724,8 +738,8 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
 #pragma unroll
       for (int k = 0; k < 4; ++k) m = valid[i][k] && sc[i][k] > m ? sc[i][k] : m;
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) { const int64_t w = __shfl_xor_sync(0xffffffffu, m, o); m = w > m ? w : m; }
-      if (kg == 0 && m > mx[2 * rg + i]) mx[2 * rg + i] = m;
+      for (int o = 1; o < 4; o <<= 1) { const int64_t w = __shfl_xor_sync(0xffffffffu, m, o); m = w > m ? w : m; }
+      if (tq == 0 && m != INT64_MIN) atomicMax(reinterpret_cast<long long*>(&mx[srow(i)]), (long long)m);
     }
   }
   // pass 2: sums of e
@@ -740,10 +754,10 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
     for (int i = 0; i < 2; ++i) {
       int64_t sacc = 0;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) sacc += valid[i][k] ? exp_lookup(a.exp_t, mx[2 * rg + i] - sc[i][k]) : 0;
+      for (int k = 0; k < 4; ++k) sacc += valid[i][k] ? exp_lookup(a.exp_t, mx[srow(i)] - sc[i][k]) : 0;
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
-      if (kg == 0) ssum[2 * rg + i] += sacc;
+      for (int o = 1; o < 4; o <<= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+      if (tq == 0 && sacc) atomicAdd(reinterpret_cast<unsigned long long*>(&ssum[srow(i)]), (unsigned long long)sacc);
     }
   }
   // pass 3: p = (e << 20) // sum (exact floor division through a per-row reciprocal and integer
@@ -774,11 +788,11 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
     for (int i = 0; i < 2; ++i)
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const int row = 2 * rg + i;
+        const int row = srow(i);
         int32_t p = 0;
         if (valid[i][k])
           p = (int32_t)floordiv_small_q(exp_lookup(a.exp_t, mx[row] - sc[i][k]) << 20, ssum[row], sinv[row]);
-        pt[row * PKT + kg + 16 * k] = p;
+        pt[row * PKT + skey(k)] = p;
       }
     __syncthreads();
     for (int t = 0; t < nk; ++t) {
@@ -799,8 +813,8 @@ cudaError_t launch_attn_prefill(const AttnArgs& a, cudaStream_t st) {
   const int rep = a.KV > 0 ? a.H / a.KV : 0;
   if (rep < 1 || a.H % a.KV || a.R < 1) return cudaErrorInvalidValue;
   if (a.hd != 128 && a.hd != 64 && a.hd != 32 && a.hd != 16) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)PRT * (a.hd + 8) * 2 + (size_t)PKT * (a.hd + 8) * 2 + (size_t)PKT * a.hd * 4 +
-                      (size_t)PRT * PKT * 4;
+  const size_t tb = (size_t)(a.hd < 32 ? 32 : a.hd) + 16;
+  const size_t smem = 2 * (size_t)PRT * tb + 2 * (size_t)PKT * tb + (size_t)PKT * a.hd * 4 + (size_t)PRT * PKT * 4;
   void (*kern)(const AttnArgs) = a.hd == 128 ? k_attn_prefill<128> : a.hd == 64 ? k_attn_prefill<64>
                                : a.hd == 32 ? k_attn_prefill<32> : k_attn_prefill<16>;
   static bool attr_set[4] = {false, false, false, false};
