@@ -302,10 +302,15 @@ def run_ours(a, rank, world, local_rank):
     rng = np.random.default_rng(100 + rank)
     prompts = rng.integers(0, c["V"], (B, PROMPT)).astype(np.int32)
     # prefill (outside the decode timing): rows of all sequences, position-major so every chunk
-    # holds B sequences; CUDA events on the model stream around the whole forward call
+    # holds B sequences; CUDA events on the model stream around the whole forward call, after one
+    # untimed prefill of the same prompts (first-launch module loading stays out of the number)
     barrier()
     ids = prompts.T.reshape(-1)
     seqs = np.tile(np.arange(B, dtype=np.int32), PROMPT)
+    for b in range(B):
+        m.new_cache(b)
+    m.forward_rows(ids, seqs, want_logits=False)
+    torch.cuda.synchronize()
     for b in range(B):
         m.new_cache(b)
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
