@@ -629,7 +629,7 @@ EXB_DEV void mma_i8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b
 }
 
 template <int HD>
-__global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
+__global__ void __launch_bounds__(PA_THREADS, 3) k_attn_prefill(const AttnArgs a) {
   extern __shared__ __align__(16) unsigned char sm[];
   constexpr int PW = HD < 32 ? 32 : HD;               // plane row: whole 32-dim MMA steps (zero tail)
   constexpr int TB = PW + 16;                          // padded plane row: fragment loads hit 32 banks
@@ -762,11 +762,14 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
   }
   // pass 3: p = (e << 20) // sum (exact floor division through a per-row reciprocal and integer
   // corrections; p <= 2^20), then out += p . v as 32 x 32 -> 64-bit products (thread: row tid / 8,
-  // dims tid % 8 + 8 i)
+  // dims 32 i + 4 (tid % 8) + (0..3): int4 reads of V, the 8 threads of a row on 32 distinct banks;
+  // head dim 16: dims tid % 8 + 8 i)
   __syncthreads();
   if (tid < PRT) sinv[tid] = ssum[tid] > 0 ? __drcp_rn((double)ssum[tid]) : 0.0;
   constexpr int DPT = HD / 8;
+  constexpr bool VEC = DPT % 4 == 0;                   // int4 runs of V (head dims >= 32)
   const int orow = tid >> 3, od = tid & 7;
+  auto dim_of = [&](int jd) { return VEC ? (jd >> 2) * 32 + od * 4 + (jd & 3) : od + 8 * jd; };
   int64_t oacc[DPT];
 #pragma unroll
   for (int i = 0; i < DPT; ++i) oacc[i] = 0;
@@ -795,17 +798,27 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(const AttnArgs a) {
         pt[row * PKT + skey(k)] = p;
       }
     __syncthreads();
+#pragma unroll 2
     for (int t = 0; t < nk; ++t) {
-      const int32_t p = pt[orow * PKT + t];
-      if (p == 0) continue;
+      const int64_t p = pt[orow * PKT + t];
+      if constexpr (VEC) {
 #pragma unroll
-      for (int i = 0; i < DPT; ++i) oacc[i] += (int64_t)p * (int64_t)vt[t * HD + od + 8 * i];
+        for (int i = 0; i < DPT / 4; ++i) {
+          const int4 v = *reinterpret_cast<const int4*>(vt + t * HD + dim_of(4 * i));
+          oacc[4 * i] += p * v.x;
+          oacc[4 * i + 1] += p * v.y;
+          oacc[4 * i + 2] += p * v.z;
+          oacc[4 * i + 3] += p * v.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < DPT; ++i) oacc[i] += p * (int64_t)vt[t * HD + dim_of(i)];
+      }
     }
   }
   if (orow < nr)
 #pragma unroll
-    for (int i = 0; i < DPT; ++i)
-      a.out[(size_t)(r0 + orow) * a.ldo + (size_t)h * HD + od + 8 * i] = shr64(oacc[i], 20);
+    for (int i = 0; i < DPT; ++i) a.out[(size_t)(r0 + orow) * a.ldo + (size_t)h * HD + dim_of(i)] = shr64(oacc[i], 20);
   tl_exit();
 }
 
