@@ -775,14 +775,14 @@ __global__ void __launch_bounds__(PA_THREADS, 3) k_attn_prefill(const AttnArgs a
   for (int i = 0; i < DPT; ++i) oacc[i] = 0;
   for (int t0 = 0; t0 < pend; t0 += PKT) {
     __syncthreads();
-    load_k(t0);
     const int nk = min(PKT, pend - t0);
-    for (int e = tid; e < PKT * (HD / 4); e += PA_THREADS) {
+    for (int e = tid; e < PKT * (HD / 4); e += PA_THREADS) {     // V tile lands during the scores
       const int t = e / (HD / 4), c4 = e - t * (HD / 4);
-      int4 v = make_int4(0, 0, 0, 0);
-      if (t < nk) v = reinterpret_cast<const int4*>(a.vc + (cbase + t0 + t) * HD)[c4];
-      reinterpret_cast<int4*>(vt)[e] = v;
+      if (t < nk) cp_async16(reinterpret_cast<int4*>(vt) + e, reinterpret_cast<const int4*>(a.vc + (cbase + t0 + t) * HD) + c4);
+      else reinterpret_cast<int4*>(vt)[e] = make_int4(0, 0, 0, 0);
     }
+    cp_async_commit();
+    load_k(t0);
     __syncthreads();
     int64_t sc[2][4];
     bool valid[2][4];
@@ -797,6 +797,7 @@ __global__ void __launch_bounds__(PA_THREADS, 3) k_attn_prefill(const AttnArgs a
           p = (int32_t)floordiv_small_q(exp_lookup(a.exp_t, mx[row] - sc[i][k]) << 20, ssum[row], sinv[row]);
         pt[row * PKT + skey(k)] = p;
       }
+    cp_async_wait<0>();
     __syncthreads();
 #pragma unroll 2
     for (int t = 0; t < nk; ++t) {
