@@ -5,13 +5,17 @@ One "step" = one greedy decode token for every sequence of the batch (the refere
 GraphDecoder.step, experiments/speed_fair_kaggle.py:639-645), after a 512-token prefill.
 Weights are a seeded random-init integer model of the 7B architecture generated in HBM
 (7.3 GB of int8 weights + int32 group scales, far larger than the 126 MB L2, so no flush is
-needed between steps).  Multi-GPU: one independent replica per GPU (weak scaling; the
-sequences are independent, so there is no collective on the data path).
+needed between steps).  Multi-GPU (torchrun, N ranks): one model tensor-parallel over the N GPUs
+(the north star's scaling for 7B+; strong scaling, integer all-reduces inside the step graph);
+``--replicas`` runs N independent replicas instead (weak scaling, no collective).
 
 --impl reference times the reference's CPU algorithm (exact_llm.IntModel decode = full-prefix
-recompute per generated token, exact_llm.py:262-268) through the numpy port under oracle/.
+recompute per generated token, exact_llm.py:262-268) through the numpy port under oracle/, on
+the same config: every timed step is one whole decoder layer of that recompute, the per-token
+rate follows from NL layers + the head (stated in the line).  It never loads the CUDA library.
 """
 import argparse
+import ctypes
 import json
 import os
 import subprocess
@@ -95,7 +99,7 @@ def commit_bench(model, T, layers=0):
     import hashlib
     import torch
     from exact_llm_b200 import ExactModel, configs
-    c = configs.arch(model, **({"NL": layers} if layers else {}))
+    c = configs.arch(model, **({"NL": layers} if layers else {}))  # noqa: F811
     m = ExactModel.synthetic(c, 1234, max_batch=1, max_seq=T + 8)
     ids = np.random.default_rng(7).integers(0, c["V"], T).astype(np.int32)
     m.commit_begin(0, T)
@@ -177,44 +181,61 @@ class Clocks:
 
 
 # ------------------------------------------------------------------ CPU baseline (numpy port of the reference)
-def cpu_decode_sample(c, prefix):
-    """Time the reference's per-token decode work on the host: exact_llm.generate re-runs IntModel
-    over the whole prefix (no KV cache), i.e. NL decoder layers + the head over `prefix` rows.
-    Bounded sample: one decoder layer + the head; returns (tok/s extrapolated, sample text)."""
-    from oracle import exact_oracle as eo
-    rng = np.random.default_rng(0)
-    D, H, KV, hd, I, V = (c[k] for k in ("D", "H", "KV", "hd", "I", "V"))
+class CpuDecodeSample:
+    """The reference's per-token decode work on the host: exact_llm.generate re-runs IntModel over
+    the whole prefix (no KV cache), i.e. NL decoder layers + the head over `prefix` rows.  One
+    sample = one decoder layer over the prefix (every op); the head is timed once on 64 of the
+    rows and scaled (its cost is linear in rows)."""
 
-    def glin(N, K, bias):
-        return eo.GroupLinear(rng.integers(-127, 128, (N, K), dtype=np.int8),
-                              rng.integers(1 << 16, 1 << 17, (N, K // 128)), rng.integers(-16384, 16384, N) if bias else None)
+    def __init__(self, c, prefix):
+        from oracle import exact_oracle as eo
+        self.eo, self.c, self.prefix = eo, c, prefix
+        rng = np.random.default_rng(0)
+        D, H, KV, hd, I, V = (c[k] for k in ("D", "H", "KV", "hd", "I", "V"))
 
-    L = dict(g1=np.full(D, 65536, np.int64), g2=np.full(D, 65536, np.int64), q=glin(H * hd, D, True),
-             k=glin(KV * hd, D, True), v=glin(KV * hd, D, True), o=glin(D, H * hd, False), gate=glin(I, D, False),
-             up=glin(I, D, False), down=glin(D, I, False))
-    head = eo.ChannelLinear(rng.integers(-127, 128, (V, D), dtype=np.int8), rng.integers(1 << 16, 1 << 17, V))
-    cos, sin = eo.rope_tables(prefix, hd, c["theta"])
-    om = eo.OracleModel(dict(c, NL=1), [L], np.full(D, 65536, np.int64), head,
-                        lambda ids: (rng.integers(-127, 128, (len(ids), D)) << 9), cos, sin)
-    x = rng.integers(-(1 << 17), 1 << 17, (prefix, D))
-    t0 = time.perf_counter()
-    a = eo.irms(x, L["g1"])
-    q = eo.rope(L["q"](a).reshape(prefix, H, hd).transpose(1, 0, 2), cos, sin)
-    k = eo.rope(L["k"](a).reshape(prefix, KV, hd).transpose(1, 0, 2), cos, sin)
-    v = L["v"](a).reshape(prefix, KV, hd).transpose(1, 0, 2)
-    out = om._attention(0, q, k, v, None, 0)
-    x = x + L["o"](out.transpose(1, 0, 2).reshape(prefix, H * hd))
-    m = eo.irms(x, L["g2"])
-    x = x + L["down"](eo.shr(eo.isilu(L["gate"](m)) * L["up"](m), 16))
-    t_layer = time.perf_counter() - t0
-    rows = min(prefix, 64)                  # the head's cost is linear in rows: time 64, scale
-    t0 = time.perf_counter()
-    head(eo.irms(x[:rows], om.gf))
-    t_head = (time.perf_counter() - t0) * prefix / rows
-    per_tok = c["NL"] * t_layer + t_head
-    return 1.0 / per_tok, (f"1 of {c['NL']} decoder layers at a {prefix}-token prefix + the head over {rows} of "
-                           f"{prefix} rows (scaled), full-prefix recompute per token as exact_llm.generate does; "
-                           f"layer {t_layer:.2f} s, head {t_head:.2f} s (extrapolated)")
+        def glin(N, K, bias):
+            return eo.GroupLinear(rng.integers(-127, 128, (N, K), dtype=np.int8),
+                                  rng.integers(1 << 16, 1 << 17, (N, K // 128)),
+                                  rng.integers(-16384, 16384, N) if bias else None)
+
+        self.L = dict(g1=np.full(D, 65536, np.int64), g2=np.full(D, 65536, np.int64), q=glin(H * hd, D, True),
+                      k=glin(KV * hd, D, True), v=glin(KV * hd, D, True), o=glin(D, H * hd, False),
+                      gate=glin(I, D, False), up=glin(I, D, False), down=glin(D, I, False))
+        self.head = eo.ChannelLinear(rng.integers(-127, 128, (V, D), dtype=np.int8), rng.integers(1 << 16, 1 << 17, V))
+        self.cos, self.sin = eo.rope_tables(prefix, hd, c["theta"])
+        self.om = eo.OracleModel(dict(c, NL=1), [self.L], np.full(D, 65536, np.int64), self.head,
+                                 lambda ids: (rng.integers(-127, 128, (len(ids), D)) << 9), self.cos, self.sin)
+        self.x = rng.integers(-(1 << 17), 1 << 17, (prefix, D))
+        self.head_rows = min(prefix, 64)
+        self.t_head = None
+
+    def layer(self):
+        eo, L, c, T = self.eo, self.L, self.c, self.prefix
+        H, KV, hd = c["H"], c["KV"], c["hd"]
+        t0 = time.perf_counter()
+        a = eo.irms(self.x, L["g1"])
+        q = eo.rope(L["q"](a).reshape(T, H, hd).transpose(1, 0, 2), self.cos, self.sin)
+        k = eo.rope(L["k"](a).reshape(T, KV, hd).transpose(1, 0, 2), self.cos, self.sin)
+        v = L["v"](a).reshape(T, KV, hd).transpose(1, 0, 2)
+        out = self.om._attention(0, q, k, v, None, 0)
+        x = self.x + L["o"](out.transpose(1, 0, 2).reshape(T, H * hd))
+        m = eo.irms(x, L["g2"])
+        x = x + L["down"](eo.shr(eo.isilu(L["gate"](m)) * L["up"](m), 16))
+        self.x_out = x
+        return time.perf_counter() - t0
+
+    def head_time(self):
+        x = getattr(self, "x_out", self.x)
+        t0 = time.perf_counter()
+        self.head(self.eo.irms(x[:self.head_rows], self.om.gf))
+        self.t_head = (time.perf_counter() - t0) * self.prefix / self.head_rows
+        return self.t_head
+
+    def describe(self, t_layer):
+        return (f"one of {self.c['NL']} decoder layers over a {self.prefix}-token prefix per timed step (full-prefix "
+                f"recompute per generated token, as exact_llm.generate does) + the head timed over {self.head_rows} "
+                f"of {self.prefix} rows and scaled; per token = {self.c['NL']} x layer {t_layer:.2f} s + head "
+                f"{self.t_head:.2f} s")
 
 
 def cpu_cores():
@@ -224,30 +245,46 @@ def cpu_cores():
         return os.cpu_count()
 
 
+def arch_config(a):
+    """The architecture dict of --model (the oracle's copy: the reference arm never loads the CUDA
+    library, and both arms describe the same workload)."""
+    from oracle import synth
+    c = synth.config(a.model, **({"NL": a.layers} if a.layers else {}))
+    c.pop("T", None)
+    return c
+
+
+def workload_config(a, c, world, tp):
+    return {"workload": f"{a.model}-arch greedy decode, batch {a.batch}, after a {PROMPT}-token uniform prompt",
+            "batch": a.batch, "prompt": PROMPT, "decode_steps": a.steps, "layers": c["NL"],
+            "parallelism": (f"tensor parallel x{world}" if tp else f"replicas x{world}" if world > 1 else "single GPU"),
+            "l2": "no flush: the weights stream from HBM every step (7.3 GB at 7B, L2 126 MB)"}
+
+
 # ------------------------------------------------------------------ reference arm
 def run_reference(a, rank, world):
     if rank != 0:
         return
-    from exact_llm_b200 import configs
-    c = configs.arch(a.model)
-    vals, samples = [], []
-    if a.warmup > 0:
-        cpu_decode_sample(c, PROMPT + 1)                      # untimed warm-up sample
-    t_start = time.time()
-    for _ in range(max(1, a.steps)):                          # bounded: stop after ~2 minutes of samples
-        v, s = cpu_decode_sample(c, PROMPT + 1)
-        vals.append(v)
-        samples.append(s)
-        if time.time() - t_start > 60:
-            break
-    val = float(np.median(vals))
+    c = arch_config(a)
+    tp = world > 1 and not a.replicas
+    smp = CpuDecodeSample(c, PROMPT + 1)
+    for _ in range(max(1, a.warmup)):                         # untimed warm-up samples
+        smp.layer()
+    smp.head_time()
+    times = [smp.layer() for _ in range(max(1, a.steps))]     # each timed step: one whole decoder layer
+    t_layer = float(np.median(times))
+    per_tok = c["NL"] * t_layer + smp.t_head
+    val = 1.0 / per_tok                                       # IntModel decodes one sequence at a time
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": world,
-            "steps": len(vals), "warmup": 1, "ms_per_step": 1000.0 / val, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int64 (float64 BLAS, exact < 2^53)", "data": "synthetic",
-            "config": {"workload": f"{a.model}-arch bs1 greedy decode after a {PROMPT}-token prompt", "batch": 1,
-                       "prompt": PROMPT, "parallelism": "host cores"},
+            "steps": len(times), "warmup": max(1, a.warmup), "ms_per_step": t_layer * 1e3, "higher_is_better": True,
+            "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "dtype": "int64 (float64 BLAS, exact < 2^53)", "data": "synthetic",
+            "config": workload_config(a, c, world, tp),
+            "timed_step": {"unit": f"one decoder layer of the {PROMPT + 1}-token full-prefix recompute",
+                           "seconds": times, "per_token_layers": c["NL"], "head_s": smp.t_head,
+                           "value_is": f"1 / ({c['NL']} x median step + head)"},
             "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cpu_cores(), "kind": "port",
-                             "sample": samples[0] + f"; median of {len(vals)} samples"},
+                             "sample": smp.describe(t_layer)},
             "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -272,7 +309,7 @@ def step_bytes(c, B, S):
 def run_ours(a, rank, world, local_rank):
     import torch
     torch.cuda.set_device(local_rank)
-    from exact_llm_b200 import ExactModel, configs
+    from exact_llm_b200 import ExactModel
     from exact_llm_b200._lib import check, lib, ptr
     dist = None
     if world > 1:
@@ -285,10 +322,10 @@ def run_ours(a, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
-    c = configs.arch(a.model, **({"NL": a.layers} if a.layers else {}))
+    c = arch_config(a)
     B, K, W = a.batch, a.steps, a.warmup
-    max_seq = PROMPT + W + 2 * K + 16
-    tp = a.tp and world > 1
+    max_seq = PROMPT + W + 3 * K + 16          # warm-up, timed steps, the two e2e loops
+    tp = world > 1 and not a.replicas
     if tp:
         # one model split over the ranks (tensor parallel): NCCL id from rank 0
         uid = [ExactModel.tp_unique_id() if rank == 0 else None]
@@ -339,21 +376,38 @@ def run_ours(a, rank, world, local_rank):
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    # e2e through the C ABI with HOST buffers: host token in, host next-token out, every step
+    # e2e through the public API with HOST buffers, as GraphDecoder.step does: host token in
+    # (pinned staging), the step's int64 logits row out to pinned host memory, every step
+    # (sequence 0; batch > 1 rows go through forward_rows with all B logits rows)
     last = tok_dev[K - 1].cpu().numpy().astype(np.int32)
     seqs_b = np.arange(B, dtype=np.int32)
+    Vg = c["V"]
+    if B > 1:
+        lg_host = torch.empty((B, Vg), dtype=torch.int64, pin_memory=True).numpy()
+        nxt_b = np.empty(B, np.int32)
     barrier()
     t0 = time.perf_counter()
     cur = last
     for _ in range(K):
-        _, cur = m.forward_rows(cur, seqs_b, want_logits=False)
+        if B == 1:
+            m.step(int(cur[0]))
+            cur = m.last_next
+        else:
+            check(lib.exb_forward(m.h, B, ptr(np.ascontiguousarray(cur, np.int32), ctypes.c_int32),
+                                  ptr(seqs_b, ctypes.c_int32), ptr(lg_host, ctypes.c_int64), ptr(nxt_b, ctypes.c_int32)))
+            cur = nxt_b
     e2e_s = time.perf_counter() - t0
+    # the same loop returning only the next token (4 bytes per row) for comparison
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        _, cur = m.forward_rows(cur, seqs_b, want_logits=False)
+    e2e_tok_s = time.perf_counter() - t0
     if dist:
-        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        t = torch.tensor([e2e_s, e2e_tok_s], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+        e2e_s, e2e_tok_s = float(t[0].item()), float(t[1].item())
     # dominant kernel: the fused gate|up GEMV of one layer, timed alone with CUDA events
-    import ctypes
     avg = ctypes.c_float()
     nbytes = ctypes.c_double()
     if B <= 4:
@@ -371,12 +425,14 @@ def run_ours(a, rank, world, local_rank):
     sb = step_bytes(c, B, S_mid)
     step_ms = ms / K
     step_gbs = sb / (step_ms * 1e-3) / 1e9
+    gpu_gbs = step_gbs / world if tp else step_gbs        # tensor parallel: each GPU streams its 1/N slice
     if rank != 0:
         m.close()                      # step graphs (NCCL inside under --tp) go before the process group
         if dist:
             dist.destroy_process_group()
         return
     value = (1 if tp else world) * B * K / (ms * 1e-3)
+    units = 1 if tp else world
     # prefill: the whole forward (every op) and the tcgen05 linear alone at the 7B gate|up shape
     prefill = {"tokens": PROMPT * B, "seconds": prefill_s, "tok_s": PROMPT * B / prefill_s,
                "effective_tops": lin_flops_fn(c) * PROMPT * B / prefill_s / 1e12,
@@ -393,13 +449,9 @@ def run_ours(a, rank, world, local_rank):
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": "int8 x int16 -> int64", "data": "synthetic",
-        "config": {"workload": f"{a.model}-arch greedy decode, batch {B}, after a {PROMPT}-token uniform prompt",
-                   "batch": B, "prompt": PROMPT, "decode_steps": K, "layers": c["NL"],
-                   "parallelism": (f"tensor parallel x{world} (NCCL, in-graph all-reduces)" if tp else
-                                   f"replicas x{world}" if world > 1 else "single GPU"),
-                   "l2": "no flush: 7.3 GB of weights stream from HBM every step (L2 126 MB)"},
-        "decode_hbm": {"bytes_per_step": sb, "achieved_gbs": step_gbs, "peak_gbs": hbm, "frac": step_gbs / hbm,
-                       "peak_source": src},
+        "config": workload_config(a, c, world, tp),
+        "decode_hbm": {"bytes_per_step": sb, "achieved_gbs": step_gbs, "per_gpu_gbs": gpu_gbs, "peak_gbs": hbm,
+                       "frac": gpu_gbs / hbm, "peak_source": src},
         "roofline": {"bound": "hbm", "kernel": kern_name,
                      "achieved": kern_gbs, "peak": hbm, "unit": "GB/s", "frac": kern_gbs / hbm,
                      "traffic": GU_TRAFFIC if a.model == "qwen2.5-7b" and B == 1 else None,   # R=1 capture
@@ -408,9 +460,12 @@ def run_ours(a, rank, world, local_rank):
                      "avg_launch_ms": avg.value, "algorithmic_bytes": nbytes.value,
                      "peak_source": src},
         "prefill": prefill,
-        "e2e": {"value": (1 if tp else world) * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * 3 * 4,
-                "d2h_bytes_per_step": 4 * B,
-                "path": "exb_forward(host ids) -> host next-token, one call per step"},
+        "e2e": {"value": units * B * K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * 3 * 4,
+                "d2h_bytes_per_step": 8 * Vg * B + 4 * B,
+                "path": "ExactModel.step(token) (GraphDecoder.step): host token in, the int64 logits row out to "
+                        "pinned host memory, one call per step",
+                "tokens_only": {"value": units * B * K / e2e_tok_s, "d2h_bytes_per_step": 4 * B,
+                                "path": "forward_rows(host ids) -> host next-token"}},
         # B <= 4: every step is one CUDA graph whose kernel nodes the engine counts at capture (embed,
         # 7 per layer, final norm, head, token feedback); wider batches launch one tensor-core chunk
         # per step (embed, 14 per layer: norms, digit planes, GEMMs, rope, attention, qrow; final
@@ -419,8 +474,11 @@ def run_ours(a, rank, world, local_rank):
         "clocks": clk.summary(),
     }
     if world == 1 and not a.no_cpu:
-        v, s = cpu_decode_sample(c, PROMPT + 1)
-        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cpu_cores(), "kind": "port", "sample": s}
+        smp = CpuDecodeSample(c, PROMPT + 1)
+        t_layer = smp.layer()
+        smp.head_time()
+        line["cpu_baseline"] = {"value": 1.0 / (c["NL"] * t_layer + smp.t_head), "unit": "tok/s", "cores": cpu_cores(),
+                                "kind": "port", "sample": smp.describe(t_layer)}
     print(json.dumps(line), flush=True)
     m.close()
     if dist:
@@ -437,7 +495,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-gemm", action="store_true", help="skip the tensor-core GEMM / int8 peak measurement")
-    ap.add_argument("--tp", action="store_true", help="with --gpus N under torchrun: one model split over the N GPUs")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with --gpus N under torchrun: N independent replicas instead of one tensor-parallel model")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens before decode (profiling uses a short one)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures only)")
     ap.add_argument("--commit", type=int, default=0, metavar="T",

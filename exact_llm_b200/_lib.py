@@ -48,6 +48,8 @@ SIGNATURES = {
     "exb_generate": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, c_i32p, ctypes.c_int, c_i32p, c_i64p]),
     "exb_generate_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
                                            ctypes.c_void_p]),
+    "exb_kv_export": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                     ctypes.c_void_p, ctypes.c_void_p]),
     "exb_trace_enable": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "exb_trace_row_len": (ctypes.c_int64, [ctypes.c_void_p]),
     "exb_trace_read": (ctypes.c_int, [ctypes.c_void_p, c_i64p, ctypes.c_int64]),

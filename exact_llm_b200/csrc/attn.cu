@@ -242,12 +242,12 @@ cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
                                     : a.hd == 32 ? k_attn_decode<32> : k_attn_decode<16>;
   if (a.hd != 128 && a.hd != 64 && a.hd != 32 && a.hd != 16) return cudaErrorInvalidValue;
   // raised once to the full budget and never lowered (see the GEMV launcher)
-  static bool attr_set[4] = {false, false, false, false};
+  static DevOnce attr_set[4];
   const int ti = a.hd == 128 ? 0 : a.hd == 64 ? 1 : a.hd == 32 ? 2 : 3;
-  if (!attr_set[ti]) {
+  if (!attr_set[ti].done()) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
-    attr_set[ti] = true;
+    attr_set[ti].set();
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CL, a.KV, a.R);
@@ -567,12 +567,12 @@ cudaError_t launch_attn_rope(const AttnArgs& a, cudaStream_t st, bool pdl) {
                : a.hd == 32 ? k_attn_rope<32, 64> : k_attn_rope<16, 64>)
             : (a.hd == 128 ? k_attn_rope<128, 128> : a.hd == 64 ? k_attn_rope<64, 128>
                : a.hd == 32 ? k_attn_rope<32, 128> : k_attn_rope<16, 128>);
-  static bool attr_set[8] = {false, false, false, false, false, false, false, false};
+  static DevOnce attr_set[8];
   const int ti = (a.hd == 128 ? 0 : a.hd == 64 ? 1 : a.hd == 32 ? 2 : 3) + (longc ? 4 : 0);
-  if (!attr_set[ti]) {
+  if (!attr_set[ti].done()) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
-    attr_set[ti] = true;
+    attr_set[ti].set();
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CL, a.H, a.R);
@@ -831,12 +831,12 @@ cudaError_t launch_attn_prefill(const AttnArgs& a, cudaStream_t st) {
   const size_t smem = 2 * (size_t)PRT * tb + 2 * (size_t)PKT * tb + (size_t)PKT * a.hd * 4 + (size_t)PRT * PKT * 4;
   void (*kern)(const AttnArgs) = a.hd == 128 ? k_attn_prefill<128> : a.hd == 64 ? k_attn_prefill<64>
                                : a.hd == 32 ? k_attn_prefill<32> : k_attn_prefill<16>;
-  static bool attr_set[4] = {false, false, false, false};
+  static DevOnce attr_set[4];
   const int ti = a.hd == 128 ? 0 : a.hd == 64 ? 1 : a.hd == 32 ? 2 : 3;
-  if (!attr_set[ti]) {
+  if (!attr_set[ti].done()) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
-    attr_set[ti] = true;
+    attr_set[ti].set();
   }
   kern<<<dim3((a.R + PRT - 1) / PRT, a.H), PA_THREADS, smem, st>>>(a);
   return cudaGetLastError();

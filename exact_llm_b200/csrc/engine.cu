@@ -58,6 +58,9 @@ struct LinInfo {                        // one logical linear (reference naming)
   int row0 = 0, row_step = 1;           // its rows in the fused matrix
   LinW* fused = nullptr;                // owning fused matrix
   int trace_off = 0;
+  int64_t g_off = 0;                    // offset in the global trace row (tensor parallel: all ranks' slices)
+  bool col_split = false;               // tensor parallel: this rank holds output columns [r_lo, r_lo + N)
+  bool kv_owner = true;                 // tensor parallel: this rank counts its k / v slice in the global key
   int mbits = 0;
   int32_t* fr_r = nullptr;              // (2, N)
   int32_t* fr_d = nullptr;              // (2, K)
@@ -106,6 +109,7 @@ struct exb_model {
   int head_grid = 0;
   int sms = 148;
   int64_t* trace = nullptr; int64_t trace_row = 0;
+  int64_t trace_row_g = 0;              // global trace row length (tensor parallel: every rank's slices)
   // Merkle trace commitment: per-row capture of X (NL+1 rows of D) and the roped K | V of every
   // layer (2 KV hd), appended with the trace row to a device log indexed by position
   bool commit_on = false; int commit_seq = 0; int commit_cap = 0;
@@ -281,16 +285,22 @@ static void plan_lins(exb_model* m) {
   if (m->tp > 1) {
     // global shapes and slice offsets of this rank (column-split q/k/v, gate/up, head; row-split o, down)
     const exb_config& g = m->cg;
+    const int mm = (m->tp % g.KV == 0) ? m->tp / g.KV : 1;   // ranks sharing one KV head
     for (auto& L : m->lins) {
       const std::string t = L.name.substr(L.name.find('.') + 1);
-      if (L.name == "head") { L.Ng = g.V; L.r_lo = m->v0; continue; }
-      if (t == "q") { L.Ng = g.H * g.hd; L.r_lo = m->qh0 * g.hd; }
-      else if (t == "k" || t == "v") { L.Ng = g.KV * g.hd; L.r_lo = m->kh0 * g.hd; }
+      if (L.name == "head") { L.Ng = g.V; L.r_lo = m->v0; L.col_split = true; continue; }
+      if (t == "q") { L.Ng = g.H * g.hd; L.r_lo = m->qh0 * g.hd; L.col_split = true; }
+      else if (t == "k" || t == "v") {
+        L.Ng = g.KV * g.hd; L.r_lo = m->kh0 * g.hd; L.col_split = true; L.kv_owner = m->tp_rank % mm == 0;
+      }
       else if (t == "o") { L.Kg = g.H * g.hd; L.c_lo = m->qh0 * g.hd; }
-      else if (t == "gate" || t == "up") { L.Ng = g.I; L.r_lo = m->ig0 * 128; }
+      else if (t == "gate" || t == "up") { L.Ng = g.I; L.r_lo = m->ig0 * 128; L.col_split = true; }
       else if (t == "down") { L.Kg = g.I; L.c_lo = m->ig0 * 128; }
     }
   }
+  int64_t goff = 0;
+  for (auto& L : m->lins) { L.g_off = goff; goff += L.Ng; }
+  m->trace_row_g = goff;
   m->trace_row = off;
 }
 
@@ -621,6 +631,9 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     }
     if (tp) {
       RUN(tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st));
+      if (m->trace_on)   // the trace records o's full sum (every rank holds it after the all-reduce)
+        RUN(cudaMemcpy2DAsync(trace_ptr(Ld.li[3]), sizeof(int64_t) * m->trace_row, m->tp_tot, sizeof(int64_t) * c.D,
+                              sizeof(int64_t) * c.D, R, cudaMemcpyDeviceToDevice, st));
       RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.o.b, m->x, c.D, st));
     }
     if (!fzn || c.n_experts) RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
@@ -648,6 +661,9 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     }
     if (tp) {
       RUN(tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st));
+      if (m->trace_on)
+        RUN(cudaMemcpy2DAsync(trace_ptr(Ld.li[6]), sizeof(int64_t) * m->trace_row, m->tp_tot, sizeof(int64_t) * c.D,
+                              sizeof(int64_t) * c.D, R, cudaMemcpyDeviceToDevice, st));
       RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.down.b, m->x, c.D, st));
     }
   }
@@ -843,7 +859,7 @@ int exb_linear_g128(const int64_t* x, int R, int K, const int8_t* w_NK, const in
   const int G = K / 128;
   L.ldm = G;
   if ((G % 4) || ((uintptr_t)M_NG & 15)) {
-    // the kernel copies scale rows with 16-byte bulk copies: re-pitch them into the scratch
+    // keep the engine's layout (scale rows padded to a multiple of 4 int32, 16-byte aligned)
     int32_t* Mp = (int32_t*)((char*)scratch + xq_bytes(R, K) + xs_bytes(R));
     L.ldm = (G + 3) & ~3;
     CK(cudaMemcpy2DAsync(Mp, (size_t)L.ldm * 4, M_NG, (size_t)G * 4, (size_t)G * 4, N, cudaMemcpyDeviceToDevice,
@@ -868,7 +884,7 @@ int exb_linear_channel(const int64_t* x, int R, int K, const int8_t* w_NK, const
   return linear_common(x, R, K, L, y, acc_out, scratch, (cudaStream_t)stream, true);
 }
 
-// Tensor-parallel shard of rank `rank` of `size` (SURVEY-style partition of the reference layer):
+// Tensor-parallel shard of rank `rank` of `size` (the reference layer's natural partition):
 // q heads split inside each KV group when size is a multiple of KV (7B TP8: 4/3 heads per rank
 // pair, one KV head each), whole KV groups per rank when KV is a multiple of size; I split by
 // 128-groups (first ranks one more); vocabulary in equal slices (the last one shorter).
@@ -1622,14 +1638,37 @@ int exb_generate_device(exb_model* m, int B, const int32_t* ids_dev, int steps, 
   return generate_common(m, B, ids_dev, nullptr, steps, nullptr, nullptr, tokens_dev);
 }
 
+// KV cache of one layer and sequence slot, positions 0..n-1, as stored: K int16 (KV, n, hd) after
+// RoPE and qrow, its per-row shift int8 (KV, n), V int32 (KV, n, hd) -- the reference cache's kq,
+// sk and v (exact_torch.py:146-149).  Tensor parallel: this rank's KV heads.
+int exb_kv_export(exb_model* m, int layer, int seq, int n, int16_t* k_host, int8_t* ks_host, int32_t* v_host) {
+  if (!m || !m->finalized) FAIL(EXB_EINVAL, "model not finalized");
+  const exb_config& c = m->c;
+  if (layer < 0 || layer >= c.NL || seq < 0 || seq >= c.max_batch || n < 0 || n > c.max_seq)
+    FAIL(EXB_EINVAL, "exb_kv_export: bad layer, sequence slot or position count");
+  if (n > m->seq_len[seq]) FAIL(EXB_EINVAL, "exb_kv_export: the sequence holds fewer positions");
+  if (n == 0) return EXB_OK;
+  const size_t row0 = (size_t)seq * c.KV * c.max_seq;                  // (seq, head 0, position 0)
+  const size_t lay = m->kv_layer_elems * layer, lay_s = (size_t)c.max_batch * c.KV * c.max_seq * layer;
+  if (k_host)
+    CK(cudaMemcpy2DAsync(k_host, sizeof(int16_t) * n * c.hd, m->kc + lay + row0 * c.hd, sizeof(int16_t) * c.max_seq * c.hd,
+                         sizeof(int16_t) * n * c.hd, c.KV, cudaMemcpyDeviceToHost, m->st));
+  if (v_host)
+    CK(cudaMemcpy2DAsync(v_host, sizeof(int32_t) * n * c.hd, m->vc + lay + row0 * c.hd, sizeof(int32_t) * c.max_seq * c.hd,
+                         sizeof(int32_t) * n * c.hd, c.KV, cudaMemcpyDeviceToHost, m->st));
+  if (ks_host)
+    CK(cudaMemcpy2DAsync(ks_host, n, m->ks + lay_s + row0, c.max_seq, n, c.KV, cudaMemcpyDeviceToHost, m->st));
+  CK(cudaStreamSynchronize(m->st));
+  return EXB_OK;
+}
+
 int exb_trace_enable(exb_model* m, int on) {
   if (!m) FAIL(EXB_EINVAL, "null model");
   if (on && m->c.n_experts) FAIL(EXB_EINVAL, "trace capture covers the dense models (the reference traces them only)");
-  if (on && m->tp > 1) FAIL(EXB_EINVAL, "trace capture runs on single-GPU models");
   m->trace_on = on != 0;
   return EXB_OK;
 }
-int64_t exb_trace_row_len(exb_model* m) { return m ? m->trace_row : -1; }
+int64_t exb_trace_row_len(exb_model* m) { return m ? (m->tp > 1 ? m->trace_row_g : m->trace_row) : -1; }
 int exb_step_launches(exb_model* m) { return m ? m->step_kernels : -1; }
 // ---- Merkle trace commitment
 int exb_commit_begin(exb_model* m, int seq, int capacity) {
@@ -1899,18 +1938,84 @@ int exb_commit_end(exb_model* m) {
   return EXB_OK;
 }
 
+// Tensor parallel: rank k's trace row, linear by linear, as (local offset, global offset, length)
+// segments -- the same walk as plan_lins over rank k's slice of the architecture.
+struct TraceSeg { int64_t loc, glob, n; };
+static std::vector<TraceSeg> tp_trace_segs(const exb_config& g, int rank, int size) {
+  int p[9];
+  std::string why;
+  std::vector<TraceSeg> out;
+  if (!tp_plan(g, rank, size, p, why)) return out;
+  const int64_t qn = (int64_t)(p[1] - p[0]) * g.hd, kn = (int64_t)(p[3] - p[2]) * g.hd, in = (int64_t)(p[5] - p[4]) * 128;
+  const int64_t Q = (int64_t)g.H * g.hd, KVn = (int64_t)g.KV * g.hd;
+  int64_t loc = 0, glob = 0;
+  auto seg = [&](int64_t n_loc, int64_t col0, int64_t n_glob) {
+    out.push_back({loc, glob + col0, n_loc});
+    loc += n_loc; glob += n_glob;
+  };
+  for (int i = 0; i < g.NL; ++i) {
+    seg(qn, (int64_t)p[0] * g.hd, Q);
+    seg(kn, (int64_t)p[2] * g.hd, KVn);
+    seg(kn, (int64_t)p[2] * g.hd, KVn);
+    seg(g.D, 0, g.D);                                        // o: the full sum on every rank
+    seg(in, (int64_t)p[4] * 128, g.I);
+    seg(in, (int64_t)p[4] * 128, g.I);
+    seg(g.D, 0, g.D);                                        // down
+  }
+  seg(p[7] - p[6], p[6], g.V);
+  return out;
+}
+
 int exb_trace_read(exb_model* m, int64_t* host, int64_t n) {
   if (!m || !host) FAIL(EXB_EINVAL, "null argument");
-  const int64_t have = (int64_t)m->trace_host.size();
-  if (n != have) FAIL(EXB_EINVAL, "trace size mismatch: expected " + std::to_string(have));
-  memcpy(host, m->trace_host.data(), sizeof(int64_t) * n);
+  if (m->tp == 1) {
+    const int64_t have = (int64_t)m->trace_host.size();
+    if (n != have) FAIL(EXB_EINVAL, "trace size mismatch: expected " + std::to_string(have));
+    memcpy(host, m->trace_host.data(), sizeof(int64_t) * n);
+    return EXB_OK;
+  }
+  // collective: every rank's local rows (padded to the longest local row) are gathered with NCCL and
+  // placed at their global columns
+  const int64_t rows = m->trace_rows;
+  if (n != rows * m->trace_row_g) FAIL(EXB_EINVAL, "trace size mismatch: expected " + std::to_string(rows * m->trace_row_g));
+  std::vector<std::vector<TraceSeg>> segs(m->tp);
+  int64_t lmax = 0;
+  for (int k = 0; k < m->tp; ++k) {
+    segs[k] = tp_trace_segs(m->cg, k, m->tp);
+    if (segs[k].empty()) FAIL(EXB_EINVAL, "tensor-parallel plan failed");
+    lmax = std::max(lmax, segs[k].back().loc + segs[k].back().n);
+  }
+  if (rows == 0) return EXB_OK;
+  int64_t *src = nullptr, *dst = nullptr;
+  CK(cudaMallocAsync(&src, sizeof(int64_t) * rows * lmax, m->st));
+  CK(cudaMallocAsync(&dst, sizeof(int64_t) * rows * lmax * m->tp, m->st));
+  std::vector<int64_t> all((size_t)rows * lmax * m->tp);
+  CK(cudaMemcpy2DAsync(src, sizeof(int64_t) * lmax, m->trace_host.data(), sizeof(int64_t) * m->trace_row,
+                       sizeof(int64_t) * m->trace_row, rows, cudaMemcpyHostToDevice, m->st));
+  const bool ok = nccl()->all_gather(src, dst, (size_t)rows * lmax, ncclInt64, m->comm, m->st) == ncclSuccess;
+  if (ok) CK(cudaMemcpyAsync(all.data(), dst, sizeof(int64_t) * all.size(), cudaMemcpyDeviceToHost, m->st));
+  cudaFreeAsync(src, m->st);
+  cudaFreeAsync(dst, m->st);
+  CK(cudaStreamSynchronize(m->st));
+  if (!ok) FAIL(EXB_ECUDA, "ncclAllGather (trace) failed");
+  for (int k = 0; k < m->tp; ++k)
+    for (int64_t r = 0; r < rows; ++r) {
+      const int64_t* srow = all.data() + ((size_t)k * rows + r) * lmax;
+      int64_t* drow = host + (size_t)r * m->trace_row_g;
+      for (const TraceSeg& sg : segs[k]) memcpy(drow + sg.glob, srow + sg.loc, sizeof(int64_t) * sg.n);
+    }
   return EXB_OK;
 }
 
+// Keys: r_host holds the GLOBAL r of every linear (2 x Ng, both primes).  Under tensor
+// parallelism every rank checks its own shard exactly -- a column-split linear with the r of its
+// own output columns (d over the full input), a row-split linear (o, down) on its partial sums
+// with the full r (d over its input slice) -- so the kernels are the single-GPU ones and no check
+// needs communication; exb_freivalds_read_keys reassembles the global d = (W M)^T r mod p.
 int exb_freivalds_set_keys(exb_model* m, const int32_t* r_host, int64_t n) {
   if (!m || !r_host) FAIL(EXB_EINVAL, "null argument");
   int64_t need = 0;
-  for (auto& L : m->lins) need += 2 * (int64_t)L.N;
+  for (auto& L : m->lins) need += 2 * (int64_t)L.Ng;
   if (n != need) FAIL(EXB_EINVAL, "freivalds keys: expected " + std::to_string(need) + " r values");
   // key storage lives in the runtime arena's tail
   size_t off = (m->roff + 255) & ~size_t(255);
@@ -1921,8 +2026,11 @@ int exb_freivalds_set_keys(exb_model* m, const int32_t* r_host, int64_t n) {
     L.fr_r = (int32_t*)(m->rarena + off); off += ((size_t)2 * L.N * 4 + 255) & ~size_t(255);
     L.fr_d = (int32_t*)(m->rarena + off); off += ((size_t)2 * L.K * 4 + 255) & ~size_t(255);
     if (off > m->rbytes) FAIL(EXB_ENOMEM, "freivalds key storage exhausted");
-    CK(cudaMemcpyAsync(L.fr_r, r_host + pos, sizeof(int32_t) * 2 * L.N, cudaMemcpyHostToDevice, m->st));
-    pos += 2 * L.N;
+    const int c0 = L.col_split ? L.r_lo : 0;                 // this rank's rows of the global r
+    for (int p = 0; p < 2; ++p)
+      CK(cudaMemcpyAsync(L.fr_r + (size_t)p * L.N, r_host + pos + (size_t)p * L.Ng + c0, sizeof(int32_t) * L.N,
+                         cudaMemcpyHostToDevice, m->st));
+    pos += 2 * (int64_t)L.Ng;
     const LinW& F = *L.fused;
     CK(launch_fr_keys(F.w, F.Mg, F.ldm, L.N, L.K, L.row0, L.row_step, L.fr_r, L.fr_d, m->st));
     L.fr_acc = acc_base + (size_t)idx * RMAX * 4;
@@ -1934,23 +2042,58 @@ int exb_freivalds_set_keys(exb_model* m, const int32_t* r_host, int64_t n) {
   return EXB_OK;
 }
 
+static constexpr int64_t FR_P1 = 2147483647, FR_P2 = 2147483629;
+
 int exb_freivalds_read_keys(exb_model* m, int32_t* d_host, int64_t n) {
   if (!m || !d_host) FAIL(EXB_EINVAL, "null argument");
   int64_t need = 0;
-  for (auto& L : m->lins) need += 2 * (int64_t)L.K;
+  for (auto& L : m->lins) need += 2 * (int64_t)L.Kg;
   if (n != need) FAIL(EXB_EINVAL, "freivalds read: expected " + std::to_string(need));
-  int64_t pos = 0;
-  for (auto& L : m->lins) {
+  for (auto& L : m->lins)
     if (!L.fr_d) FAIL(EXB_EINVAL, "keys not set");
-    CK(cudaMemcpy(d_host + pos, L.fr_d, sizeof(int32_t) * 2 * L.K, cudaMemcpyDeviceToHost));
-    pos += 2 * L.K;
+  if (m->tp == 1) {
+    int64_t pos = 0;
+    for (auto& L : m->lins) {
+      CK(cudaMemcpy(d_host + pos, L.fr_d, sizeof(int32_t) * 2 * L.K, cudaMemcpyDeviceToHost));
+      pos += 2 * L.K;
+    }
+    return EXB_OK;
+  }
+  // collective: each rank's share of the global d (column-split: d over the full input, counted once
+  // per distinct slice; row-split: d of its input columns), summed over the ranks with NCCL, mod p
+  std::vector<int64_t> part((size_t)n, 0);
+  int64_t pos = 0;
+  std::vector<int32_t> d;
+  for (auto& L : m->lins) {
+    d.resize((size_t)2 * L.K);
+    CK(cudaMemcpy(d.data(), L.fr_d, sizeof(int32_t) * 2 * L.K, cudaMemcpyDeviceToHost));
+    if (L.col_split ? L.kv_owner : true) {
+      const int k0 = L.col_split ? 0 : L.c_lo;
+      for (int p = 0; p < 2; ++p)
+        for (int k = 0; k < L.K; ++k) part[pos + (size_t)p * L.Kg + k0 + k] = d[(size_t)p * L.K + k];
+    }
+    pos += 2 * (int64_t)L.Kg;
+  }
+  int64_t* buf = nullptr;
+  CK(cudaMallocAsync(&buf, sizeof(int64_t) * n, m->st));
+  CK(cudaMemcpyAsync(buf, part.data(), sizeof(int64_t) * n, cudaMemcpyHostToDevice, m->st));
+  const bool ok = nccl()->all_reduce(buf, buf, (size_t)n, ncclInt64, ncclSum, m->comm, m->st) == ncclSuccess;
+  if (ok) CK(cudaMemcpyAsync(part.data(), buf, sizeof(int64_t) * n, cudaMemcpyDeviceToHost, m->st));
+  cudaFreeAsync(buf, m->st);
+  CK(cudaStreamSynchronize(m->st));
+  if (!ok) FAIL(EXB_ECUDA, "ncclAllReduce (Freivalds keys) failed");
+  pos = 0;
+  for (auto& L : m->lins) {
+    for (int p = 0; p < 2; ++p)
+      for (int k = 0; k < L.Kg; ++k)
+        d_host[pos + (size_t)p * L.Kg + k] = (int32_t)(part[pos + (size_t)p * L.Kg + k] % (p ? FR_P2 : FR_P1));
+    pos += 2 * (int64_t)L.Kg;
   }
   return EXB_OK;
 }
 
 int exb_freivalds_enable(exb_model* m, int on) {
   if (!m) FAIL(EXB_EINVAL, "null model");
-  if (on && m->tp > 1) FAIL(EXB_EINVAL, "the Freivalds self-check runs on single-GPU models");
   if (on && (m->lins.empty() || !m->lins[0].fr_r)) FAIL(EXB_EINVAL, "set keys first");
   m->fr_on = on != 0;
   if (on) { CK(cudaMemset(m->fr_fail, 0, sizeof(int))); m->fr_checks = 0; }
@@ -1962,8 +2105,20 @@ int exb_freivalds_status(exb_model* m, int64_t* checks, int64_t* failures) {
   int f = 0;
   CK(cudaStreamSynchronize(m->st));
   CK(cudaMemcpy(&f, m->fr_fail, sizeof(int), cudaMemcpyDeviceToHost));
-  if (checks) *checks = m->fr_checks;
-  if (failures) *failures = f;
+  int64_t v[2] = {m->fr_checks, f};
+  if (m->tp > 1) {
+    // collective: totals over the ranks (each rank checks its own shard)
+    int64_t* buf = nullptr;
+    CK(cudaMallocAsync(&buf, sizeof v, m->st));
+    CK(cudaMemcpyAsync(buf, v, sizeof v, cudaMemcpyHostToDevice, m->st));
+    const bool ok = nccl()->all_reduce(buf, buf, 2, ncclInt64, ncclSum, m->comm, m->st) == ncclSuccess;
+    if (ok) CK(cudaMemcpyAsync(v, buf, sizeof v, cudaMemcpyDeviceToHost, m->st));
+    cudaFreeAsync(buf, m->st);
+    CK(cudaStreamSynchronize(m->st));
+    if (!ok) FAIL(EXB_ECUDA, "ncclAllReduce (Freivalds status) failed");
+  }
+  if (checks) *checks = v[0];
+  if (failures) *failures = v[1];
   return EXB_OK;
 }
 

@@ -10,6 +10,15 @@ namespace exb {
 // message returned by exb_last_error() for the calling thread
 void set_last_error(const std::string& msg);
 
+// One-time work per device (a kernel's function attributes belong to one device's context): bit d
+// is set once device d is done.  Setting an attribute twice is harmless, so the races are benign.
+struct DevOnce {
+  unsigned long long bits = 0;
+  static int dev() { int d = 0; cudaGetDevice(&d); return d & 63; }
+  bool done() const { return (__atomic_load_n(&bits, __ATOMIC_ACQUIRE) >> dev()) & 1ull; }
+  void set() { __atomic_fetch_or(&bits, 1ull << dev(), __ATOMIC_RELEASE); }
+};
+
 enum GenKind { GEN_WEIGHT = 0, GEN_SCALE32 = 1, GEN_SCALE64 = 2, GEN_BIAS = 3, GEN_GAIN = 4 };
 cudaError_t gen_tensor(int kind, uint64_t seed, uint64_t stream, int64_t n, int64_t K, void* out, cudaStream_t st);
 int64_t isqrt_host(int64_t n);
@@ -19,8 +28,8 @@ int64_t isqrt_host(int64_t n);
 // scales (N,).  For a fused SwiGLU pair the rows are interleaved: row 2j = gate j, 2j+1 = up j.
 struct LinW {
   const int8_t* w = nullptr;
-  const int32_t* Mg = nullptr;     // group-128 scales (N, ldm), ldm >= K/128, rows 16-byte aligned
-  int ldm = 0;                     // row pitch of Mg in int32 (a multiple of 4)
+  const int32_t* Mg = nullptr;     // group-128 scales (N, ldm), ldm >= K/128, read 4 bytes at a time
+  int ldm = 0;                     // row pitch of Mg in int32 (the engine pads it to a multiple of 4)
   const int64_t* Mc = nullptr;     // per-channel scales (N) or nullptr
   const int64_t* b = nullptr;      // bias (N) Q16 or nullptr
   int N = 0, K = 0;

@@ -435,11 +435,11 @@ bool gemm_tc_supported(const LinW& L, int epi) {
 template <int BN>
 static cudaError_t tc_launch(dim3 grid, const CUtensorMap& mA, const CUtensorMap& mLo, const CUtensorMap& mHi,
                              const TcArgs& a, bool pdl, cudaStream_t st) {
-  static bool attr = false;                 // raised once to the full budget, never lowered
-  if (!attr) {
+  static DevOnce attr;                 // raised once to the full budget, never lowered
+  if (!attr.done()) {
     cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcGeo<BN>::SMEM);
     if (e != cudaSuccess) return e;
-    attr = true;
+    attr.set();
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;

@@ -348,11 +348,11 @@ static cudaError_t launch_t(const GemvArgs& a, size_t smem, cudaStream_t st, boo
   // The max-dynamic-shared-memory attribute is raised once to the full budget and never lowered:
   // launches of one instantiation use different sizes, and a captured graph node (or a profiler
   // replay) must never find a smaller maximum than it was launched with.
-  static bool attr_set = false;
-  if (!attr_set) {
+  static DevOnce attr_set;
+  if (!attr_set.done()) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_SMEM_MAX);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_set.set();
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.grid);
@@ -462,11 +462,11 @@ cudaError_t launch_gemv_op(const int16_t* x16, const int8_t* wT, const int64_t* 
   if (K % 128 != 0 || N <= 0) return cudaErrorInvalidValue;
   const size_t smem = (size_t)K * 2;
   if (smem > DYN_SMEM_MAX) return cudaErrorInvalidValue;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static DevOnce attr_set;
+  if (!attr_set.done()) {
     cudaError_t e = cudaFuncSetAttribute(k_gemv_op, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_SMEM_MAX);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_set.set();
   }
   int blocks = (N + 7) / 8;
   if (blocks > 148 * 8) blocks = 148 * 8;

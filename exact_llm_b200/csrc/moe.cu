@@ -251,13 +251,13 @@ cudaError_t launch_moe(const MoeArgs& a, int64_t* x, int ldx, cudaStream_t st) {
   k_moe_plan<<<1, 256, 0, st>>>(a);
   int nmax = 2 * a.IMAX > a.D ? 2 * a.IMAX : a.D;
   const size_t smem_g = (size_t)MOE_RB * (a.D > a.IMAX ? a.D : a.IMAX) * 2;
-  static bool attr = false;
-  if (!attr) {
+  static DevOnce attr;
+  if (!attr.done()) {
     cudaError_t e = cudaFuncSetAttribute(k_moe_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_moe_act, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     if (e != cudaSuccess) return e;
-    attr = true;
+    attr.set();
   }
   k_moe_gemv<<<dim3((nmax + MOE_CH - 1) / MOE_CH, a.NE + 1), MOE_THREADS, smem_g, st>>>(a, 0);
   k_moe_act<<<a.R * (a.TOPK + 1), MOE_THREADS, (size_t)a.IMAX * 8, st>>>(a);

@@ -88,11 +88,11 @@ cudaError_t launch_embed_norm(const int8_t* emb, const int64_t* emb_q16, int emb
                               int D, const int64_t* g, int64_t* x, int16_t* xq, int ldq, int32_t* xs,
                               cudaStream_t st, bool pdl) {
   const size_t smem = (size_t)D * 8;
-  static bool attr_set = false;   // raised once to the full budget, never lowered
-  if (!attr_set) {
+  static DevOnce attr_set;   // raised once to the full budget, never lowered
+  if (!attr_set.done()) {
     cudaError_t e = cudaFuncSetAttribute(k_embed_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_set.set();
   }
   void* args[] = {(void*)&emb, (void*)&emb_q16, (void*)&emb_shift, (void*)&ids, (void*)&D, (void*)&g, (void*)&x,
                   (void*)&xq, (void*)&ldq, (void*)&xs};
@@ -128,11 +128,11 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restric
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
                           int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig, int64_t* xcap, int64_t ldcap) {
   const size_t smem = (size_t)D * 16;
-  static bool attr_set = false;   // raised once to the full budget, never lowered
-  if (!attr_set) {
+  static DevOnce attr_set;   // raised once to the full budget, never lowered
+  if (!attr_set.done()) {
     cudaError_t e = cudaFuncSetAttribute(k_norm_q, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_set.set();
   }
   void* args[] = {(void*)&x,  (void*)&ldx, (void*)&g,   (void*)&D,    (void*)&xq,
                   (void*)&ldq, (void*)&xs,  (void*)&dig, (void*)&xcap, (void*)&ldcap};
@@ -154,11 +154,11 @@ cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, i
                          cudaStream_t st, bool pdl) {
   const size_t smem = (size_t)K * 8;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;   // one row staged in shared memory
-  static bool attr_set = false;   // raised once to the full budget, never lowered
-  if (!attr_set) {
+  static DevOnce attr_set;   // raised once to the full budget, never lowered
+  if (!attr_set.done()) {
     cudaError_t e = cudaFuncSetAttribute(k_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_set.set();
   }
   void* args[] = {(void*)&x, (void*)&ldx, (void*)&K, (void*)&xq, (void*)&ldq, (void*)&xs};
   return launch_simple((const void*)k_quant, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);

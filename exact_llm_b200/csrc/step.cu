@@ -711,10 +711,10 @@ static int step_sm_count() {
 
 template <int R>
 static cudaError_t step_attr() {
-  static bool done = false;               // raised once to the ceiling, never lowered
-  if (done) return cudaSuccess;
+  static DevOnce done;                    // raised once to the ceiling, never lowered
+  if (done.done()) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(k_step<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, STEP_SMEM_MAX);
-  if (e == cudaSuccess) done = true;
+  if (e == cudaSuccess) done.set();
   return e;
 }
 

@@ -310,11 +310,11 @@ cudaError_t launch_verify(const VerifyArgs& a, int n_cells, int n_leaves, const 
     if (e != cudaSuccess) return e;
   }
   const size_t smem = (((size_t)a.q16_len * 2 + 15) & ~(size_t)15) + (size_t)a.D * 16;
-  static bool attr = false;
-  if (!attr) {
+  static DevOnce attr;
+  if (!attr.done()) {
     cudaError_t e = cudaFuncSetAttribute(k_verify_cells, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
-    attr = true;
+    attr.set();
   }
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   k_verify_cells<<<n_cells, VT, smem, st>>>(a);

@@ -221,6 +221,45 @@ class ExactModel:
         tokens = [first] + [int(t) for t in toks[0, :-1]]
         return lg, [rows[s, 0] for s in range(steps)], tokens
 
+    def step(self, token, cache=None):
+        """GraphDecoder.step(token) (experiments/speed_fair_kaggle.py:639-645): append one token to
+        the sequence of ``cache`` (slot 0 by default), run one decode step (a captured CUDA graph),
+        and return its int64 Q16 logits, shape (1, V).  The row lands in a pinned host buffer that
+        the next call reuses: copy it to keep it.  ``last_next`` holds the greedy token (the
+        lowest index of the row's maximum)."""
+        slot = 0 if cache is None else cache.slot
+        if getattr(self, "_step_buf", None) is None:
+            import torch
+            self._step_t = torch.empty((1, self.c["V"]), dtype=torch.int64, pin_memory=True)
+            self._step_buf = self._step_t.numpy()
+            self._step_ids = np.empty(1, np.int32)
+            self._step_seq = np.empty(1, np.int32)
+            self._step_next = np.empty(1, np.int32)
+        self._step_ids[0] = int(token)
+        self._step_seq[0] = slot
+        self._rows = 1
+        check(lib.exb_forward(self.h, 1, ptr(self._step_ids, ctypes.c_int32), ptr(self._step_seq, ctypes.c_int32),
+                              ptr(self._step_buf, ctypes.c_int64), ptr(self._step_next, ctypes.c_int32)))
+        self.last_next = self._step_next
+        return self._step_buf
+
+    def kv_cache(self, layer, cache=None):
+        """The KV cache of one layer as the reference's TModel keeps it (exact_torch.py:140,
+        146-149): dict(kq=int64 (KV, n, hd), sk=int64 (KV, n, 1), v=int64 (KV, n, hd)) over the n
+        positions of the sequence (slot 0 by default; tensor parallel: this rank's KV heads)."""
+        slot = 0 if cache is None else cache.slot
+        n = lib.exb_seq_len(self.h, slot)
+        KV = self.c["KV"]
+        if self.tp is not None and int(self.tp[1]) > 1:
+            p = self.tp_plan(self.c, int(self.tp[0]), int(self.tp[1]))
+            KV = p["kh1"] - p["kh0"]
+        hd = self.c["hd"]
+        k = np.empty((KV, n, hd), np.int16)
+        ks = np.empty((KV, n), np.int8)
+        v = np.empty((KV, n, hd), np.int32)
+        check(lib.exb_kv_export(self.h, int(layer), slot, n, k.ctypes.data, ks.ctypes.data, v.ctypes.data))
+        return dict(kq=k.astype(np.int64), sk=ks.astype(np.int64)[..., None], v=v.astype(np.int64))
+
     def moe_selections(self, layer):
         """Router top-k experts of every row of the last forward call at `layer`: int32 (rows, topk)."""
         k = int(self.c["TOPK"])

@@ -57,7 +57,8 @@ int exb_gemv(const int16_t* x16, const int8_t* wT, const int64_t* Mg, int K, int
  * xq, s = qrow(x); tot = sum_g M_g (xq_g . W_g); y = shr(tot, 28 - s) + b.
  * w_NK int8 (N, K); M_NG int32 (N, K/128); bias int64 (N) or NULL; y int64 (R, N);
  * tot_out int64 (R, N) or NULL.  `scratch` = exb_linear_g128_scratch_bytes(R, K, N) device bytes
- * (quantised rows, shifts, and a 16-byte-pitched copy of the scales when K/128 is not a multiple of 4). */
+ * (quantised rows, shifts, int8 digit planes from 16 rows, and a copy of the scales with rows
+ * padded to a multiple of 4 int32 -- the engine's own layout -- when K/128 is not one). */
 size_t exb_linear_g128_scratch_bytes(int R, int K, int N);
 int exb_linear_g128(const int64_t* x, int R, int K, const int8_t* w_NK, const int32_t* M_NG, const int64_t* bias,
                     int N, int64_t* y, int64_t* tot_out, void* scratch, void* stream);
@@ -66,10 +67,13 @@ int exb_linear_g128(const int64_t* x, int R, int K, const int8_t* w_NK, const in
  * that fix their HBM budget at start-up (every byte reserved for weights and KV caches) and plugin
  * hosts that own the allocator.  No counterpart in the reference (its torch path allocates per
  * call).  Same arguments and bit-identical results as exb_linear_g128, minus `scratch`.
- * The scratch is a fixed array inside the library: every GPU that loads it holds about 8 MiB until
- * exit.  Limits: R * K <= EXB_NOALLOC_MAX_XQ and R <= EXB_NOALLOC_MAX_ROWS (else EXB_EINVAL, nothing
- * launched).  The first call on a device looks the array's device address up (make it before any
- * stream capture on that device).  All calls on a device share the array: calls whose GPU work
+ * The scratch is a fixed array inside the library: every GPU that loads it holds about 24 MiB until
+ * exit.  Limits: R * K <= EXB_NOALLOC_MAX_XQ, R <= EXB_NOALLOC_MAX_ROWS and K <= 25600 (else
+ * EXB_EINVAL with a message, nothing launched).  From 16 rows with N a multiple of 128 it runs the
+ * tcgen05 GEMM (one pass over the weights); below that, or for other N, the CUDA-core GEMV, which
+ * reads the weights once per 4 rows.  Alignment: w and x 16 bytes, M 4 bytes (any K/128), y, tot,
+ * bias 8 bytes.  The first call on a device looks the array's device address up (make it before
+ * any stream capture on that device).  All calls on a device share the array: calls whose GPU work
  * overlaps (different streams, no ordering) race and must be ordered by the caller.  Calls no
  * cudaMalloc, cudaFree or allocating library routine. */
 #define EXB_NOALLOC_MAX_XQ (1 << 22)
@@ -124,6 +128,15 @@ int exb_generate(exb_model* m, int B, const int32_t* first_ids, int steps, int32
 /* Same loop on device buffers only (ids_dev B int32 in, tokens_dev B x steps int32 out), on the
  * model's stream; no host synchronisation. */
 int exb_generate_device(exb_model* m, int B, const int32_t* ids_dev, int steps, int32_t* tokens_dev);
+
+/* KV cache export (exact_torch.py:140, 146-149: TModel's cache entries kq, sk, v; the static
+ * GraphDecoder cache of experiments/speed_fair_kaggle.py:596-606, 617-618): positions 0..n-1 of
+ * sequence slot `seq` at layer `layer`, into HOST buffers (any may be NULL):
+ *   k_host  int16 (KV, n, hd)  K after RoPE, per (head, position) row quantised by qrow
+ *   ks_host int8  (KV, n)      that row's shift sk
+ *   v_host  int32 (KV, n, hd)  V, Q16 (the reference keeps it in int64; |V| < 2^31 is checked)
+ * n must not exceed the sequence's length.  Tensor parallel: this rank's KV heads. */
+int exb_kv_export(exb_model* m, int layer, int seq, int n, int16_t* k_host, int8_t* ks_host, int32_t* v_host);
 
 /* Trace capture (experiments/prover_commit_cost_gpu_kaggle.py:727-742): when on, every forward
  * row records the raw accumulator of every linear (tot for group-128, acc for per-channel) in

@@ -113,6 +113,32 @@ class Recorder:
         return y
 
 
+class OutRecorder:
+    """Wraps a reference linear and keeps the output of its latest call.  On the K and V
+    projections this gives the reference's KV cache: K = qrow(rope(k)) per (head, position) row
+    with its shift, V = the Q16 projection (exact_torch.py:146-149)."""
+
+    def __init__(self, inner):
+        self.inner, self.last = inner, None
+
+    def __call__(self, x):
+        self.last = self.inner(x)
+        return self.last
+
+
+class RowsHead:
+    """The reference head applied to selected rows only.  Every output row of QLin.__call__
+    depends on its own input row alone (qrow, the product and the drop rule are per row,
+    exact_llm.py:89-96), so these rows equal the same rows of the head over all positions."""
+
+    def __init__(self, inner, rows):
+        self.inner, self.rows = inner, rows
+
+    def __call__(self, x):
+        idx = [r if r >= 0 else x.shape[0] + r for r in self.rows]
+        return self.inner(x[idx])
+
+
 def ref_int_model(ex, om, record=None):
     c = dict(om.c)
     m = ex.IntModel.__new__(ex.IntModel)
@@ -464,9 +490,138 @@ def g_moe(ex, G):
         print(key, h16(lg), toks, flush=True)
 
 
+def _kv_hashes(ex, rm, li, T):
+    """Hashes of the reference KV cache of layer li over T positions, from the K and V
+    projection outputs of the latest call that covered all T rows (block_row projects k and v
+    for every position of its input, exact_llm.py:339-348): kq, sk = qrow(rope(k)) per (KV head,
+    position) row, v as it is (exact_torch.py:146-149)."""
+    c = rm.c
+    KV, hd = c["KV"], c["hd"]
+    k = rm.layers[li]["k"].last
+    v = rm.layers[li]["v"].last
+    assert k.shape[0] == T and v.shape[0] == T
+    kr = rm.rope(k.reshape(T, KV, hd).transpose(1, 0, 2))
+    kq = np.empty_like(kr)
+    sk = np.empty((KV, T, 1), np.int64)
+    for kh in range(KV):
+        kq[kh], sk[kh] = ex.qrow(kr[kh])
+    return dict(k=h16(kq), sk=h16(sk), v=h16(np.ascontiguousarray(v.reshape(T, KV, hd).transpose(1, 0, 2))),
+                k_row0=[int(t) for t in kq[0, 0, :8]], sk_head0=[int(t) for t in sk[0, :8, 0]])
+
+
+def _long_case(ex, G, key, cfg, seed, T, steps, prompt_seed, rows):
+    """Long-prompt parity by the reference's own per-layer machinery: forward_record over the
+    prompt (exact_llm.py:359-363, every layer input x_l of every position), the head on the
+    selected rows, then greedy decode where each new position runs block_row through every layer
+    (exact_llm.py:339-358) on the layer inputs of all earlier positions -- the same rows a full
+    recompute of the extended prompt gives, since every layer is causal.  Records hashes of the
+    selected prefill rows, the tokens, every decode row and the KV cache of every layer."""
+    om = synth.build_model(cfg, seed)
+    rm = ref_int_model(ex, om)
+    for L in rm.layers:
+        L["k"], L["v"] = OutRecorder(L["k"]), OutRecorder(L["v"])
+    head = rm.head
+    rm.head = RowsHead(head, rows)
+    ids = [int(t) for t in synth.prompt_ids(prompt_seed, 1, T, cfg["V"])[0]]
+    t0 = time.time()
+    xs, lg = ex.forward_record(rm, ids)
+    pre_s = time.time() - t0
+    print(key, "prefill", round(pre_s, 1), "s", flush=True)
+    xs = [np.array(x) for x in xs]
+    toks, rows_h, row8 = [], [], []
+    nxt = int(lg[-1].argmax()) if rows[-1] == -1 else None
+    assert nxt is not None, "the last selected row must be the prompt's last row (the greedy token)"
+    cur = list(ids)
+    for s in range(steps):
+        toks.append(nxt)
+        cur.append(nxt)
+        t = len(cur) - 1
+        x = np.rint(np.asarray(rm.emb[[nxt]], dtype=np.float64) * ex.ONE).astype(np.int64)
+        xs[0] = np.concatenate([xs[0], x])
+        for li, L in enumerate(rm.layers):
+            xn = ex.block_row(rm, L, xs[li], t)
+            xs[li + 1] = np.concatenate([xs[li + 1], xn[None]])
+        row = head(ex.irms(xs[-1][t:t + 1], rm.gf))[0]
+        rows_h.append(h16(row))
+        row8.append([int(v) for v in row[:8]])
+        nxt = int(row.argmax())
+        print(key, "step", s, nxt, round(time.time() - t0, 1), flush=True)
+    S = len(cur)
+    kv = [_kv_hashes(ex, rm, li, S) for li in range(cfg["NL"])]
+    ent = dict(config=cfg, seed=seed, prompt_seed=prompt_seed, T=T, prompt=ids, rows=rows, prefill_all=h16(lg),
+               prefill_rows=[h16(r) for r in lg] if len(rows) <= 16 else None, prefill_last8=[int(v) for v in lg[-1][:8]],
+               tokens=toks, step_rows=rows_h, step_row8=row8, kv=kv, S=S, prefill_s=round(pre_s, 1),
+               x_last=[h16(x[-1]) for x in xs])
+    G.setdefault("long", {})[key] = ent
+    print(key, "tokens", toks, "kv0", kv[0]["k"], flush=True)
+
+
+def g_long(ex, G):
+    """BASELINE configs 3 and 5 at their real prompt lengths: the 7B architecture (2 layers) after a
+    512-token prompt (every prefill row, 4 decode steps) and the 14B architecture (1 layer) after a
+    4096-token prompt (rows 999, 2047, 3000 and the last 8; 3 decode steps)."""
+    _long_case(ex, G, "qwen2.5-7b-L2-p512", synth.config("qwen2.5-7b", NL=2), 71, 512, 4, 72,
+               list(range(-512, 0)))
+    _long_case(ex, G, "qwen2.5-14b-L1-p4096", synth.config("qwen2.5-14b", NL=1), 141, 4096, 3, 142,
+               [999, 2047, 3000] + list(range(-8, 0)))
+
+
+def g_moe_wide(ex, G):
+    """BASELINE config 4's workload shape on one Qwen1.5-MoE layer: 32 sequences of 256 uniform
+    prompt tokens, the router's top-4 experts of every token (MoEInt.moe, experiments/
+    moe_exact_kaggle.py:454-467), the last prompt row's logits and 3 greedy steps per sequence
+    (the reference's full recompute per step)."""
+    cfg = synth.config("qwen1.5-moe-a2.7b", NL=1)
+    seed, B, T, steps = 43, 32, 256, 3
+    om = synth.build_model(cfg, seed)
+    rm = ref_moe_model(ex, om)
+    head = rm.head
+    rm.head = RowsHead(head, [-1])
+    prompts = synth.prompt_ids(44, B, T, cfg["V"])
+    seqs = []
+    t0 = time.time()
+    for b in range(B):
+        ids = [int(t) for t in prompts[b]]
+        st = {}
+        lg = rm(ids, st)
+        sel = np.concatenate(st[0]).astype(np.int64)
+        cur = list(ids)
+        toks, rows_h = [], []
+        nxt = int(lg[-1].argmax())
+        for _ in range(steps):
+            toks.append(nxt)
+            cur.append(nxt)
+            row = rm(cur)[-1]
+            rows_h.append(h16(row))
+            nxt = int(row.argmax())
+        seqs.append(dict(last=h16(lg[-1]), sel=h16(sel), sel_head=sel[:4].tolist(), tokens=toks, rows=rows_h))
+        print("moe-wide", b, toks, round(time.time() - t0, 1), flush=True)
+    G["moe_wide"] = dict(config=cfg, seed=seed, prompt_seed=44, B=B, T=T, steps=steps, seqs=seqs)
+
+
+def g_freivalds_7b(ex, G):
+    """Freivalds keys at the 7B architecture's shapes (2 layers): the reference's keys_group /
+    keys_channel (experiments/gpu_engine_trace_verify_kaggle.py:802-819, rng seeded 2026, drawn
+    in layer / linear order, then the head), hashed per linear and prime."""
+    cfg = synth.config("qwen2.5-7b", NL=2)
+    om = synth.build_model(cfg, 7)
+    rm = ref_int_model(ex, om)
+    fr_ns = dict(ex._fr_ns)
+    fr_ns["rng"] = np.random.default_rng(2026)
+    ent = {}
+    t0 = time.time()
+    for li, L in enumerate(rm.layers):
+        for nm in ("q", "k", "v", "o", "gate", "up", "down"):
+            ent[f"L{li}.{nm}"] = [h16(d) for _, _, d in fr_ns["keys_group"](L[nm])]
+            print("fr7b", li, nm, round(time.time() - t0, 1), flush=True)
+    ent["head"] = [h16(d) for _, _, d in fr_ns["keys_channel"](rm.head)]
+    G["freivalds_7b"] = dict(model="qwen2.5-7b-L2", seed=7, d=ent)
+
+
 BUILDERS = dict(tables=g_tables, gemv_kat=g_gemv_kat, models=g_models, freivalds=g_freivalds,
                 pre_tiny=g_pre_tiny, moe=g_moe, linear=g_linear, config1=g_config1, big=g_big_layers,
-                commit=g_commit, sampler=g_sampler, convert=g_convert, verify=g_verify)
+                commit=g_commit, sampler=g_sampler, convert=g_convert, verify=g_verify, long=g_long,
+                moe_wide=g_moe_wide, freivalds_7b=g_freivalds_7b)
 
 
 def main():

@@ -80,14 +80,31 @@ def test_tp_plan_agrees_across_gloo_ranks():
     assert res[0][0]["qh1"] == res[0][1]["qh0"] and res[0][0]["ig1"] == res[0][1]["ig0"]
 
 
+def _run_tp(key, mode, port, n=2):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "30", "900", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        f"--nproc-per-node={n}", "--master-addr", "127.0.0.1", "--master-port", str(port),
+                        os.path.join(ROOT, "tests", "tp_worker.py"), key, mode],
+                       capture_output=True, text=True, timeout=1000, env=env)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("key", ["qwen2.5-7b-L2", "qwen2.5-14b-L1"])
 def test_tp2_matches_reference_fixture(golden, key):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-                        "--master-addr", "127.0.0.1", "--master-port", "29731", os.path.join(ROOT, "tests", "tp_worker.py"),
-                        key], capture_output=True, text=True, timeout=600, env=env)
-    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    _run_tp(key, "greedy", 29731)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("key", ["qwen2.5-7b-L2", "qwen2.5-14b-L1"])
+def test_tp2_trace_and_freivalds_match_reference(golden, key):
+    """BASELINE config 5's capture under tensor parallelism: global trace hashes, step digests and
+    Freivalds keys equal the reference's; every shard's self-check passes honestly and a tampered
+    shard is caught."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    _run_tp(key, "trace", 29733)

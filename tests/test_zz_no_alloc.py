@@ -45,11 +45,27 @@ def _linear_pair(torch, L, seed, R, K, N):
 
 def test_noalloc_linear_matches_scratch_linear_twice():
     torch, L = _setup()
-    # call 1 and call 2 in a row, different shapes: the second reuses the fixed array
-    for seed, R, K, N in ((21, 16, 3584, 4608), (22, 3, 18944, 3584)):
+    # calls in a row with different shapes, so each call runs on the previous call's leftovers in
+    # the fixed array: the tensor-core path (16 rows), the GEMV (3 rows), then scale rows of 3 and
+    # 5 int32 (K = 384, 640: not a multiple of 4 groups) on both paths
+    for seed, R, K, N in ((21, 16, 3584, 4608), (22, 3, 18944, 3584), (23, 5, 384, 1000), (24, 40, 640, 256),
+                          (25, 2, 640, 384)):
         y, t, y_ref, t_ref = _linear_pair(torch, L, seed, R, K, N)
         assert np.array_equal(t, t_ref), (R, K, N)
         assert np.array_equal(y, y_ref), (R, K, N)
+
+
+def test_noalloc_linear_on_a_second_device():
+    """Per-device state (the array's address, the kernels' shared-memory attributes) is set up for
+    each device it is used on: the same calls on GPU 1 after GPU 0 in one process."""
+    torch, L = _setup()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            for seed, R, K, N in ((31, 4, 18944, 3584), (32, 16, 3584, 4608)):
+                y, t, y_ref, t_ref = _linear_pair(torch, L, seed, R, K, N)
+                assert np.array_equal(t, t_ref) and np.array_equal(y, y_ref), (dev, R, K, N)
 
 
 def test_noalloc_rejects_oversize_requests():
@@ -60,3 +76,7 @@ def test_noalloc_rejects_oversize_requests():
                                        128, ctypes.c_void_p(16), None, None)
     assert rc == 1
     assert b"exceeds the fixed scratch" in L.lib.exb_last_error()
+    rc = L.lib.exb_linear_g128_noalloc(ctypes.c_void_p(16), 1, 25728, ctypes.c_void_p(16), ctypes.c_void_p(16), None,
+                                       128, ctypes.c_void_p(16), None, None)
+    assert rc == 1
+    assert b"exceeds 25600" in L.lib.exb_last_error()
