@@ -335,6 +335,9 @@ def run_ours(a, rank, world, local_rank):
         m.finalize()
     else:
         m = ExactModel.synthetic(c, 1234, max_batch=B, max_seq=max_seq)
+    for opt in a.option:
+        name, val = opt.split("=")
+        m.set_option(name, int(val))
     stream = torch.cuda.ExternalStream(m.stream)
     rng = np.random.default_rng(100 + rank)
     prompts = rng.integers(0, c["V"], (B, PROMPT)).astype(np.int32)
@@ -499,6 +502,8 @@ def main():
                     help="with --gpus N under torchrun: N independent replicas instead of one tensor-parallel model")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens before decode (profiling uses a short one)")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (small ncu captures only)")
+    ap.add_argument("--option", action="append", default=[], metavar="NAME=VALUE",
+                    help="engine option for the timed model (exb_set_option; results never change)")
     ap.add_argument("--commit", type=int, default=0, metavar="T",
                     help="only the Merkle trace commitment of T logged 7B positions: GPU vs host hashlib")
     ap.add_argument("--linear", type=int, default=0, metavar="T",

@@ -104,6 +104,8 @@ struct exb_model {
   int16_t* qq = nullptr; int32_t* qs = nullptr;
   int32_t* next_tok = nullptr;
   unsigned long long *amax_o = nullptr, *amax_h = nullptr;   // per-row max |x| published by producers
+  unsigned long long *nstat_a = nullptr, *nstat_b = nullptr; // per-row (max |x|, sum x^2) of the residual
+                                                             // stream before norm1 / norm2 (fuse level 3)
   unsigned int* ticket = nullptr;                            // last-CTA election counter
   unsigned long long* head_part = nullptr; unsigned int* head_ticket = nullptr;
   int head_grid = 0;
@@ -143,6 +145,11 @@ struct exb_model {
   int tp = 1, tp_rank = 0;
   int qh0 = 0, qh1 = 0, kh0 = 0, kh1 = 0, ig0 = 0, ig1 = 0, v0 = 0, v1 = 0, vmax = 0;
   ncclComm_t comm = nullptr;
+  // one-shot peer-memory all-reduce (tpcomm.cu); NCCL when the peers cannot be mapped or "tpar" is 0
+  TpComm tpc;
+  bool tpc_on = false, tpar = true;
+  char* tpc_local = nullptr;
+  unsigned long long* tpc_epoch = nullptr;
   int64_t* tp_tot = nullptr;                // (RMAX, D) partial sums of o / down
   int64_t* tp_hval = nullptr;               // (RMAX) shard best logit
   int64_t* tp_hmax = nullptr;               // (RMAX) all-reduced best logit
@@ -165,8 +172,9 @@ struct exb_model {
   // persistent decode-step kernel (step.cu): per-layer descriptors and accumulators
   bool step_on = false;
   bool tc_on = true;                    // multi-row chunks on the tensor-core GEMM
-  int fuse_in = 1;                      // GEMVs build their int16 input rows: 1 = qrow prologue (o, down),
-                                        // 2 = also the norm (q|k|v, gate|up, head), 0 = separate kernels
+  int fuse_in = 3;                      // GEMVs build their int16 input rows: 1 = qrow prologue (o, down),
+                                        // 2 = also the norm (q|k|v, gate|up, head), 3 = the norm from the
+                                        // row statistics the residual producers publish, 0 = separate kernels
   bool attn_fused = true;               // decode: RoPE + cache write inside the attention kernel
   bool attn_prefill = true;             // prefill chunks of one sequence: query-tile attention kernel
   bool tc_decode = false;               // decode-step linears on the tcgen05 GEMM (8-row tiles, split-K)
@@ -325,6 +333,8 @@ static void plan_runtime(exb_model* m) {
   m->next_tok = ralloc<int32_t>(m, RMAX);
   m->amax_o = ralloc<unsigned long long>(m, RMAX);
   m->amax_h = ralloc<unsigned long long>(m, RMAX);
+  m->nstat_a = ralloc<unsigned long long>(m, 2 * RMAX);
+  m->nstat_b = ralloc<unsigned long long>(m, 2 * RMAX);
   m->ticket = ralloc<unsigned int>(m, 4);
   m->head_part = ralloc<unsigned long long>(m, (size_t)m->head_grid * RMAX * 2);
   m->head_ticket = ralloc<unsigned int>(m, 1);
@@ -500,8 +510,11 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     }
   }
   if (m->fr_on) RUN(cudaMemsetAsync(m->fr_acc, 0, sizeof(unsigned long long) * m->n_lin * RMAX * 4, st));
+  // norm from published row statistics (fuse level 3): dense single-GPU models without capture
+  const bool fzs = m->fuse_in >= 3 && !m->fr_on && !cm && !tp && !c.n_experts && !m->emb_q16;
   if (m->emb_q16) RUN(launch_embed64(m->emb_q16, ids, R, c.D, m->x, st, false));   // general Q16 rows
-  else RUN(launch_embed(m->emb, c.emb_shift, ids, R, c.D, m->x, st, false));        // int8 rows << shift
+  else RUN(launch_embed(m->emb, c.emb_shift, ids, R, c.D, m->x, st, false,          // int8 rows << shift
+                        fzs ? m->nstat_a : nullptr));
   const int Hd = c.H * c.hd;
   AttnArgs aa;
   aa.qkv = m->qkv; aa.ldqkv = m->Nqkv; aa.row_seq = seq; aa.row_pos = pos;
@@ -511,6 +524,26 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
   // INV = round(2^16 / sqrt(hd)) (exact_llm.py:164): correctly rounded sqrt and division, ties to even
   aa.inv = (int64_t)std::nearbyint(65536.0 / std::sqrt((double)c.hd));
   auto trace_ptr = [&](int li) -> int64_t* { return m->trace_on ? m->trace + m->lins[li].trace_off : nullptr; };
+  // tensor-parallel all-reduces: the one-shot peer-memory kernel, else NCCL (both inside the graph)
+  const bool tpc = tp && m->tpc_on && m->tpar;
+  auto ar = [&](const void* src, void* dst, size_t n, ncclDataType_t t, ncclRedOp_t op, int myop) -> cudaError_t {
+    if (tpc) return launch_tp_allreduce(m->tpc, src, dst, (int)n, myop, TpResid(), st);
+    return tp_allreduce(m, src, dst, n, t, op, st);
+  };
+  // SUM of a row-split linear's partial sums, then x += shr(tot, 28 - s) + b (and the trace copy)
+  auto ar_resid = [&](const int64_t* bias, int64_t* trace_dst) -> cudaError_t {
+    if (tpc) {
+      TpResid rz;
+      rz.x = m->x; rz.ldx = c.D; rz.N = c.D; rz.xs = m->xs; rz.b = bias; rz.tot = trace_dst; rz.ldt = (int)m->trace_row;
+      return launch_tp_allreduce(m->tpc, m->tp_tot, nullptr, R * c.D, 1, rz, st);
+    }
+    cudaError_t e2 = tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st);
+    if (e2 == cudaSuccess && trace_dst)
+      e2 = cudaMemcpy2DAsync(trace_dst, sizeof(int64_t) * m->trace_row, m->tp_tot, sizeof(int64_t) * c.D,
+                             sizeof(int64_t) * c.D, R, cudaMemcpyDeviceToDevice, st);
+    if (e2 == cudaSuccess) e2 = launch_tp_resid(m->tp_tot, R, c.D, m->xs, bias, m->x, c.D, st);
+    return e2;
+  };
   auto set_fr = [&](GemvArgs& g, std::initializer_list<int> lis, int nseg_start_override = -1) {
     (void)nseg_start_override;
     if (!m->fr_on) return;
@@ -597,15 +630,17 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     // o and down: qrow in the prologue (not under tensor parallelism: the residual update after the
     // all-reduce requantises with the row shift the separate qrow kernel publishes in m->xs)
     const bool fz = m->fuse_in >= 1 && !m->fr_on && !tp;
-    const bool fzn = m->fuse_in >= 2 && !m->fr_on && !cm;  // q|k|v and gate|up: norm in the prologue
-    if (!fzn)
+    const bool fzn = m->fuse_in == 2 && !m->fr_on && !cm;  // q|k|v and gate|up: norm in the prologue
+    if (!fzn && !fzs)
       RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, nullptr,
                         cm ? m->cap + (size_t)i * c.D : nullptr, m->cap_row));
     {
       GemvArgs g; base(g, Ld.qkv);
       if (fzn) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g1; }
+      if (fzs) { g.xin = XIN_NORMST; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g1; g.nstat_in = m->nstat_a; }
       g.epi = EPI_STORE; g.out = m->qkv; g.ldo = m->Nqkv; g.raw = trace_ptr(Ld.li[0]);
       g.zero = m->amax_o; g.nzero = RMAX;
+      if (fzs) { g.zero2 = m->nstat_b; g.nzero2 = 2 * RMAX; }            // o accumulates norm2's statistics
       set_fr(g, {Ld.li[0], Ld.li[1], Ld.li[2]});
       RUN(launch_gemv(g, st, pdl));
     }
@@ -618,25 +653,20 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       RUN(launch_attn_decode(aa, st, pdl));
     }
     // tensor parallel: the qrow of o's input needs the max over every rank's heads
-    if (tp) RUN(tp_allreduce(m, m->amax_o, m->amax_o, R, ncclUint64, ncclMax, st));
+    if (tp) RUN(ar(m->amax_o, m->amax_o, R, ncclUint64, ncclMax, 0));
     if (!fz) RUN(launch_quant_known(m->ao, Hd, R, Hd, m->amax_o, m->xq, m->KMAX, m->xs, st, pdl && !tp));
     {
       GemvArgs g; base(g, Ld.o);
       if (fz) { g.xin = XIN_QUANT; g.x64 = m->ao; g.ldx64 = Hd; g.amax_in = m->amax_o; }
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[3]);
       g.zero = m->amax_h; g.nzero = RMAX;
+      if (fzs) g.nstat_out = m->nstat_b;
       if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own heads
       set_fr(g, {Ld.li[3]});
       RUN(launch_gemv(g, st, pdl));
     }
-    if (tp) {
-      RUN(tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st));
-      if (m->trace_on)   // the trace records o's full sum (every rank holds it after the all-reduce)
-        RUN(cudaMemcpy2DAsync(trace_ptr(Ld.li[3]), sizeof(int64_t) * m->trace_row, m->tp_tot, sizeof(int64_t) * c.D,
-                              sizeof(int64_t) * c.D, R, cudaMemcpyDeviceToDevice, st));
-      RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.o.b, m->x, c.D, st));
-    }
-    if (!fzn || c.n_experts) RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    if (tp) RUN(ar_resid(Ld.o.b, trace_ptr(Ld.li[3])));   // the trace records o's full sum
+    if ((!fzn && !fzs) || c.n_experts) RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     if (c.n_experts) {
       RUN(launch_moe(moe_args(m, i, R, m->xq, m->KMAX, m->xs, g_hist_row0), m->x, c.D, st));
       continue;
@@ -644,31 +674,30 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     {
       GemvArgs g; base(g, Ld.gu);
       if (fzn) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g2; }
+      if (fzs) {
+        g.xin = XIN_NORMST; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g2; g.nstat_in = m->nstat_b;
+        g.zero2 = m->nstat_a; g.nzero2 = 2 * RMAX;                       // down accumulates the next norm1's
+      }
       g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.amax_out = m->amax_h;
       g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]);
       set_fr(g, {Ld.li[4], Ld.li[5]});
       RUN(launch_gemv(g, st, pdl));
     }
-    if (tp) RUN(tp_allreduce(m, m->amax_h, m->amax_h, R, ncclUint64, ncclMax, st));
+    if (tp) RUN(ar(m->amax_h, m->amax_h, R, ncclUint64, ncclMax, 0));
     if (!fz) RUN(launch_quant_known(m->hb, c.I, R, c.I, m->amax_h, m->xq, m->KMAX, m->xs, st, pdl && !tp));
     {
       GemvArgs g; base(g, Ld.down);
       if (fz) { g.xin = XIN_QUANT; g.x64 = m->hb; g.ldx64 = c.I; g.amax_in = m->amax_h; }
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[6]);
+      if (fzs) g.nstat_out = m->nstat_a;
       if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own groups
       set_fr(g, {Ld.li[6]});
       RUN(launch_gemv(g, st, pdl));
     }
-    if (tp) {
-      RUN(tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st));
-      if (m->trace_on)
-        RUN(cudaMemcpy2DAsync(trace_ptr(Ld.li[6]), sizeof(int64_t) * m->trace_row, m->tp_tot, sizeof(int64_t) * c.D,
-                              sizeof(int64_t) * c.D, R, cudaMemcpyDeviceToDevice, st));
-      RUN(launch_tp_resid(m->tp_tot, R, c.D, m->xs, Ld.down.b, m->x, c.D, st));
-    }
+    if (tp) RUN(ar_resid(Ld.down.b, trace_ptr(Ld.li[6])));
   }
-  const bool fzh = m->fuse_in >= 2 && !m->fr_on && !cm;
-  if (!fzh)
+  const bool fzh = m->fuse_in == 2 && !m->fr_on && !cm;
+  if (!fzh && !fzs)
     RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, nullptr,
                       cm ? m->cap + (size_t)c.NL * c.D : nullptr, m->cap_row));
   {
@@ -676,6 +705,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     g.L = m->head; g.R = R; g.err = m->err; g.ldr = (int)m->trace_row;
     g.xq = m->xq; g.xs = m->xs; g.ldx = m->KMAX;
     if (fzh) { g.xin = XIN_NORM; g.x64 = m->x; g.ldx64 = c.D; g.gain = m->gf; }
+    if (fzs) { g.xin = XIN_NORMST; g.x64 = m->x; g.ldx64 = c.D; g.gain = m->gf; g.nstat_in = m->nstat_a; }
     g.epi = EPI_HEAD; g.out = (want_logits || smp) ? m->logits : nullptr; g.ldo = tp ? m->vmax : c.V;
     g.raw = trace_ptr(m->n_lin - 1);
     g.head_part = m->head_part; g.head_ticket = m->head_ticket; g.next_tok = m->next_tok; g.grid = m->head_grid;
@@ -685,9 +715,9 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
   }
   if (tp) {
     // greedy over the vocabulary slices: the largest value, then the lowest index holding it
-    RUN(tp_allreduce(m, m->tp_hval, m->tp_hmax, R, ncclInt64, ncclMax, st));
+    RUN(ar(m->tp_hval, m->tp_hmax, R, ncclInt64, ncclMax, 3));
     RUN(launch_tp_pick(m->tp_hval, m->tp_hmax, m->next_tok, m->v0, R, st));
-    RUN(tp_allreduce(m, m->next_tok, m->next_tok, R, ncclInt32, ncclMin, st));
+    RUN(ar(m->next_tok, m->next_tok, R, ncclInt32, ncclMin, 2));
   }
   if (smp)   // replaces the head's greedy choice; advances each row's sampling position
     RUN(launch_sample(R, m->logits, c.V, c.V, m->samp_seed, m->samp_pos, true, m->samp_tnum, m->exp_t, m->next_tok,
@@ -954,6 +984,63 @@ int exb_tp_unique_id(uint8_t* out128) {
   return EXB_OK;
 }
 
+// The one-shot all-reduce's buffers: one per rank, zeroed, exported with CUDA IPC, the handles
+// all-gathered with NCCL and every peer's buffer mapped here.  Collective (every rank calls it
+// from create).  Any failure leaves tpc_on false: the step graph then uses NCCL.
+static void tp_comm_setup(exb_model* m) {
+  const int P = m->tp;
+  if (P > TPC_MAX_RANKS) return;
+  const int nblk = (RMAX * m->c.D + TPC_CH - 1) / TPC_CH;      // the largest call: R x D partial sums
+  const size_t bytes = tp_comm_bytes(P, nblk);
+  bool ok = cudaMalloc(&m->tpc_local, bytes) == cudaSuccess &&
+            cudaMalloc(&m->tpc_epoch, sizeof(unsigned long long) * nblk) == cudaSuccess &&
+            cudaMemset(m->tpc_local, 0, bytes) == cudaSuccess &&
+            cudaMemset(m->tpc_epoch, 0, sizeof(unsigned long long) * nblk) == cudaSuccess;
+  cudaIpcMemHandle_t mine;
+  if (ok) ok = cudaIpcGetMemHandle(&mine, m->tpc_local) == cudaSuccess;
+  // every rank takes part in the exchange, also after a local failure (a zeroed handle marks it)
+  if (!ok) memset(&mine, 0, sizeof mine);
+  std::vector<cudaIpcMemHandle_t> all(P);
+  char* dbuf = nullptr;
+  if (cudaMalloc(&dbuf, sizeof(cudaIpcMemHandle_t) * (P + 1)) != cudaSuccess) { cudaGetLastError(); return; }
+  cudaMemcpy(dbuf + sizeof(cudaIpcMemHandle_t) * P, &mine, sizeof mine, cudaMemcpyHostToDevice);
+  const bool gathered = nccl()->all_gather(dbuf + sizeof(cudaIpcMemHandle_t) * P, dbuf, sizeof(cudaIpcMemHandle_t),
+                                           ncclUint8, m->comm, m->st) == ncclSuccess;
+  if (gathered) cudaMemcpyAsync(all.data(), dbuf, sizeof(cudaIpcMemHandle_t) * P, cudaMemcpyDeviceToHost, m->st);
+  cudaStreamSynchronize(m->st);
+  cudaFree(dbuf);
+  ok = ok && gathered;
+  const cudaIpcMemHandle_t zero{};
+  for (int q = 0; q < P && ok; ++q) {
+    if (memcmp(&all[q], &zero, sizeof zero) == 0) ok = false;
+    if (q != m->tp_rank && ok) {       // mapping a peer's buffer enables the peer access it needs
+      void* p = nullptr;
+      ok = cudaIpcOpenMemHandle(&p, all[q], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+      m->tpc.base[q] = (char*)p;
+    }
+  }
+  // agree: the kernel runs only if every rank mapped every peer (an int MIN over the ranks)
+  int* flag = nullptr;
+  int v = ok ? 1 : 0;
+  if (cudaMalloc(&flag, sizeof(int)) == cudaSuccess) {
+    cudaMemcpy(flag, &v, sizeof v, cudaMemcpyHostToDevice);
+    if (nccl()->all_reduce(flag, flag, 1, ncclInt32, ncclMin, m->comm, m->st) == ncclSuccess) {
+      cudaMemcpyAsync(&v, flag, sizeof v, cudaMemcpyDeviceToHost, m->st);
+      cudaStreamSynchronize(m->st);
+    } else {
+      v = 0;
+    }
+    cudaFree(flag);
+  } else {
+    v = 0;
+  }
+  cudaGetLastError();
+  m->tpc.rank = m->tp_rank; m->tpc.size = P; m->tpc.nblk = nblk;
+  m->tpc.base[m->tp_rank] = m->tpc_local;
+  m->tpc.epoch = m->tpc_epoch; m->tpc.err = m->err;
+  m->tpc_on = v == 1;
+}
+
 static int create_impl(const exb_config* cfg, int rank, int size, const uint8_t* uid, exb_model** out) {
   if (!cfg || !out) FAIL(EXB_EINVAL, "null argument");
   int plan[9];
@@ -1022,6 +1109,7 @@ static int create_impl(const exb_config* cfg, int rank, int size, const uint8_t*
       exb_model_destroy(m);
       FAIL(EXB_ECUDA, "ncclCommInitRank failed");
     }
+    tp_comm_setup(m);            // collective; NCCL stays the all-reduce when the peers cannot be mapped
   }
   *out = m;
   return EXB_OK;
@@ -1029,6 +1117,10 @@ static int create_impl(const exb_config* cfg, int rank, int size, const uint8_t*
 
 void exb_model_destroy(exb_model* m) {
   if (!m) return;
+  for (int q = 0; q < TPC_MAX_RANKS; ++q)
+    if (q != m->tp_rank && m->tpc.base[q]) cudaIpcCloseMemHandle(m->tpc.base[q]);
+  cudaFree(m->tpc_local);
+  cudaFree(m->tpc_epoch);
   for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
   if (m->st) cudaStreamSynchronize(m->st);
   cudaFree(m->warena);
@@ -2128,6 +2220,7 @@ int exb_set_option(exb_model* m, const char* name, int64_t value) {
   if (n == "step") m->step_on = value != 0;
   else if (n == "tc") m->tc_on = value != 0;
   else if (n == "fuse") m->fuse_in = (int)value;
+  else if (n == "tpar") m->tpar = value != 0;
   else if (n == "attn") m->attn_fused = value != 0;
   else if (n == "pattn") m->attn_prefill = value != 0;
   else if (n == "tcd") m->tc_decode = value != 0;

@@ -81,6 +81,8 @@ enum XIn {
   XIN_Q16 = 0,       // xq (R, ldx) int16 + shifts xs (R), already quantised
   XIN_NORM = 1,      // x64 rows: xq, s = qrow(irms(x, gain))          (every CTA computes it)
   XIN_QUANT = 2,     // x64 rows: xq = clip(shr(x, s)), s from the producer's published max |x|
+  XIN_NORMST = 3,    // x64 rows: xq, s = qrow(irms(x, gain)) from the producers' published row
+                     // statistics (max |x|, sum x^2): one reduction per CTA instead of three
 };
 
 struct GemvArgs {
@@ -91,12 +93,15 @@ struct GemvArgs {
   const int64_t* x64 = nullptr; int ldx64 = 0;  // XIN_NORM / XIN_QUANT source rows (int64 Q16)
   const int64_t* gain = nullptr;                // XIN_NORM gains
   const unsigned long long* amax_in = nullptr;  // XIN_QUANT per-row max |x|
+  const unsigned long long* nstat_in = nullptr; // XIN_NORMST per-row (max |x|, sum x^2), 2 words per row
   int rb = 0;                                   // columns per warp block (0: chosen by the launcher)
   int pre = -1;                                 // first load batch copied to shared memory before the
                                                 // PDL wait: -1 where two CTAs per SM still fit, 0 never
   int pre_off = 0;                              // set by the launcher: byte offset of that area
   unsigned long long* amax_out = nullptr;       // epilogue: per-row max |output| (atomicMax)
   unsigned long long* zero = nullptr; int nzero = 0;   // CTA 0 clears these words (for a later producer)
+  unsigned long long* zero2 = nullptr; int nzero2 = 0; // a second range
+  unsigned long long* nstat_out = nullptr;      // EPI_RESID: per row atomicMax max |x_new|, atomicAdd sum x_new^2
   int tail = TAIL_NONE;
   unsigned int* ticket = nullptr;
   const int64_t* tail_x = nullptr; int tail_ldx = 0; int tail_K = 0;
@@ -135,6 +140,26 @@ int gemv_grid(int N, bool swiglu);
 cudaError_t launch_gemv_op(const int16_t* x16, const int8_t* wT, const int64_t* Mg, int K, int N, int64_t* out,
                            cudaStream_t st);
 
+// One-shot tensor-parallel all-reduce over NVLink peer memory (tpcomm.cu)
+constexpr int TPC_CH = 1024;                  // 8-byte elements per CTA slice
+constexpr int TPC_MAX_RANKS = 8;
+struct TpComm {
+  int rank = 0, size = 1, nblk = 0;
+  char* base[TPC_MAX_RANKS] = {};             // every rank's buffer, mapped into this process
+  unsigned long long* epoch = nullptr;        // (nblk) this rank's call counters, one per slice
+  int* err = nullptr;                         // device error word (wait timeout)
+};
+struct TpResid {                              // int64 SUM fused with the residual update
+  int64_t* x = nullptr; int ldx = 0; int N = 0;
+  const int32_t* xs = nullptr; const int64_t* b = nullptr;
+  int64_t* tot = nullptr; int ldt = 0;        // optional copy of the full sums (trace)
+};
+// op 0: uint64 max, 1: int64 sum (with rz.x: x[r, j] += shr(sum, 28 - xs[r]) + b[j]), 2: int32 min,
+// 3: int64 max
+cudaError_t launch_tp_allreduce(const TpComm& c, const void* src, void* dst, int n, int op, const TpResid& rz,
+                                cudaStream_t st);
+size_t tp_comm_bytes(int size, int nblk);
+
 // tensor parallel helpers (rowops.cu)
 // x[r, n] += shr(tot[r, n], 28 - xs[r]) (+ b[n]): the residual update after an all-reduced partial sum
 cudaError_t launch_tp_resid(const int64_t* tot, int R, int N, const int32_t* xs, const int64_t* b, int64_t* x, int ldx,
@@ -143,8 +168,9 @@ cudaError_t launch_tp_resid(const int64_t* tot, int R, int N, const int32_t* xs,
 cudaError_t launch_tp_pick(const int64_t* val, const int64_t* gmax, int32_t* idx, int v0, int R, cudaStream_t st);
 
 // per-row kernels
+// nstat (optional): per row (max |x|, sum x^2) of the embedded row, for a XIN_NORMST consumer
 cudaError_t launch_embed(const int8_t* emb, int emb_shift, const int32_t* ids, int R, int D, int64_t* x,
-                         cudaStream_t st, bool pdl);
+                         cudaStream_t st, bool pdl, unsigned long long* nstat = nullptr);
 cudaError_t launch_embed64(const int64_t* emb_q16, const int32_t* ids, int R, int D, int64_t* x, cudaStream_t st,
                            bool pdl);
 // dig (optional): int8 digit planes of the rows for the tensor-core decode GEMM (TC_DECODE_ROWS-row planes)

@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
       EpiState& E = est[warp][lane][r];
       for (int q = 0; q < 3; ++q) E.frl[q][0] = E.frl[q][1] = 0;
       E.omax = 0;
+      E.ssq = 0;
       E.best_v = INT64_MIN;
       E.best_n = 0x7fffffff;
     }
@@ -114,6 +115,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   pdl_wait();
   if (blockIdx.x == 0 && a.zero)
     for (int i = threadIdx.x; i < a.nzero; i += GEMV_THREADS) a.zero[i] = 0;
+  if (blockIdx.x == 0 && a.zero2)
+    for (int i = threadIdx.x; i < a.nzero2; i += GEMV_THREADS) a.zero2[i] = 0;
   if (a.xin == XIN_Q16) {
     const int n16 = K >> 3;                                   // int4 per activation row
     for (int i = threadIdx.x; i < R * n16; i += GEMV_THREADS) {
@@ -121,6 +124,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
       reinterpret_cast<int4*>(xs + (size_t)r * K)[c] = reinterpret_cast<const int4*>(a.xq + (size_t)r * a.ldx)[c];
     }
     if (threadIdx.x < R) sh_s[threadIdx.x] = a.xs[threadIdx.x];
+  } else if (a.xin == XIN_NORMST) {
+    // the norm from the row statistics the producers published (max |x|, sum x^2); the full
+    // routine when irms would shift the row (max |x| >= 2^24) or the row is too long for registers
+    int64_t* ys = reinterpret_cast<int64_t*>(smem_raw + (((size_t)R * K * 2 + 127) & ~(size_t)127));
+    for (int r = 0; r < R; ++r) {
+      const uint64_t mx = __ldcg(a.nstat_in + 2 * r), ss = __ldcg(a.nstat_in + 2 * r + 1);
+      if (!row_norm_q_stats<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, mx, ss, xs + (size_t)r * K, &sh_s[r],
+                                          rred))
+        row_norm_q_any<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, xs + (size_t)r * K, &sh_s[r], ys, rred);
+    }
   } else if (a.xin == XIN_NORM) {
     // xq, s = qrow(irms(x, g)) for every row, computed by this CTA (exact_llm.py:100-106, 41-46)
     int64_t* ys = reinterpret_cast<int64_t*>(smem_raw + (((size_t)R * K * 2 + 127) & ~(size_t)127));
@@ -222,13 +235,14 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   __syncwarp();
   tl_point(1);
   // fold this warp's epilogue states (one per column-block entry) into lane-0 values
-  uint64_t omax[R];
+  uint64_t omax[R], ssq[R];
   int64_t best_v[R];
   int best_n[R];
   unsigned long long frl[R][3][2];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     omax[r] = 0;
+    ssq[r] = 0;
     best_v[r] = INT64_MIN;
     best_n[r] = 0x7fffffff;
 #pragma unroll
@@ -236,6 +250,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     for (int b = 0; b < RB; ++b) {
       const EpiState& E = est[warp][b][r];
       omax[r] = E.omax > omax[r] ? E.omax : omax[r];
+      ssq[r] += E.ssq;
       if (E.best_v > best_v[r] || (E.best_v == best_v[r] && E.best_n < best_n[r])) { best_v[r] = E.best_v; best_n[r] = E.best_n; }
 #pragma unroll
       for (int q = 0; q < 3; ++q) { frl[r][q][0] += E.frl[q][0]; frl[r][q][1] += E.frl[q][1]; }
@@ -250,6 +265,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     for (int r = 0; r < R; ++r) {
       const uint64_t v = block_max_u64<GEMV_THREADS>(lane == 0 ? omax[r] : 0, rred);
       if (threadIdx.x == 0 && v) atomicMax(a.amax_out + r, (unsigned long long)v);
+    }
+  }
+  // ---- residual row statistics for the next norm (max |x_new|, sum x_new^2), one atomic each per CTA
+  if (a.nstat_out) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint64_t v = block_max_u64<GEMV_THREADS>(lane == 0 ? omax[r] : 0, rred);
+      if (threadIdx.x == 0 && v) atomicMax(a.nstat_out + 2 * r, (unsigned long long)v);
+      const uint64_t sq = (uint64_t)block_sum_i64<GEMV_THREADS>(lane == 0 ? (int64_t)ssq[r] : 0, rred);
+      if (threadIdx.x == 0 && sq) atomicAdd(a.nstat_out + 2 * r + 1, (unsigned long long)sq);
     }
   }
   // ---- Freivalds: per-CTA partial sums -> one atomic per (segment, row, prime)
@@ -414,7 +439,9 @@ cudaError_t launch_gemv(const GemvArgs& a0, cudaStream_t st, bool pdl) {
     a.rb = units <= a.grid * NCW * 2 ? 1 : 4;
   }
   size_t smem = (((size_t)a.R * a.L.K * 2 + 127) & ~(size_t)127);
-  if (a.xin == XIN_NORM) smem += (size_t)a.L.K * 16;                                       // row + gains
+  if (a.xin == XIN_NORM || (a.xin == XIN_NORMST && a.L.K > 12 * GEMV_THREADS))
+    smem += (size_t)a.L.K * 16;                                                              // row + gains
+  if (a.xin == XIN_NORMST && !a.nstat_in) return cudaErrorInvalidValue;
   if (a.tail == TAIL_NORM && smem < (size_t)a.tail_K * 16) smem = (size_t)a.tail_K * 16;   // tail stages row + gains
   if (smem > DYN_SMEM_MAX) return cudaErrorInvalidValue;
   a.pre_off = 0;

@@ -44,7 +44,8 @@ EXB_DEV int64_t requant1(const LinW& L, int n, int64_t tot, int s) {
 // Per-(epilogue lane, activation row) accumulators, kept in shared memory to spare registers.
 struct EpiState {
   unsigned long long frl[3][2];   // Freivalds left-hand side residue sums (segment, prime)
-  uint64_t omax;                  // max |output| (SwiGLU)
+  uint64_t omax;                  // max |output| (SwiGLU), max |x_new| (residual statistics)
+  uint64_t ssq;                   // sum of x_new^2 (residual statistics; exact while max |x_new| < 2^24)
   int64_t best_v;                 // greedy argmax value / index
   int best_n;
 };
@@ -94,7 +95,13 @@ EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, 
   if (a.epi == EPI_RESID) {
     // the residual row may have been written by another CTA of a persistent kernel: read it from L2
     int64_t* o = a.out + (size_t)r * a.ldo + n;
-    *o = (int64_t)((uint64_t)__ldcg(reinterpret_cast<const long long*>(o)) + (uint64_t)y);
+    const int64_t xn = (int64_t)((uint64_t)__ldcg(reinterpret_cast<const long long*>(o)) + (uint64_t)y);
+    *o = xn;
+    if (a.nstat_out) {
+      const uint64_t ax = uabs64(xn);
+      omax = ax > omax ? ax : omax;
+      E.ssq += (uint64_t)xn * (uint64_t)xn;          // wraps harmlessly when max |x_new| >= 2^24 (unused then)
+    }
   } else if (a.out) {
     a.out[(size_t)r * a.ldo + n] = y;
   }

@@ -196,6 +196,59 @@ EXB_DEV void row_norm_q_regs(const int64_t* __restrict__ xr, const int64_t* __re
   __syncthreads();
 }
 
+// irms + qrow of one row from its published statistics m = max |x| and ss = sum x^2 (summed by the
+// CTAs that produced the row).  When m < 2^24 the shift k of irms is 0, so ss is exactly
+// sum(shr(x, k)^2) and only the qrow maximum is left to reduce; otherwise (k > 0) returns false
+// and the caller runs the full routine.  Row in registers (D <= EPT * NT).
+template <int NT, int EPT>
+EXB_DEV bool row_norm_q_stats_regs(const int64_t* __restrict__ xr, const int64_t* __restrict__ g, int D, uint64_t m,
+                                   uint64_t ss, int16_t* __restrict__ xq, int32_t* __restrict__ xs_out, uint64_t* red) {
+  if (bitlen64(m) > 24) return false;
+  int64_t v[EPT], gv[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int i = threadIdx.x + j * NT;
+    v[j] = i < D ? ld_cg(xr + i) : 0;
+    gv[j] = i < D ? __ldg(g + i) : 0;
+  }
+  // ms = ss // D + 1, r = max(isqrt(ms), 1)   (exact_llm.py:103-104)
+  const double invD = 1.0 / (double)D;
+  int64_t q = __double2ll_rz(__ll2double_rn((int64_t)ss) * invD);
+  int64_t rem = (int64_t)ss - q * (int64_t)D;
+  while (rem < 0) { q -= 1; rem += D; }
+  while (rem >= D) { q += 1; rem -= D; }
+  int64_t rt = isqrt_ref(q + 1);
+  rt = rt > 1 ? rt : 1;
+  const NormDiv nd = make_norm_div(rt, 0);
+  uint64_t m2 = 0;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int64_t y = norm_div(v[j], nd);
+    v[j] = shr_nn((int64_t)((uint64_t)y * (uint64_t)gv[j]), 16);
+    const uint64_t u = uabs64(v[j]);
+    m2 = u > m2 ? u : m2;
+  }
+  m2 = block_max_fast<NT>(m2, red);
+  const int s = qrow_shift(m2);
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int i = threadIdx.x + j * NT;
+    if (i < D) xq[i] = qrow_value(v[j], s);
+  }
+  if (threadIdx.x == 0) *xs_out = s;
+  __syncthreads();
+  return true;
+}
+
+template <int NT>
+EXB_DEV bool row_norm_q_stats(const int64_t* __restrict__ xr, const int64_t* __restrict__ g, int D, uint64_t m,
+                              uint64_t ss, int16_t* __restrict__ xq, int32_t* __restrict__ xs_out, uint64_t* red) {
+  if (D <= 4 * NT) return row_norm_q_stats_regs<NT, 4>(xr, g, D, m, ss, xq, xs_out, red);
+  if (D <= 8 * NT) return row_norm_q_stats_regs<NT, 8>(xr, g, D, m, ss, xq, xs_out, red);
+  if (D <= 12 * NT) return row_norm_q_stats_regs<NT, 12>(xr, g, D, m, ss, xq, xs_out, red);
+  return false;
+}
+
 // irms + qrow of one row: registers when D <= 12 NT, else staged in shared memory (`ys`, 2*D int64)
 template <int NT>
 EXB_DEV void row_norm_q_any(const int64_t* __restrict__ xr, const int64_t* __restrict__ g, int D,

@@ -27,19 +27,35 @@ static cudaError_t launch_simple(const void* fn, dim3 grid, dim3 block, size_t s
 }
 
 // ---------------------------------------------------------------- embedding: x = emb[id] << shift
-__global__ void k_embed(const int8_t* __restrict__ emb, int shift, const int32_t* __restrict__ ids, int D,
-                        int64_t* __restrict__ x) {
+// With `nstat`, the row's (max |x|, sum x^2) for a consumer that finishes the norm from them.
+EXB_DEV void embed_stats(uint64_t m, uint64_t ss, unsigned long long* nstat) {
+  __shared__ uint64_t red[33];
+  m = block_max_u64<256>(m, red);
+  ss = (uint64_t)block_sum_i64<256>((int64_t)ss, red);
+  if (threadIdx.x == 0) { nstat[0] = m; nstat[1] = ss; }
+}
+
+__global__ void __launch_bounds__(256) k_embed(const int8_t* __restrict__ emb, int shift, const int32_t* __restrict__ ids,
+                                               int D, int64_t* __restrict__ x, unsigned long long* __restrict__ nstat) {
   pdl_wait();
   const int r = blockIdx.x;
   const int8_t* e = emb + (size_t)ids[r] * D;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) x[(size_t)r * D + i] = (int64_t)e[i] << shift;
+  uint64_t m = 0, ss = 0;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const int64_t v = (int64_t)e[i] << shift;
+    x[(size_t)r * D + i] = v;
+    const uint64_t a = uabs64(v);
+    m = a > m ? a : m;
+    ss += (uint64_t)v * (uint64_t)v;
+  }
+  if (nstat) embed_stats(m, ss, nstat + 2 * r);
   pdl_launch_dependents();
   tl_exit();
 }
 
 cudaError_t launch_embed(const int8_t* emb, int emb_shift, const int32_t* ids, int R, int D, int64_t* x,
-                         cudaStream_t st, bool pdl) {
-  void* args[] = {(void*)&emb, (void*)&emb_shift, (void*)&ids, (void*)&D, (void*)&x};
+                         cudaStream_t st, bool pdl, unsigned long long* nstat) {
+  void* args[] = {(void*)&emb, (void*)&emb_shift, (void*)&ids, (void*)&D, (void*)&x, (void*)&nstat};
   return launch_simple((const void*)k_embed, dim3(R), dim3(256), 0, st, pdl, args);
 }
 

@@ -230,12 +230,19 @@ int exb_model_create_tp(const exb_config* cfg, int rank, int size, const uint8_t
  *   "tc"      1 (default): forward calls of >= 16 rows run their linears on the tcgen05 tensor-core
  *             GEMM in chunks of 256 rows; 0: 4-row CUDA-core GEMV passes
  *   "pf_kb"   per-CTA L2 prefetch of the next weight slices where HBM would idle, KiB (default 64; 0 = off)
- *   "fuse"    decode GEMVs build their own int16 input rows: 1 (default) the qrow of the o and down
- *             inputs; 2 also the RMSNorm of the q|k|v, gate|up and head inputs; 0 separate kernels
+ *   "fuse"    decode GEMVs build their own int16 input rows: 1 the qrow of the o and down inputs;
+ *             2 also the RMSNorm of the q|k|v, gate|up and head inputs, each CTA computing it whole;
+ *             3 (default) the qrow prologues and the RMSNorm finished in the q|k|v, gate|up and head
+ *             prologues from the row statistics (max |x|, sum x^2) that the embedding and the o and
+ *             down epilogues publish (no norm kernels; dense single-GPU models without commitment
+ *             capture or Freivalds, else level 1); 0 separate kernels
  *   "attn"    1 (default): decode RoPE + K/V cache write inside the attention kernel; 0 separate
  *   "pattn"   1 (default): prefill chunks of one sequence run the query-tile attention kernel;
  *             0: the per-row kernel
  *   "tcd"     1: decode-step linears on the tcgen05 GEMM (8-row tiles); 0 (default) CUDA-core GEMVs
+ *   "tpar"    tensor parallel: 1 (default) the step's all-reduces run as one-shot kernels over the peers'
+ *             memory (CUDA IPC mappings over NVLink, bounded flag waits), NCCL where the peers could
+ *             not be mapped; 0 NCCL
  * Cached step graphs are dropped. */
 int exb_set_option(exb_model* m, const char* name, int64_t value);
 
