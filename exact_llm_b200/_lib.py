@@ -82,8 +82,6 @@ SIGNATURES = {
                                         ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)]),
     "exb_profile_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float), ctypes.c_int,
                                         ctypes.POINTER(ctypes.c_int)]),
-    "exb_profile_persistent": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint64),
-                                              ctypes.c_int64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "exb_model_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
     "exb_model_weight_bytes": (ctypes.c_size_t, [ctypes.c_void_p]),
     "exb_gen_tensor": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64,

@@ -427,7 +427,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
     if (tb > 0) {
       __syncthreads();
       stage_k(tb, nt);
-      patch(tb, nt, true, false);
+      __syncthreads();                                   // the staged tile before this step's rows overwrite
+      patch(tb, nt, true, false);                        // theirs (else a stale cache row can win the race)
       __syncthreads();
     }
     for (int p0 = 0; p0 < 2 * TILE; p0 += ATT_THREADS) {
@@ -510,6 +511,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
       __syncthreads();
       if (tb > 0) {
         stage_v(tb, nt);
+        __syncthreads();                                 // as for the K tiles
         patch(tb, nt, false, true);
         __syncthreads();
       }

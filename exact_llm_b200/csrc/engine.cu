@@ -43,7 +43,6 @@ void exb::set_last_error(const std::string& msg) { g_err = msg; }
   } while (0)
 
 static constexpr int RMAX = 4;          // activation rows per GEMV pass (CUDA-core decode path)
-static constexpr int STEP_ROWS = 2;     // rows the persistent step kernel takes (batch <= 2)
 static constexpr int MOE_ROWS = 256;    // rows per MoE block call (the tensor-core chunk size)
 static constexpr int SEL_CAP = 4096;    // rows of router selections kept for inspection
 static constexpr int EXP_LEN_H = 256 * 40 + 2, SILU_LEN_H = 32 * 256 + 2;
@@ -170,9 +169,8 @@ struct exb_model {
   int32_t *p_xs = nullptr, *p_qs = nullptr, *p_next = nullptr;
   void* p_dig = nullptr;
   // persistent decode-step kernel (step.cu): per-layer descriptors and accumulators
-  bool step_on = false;
   bool tc_on = true;                    // multi-row chunks on the tensor-core GEMM
-  int fuse_in = 3;                      // GEMVs build their int16 input rows: 1 = qrow prologue (o, down),
+  int fuse_in = 1;                      // GEMVs build their int16 input rows: 1 = qrow prologue (o, down),
                                         // 2 = also the norm (q|k|v, gate|up, head), 3 = the norm from the
                                         // row statistics the residual producers publish, 0 = separate kernels
   bool attn_fused = true;               // decode: RoPE + cache write inside the attention kernel
@@ -181,10 +179,6 @@ struct exb_model {
   uint8_t* dq = nullptr;                // digit planes of the decode rows (2 x TC_DECODE_ROWS x KMAX)
   int64_t* tc_tot = nullptr;            // split-K partial sums (TC_DECODE_ROWS x NMAX)
   unsigned int* tc_tickets = nullptr;   // split-K last-CTA counters (NMAX / 128)
-  int pf_bytes = 64 * 1024;
-  StepLayer* step_layers = nullptr;
-  int64_t* s_att = nullptr; long long* s_gmax = nullptr; unsigned long long* s_gsum = nullptr;
-  unsigned long long* s_amax_h = nullptr; int16_t* s_hq = nullptr; unsigned int* s_bar = nullptr;
 };
 
 // ------------------------------------------------------------------------------------------ helpers
@@ -377,13 +371,6 @@ static void plan_runtime(exb_model* m) {
   m->dq = ralloc<uint8_t>(m, (size_t)2 * TC_DECODE_ROWS * m->KMAX);
   m->tc_tot = ralloc<int64_t>(m, (size_t)TC_DECODE_ROWS * m->NMAX);
   m->tc_tickets = ralloc<unsigned int>(m, m->NMAX / 128 + 1);
-  m->step_layers = ralloc<StepLayer>(m, c.NL);
-  m->s_att = ralloc<int64_t>(m, (size_t)c.NL * STEP_ROWS * c.H * c.hd);
-  m->s_gmax = ralloc<long long>(m, (size_t)c.NL * STEP_ROWS * c.H);
-  m->s_gsum = ralloc<unsigned long long>(m, (size_t)c.NL * STEP_ROWS * c.H);
-  m->s_amax_h = ralloc<unsigned long long>(m, (size_t)c.NL * STEP_ROWS);
-  m->s_hq = ralloc<int16_t>(m, (size_t)STEP_ROWS * c.I);
-  m->s_bar = ralloc<unsigned int>(m, 2);
 }
 
 // ------------------------------------------------------------------------------------------ step
@@ -449,36 +436,6 @@ static MoeArgs moe_args(exb_model* m, int i, int R, const int16_t* xq, int ldq, 
 }
 static int g_hist_row0 = -1;                             // selection-history row of the step being enqueued
 
-// Arguments of the persistent step kernel, when it can run this step: group-128 model, R <= 2
-// rows, no trace or Freivalds capture (those stay on the per-kernel path), int8 embedding rows.
-static bool step_args(exb_model* m, int R, const int32_t* ids, const int32_t* seq, const int32_t* pos,
-                      bool want_logits, StepArgs& a) {
-  const exb_config& c = m->c;
-  if (!m->step_on || !m->group || m->trace_on || m->fr_on || m->emb_q16 || R < 1 || R > STEP_ROWS || m->tp > 1 ||
-      m->samp_active)
-    return false;
-  a.layers = m->step_layers; a.NL = c.NL; a.R = R; a.D = c.D; a.H = c.H; a.KV = c.KV; a.hd = c.hd; a.I = c.I;
-  a.V = c.V; a.Nqkv = m->Nqkv; a.Smax = c.max_seq; a.Tmax = c.rope_len; a.max_batch = c.max_batch;
-  a.emb = m->emb; a.emb_shift = c.emb_shift; a.gf = m->gf; a.head = m->head;
-  a.ids = ids; a.seq = seq; a.pos = pos;
-  a.exp_t = m->exp_t; a.silu_t = m->silu_t; a.cos_t = m->cos_t; a.sin_t = m->sin_t;
-  a.inv = (int64_t)std::nearbyint(65536.0 / std::sqrt((double)c.hd));
-  a.kc = m->kc; a.ks = m->ks; a.vc = m->vc; a.kv_layer_elems = m->kv_layer_elems;
-  a.ks_layer_elems = (size_t)c.max_batch * c.KV * c.max_seq;
-  a.x = m->x; a.qkv = m->qkv; a.hb = m->hb; a.hq = m->s_hq;
-  a.att = m->s_att; a.gmax = m->s_gmax; a.gsum = m->s_gsum; a.amax_h = m->s_amax_h;
-  a.logits = want_logits ? m->logits : nullptr;
-  a.head_part = m->head_part; a.head_ticket = m->head_ticket; a.next_tok = m->next_tok;
-  a.bar = m->s_bar; a.err = m->err; a.pf_bytes = m->pf_bytes; a.KMAX = m->KMAX;
-  // the attention split depends on the grid, the grid on the shared memory the split needs
-  a.att_split = 1; a.att_chunk_max = 1;
-  const int g0 = step_grid(a, nullptr);
-  if (g0 <= 0 || g0 > m->head_grid) return false;
-  a.att_split = std::max(1, std::min(32, g0 / (R * c.KV)));
-  a.att_chunk_max = (c.max_seq + a.att_split - 1) / a.att_split;
-  return step_grid(a, nullptr) == g0;
-}
-
 static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const int32_t* seq, const int32_t* pos,
                                 bool want_logits, cudaStream_t st) {
   const exb_config& c = m->c;
@@ -501,17 +458,9 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       g_prof->push_back(ev);                                      \
     }                                                             \
   } while (0)
-  if (!g_prof) {
-    StepArgs sa;
-    if (step_args(m, R, ids, seq, pos, want_logits, sa)) {
-      RUN(cudaMemsetAsync(m->s_bar, 0, 2 * sizeof(unsigned int), st));
-      RUN(launch_step(sa, st));
-      return cudaSuccess;
-    }
-  }
   if (m->fr_on) RUN(cudaMemsetAsync(m->fr_acc, 0, sizeof(unsigned long long) * m->n_lin * RMAX * 4, st));
   // norm from published row statistics (fuse level 3): dense single-GPU models without capture
-  const bool fzs = m->fuse_in >= 3 && !m->fr_on && !cm && !tp && !c.n_experts && !m->emb_q16;
+  const bool fzs = m->fuse_in >= 3 && !m->fr_on && !cm && !tp && !c.n_experts && !m->emb_q16 && !tcd;
   if (m->emb_q16) RUN(launch_embed64(m->emb_q16, ids, R, c.D, m->x, st, false));   // general Q16 rows
   else RUN(launch_embed(m->emb, c.emb_shift, ids, R, c.D, m->x, st, false,          // int8 rows << shift
                         fzs ? m->nstat_a : nullptr));
@@ -1426,16 +1375,8 @@ int exb_model_finalize(exb_model* m) {
     if (L.fused->Mc && !L.fused->nodrop && !moe_lin(L.name))
       FAIL(EXB_EINVAL, "per-channel linear " + L.name + " may trigger the overflow drop rule; the fused decode path "
                        "requires bitlen(K*32767*127) + bitlen(max M) <= 62");
-  std::vector<StepLayer> sl(c.NL);
-  for (int i = 0; i < c.NL; ++i) {
-    sl[i].qkv = m->L[i].qkv; sl[i].o = m->L[i].o; sl[i].gu = m->L[i].gu; sl[i].down = m->L[i].down;
-    sl[i].g1 = m->L[i].g1; sl[i].g2 = m->L[i].g2;
-  }
-  CK(cudaMemcpy(m->step_layers, sl.data(), sizeof(StepLayer) * c.NL, cudaMemcpyHostToDevice));
-  if (const char* v = getenv("EXB_STEP")) m->step_on = atoi(v) != 0;
   if (const char* v = getenv("EXB_FUSE")) m->fuse_in = atoi(v);
   if (const char* v = getenv("EXB_TCD")) m->tc_decode = atoi(v) != 0;
-  if (const char* v = getenv("EXB_PF_KB")) m->pf_bytes = std::max(0, atoi(v)) * 1024;
   m->finalized = true;
   return EXB_OK;
 }
@@ -2217,50 +2158,18 @@ int exb_freivalds_status(exb_model* m, int64_t* checks, int64_t* failures) {
 int exb_set_option(exb_model* m, const char* name, int64_t value) {
   if (!m || !name) FAIL(EXB_EINVAL, "null argument");
   const std::string n(name);
-  if (n == "step") m->step_on = value != 0;
-  else if (n == "tc") m->tc_on = value != 0;
+  if (n == "tc") m->tc_on = value != 0;
   else if (n == "fuse") m->fuse_in = (int)value;
   else if (n == "tpar") m->tpar = value != 0;
+
   else if (n == "attn") m->attn_fused = value != 0;
   else if (n == "pattn") m->attn_prefill = value != 0;
   else if (n == "tcd") m->tc_decode = value != 0;
-  else if (n == "pf_kb") {
-    if (value < 0 || value > 1024) FAIL(EXB_EINVAL, "pf_kb: 0..1024");
-    m->pf_bytes = (int)value * 1024;
-  } else FAIL(EXB_EINVAL, "unknown option " + n);
+  else FAIL(EXB_EINVAL, "unknown option " + n);
   CK(cudaStreamSynchronize(m->st));
   for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
   m->graphs.clear();
   return EXB_OK;
-}
-
-int exb_profile_persistent(exb_model* m, int B, uint64_t* host, int64_t n, int* nbar, int* grid) {
-  if (!m || !m->finalized || B < 1 || B > STEP_ROWS || !host || !nbar || !grid)
-    FAIL(EXB_EINVAL, "exb_profile_persistent: bad arguments");
-  for (int b = 0; b < B; ++b)
-    if (m->seq_len[b] >= m->c.max_seq) FAIL(EXB_EINVAL, "exb_profile_persistent: sequence full");
-  std::vector<int32_t> h(3 * RMAX, 0);
-  for (int b = 0; b < B; ++b) { h[RMAX + b] = b; h[2 * RMAX + b] = m->seq_len[b]; }
-  CK(cudaMemcpyAsync(m->row_ids, h.data(), sizeof(int32_t) * 3 * RMAX, cudaMemcpyHostToDevice, m->st));
-  StepArgs sa;
-  if (!step_args(m, B, m->row_ids, m->row_seq, m->row_pos, false, sa))
-    FAIL(EXB_EINVAL, "exb_profile_persistent: the persistent kernel does not take this model/step");
-  const int g = step_grid(sa, nullptr);
-  const int nb = 1 + 8 * m->c.NL;
-  if (n < (int64_t)3 * nb * g) FAIL(EXB_EINVAL, "exb_profile_persistent: buffer too small");
-  unsigned long long* d = nullptr;
-  CK(cudaMalloc(&d, sizeof(unsigned long long) * 3 * nb * g));
-  CK(cudaMemsetAsync(d, 0, sizeof(unsigned long long) * 3 * nb * g, m->st));
-  sa.prof = d;
-  CK(cudaMemsetAsync(m->s_bar, 0, 2 * sizeof(unsigned int), m->st));
-  cudaError_t e = launch_step(sa, m->st);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(host, d, sizeof(unsigned long long) * 3 * nb * g, cudaMemcpyDeviceToHost, m->st);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(m->st);
-  cudaFree(d);
-  if (e != cudaSuccess) FAIL(EXB_ECUDA, std::string("exb_profile_persistent: ") + cudaGetErrorString(e));
-  *nbar = nb;
-  *grid = g;
-  return check_device_errors(m);   // the step wrote position seq_len (not advanced): harmless
 }
 
 int exb_moe_selections(exb_model* m, int layer, int32_t* host, int64_t n) {

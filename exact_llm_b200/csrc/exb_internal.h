@@ -329,50 +329,5 @@ cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32
                            int64_t* raw, int64_t* raw2, int ldr, const int32_t* silu_t, int* err, cudaStream_t st,
                            const TcDecode* dec = nullptr);
 
-// ---------------------------------------------------------------- persistent decode step
-// One layer's linears and norm gains, as the persistent step kernel reads them (device array).
-struct StepLayer {
-  LinW qkv, o, gu, down;
-  const int64_t* g1 = nullptr;
-  const int64_t* g2 = nullptr;
-};
-
-// Everything one decode step of R rows touches.  Accumulators that are summed with atomics are
-// per layer (att, gmax, gsum, amax_h), so no phase has to clear a buffer another CTA may still
-// read; the kernel clears them all in its first phase.
-struct StepArgs {
-  const StepLayer* layers = nullptr;
-  int NL = 0, R = 1, D = 0, H = 0, KV = 0, hd = 0, I = 0, V = 0, Nqkv = 0, Smax = 0, Tmax = 0, max_batch = 0;
-  const int8_t* emb = nullptr; int emb_shift = 0;
-  const int64_t* gf = nullptr;
-  LinW head;
-  const int32_t* ids = nullptr; const int32_t* seq = nullptr; const int32_t* pos = nullptr;   // (R) rows
-  const int32_t* exp_t = nullptr; const int32_t* silu_t = nullptr;
-  const int32_t* cos_t = nullptr; const int32_t* sin_t = nullptr;
-  int64_t inv = 0;                                 // round(2^16 / sqrt(hd))
-  int16_t* kc = nullptr; int8_t* ks = nullptr; int32_t* vc = nullptr;   // layer 0; layer l at + l * stride
-  size_t kv_layer_elems = 0, ks_layer_elems = 0;
-  int64_t* x = nullptr;                            // (R, D) residual rows
-  int64_t* qkv = nullptr;                          // (R, Nqkv)
-  int64_t* hb = nullptr;                           // (R, I) SwiGLU output
-  int16_t* hq = nullptr;                           // (R, I) qrow(hb)
-  int64_t* att = nullptr;                          // (NL, R, H*hd) sum_t p_t v_t (before the final shr)
-  long long* gmax = nullptr;                       // (NL, R, H) score max
-  unsigned long long* gsum = nullptr;              // (NL, R, H) sum of e
-  unsigned long long* amax_h = nullptr;            // (NL, R) max |h|
-  int64_t* logits = nullptr;                       // (R, V) or nullptr
-  unsigned long long* head_part = nullptr; unsigned int* head_ticket = nullptr;
-  int32_t* next_tok = nullptr;
-  unsigned int* bar = nullptr;                     // [0] barrier arrivals, [1] abort flag (zeroed per launch)
-  int* err = nullptr;
-  int att_split = 1;                               // CTAs per (row, KV head) in the attention phases
-  int att_chunk_max = 1;                           // key positions per attention CTA, upper bound
-  int pf_bytes = 0;                                // per-CTA L2 prefetch of upcoming weight slices (bytes)
-  int KMAX = 0;
-  unsigned long long* prof = nullptr;             // profiling: (2 * barriers, grid) arrive/release times
-};
-// grid and dynamic shared memory of the step kernel for these arguments (0 grid: not supported)
-int step_grid(const StepArgs& a, size_t* smem);
-cudaError_t launch_step(const StepArgs& a, cudaStream_t st);
 
 }  // namespace exb

@@ -269,8 +269,8 @@ class ExactModel:
         return buf
 
     def set_option(self, name, value):
-        """Engine option (results never change): "step" (persistent decode kernel on/off),
-        "pf_kb" (its per-warp L2 prefetch distance in KiB)."""
+        """Engine option (results never change; names and values in include/exactb200.h): "tc", "fuse",
+        "attn", "pattn", "tcd", "tpar"."""
         check(lib.exb_set_option(self.h, name.encode(), int(value)))
 
     # ------------------------------------------------------------------ trace + Freivalds

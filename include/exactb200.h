@@ -225,14 +225,11 @@ int exb_tp_unique_id(uint8_t* out128);
 int exb_model_create_tp(const exb_config* cfg, int rank, int size, const uint8_t* unique_id, exb_model** out);
 
 /* Engine options (no counterpart in the reference; they change speed, never results):
- *   "step"    1: decode steps of <= 2 rows without trace/Freivalds capture run as one persistent
- *             kernel (grid barriers between phases); 0 (default): one kernel per operation
  *   "tc"      1 (default): forward calls of >= 16 rows run their linears on the tcgen05 tensor-core
  *             GEMM in chunks of 256 rows; 0: 4-row CUDA-core GEMV passes
- *   "pf_kb"   per-CTA L2 prefetch of the next weight slices where HBM would idle, KiB (default 64; 0 = off)
- *   "fuse"    decode GEMVs build their own int16 input rows: 1 the qrow of the o and down inputs;
+ *   "fuse"    decode GEMVs build their own int16 input rows: 1 (default) the qrow of the o and down inputs;
  *             2 also the RMSNorm of the q|k|v, gate|up and head inputs, each CTA computing it whole;
- *             3 (default) the qrow prologues and the RMSNorm finished in the q|k|v, gate|up and head
+ *             3 the qrow prologues and the RMSNorm finished in the q|k|v, gate|up and head
  *             prologues from the row statistics (max |x|, sum x^2) that the embedding and the o and
  *             down epilogues publish (no norm kernels; dense single-GPU models without commitment
  *             capture or Freivalds, else level 1); 0 separate kernels
@@ -267,13 +264,6 @@ int exb_bench_linear(exb_model* m, int layer, int which, int R, int reps, float*
  * launch overlap) with a CUDA event after every launch; ms_out[i] = duration of launch i.  The step
  * writes the KV cache at each sequence's current length without advancing it. */
 int exb_profile_step(exb_model* m, int B, float* ms_out, int max_n, int* n_out);
-
-/* Profiling the persistent decode-step kernel: one step for sequences 0..B-1 (B <= 2, not
- * advanced), with a global-timer stamp (ns) when each CTA arrives at and leaves each grid barrier:
- * host[(2k) * grid + c] = arrival of CTA c at barrier k, host[(2k + 1) * grid + c] = release,
- * host[(2 nbar + k) * grid + c] = end of the prologue of the GEMV phase after barrier k - 1 (0 if none).
- * Barriers: 0 after the embedding, then 8 per layer (q|k|v, attention x3, o, gate|up, qrow(h), down). */
-int exb_profile_persistent(exb_model* m, int B, uint64_t* host, int64_t n, int* nbar, int* grid);
 
 /* raw pointers for benchmarks / interop */
 void* exb_model_stream(exb_model* m);

@@ -61,9 +61,10 @@ def trace_mode(m, g, G, key, rank, world):
     parts["honest"] = fails == 0 and checks == world * len(g["prompt"]) * len(lins)
     c = m.c
     from oracle import synth
-    w = synth.gen_weight(g["seed"], synth.layer_stream(1, synth.LIN_STREAM["k"]), c["KV"] * c["hd"], c["D"])
+    li = c["NL"] - 1
+    w = synth.gen_weight(g["seed"], synth.layer_stream(li, synth.LIN_STREAM["k"]), c["KV"] * c["hd"], c["D"])
     w[3, 5] = np.int8(w[3, 5] + (1 if w[3, 5] < 127 else -1))
-    m.set_tensor("L1.k.w", w)                           # lands in the shard holding KV head 0
+    m.set_tensor(f"L{li}.k.w", w)                       # lands in the shard holding KV head 0
     m(g["prompt"])
     _, fails = m.freivalds_status()
     parts["tamper_caught"] = fails > 0
