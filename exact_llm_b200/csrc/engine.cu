@@ -170,6 +170,7 @@ struct exb_model {
   void* p_dig = nullptr;
   // persistent decode-step kernel (step.cu): per-layer descriptors and accumulators
   bool tc_on = true;                    // multi-row chunks on the tensor-core GEMM
+  bool tail_norm = false;               // decode: the o and down GEMVs finish the next norm in their last CTA
   int fuse_in = 1;                      // GEMVs build their int16 input rows: 1 = qrow prologue (o, down),
                                         // 2 = also the norm (q|k|v, gate|up, head), 3 = the norm from the
                                         // row statistics the residual producers publish, 0 = separate kernels
@@ -461,8 +462,14 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
   if (m->fr_on) RUN(cudaMemsetAsync(m->fr_acc, 0, sizeof(unsigned long long) * m->n_lin * RMAX * 4, st));
   // norm from published row statistics (fuse level 3): dense single-GPU models without capture
   const bool fzs = m->fuse_in >= 3 && !m->fr_on && !cm && !tp && !c.n_experts && !m->emb_q16 && !tcd;
-  if (m->emb_q16) RUN(launch_embed64(m->emb_q16, ids, R, c.D, m->x, st, false));   // general Q16 rows
-  else RUN(launch_embed(m->emb, c.emb_shift, ids, R, c.D, m->x, st, false,          // int8 rows << shift
+  // norms as the last-CTA tails of the o and down GEMVs, from the row statistics their CTAs publish
+  // (the embedding kernel norms layer 0's input): no norm kernels
+  const bool ftail = m->tail_norm && m->fuse_in == 1 && !m->fr_on && !cm && !tp && !c.n_experts && !tcd;
+  if (ftail)
+    RUN(launch_embed_norm(m->emb_q16 ? nullptr : m->emb, m->emb_q16, c.emb_shift, ids, R, c.D, m->L[0].g1, m->x,
+                          m->xq, m->KMAX, m->xs, st, false));
+  else if (m->emb_q16) RUN(launch_embed64(m->emb_q16, ids, R, c.D, m->x, st, false));   // general Q16 rows
+  else RUN(launch_embed(m->emb, c.emb_shift, ids, R, c.D, m->x, st, false,               // int8 rows << shift
                         fzs ? m->nstat_a : nullptr));
   const int Hd = c.H * c.hd;
   AttnArgs aa;
@@ -479,18 +486,21 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     if (tpc) return launch_tp_allreduce(m->tpc, src, dst, (int)n, myop, TpResid(), st);
     return tp_allreduce(m, src, dst, n, t, op, st);
   };
-  // SUM of a row-split linear's partial sums, then x += shr(tot, 28 - s) + b (and the trace copy)
-  auto ar_resid = [&](const int64_t* bias, int64_t* trace_dst) -> cudaError_t {
+  // SUM of a row-split linear's partial sums, then x += shr(tot, 28 - s) + b (and the trace copy);
+  // s = the shift of the linear's input row: from the all-reduced max when its GEMV built the row
+  // in its prologue (amax given), else the one the separate qrow kernel wrote to m->xs
+  auto ar_resid = [&](const int64_t* bias, int64_t* trace_dst, const unsigned long long* amax) -> cudaError_t {
     if (tpc) {
       TpResid rz;
-      rz.x = m->x; rz.ldx = c.D; rz.N = c.D; rz.xs = m->xs; rz.b = bias; rz.tot = trace_dst; rz.ldt = (int)m->trace_row;
+      rz.x = m->x; rz.ldx = c.D; rz.N = c.D; rz.xs = m->xs; rz.b = bias; rz.amax = amax;
+      rz.tot = trace_dst; rz.ldt = (int)m->trace_row;
       return launch_tp_allreduce(m->tpc, m->tp_tot, nullptr, R * c.D, 1, rz, st);
     }
     cudaError_t e2 = tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st);
     if (e2 == cudaSuccess && trace_dst)
       e2 = cudaMemcpy2DAsync(trace_dst, sizeof(int64_t) * m->trace_row, m->tp_tot, sizeof(int64_t) * c.D,
                              sizeof(int64_t) * c.D, R, cudaMemcpyDeviceToDevice, st);
-    if (e2 == cudaSuccess) e2 = launch_tp_resid(m->tp_tot, R, c.D, m->xs, bias, m->x, c.D, st);
+    if (e2 == cudaSuccess) e2 = launch_tp_resid(m->tp_tot, R, c.D, m->xs, bias, m->x, c.D, st, amax);
     return e2;
   };
   auto set_fr = [&](GemvArgs& g, std::initializer_list<int> lis, int nseg_start_override = -1) {
@@ -576,11 +586,11 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     // fused inputs: each GEMV CTA computes its int16 rows in its prologue (qrow with the
     // producer's published max at level 1, also the norm at level 2) while its first weight bytes
     // stream into L2
-    // o and down: qrow in the prologue (not under tensor parallelism: the residual update after the
-    // all-reduce requantises with the row shift the separate qrow kernel publishes in m->xs)
-    const bool fz = m->fuse_in >= 1 && !m->fr_on && !tp;
+    // o and down: qrow in the prologue from the producer's published (under tensor parallelism:
+    // all-reduced) row max; the residual update after the all-reduce derives the shift from it
+    const bool fz = m->fuse_in >= 1 && !m->fr_on;
     const bool fzn = m->fuse_in == 2 && !m->fr_on && !cm;  // q|k|v and gate|up: norm in the prologue
-    if (!fzn && !fzs)
+    if (!fzn && !fzs && !ftail)
       RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, nullptr,
                         cm ? m->cap + (size_t)i * c.D : nullptr, m->cap_row));
     {
@@ -589,7 +599,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       if (fzs) { g.xin = XIN_NORMST; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g1; g.nstat_in = m->nstat_a; }
       g.epi = EPI_STORE; g.out = m->qkv; g.ldo = m->Nqkv; g.raw = trace_ptr(Ld.li[0]);
       g.zero = m->amax_o; g.nzero = RMAX;
-      if (fzs) { g.zero2 = m->nstat_b; g.nzero2 = 2 * RMAX; }            // o accumulates norm2's statistics
+      if (fzs || ftail) { g.zero2 = m->nstat_b; g.nzero2 = 2 * RMAX; }   // o accumulates norm2's statistics
       set_fr(g, {Ld.li[0], Ld.li[1], Ld.li[2]});
       RUN(launch_gemv(g, st, pdl));
     }
@@ -609,13 +619,17 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       if (fz) { g.xin = XIN_QUANT; g.x64 = m->ao; g.ldx64 = Hd; g.amax_in = m->amax_o; }
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[3]);
       g.zero = m->amax_h; g.nzero = RMAX;
-      if (fzs) g.nstat_out = m->nstat_b;
+      if (fzs || ftail) g.nstat_out = m->nstat_b;
+      if (ftail) {   // norm2 in the last CTA: xq, s = qrow(irms(x, g2)) for the gate|up GEMV
+        g.tail = TAIL_NORM; g.ticket = m->ticket; g.tail_x = m->x; g.tail_ldx = c.D; g.tail_K = c.D;
+        g.tail_gain = Ld.g2; g.tail_nstat = m->nstat_b; g.tail_xq = m->xq; g.tail_ldq = m->KMAX; g.tail_xs = m->xs;
+      }
       if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own heads
       set_fr(g, {Ld.li[3]});
       RUN(launch_gemv(g, st, pdl));
     }
-    if (tp) RUN(ar_resid(Ld.o.b, trace_ptr(Ld.li[3])));   // the trace records o's full sum
-    if ((!fzn && !fzs) || c.n_experts) RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    if (tp) RUN(ar_resid(Ld.o.b, trace_ptr(Ld.li[3]), fz ? m->amax_o : nullptr));   // trace: o's full sum
+    if ((!fzn && !fzs && !ftail) || c.n_experts) RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     if (c.n_experts) {
       RUN(launch_moe(moe_args(m, i, R, m->xq, m->KMAX, m->xs, g_hist_row0), m->x, c.D, st));
       continue;
@@ -627,6 +641,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
         g.xin = XIN_NORMST; g.x64 = m->x; g.ldx64 = c.D; g.gain = Ld.g2; g.nstat_in = m->nstat_b;
         g.zero2 = m->nstat_a; g.nzero2 = 2 * RMAX;                       // down accumulates the next norm1's
       }
+      if (ftail) { g.zero2 = m->nstat_a; g.nzero2 = 2 * RMAX; }
       g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.amax_out = m->amax_h;
       g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]);
       set_fr(g, {Ld.li[4], Ld.li[5]});
@@ -638,15 +653,20 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       GemvArgs g; base(g, Ld.down);
       if (fz) { g.xin = XIN_QUANT; g.x64 = m->hb; g.ldx64 = c.I; g.amax_in = m->amax_h; }
       g.epi = EPI_RESID; g.out = m->x; g.ldo = c.D; g.raw = trace_ptr(Ld.li[6]);
-      if (fzs) g.nstat_out = m->nstat_a;
+      if (fzs || ftail) g.nstat_out = m->nstat_a;
+      if (ftail) {   // the next layer's norm1 (or the final norm) in the last CTA
+        g.tail = TAIL_NORM; g.ticket = m->ticket; g.tail_x = m->x; g.tail_ldx = c.D; g.tail_K = c.D;
+        g.tail_gain = i + 1 < c.NL ? m->L[i + 1].g1 : m->gf; g.tail_nstat = m->nstat_a;
+        g.tail_xq = m->xq; g.tail_ldq = m->KMAX; g.tail_xs = m->xs;
+      }
       if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own groups
       set_fr(g, {Ld.li[6]});
       RUN(launch_gemv(g, st, pdl));
     }
-    if (tp) RUN(ar_resid(Ld.down.b, trace_ptr(Ld.li[6])));
+    if (tp) RUN(ar_resid(Ld.down.b, trace_ptr(Ld.li[6]), fz ? m->amax_h : nullptr));
   }
   const bool fzh = m->fuse_in == 2 && !m->fr_on && !cm;
-  if (!fzh && !fzs)
+  if (!fzh && !fzs && !ftail)
     RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, nullptr,
                       cm ? m->cap + (size_t)c.NL * c.D : nullptr, m->cap_row));
   {
@@ -2161,6 +2181,7 @@ int exb_set_option(exb_model* m, const char* name, int64_t value) {
   if (n == "tc") m->tc_on = value != 0;
   else if (n == "fuse") m->fuse_in = (int)value;
   else if (n == "tpar") m->tpar = value != 0;
+  else if (n == "tail") m->tail_norm = value != 0;
 
   else if (n == "attn") m->attn_fused = value != 0;
   else if (n == "pattn") m->attn_prefill = value != 0;

@@ -107,6 +107,8 @@ struct GemvArgs {
   const int64_t* tail_x = nullptr; int tail_ldx = 0; int tail_K = 0;
   const int64_t* tail_gain = nullptr;
   const unsigned long long* tail_amax = nullptr;
+  const unsigned long long* tail_nstat = nullptr;   // TAIL_NORM: the row statistics (max |x|, sum x^2) the
+                                                    // kernel's CTAs published (nstat_out), when given
   int16_t* tail_xq = nullptr; int tail_ldq = 0; int32_t* tail_xs = nullptr;
   AttnArgs rope;
   LinW L;
@@ -152,6 +154,7 @@ struct TpComm {
 struct TpResid {                              // int64 SUM fused with the residual update
   int64_t* x = nullptr; int ldx = 0; int N = 0;
   const int32_t* xs = nullptr; const int64_t* b = nullptr;
+  const unsigned long long* amax = nullptr;   // when set, the row shift is qrow_shift(amax[r]) (not xs)
   int64_t* tot = nullptr; int ldt = 0;        // optional copy of the full sums (trace)
 };
 // op 0: uint64 max, 1: int64 sum (with rz.x: x[r, j] += shr(sum, 28 - xs[r]) + b[j]), 2: int32 min,
@@ -162,8 +165,9 @@ size_t tp_comm_bytes(int size, int nblk);
 
 // tensor parallel helpers (rowops.cu)
 // x[r, n] += shr(tot[r, n], 28 - xs[r]) (+ b[n]): the residual update after an all-reduced partial sum
+// (amax given: the shift of row r is qrow_shift(amax[r]), the max the consumer GEMV's qrow used)
 cudaError_t launch_tp_resid(const int64_t* tot, int R, int N, const int32_t* xs, const int64_t* b, int64_t* x, int ldx,
-                            cudaStream_t st);
+                            cudaStream_t st, const unsigned long long* amax = nullptr);
 // next[r] = v0 + idx[r] when val[r] equals the all-reduced maximum gmax[r], else INT32_MAX (min-reduced next)
 cudaError_t launch_tp_pick(const int64_t* val, const int64_t* gmax, int32_t* idx, int v0, int R, cudaStream_t st);
 

@@ -352,9 +352,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     if (a.tail == TAIL_ROPE) {
       rope_cache_rows<GEMV_THREADS>(a.rope);
     } else if (a.tail == TAIL_NORM) {
-      for (int r = 0; r < R; ++r)
-        row_norm_q_any<GEMV_THREADS>(a.tail_x + (size_t)r * a.tail_ldx, a.tail_gain, a.tail_K,
-                                 a.tail_xq + (size_t)r * a.tail_ldq, a.tail_xs + r, ys, rred);
+      for (int r = 0; r < R; ++r) {
+        bool done = false;
+        if (a.tail_nstat)     // the statistics every CTA published before the election
+          done = row_norm_q_stats<GEMV_THREADS>(a.tail_x + (size_t)r * a.tail_ldx, a.tail_gain, a.tail_K,
+                                                __ldcg(a.tail_nstat + 2 * r), __ldcg(a.tail_nstat + 2 * r + 1),
+                                                a.tail_xq + (size_t)r * a.tail_ldq, a.tail_xs + r, rred);
+        if (!done)
+          row_norm_q_any<GEMV_THREADS>(a.tail_x + (size_t)r * a.tail_ldx, a.tail_gain, a.tail_K,
+                                       a.tail_xq + (size_t)r * a.tail_ldq, a.tail_xs + r, ys, rred);
+      }
     } else {
       for (int r = 0; r < R; ++r) {
         const int s = qrow_shift(__ldcg(a.tail_amax + r));

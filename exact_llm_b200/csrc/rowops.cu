@@ -298,19 +298,21 @@ cudaError_t launch_head_rows(const int64_t* acc, int ld, int R, const LinW& L, c
 
 // ---------------------------------------------------------------- tensor parallel helpers
 __global__ void k_tp_resid(const int64_t* __restrict__ tot, int N, const int32_t* __restrict__ xs,
-                           const int64_t* __restrict__ b, int64_t* __restrict__ x, int ldx) {
+                           const int64_t* __restrict__ b, int64_t* __restrict__ x, int ldx,
+                           const unsigned long long* __restrict__ amax) {
   const int r = blockIdx.y;
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
-  int64_t y = shr64(tot[(size_t)r * N + n], 28 - xs[r]);
+  const int sh = amax ? qrow_shift(__ldcg(amax + r)) : xs[r];
+  int64_t y = shr64(tot[(size_t)r * N + n], 28 - sh);
   if (b) y = (int64_t)((uint64_t)y + (uint64_t)b[n]);
   int64_t* o = x + (size_t)r * ldx + n;
   *o = (int64_t)((uint64_t)*o + (uint64_t)y);
 }
 
 cudaError_t launch_tp_resid(const int64_t* tot, int R, int N, const int32_t* xs, const int64_t* b, int64_t* x, int ldx,
-                            cudaStream_t st) {
-  k_tp_resid<<<dim3((N + 255) / 256, R), 256, 0, st>>>(tot, N, xs, b, x, ldx);
+                            cudaStream_t st, const unsigned long long* amax) {
+  k_tp_resid<<<dim3((N + 255) / 256, R), 256, 0, st>>>(tot, N, xs, b, x, ldx, amax);
   return cudaGetLastError();
 }
 

@@ -66,7 +66,8 @@ __global__ void __launch_bounds__(TPC_THREADS) k_tp_allreduce(TpComm c, const vo
     unsigned long long* d = tpc_data(c, q, set, blk, c.rank);
     for (int i = i0 + tid; i < i1; i += TPC_THREADS) d[i - i0] = word(i);
   }
-  __threadfence_system();
+  // the CTA barrier orders every thread's stores before the signalling threads' system-scope fence
+  // and release store (one fence per peer flag, not one per thread)
   __syncthreads();
   if (tid < c.size && tid != c.rank) {
     __threadfence_system();
@@ -105,7 +106,8 @@ __global__ void __launch_bounds__(TPC_THREADS) k_tp_allreduce(TpComm c, const vo
     }
     if (rz.x) {
       const int r = i / rz.N, j = i - r * rz.N;
-      int64_t y = shr64((int64_t)v, 28 - rz.xs[r]);
+      const int sh = rz.amax ? qrow_shift(__ldcg(rz.amax + r)) : rz.xs[r];
+      int64_t y = shr64((int64_t)v, 28 - sh);
       if (rz.b) y = (int64_t)((uint64_t)y + (uint64_t)rz.b[j]);
       int64_t* o = rz.x + (size_t)r * rz.ldx + j;
       *o = (int64_t)((uint64_t)*o + (uint64_t)y);

@@ -233,6 +233,10 @@ int exb_model_create_tp(const exb_config* cfg, int rank, int size, const uint8_t
  *             prologues from the row statistics (max |x|, sum x^2) that the embedding and the o and
  *             down epilogues publish (no norm kernels; dense single-GPU models without commitment
  *             capture or Freivalds, else level 1); 0 separate kernels
+ *   "tail"    1: with fuse 1, the RMSNorm + qrow rows of the gate|up input and of the next layer's q|k|v
+ *             (or the head's) input are made by the last CTA of the o / down GEMV from the row
+ *             statistics (max |x|, sum x^2) their CTAs publish, and layer 0's by the embedding kernel:
+ *             no norm kernels in the decode step; 0 (default) separate norm kernels
  *   "attn"    1 (default): decode RoPE + K/V cache write inside the attention kernel; 0 separate
  *   "pattn"   1 (default): prefill chunks of one sequence run the query-tile attention kernel;
  *             0: the per-row kernel

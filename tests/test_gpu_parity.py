@@ -204,20 +204,22 @@ def test_synthetic_models_vs_reference(golden, cuda_ok, key):
 def test_fused_gemv_inputs_match_separate_kernels(cuda_ok, emb_shift):
     """GEMVs that build their int16 input rows in their prologue (qrow from the producer's published
     max; the norm computed whole by every CTA; the norm finished from the row statistics the
-    producers publish) give the logits and tokens of the separate row kernels.  emb_shift 20 makes
+    producers publish), and norms run as the last-CTA tails of the o and down GEMVs, give the
+    logits and tokens of the separate row kernels.  emb_shift 20 makes
     max |x| >= 2^24, where irms shifts the row and the statistics prologue takes the full routine."""
     from exact_llm_b200 import ExactModel, configs
     c = configs.arch("qwen2.5-7b", NL=2)
     m = ExactModel.synthetic(c, 55, max_batch=1, max_seq=64, emb_shift=emb_shift)
     prompt = np.random.default_rng(9).integers(0, c["V"], 7).astype(np.int32)
     out = {}
-    for fz in (3, 2, 1, 0):
+    for fz, tail in ((3, 0), (2, 0), (1, 1), (1, 0), (0, 0)):
         m.set_option("fuse", fz)
-        out[fz] = m.greedy(prompt, 6)
-    for fz in (3, 2, 1):
-        assert np.array_equal(out[fz][0], out[0][0]), fz
-        assert out[fz][2] == out[0][2], fz
-        assert all(np.array_equal(a, b) for a, b in zip(out[fz][1], out[0][1])), fz
+        m.set_option("tail", tail)
+        out[fz, tail] = m.greedy(prompt, 6)
+    for key in ((3, 0), (2, 0), (1, 1), (1, 0)):
+        assert np.array_equal(out[key][0], out[0, 0][0]), key
+        assert out[key][2] == out[0, 0][2], key
+        assert all(np.array_equal(a, b) for a, b in zip(out[key][1], out[0, 0][1])), key
 
 
 @pytest.mark.parametrize("B", [1, 3])

@@ -240,3 +240,30 @@ def test_weightless_verifier_matches_reference(golden):
         opened = eo.open_cell(trs[sc], NL, levels[sc], cell, lie=lie)
         ok, why = eo.verify_cell(om, keys, levels[sc][-1][0], T, cell, opened, ids)
         assert (ok, why) == (case["ok"], case["why"]), case
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("key", ["qwen2.5-7b-L2-p512", "qwen2.5-14b-L1-p4096"])
+def test_long_prompt_fixtures(golden, key):
+    """The oracle's KV-cache path (prefill, then one row per decode step) against the long-prompt
+    fixtures the reference recorded with forward_record + block_row: the selected prefill rows,
+    the tokens, every decode row and the layer-0 KV cache.  About 1 min (7B) / 15 min (14B)."""
+    g = golden["long"][key]
+    om = synth.build_model(dict(g["config"]), g["seed"])
+    cache = om.new_cache()
+    T = g["T"]
+    rows = g["rows"]
+    lg = om.forward(g["prompt"], cache)
+    if g["prefill_rows"] is not None:
+        assert [eo.h16(lg[r]) for r in rows] == g["prefill_rows"]
+    else:
+        assert eo.h16(lg) == g["prefill_all"]
+    nxt = int(lg[-1].argmax())
+    for s, tok in enumerate(g["tokens"]):
+        assert tok == nxt, s
+        row = om.forward([tok], cache)[0]
+        assert eo.h16(row) == g["step_rows"][s], s
+        nxt = int(row.argmax())
+    kq, sk, v = cache["layers"][0]
+    assert cache["n"] == g["S"] == T + len(g["tokens"])
+    assert [eo.h16(kq), eo.h16(sk), eo.h16(v)] == [g["kv"][0]["k"], g["kv"][0]["sk"], g["kv"][0]["v"]]
