@@ -34,13 +34,18 @@ constexpr int TC_A_BYTES = TC_BM * 128;                 // one group of 128 weig
 constexpr uint32_t TC_WAIT_LIMIT = 1u << 24;
 
 // Tile geometry for BN activation rows per tile (MMA N = 8, 64 or 128).  Every epilogue thread owns
-// one output row (TMEM lane) and CW activation columns; BN = 128 takes 8 epilogue warps.
+// one output row (TMEM lane) and CW activation columns; BN = 128 takes 16 epilogue warps (four per
+// TMEM lane quarter, 32 columns each), so each scheduler has four folding warps to hide the TMEM
+// load latency behind.
+#ifndef EXB_TC_EPI16
+#define EXB_TC_EPI16 1
+#endif
 template <int BN>
 struct TcGeo {
   static constexpr int B_BYTES = BN * 128;              // one group of BN activation rows, one digit
   static constexpr int STAGE_BYTES = TC_A_BYTES + 2 * B_BYTES;
-  static constexpr int EPI_WARPS = BN >= 64 ? 4 * (BN / 64) : 4;
-  static constexpr int CW = BN >= 64 ? 64 : BN;         // columns per epilogue thread
+  static constexpr int EPI_WARPS = (BN == 128 && EXB_TC_EPI16) ? 16 : BN >= 64 ? 4 * (BN / 64) : 4;
+  static constexpr int CW = BN * 4 / EPI_WARPS;         // columns per epilogue thread
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int TMEM_COLS = 4 * BN < 32 ? 32 : 4 * BN;   // 2 buffers x 2 digits x BN
   static constexpr int SMEM = TC_STAGES * STAGE_BYTES + 1024;   // + alignment slack
@@ -102,7 +107,24 @@ EXB_DEV void tmem_ld8(uint32_t taddr, int32_t* v) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = (int32_t)r[i];
 }
+// 16 consecutive 32-bit TMEM columns of this thread's lane
+EXB_DEV void tmem_ld16(uint32_t taddr, int32_t* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = (int32_t)r[i];
+}
 EXB_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// t + a * b with a 32 x 32 -> 64-bit product (one multiply-add; wraps modulo 2^64 like numpy)
+EXB_DEV int64_t mad_wide(int32_t a, int32_t b, int64_t t) {
+  int64_t d;
+  asm("mad.wide.s32 %0, %1, %2, %3;" : "=l"(d) : "r"(a), "r"(b), "l"(t));
+  return d;
+}
 
 // Shared-memory matrix descriptor: K-major operand in the 128-byte swizzled layout written by
 // TMA (rows of 128 bytes, 8-row core groups 1024 bytes apart), advanced by 32 bytes per K-step.
@@ -282,21 +304,27 @@ __global__ void __launch_bounds__(TcGeo<BN>::THREADS, 1)
       }
       tc_fence_after();
       const uint32_t t_lo = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * BN + hc * CW);
+      // TMEM columns per load: 16 where the registers allow (BN = 64), else 8 (the 16-warp epilogue
+      // of BN = 128 runs at 96 registers per thread and would spill)
+      constexpr int CH = (CW >= 16 && BN < 128) ? 16 : 8;
 #pragma unroll
-      for (int c = 0; c < CW / 8; ++c) {
-        int32_t lo[8], hi[8];
-        tmem_ld8(t_lo + c * 8, lo);
-        tmem_ld8(t_lo + BN + c * 8, hi);
+      for (int c = 0; c < CW / CH; ++c) {
+        int32_t lo[CH], hi[CH];
+        if constexpr (CH == 16) {
+          tmem_ld16(t_lo + c * CH, lo);
+          tmem_ld16(t_lo + BN + c * CH, hi);
+        } else {
+          tmem_ld8(t_lo + c * CH, lo);
+          tmem_ld8(t_lo + BN + c * CH, hi);
+        }
         tmem_wait_ld();
-        if (c == CW / 8 - 1) {
+        if (c == CW / CH - 1) {
           tc_fence_before();
           mbar_arrive(&acce[b]);        // buffer b may be overwritten by the next-but-one group
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int32_t accg = hi[e] * 256 + lo[e];        // exact group sum (|.| < 2^30)
-          tot[c * 8 + e] = (int64_t)((uint64_t)tot[c * 8 + e] + (uint64_t)((int64_t)accg * mv));
-        }
+        for (int e = 0; e < CH; ++e)    // exact group sum 256 hi + lo (|.| < 2^30), times the scale
+          tot[c * CH + e] = mad_wide(hi[e] * 256 + lo[e], mv, tot[c * CH + e]);
       }
     }
     pdl_launch_dependents();

@@ -212,14 +212,16 @@ def test_fused_gemv_inputs_match_separate_kernels(cuda_ok, emb_shift):
     m = ExactModel.synthetic(c, 55, max_batch=1, max_seq=64, emb_shift=emb_shift)
     prompt = np.random.default_rng(9).integers(0, c["V"], 7).astype(np.int32)
     out = {}
-    for fz, tail in ((3, 0), (2, 0), (1, 1), (1, 0), (0, 0)):
-        m.set_option("fuse", fz)
-        m.set_option("tail", tail)
-        out[fz, tail] = m.greedy(prompt, 6)
-    for key in ((3, 0), (2, 0), (1, 1), (1, 0)):
-        assert np.array_equal(out[key][0], out[0, 0][0]), key
-        assert out[key][2] == out[0, 0][2], key
-        assert all(np.array_equal(a, b) for a, b in zip(out[key][1], out[0, 0][1])), key
+    variants = ((3, 0), (2, 0), (1, 1), (1, 0), (0, 0))
+    for key in variants:            # fuse level, norm tails
+        for name, v in zip(("fuse", "tail"), key):
+            m.set_option(name, v)
+        out[key] = m.greedy(prompt, 6)
+    ref = out[0, 0]
+    for key in variants[:-1]:
+        assert np.array_equal(out[key][0], ref[0]), key
+        assert out[key][2] == ref[2], key
+        assert all(np.array_equal(a, b) for a, b in zip(out[key][1], ref[1])), key
 
 
 @pytest.mark.parametrize("B", [1, 3])
