@@ -149,6 +149,12 @@ struct exb_model {
   bool tpc_on = false, tpar = true;
   char* tpc_local = nullptr;
   unsigned long long* tpc_epoch = nullptr;
+  // fused exchanges (tpx.cuh) in the same mapped buffers, after the all-reduce area; "tpx" 0: the
+  // all-reduce kernels instead
+  TpX tpx;
+  bool tpx_opt = true;
+  unsigned long long* tpx_ep = nullptr;     // (4) exchange counters
+  unsigned int* tpx_tickets = nullptr;      // (2) last-CTA tickets: attention, GEMVs
   int64_t* tp_tot = nullptr;                // (RMAX, D) partial sums of o / down
   int64_t* tp_hval = nullptr;               // (RMAX) shard best logit
   int64_t* tp_hmax = nullptr;               // (RMAX) all-reduced best logit
@@ -482,8 +488,18 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
   auto trace_ptr = [&](int li) -> int64_t* { return m->trace_on ? m->trace + m->lins[li].trace_off : nullptr; };
   // tensor-parallel all-reduces: the one-shot peer-memory kernel, else NCCL (both inside the graph)
   const bool tpc = tp && m->tpc_on && m->tpar;
+  // fused exchanges: no all-reduce kernels in the layers (the producers write into the peers' memory,
+  // the consumers wait for their flags); the trace / Freivalds / commitment captures keep the
+  // all-reduce kernels, which also give them the full sums
+  const bool tpf = tpc && m->tpx_opt && m->fuse_in == 1 && m->attn_fused && !m->trace_on && !m->fr_on && !cm &&
+                   !c.n_experts;
+  // this rank's own partial-sum slot of a row-split linear (which 0: o, 1: down)
+  auto own_slot = [&](int which) {
+    return reinterpret_cast<int64_t*>(m->tpx.base[m->tp_rank]) + (size_t)2 * m->tp * TPX_ROWS +
+           ((size_t)which * m->tp + m->tp_rank) * TPX_ROWS * c.D;
+  };
   auto ar = [&](const void* src, void* dst, size_t n, ncclDataType_t t, ncclRedOp_t op, int myop) -> cudaError_t {
-    if (tpc) return launch_tp_allreduce(m->tpc, src, dst, (int)n, myop, TpResid(), st);
+    if (tpc) return launch_tp_allreduce(m->tpc, src, dst, (int)n, myop, TpResid(), st, pdl);
     return tp_allreduce(m, src, dst, n, t, op, st);
   };
   // SUM of a row-split linear's partial sums, then x += shr(tot, 28 - s) + b (and the trace copy);
@@ -494,7 +510,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       TpResid rz;
       rz.x = m->x; rz.ldx = c.D; rz.N = c.D; rz.xs = m->xs; rz.b = bias; rz.amax = amax;
       rz.tot = trace_dst; rz.ldt = (int)m->trace_row;
-      return launch_tp_allreduce(m->tpc, m->tp_tot, nullptr, R * c.D, 1, rz, st);
+      return launch_tp_allreduce(m->tpc, m->tp_tot, nullptr, R * c.D, 1, rz, st, pdl);
     }
     cudaError_t e2 = tp_allreduce(m, m->tp_tot, m->tp_tot, (size_t)R * c.D, ncclInt64, ncclSum, st);
     if (e2 == cudaSuccess && trace_dst)
@@ -530,6 +546,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
   //   quant         xq = qrow(h)
   //   down GEMV     x += down(h)
   aa.amax_out = m->amax_o;
+  if (tpf) { aa.tpx = m->tpx; aa.tpx_pub = true; aa.tpx_ticket = m->tpx_tickets; }
   for (int i = 0; i < c.NL; ++i) {
     LayerDev& Ld = m->L[i];
     const size_t kvoff = m->kv_layer_elems * i;
@@ -590,7 +607,10 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
     // all-reduced) row max; the residual update after the all-reduce derives the shift from it
     const bool fz = m->fuse_in >= 1 && !m->fr_on;
     const bool fzn = m->fuse_in == 2 && !m->fr_on && !cm;  // q|k|v and gate|up: norm in the prologue
-    if (!fzn && !fzs && !ftail)
+    if (tpf && i > 0)   // the previous layer's down exchange, residual update and this norm
+      RUN(launch_tpx_norm(m->tpx, TPX_SUM_D, m->L[i - 1].down.b, m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st,
+                          pdl));
+    else if (!fzn && !fzs && !ftail)
       RUN(launch_norm_q(m->x, c.D, Ld.g1, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, nullptr,
                         cm ? m->cap + (size_t)i * c.D : nullptr, m->cap_row));
     {
@@ -612,7 +632,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       RUN(launch_attn_decode(aa, st, pdl));
     }
     // tensor parallel: the qrow of o's input needs the max over every rank's heads
-    if (tp) RUN(ar(m->amax_o, m->amax_o, R, ncclUint64, ncclMax, 0));
+    if (tp && !tpf) RUN(ar(m->amax_o, m->amax_o, R, ncclUint64, ncclMax, 0));
     if (!fz) RUN(launch_quant_known(m->ao, Hd, R, Hd, m->amax_o, m->xq, m->KMAX, m->xs, st, pdl && !tp));
     {
       GemvArgs g; base(g, Ld.o);
@@ -625,11 +645,18 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
         g.tail_gain = Ld.g2; g.tail_nstat = m->nstat_b; g.tail_xq = m->xq; g.tail_ldq = m->KMAX; g.tail_xs = m->xs;
       }
       if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own heads
+      if (tpf) {
+        g.tpx = m->tpx; g.tpx_in = TPX_AMAX_O; g.tpx_out = TPX_SUM_O; g.tpx_ticket = m->tpx_tickets + 1;
+        g.raw = own_slot(0);
+      }
       set_fr(g, {Ld.li[3]});
       RUN(launch_gemv(g, st, pdl));
     }
-    if (tp) RUN(ar_resid(Ld.o.b, trace_ptr(Ld.li[3]), fz ? m->amax_o : nullptr));   // trace: o's full sum
-    if ((!fzn && !fzs && !ftail) || c.n_experts) RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    if (tp && !tpf) RUN(ar_resid(Ld.o.b, trace_ptr(Ld.li[3]), fz ? m->amax_o : nullptr));   // trace: o's full sum
+    if (tpf)
+      RUN(launch_tpx_norm(m->tpx, TPX_SUM_O, Ld.o.b, m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
+    else if ((!fzn && !fzs && !ftail) || c.n_experts)
+      RUN(launch_norm_q(m->x, c.D, Ld.g2, R, c.D, m->xq, m->KMAX, m->xs, st, pdl));
     if (c.n_experts) {
       RUN(launch_moe(moe_args(m, i, R, m->xq, m->KMAX, m->xs, g_hist_row0), m->x, c.D, st));
       continue;
@@ -644,10 +671,11 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       if (ftail) { g.zero2 = m->nstat_a; g.nzero2 = 2 * RMAX; }
       g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.amax_out = m->amax_h;
       g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]);
+      if (tpf) { g.tpx = m->tpx; g.tpx_out = TPX_AMAX_H; g.tpx_ticket = m->tpx_tickets + 1; }
       set_fr(g, {Ld.li[4], Ld.li[5]});
       RUN(launch_gemv(g, st, pdl));
     }
-    if (tp) RUN(ar(m->amax_h, m->amax_h, R, ncclUint64, ncclMax, 0));
+    if (tp && !tpf) RUN(ar(m->amax_h, m->amax_h, R, ncclUint64, ncclMax, 0));
     if (!fz) RUN(launch_quant_known(m->hb, c.I, R, c.I, m->amax_h, m->xq, m->KMAX, m->xs, st, pdl && !tp));
     {
       GemvArgs g; base(g, Ld.down);
@@ -660,13 +688,20 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
         g.tail_xq = m->xq; g.tail_ldq = m->KMAX; g.tail_xs = m->xs;
       }
       if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own groups
+      if (tpf) {
+        g.tpx = m->tpx; g.tpx_in = TPX_AMAX_H; g.tpx_out = TPX_SUM_D; g.tpx_ticket = m->tpx_tickets + 1;
+        g.raw = own_slot(1);
+      }
       set_fr(g, {Ld.li[6]});
       RUN(launch_gemv(g, st, pdl));
     }
-    if (tp) RUN(ar_resid(Ld.down.b, trace_ptr(Ld.li[6]), fz ? m->amax_h : nullptr));
+    if (tp && !tpf) RUN(ar_resid(Ld.down.b, trace_ptr(Ld.li[6]), fz ? m->amax_h : nullptr));
   }
   const bool fzh = m->fuse_in == 2 && !m->fr_on && !cm;
-  if (!fzh && !fzs && !ftail)
+  if (tpf)
+    RUN(launch_tpx_norm(m->tpx, TPX_SUM_D, m->L[c.NL - 1].down.b, m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st,
+                        pdl));
+  else if (!fzh && !fzs && !ftail)
     RUN(launch_norm_q(m->x, c.D, m->gf, R, c.D, m->xq, m->KMAX, m->xs, st, pdl, nullptr,
                       cm ? m->cap + (size_t)c.NL * c.D : nullptr, m->cap_row));
   {
@@ -960,11 +995,17 @@ static void tp_comm_setup(exb_model* m) {
   const int P = m->tp;
   if (P > TPC_MAX_RANKS) return;
   const int nblk = (RMAX * m->c.D + TPC_CH - 1) / TPC_CH;      // the largest call: R x D partial sums
-  const size_t bytes = tp_comm_bytes(P, nblk);
+  static_assert(RMAX <= TPX_ROWS, "exchange slots hold every row of a decode pass");
+  const size_t ar_bytes = tp_comm_bytes(P, nblk);
+  const size_t bytes = ar_bytes + tpx_bytes(P, m->c.D);
   bool ok = cudaMalloc(&m->tpc_local, bytes) == cudaSuccess &&
             cudaMalloc(&m->tpc_epoch, sizeof(unsigned long long) * nblk) == cudaSuccess &&
+            cudaMalloc(&m->tpx_ep, sizeof(unsigned long long) * 4) == cudaSuccess &&
+            cudaMalloc(&m->tpx_tickets, sizeof(unsigned int) * 2) == cudaSuccess &&
             cudaMemset(m->tpc_local, 0, bytes) == cudaSuccess &&
-            cudaMemset(m->tpc_epoch, 0, sizeof(unsigned long long) * nblk) == cudaSuccess;
+            cudaMemset(m->tpc_epoch, 0, sizeof(unsigned long long) * nblk) == cudaSuccess &&
+            cudaMemset(m->tpx_ep, 0, sizeof(unsigned long long) * 4) == cudaSuccess &&
+            cudaMemset(m->tpx_tickets, 0, sizeof(unsigned int) * 2) == cudaSuccess;
   cudaIpcMemHandle_t mine;
   if (ok) ok = cudaIpcGetMemHandle(&mine, m->tpc_local) == cudaSuccess;
   // every rank takes part in the exchange, also after a local failure (a zeroed handle marks it)
@@ -1008,6 +1049,9 @@ static void tp_comm_setup(exb_model* m) {
   m->tpc.base[m->tp_rank] = m->tpc_local;
   m->tpc.epoch = m->tpc_epoch; m->tpc.err = m->err;
   m->tpc_on = v == 1;
+  m->tpx.rank = m->tp_rank; m->tpx.size = P; m->tpx.D = m->c.D;
+  for (int q = 0; q < P; ++q) m->tpx.base[q] = m->tpc.base[q] ? m->tpc.base[q] + ar_bytes : nullptr;
+  m->tpx.ep = m->tpx_ep; m->tpx.err = m->err;
 }
 
 static int create_impl(const exb_config* cfg, int rank, int size, const uint8_t* uid, exb_model** out) {
@@ -1090,6 +1134,8 @@ void exb_model_destroy(exb_model* m) {
     if (q != m->tp_rank && m->tpc.base[q]) cudaIpcCloseMemHandle(m->tpc.base[q]);
   cudaFree(m->tpc_local);
   cudaFree(m->tpc_epoch);
+  cudaFree(m->tpx_ep);
+  cudaFree(m->tpx_tickets);
   for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
   if (m->st) cudaStreamSynchronize(m->st);
   cudaFree(m->warena);
@@ -1416,20 +1462,24 @@ int exb_seq_len(exb_model* m, int seq) {
 // (gemm_tc.cu) instead of the CUDA-core GEMV: the same kernels for norm, RoPE/cache, attention
 // and qrow, the same integer results.  Rows keep their order; rows of one sequence in one chunk
 // see each other through the KV cache (written before the attention launch).
-static constexpr int PCH = 256;            // rows per tensor-core chunk
+static constexpr int PCH = 512;            // rows per tensor-core chunk (layout of the host staging rows)
+
+// Rows per chunk: 512 (a 512-token prompt is one chunk, and the narrow linears q|k|v, o and down
+// get 4 activation tiles per weight tile instead of 2); MoE blocks take at most MOE_ROWS rows.
+static int chunk_rows(const exb_model* m) { return m->c.n_experts ? std::min(PCH, MOE_ROWS) : PCH; }
 
 static int prefill_alloc(exb_model* m) {
   if (m->pch) return EXB_OK;
   const exb_config& c = m->c;
-  const int P = PCH, Hd = c.H * c.hd;
+  const int P = chunk_rows(m), Hd = c.H * c.hd;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = (off + bytes + 255) & ~size_t(255); return o; };
-  const size_t o_rows = take(sizeof(int32_t) * 3 * P), o_x = take(8ull * P * c.D), o_qkv = take(8ull * P * m->Nqkv),
+  const size_t o_rows = take(sizeof(int32_t) * 3 * PCH), o_x = take(8ull * P * c.D), o_qkv = take(8ull * P * m->Nqkv),
                o_ao = take(8ull * P * Hd), o_hb = take(8ull * P * c.I), o_raw = take(8ull * P * c.V),
                o_xq = take(2ull * P * m->KMAX), o_qq = take(2ull * P * Hd), o_xs = take(4ull * P),
                o_qs = take(4ull * P * c.H), o_next = take(4ull * P), o_dig = take(gemm_tc_digit_bytes(P, m->KMAX));
   CK(cudaMalloc(&m->p_arena, off));
-  CK(cudaMallocHost(&m->p_hrows, sizeof(int32_t) * 3 * P));
+  CK(cudaMallocHost(&m->p_hrows, sizeof(int32_t) * 3 * PCH));
   char* b = m->p_arena;
   m->p_rows = (int32_t*)(b + o_rows); m->p_x = (int64_t*)(b + o_x); m->p_qkv = (int64_t*)(b + o_qkv);
   m->p_ao = (int64_t*)(b + o_ao); m->p_hb = (int64_t*)(b + o_hb); m->p_raw = (int64_t*)(b + o_raw);
@@ -1556,7 +1606,7 @@ int exb_forward(exb_model* m, int n, const int32_t* ids, const int32_t* seqs, in
     int rc = prefill_alloc(m);
     if (rc) return rc;
     while (n - r_tc >= TC_MIN_ROWS) {
-      const int R = std::min(PCH, n - r_tc);
+      const int R = std::min(chunk_rows(m), n - r_tc);
       for (int r = 0; r < R; ++r) {
         m->p_hrows[r] = ids[r_tc + r]; m->p_hrows[PCH + r] = seqs[r_tc + r]; m->p_hrows[2 * PCH + r] = pos[r_tc + r];
       }
@@ -1608,7 +1658,8 @@ static int ensure_gen(exb_model* m, int B, int steps) {
 static int generate_wide(exb_model* m, int B, const int32_t* ids_dev_or_null, const int32_t* ids_host, int steps,
                          int32_t* tokens_host, int64_t* logits_host, int32_t* tokens_dev) {
   const exb_config& c = m->c;
-  if (B > PCH || !prefill_tc_ok(m)) FAIL(EXB_EINVAL, "generate: B > 4 needs the tensor-core path and B <= 256");
+  if (B > chunk_rows(m) || !prefill_tc_ok(m))
+    FAIL(EXB_EINVAL, "generate: B > 4 needs the tensor-core path and B <= 512 (256 for MoE)");
   int rc = prefill_alloc(m);
   if (rc) return rc;
   std::vector<int32_t> cur(B), nxt(B), toks((size_t)B * steps);
@@ -2181,6 +2232,7 @@ int exb_set_option(exb_model* m, const char* name, int64_t value) {
   if (n == "tc") m->tc_on = value != 0;
   else if (n == "fuse") m->fuse_in = (int)value;
   else if (n == "tpar") m->tpar = value != 0;
+  else if (n == "tpx") m->tpx_opt = value != 0;
   else if (n == "tail") m->tail_norm = value != 0;
 
   else if (n == "attn") m->attn_fused = value != 0;

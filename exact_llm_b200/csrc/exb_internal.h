@@ -38,6 +38,26 @@ struct LinW {
 };
 
 // attention
+// Fused tensor-parallel exchanges of the decode step (tpx.cuh): the kernel that produces a value
+// writes it into every rank's exchange area (peer memory mapped with CUDA IPC) and raises its
+// flag there; the kernel that consumes it waits for every peer's flag and reduces locally.
+constexpr int TPX_MAX_RANKS = 8;
+constexpr int TPX_ROWS = 4;                   // activation rows per decode step (the GEMV pass)
+enum TpxType {
+  TPX_AMAX_O = 0,    // MAX of the attention output's row max (o's qrow shift)
+  TPX_SUM_O = 1,     // SUM of o's partial sums (row-split by heads)
+  TPX_AMAX_H = 2,    // MAX of the MLP activation's row max (down's qrow shift)
+  TPX_SUM_D = 3,     // SUM of down's partial sums (row-split by groups of I)
+};
+struct TpX {
+  int rank = 0, size = 1;
+  int D = 0;                                  // width of the partial-sum rows
+  char* base[TPX_MAX_RANKS] = {};             // every rank's exchange area, mapped into this process
+  unsigned long long* ep = nullptr;           // (4) this rank's exchange counters, one per type
+  int* err = nullptr;                         // device error word (wait timeout)
+};
+size_t tpx_bytes(int size, int D);
+
 struct AttnArgs {
   const int64_t* qkv = nullptr; int ldqkv = 0;  // (R, (H + 2KV) hd) projected q|k|v (before RoPE)
   const int32_t* row_seq = nullptr;             // (R) sequence slot of each row
@@ -58,6 +78,10 @@ struct AttnArgs {
   int16_t* xq_out = nullptr; int ldq = 0; int32_t* xs_out = nullptr;   // last CTA: qrow(out) rows
   int64_t* kr_out = nullptr; int64_t ldkr = 0;  // trace commitment: roped K | V rows (R, 2 KV hd)
   int* err = nullptr;
+  // tensor parallel: the last CTA publishes the final amax_out rows as exchange TPX_AMAX_O
+  TpX tpx;
+  bool tpx_pub = false;
+  unsigned int* tpx_ticket = nullptr;
 };
 enum Epi {
   EPI_STORE = 0,     // out[r, n] = requant(tot)
@@ -135,6 +159,13 @@ struct GemvArgs {
   int64_t* head_val = nullptr;                  // (R) best value next to next_tok (tensor parallel)
   int* err = nullptr;
   int grid = 0;
+  // tensor parallel (fused exchanges): tpx_in (XIN_QUANT) takes the row max over the ranks from
+  // exchange TPX_AMAX_O / TPX_AMAX_H; tpx_out publishes this kernel's result as exchange tpx_out:
+  // TPX_SUM_O / TPX_SUM_D (EPI_RAW: `raw` is this rank's own slot, the peers' slots are written
+  // from the epilogue) or TPX_AMAX_H (the final amax_out rows, from the last CTA)
+  TpX tpx;
+  int tpx_in = -1, tpx_out = -1;
+  unsigned int* tpx_ticket = nullptr;
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl);
@@ -160,7 +191,11 @@ struct TpResid {                              // int64 SUM fused with the residu
 // op 0: uint64 max, 1: int64 sum (with rz.x: x[r, j] += shr(sum, 28 - xs[r]) + b[j]), 2: int32 min,
 // 3: int64 max
 cudaError_t launch_tp_allreduce(const TpComm& c, const void* src, void* dst, int n, int op, const TpResid& rz,
-                                cudaStream_t st);
+                                cudaStream_t st, bool pdl = false);
+// Consumer of TPX_SUM_O / TPX_SUM_D fused with the next norm: x[r] += shr(sum over ranks, 28 - s) + b with
+// s = qrow_shift(max over ranks of TPX_AMAX_O / TPX_AMAX_H), then xq, xs = qrow(irms(x[r], g)).
+cudaError_t launch_tpx_norm(const TpX& x, int sum_type, const int64_t* bias, int64_t* xr, int ldx, const int64_t* g,
+                            int R, int D, int16_t* xq, int ldq, int32_t* xs, cudaStream_t st, bool pdl);
 size_t tp_comm_bytes(int size, int nblk);
 
 // tensor parallel helpers (rowops.cu)

@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "exb_internal.h"
 #include "rowdev.cuh"
+#include "tpx.cuh"
 #include "gemvdev.cuh"
 
 namespace exb {
@@ -140,9 +141,11 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     for (int r = 0; r < R; ++r)
       row_norm_q_any<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, xs + (size_t)r * K, &sh_s[r], ys, rred);
   } else {
-    // xq = clip(shr(x, s)) with s from the producer's published row max (exact_llm.py:41-46)
+    // xq = clip(shr(x, s)) with s from the producer's published row max (exact_llm.py:41-46); under
+    // tensor parallelism the max over every rank's rows, from the fused exchange
+    if (a.tpx_in >= 0) tpx_wait(a.tpx, a.tpx_in, R);
     for (int r = 0; r < R; ++r) {
-      const int s = qrow_shift(__ldcg(a.amax_in + r));
+      const int s = a.tpx_in >= 0 ? tpx_shift(a.tpx, a.tpx_in == TPX_AMAX_O ? 0 : 1, r) : qrow_shift(__ldcg(a.amax_in + r));
       row_quant_known<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, K, s, xs + (size_t)r * K);
       if (threadIdx.x == 0) sh_s[r] = s;
     }
@@ -343,6 +346,14 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
       }
       a.next_tok[r] = bn;
       if (a.head_val) a.head_val[r] = bv;                  // tensor parallel: the shard's best value
+    }
+  }
+  // ---- tensor parallel: the last CTA publishes this kernel's exchange (every CTA's peer stores
+  // are ordered before its ticket by the election's fence and barrier)
+  if (a.tpx_out >= 0) {
+    if (last_cta(a.tpx_ticket, gridDim.x)) {
+      if (a.tpx_out == TPX_AMAX_H) tpx_publish_max(a.tpx, TPX_AMAX_H, a.amax_out, R);
+      else tpx_signal(a.tpx, a.tpx_out);
     }
   }
   // ---- last CTA: build the next GEMV's int16 input rows from this kernel's complete output;

@@ -6,6 +6,7 @@
 #include "common.cuh"
 #include "exb_internal.h"
 #include "rowdev.cuh"
+#include "tpx.cuh"
 
 namespace exb {
 
@@ -178,6 +179,53 @@ cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, i
   }
   void* args[] = {(void*)&x, (void*)&ldx, (void*)&K, (void*)&xq, (void*)&ldq, (void*)&xs};
   return launch_simple((const void*)k_quant, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
+}
+
+// ---------------------------------------------------------------- tensor parallel: exchange + norm
+// Consumer of a row-split linear's fused exchange (TPX_SUM_O after o, TPX_SUM_D after down) and the
+// norm that follows it, one CTA per row: x[r, j] += shr(sum over ranks, 28 - s) + b[j]
+// (exact_llm.py:89-96 on the full accumulator), s = qrow_shift of the max over ranks of the linear's
+// input row max, then xq, s' = qrow(irms(x[r], g)) (exact_llm.py:100-106, 41-46).
+__global__ void __launch_bounds__(ROW_THREADS) k_tpx_norm(const TpX x, int sum_type, const int64_t* __restrict__ bias,
+                                                          int64_t* __restrict__ xr, int ldx,
+                                                          const int64_t* __restrict__ g, int D,
+                                                          int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs) {
+  extern __shared__ int64_t ys[];
+  __shared__ uint64_t red[33];
+  pdl_wait();
+  pdl_launch_dependents();
+  tpx_wait(x, sum_type, 1);
+  const int r = blockIdx.x;
+  const int which = sum_type == TPX_SUM_O ? 0 : 1;
+  const int sh = tpx_shift(x, which, r);
+  int64_t* row = xr + (size_t)r * ldx;
+  for (int j = threadIdx.x; j < D; j += ROW_THREADS) {
+    uint64_t tot = 0;
+    for (int q = 0; q < x.size; ++q) tot += (uint64_t)ld_cg(tpx_sum_slot(x, x.rank, which, q) + (size_t)r * x.D + j);
+    int64_t y = shr64((int64_t)tot, 28 - sh);
+    if (bias) y = (int64_t)((uint64_t)y + (uint64_t)bias[j]);
+    row[j] = (int64_t)((uint64_t)row[j] + (uint64_t)y);
+  }
+  __syncthreads();
+  row_norm_q_any<ROW_THREADS>(row, g, D, xq + (size_t)r * ldq, xs + r, ys, red);
+  tl_exit();
+}
+
+cudaError_t launch_tpx_norm(const TpX& x, int sum_type, const int64_t* bias, int64_t* xr, int ldx, const int64_t* g,
+                            int R, int D, int16_t* xq, int ldq, int32_t* xs, cudaStream_t st, bool pdl) {
+  if (R < 1 || R > TPX_ROWS || D != x.D || x.size < 2 || (sum_type != TPX_SUM_O && sum_type != TPX_SUM_D))
+    return cudaErrorInvalidValue;
+  const size_t smem = (size_t)D * 16;
+  static DevOnce attr_set;   // raised once to the full budget, never lowered
+  if (!attr_set.done()) {
+    cudaError_t e = cudaFuncSetAttribute(k_tpx_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set.set();
+  }
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  void* args[] = {(void*)&x, (void*)&sum_type, (void*)&bias, (void*)&xr, (void*)&ldx, (void*)&g,
+                  (void*)&D, (void*)&xq, (void*)&ldq, (void*)&xs};
+  return launch_simple((const void*)k_tpx_norm, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
 }
 
 // ---------------------------------------------------------------- qrow with a published row max

@@ -16,20 +16,12 @@
 // returns (the step's result is then invalid and the host reports the error).
 #include "common.cuh"
 #include "exb_internal.h"
+#include "tpx.cuh"
 
 namespace exb {
 
 constexpr int TPC_THREADS = 256;
 constexpr unsigned TPC_SPIN_LIMIT = 1u << 21;      // flag polls (back-off to 1 us): about 2 s
-
-EXB_DEV unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-EXB_DEV void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
 
 // buffer layout of one rank: data[2][nblk][size][CH] (8-byte words), then flags[2][nblk][size]
 EXB_DEV unsigned long long* tpc_data(const TpComm& c, int q, int set, int blk, int slot) {
@@ -49,6 +41,10 @@ __global__ void __launch_bounds__(TPC_THREADS) k_tp_allreduce(TpComm c, const vo
   const int i0 = blk * TPC_CH, i1 = min(n, i0 + TPC_CH);
   __shared__ unsigned long long e_s;
   __shared__ int timeout_s;
+  // launched as a programmatic dependent: wait for the producer of `src`, then let the next kernel
+  // launch at once (its CTAs stage their weights while this exchange crosses NVLink)
+  pdl_wait();
+  pdl_launch_dependents();
   if (tid == 0) {
     e_s = c.epoch[blk] + 1;
     timeout_s = 0;
@@ -91,6 +87,7 @@ __global__ void __launch_bounds__(TPC_THREADS) k_tp_allreduce(TpComm c, const vo
       set_err(c.err, ERR_WAIT_TIMEOUT);
       c.epoch[blk] = e;
     }
+    tl_exit();
     return;
   }
   // 3. reduce the slots locally
@@ -120,19 +117,32 @@ __global__ void __launch_bounds__(TPC_THREADS) k_tp_allreduce(TpComm c, const vo
   }
   __syncthreads();
   if (tid == 0) c.epoch[blk] = e;
+  tl_exit();
 }
 
 cudaError_t launch_tp_allreduce(const TpComm& c, const void* src, void* dst, int n, int op, const TpResid& rz,
-                                cudaStream_t st) {
+                                cudaStream_t st, bool pdl) {
   if (n <= 0) return cudaSuccess;
   const int nb = (n + TPC_CH - 1) / TPC_CH;
   if (nb > c.nblk || c.size > TPC_MAX_RANKS) return cudaErrorInvalidValue;
-  k_tp_allreduce<<<nb, TPC_THREADS, 0, st>>>(c, src, dst, n, op, rz);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nb);
+  cfg.blockDim = dim3(TPC_THREADS);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_tp_allreduce, c, src, dst, n, op, rz);
 }
 
 size_t tp_comm_bytes(int size, int nblk) {
   return ((size_t)2 * nblk * size * TPC_CH + (size_t)2 * nblk * size) * 8;
+}
+
+size_t tpx_bytes(int size, int D) {
+  return ((size_t)2 * size * TPX_ROWS + (size_t)2 * size * TPX_ROWS * D + (size_t)4 * size) * 8;
 }
 
 }  // namespace exb

@@ -270,7 +270,7 @@ class ExactModel:
 
     def set_option(self, name, value):
         """Engine option (results never change; names and values in include/exactb200.h): "tc", "fuse",
-        "attn", "pattn", "tcd", "tpar"."""
+        "attn", "pattn", "tcd", "tpar", "tpx", "tail"."""
         check(lib.exb_set_option(self.h, name.encode(), int(value)))
 
     # ------------------------------------------------------------------ trace + Freivalds

@@ -226,7 +226,7 @@ int exb_model_create_tp(const exb_config* cfg, int rank, int size, const uint8_t
 
 /* Engine options (no counterpart in the reference; they change speed, never results):
  *   "tc"      1 (default): forward calls of >= 16 rows run their linears on the tcgen05 tensor-core
- *             GEMM in chunks of 256 rows; 0: 4-row CUDA-core GEMV passes
+ *             GEMM in chunks of 512 rows (256 for MoE); 0: 4-row CUDA-core GEMV passes
  *   "fuse"    decode GEMVs build their own int16 input rows: 1 (default) the qrow of the o and down inputs;
  *             2 also the RMSNorm of the q|k|v, gate|up and head inputs, each CTA computing it whole;
  *             3 the qrow prologues and the RMSNorm finished in the q|k|v, gate|up and head
@@ -244,6 +244,11 @@ int exb_model_create_tp(const exb_config* cfg, int rank, int size, const uint8_t
  *   "tpar"    tensor parallel: 1 (default) the step's all-reduces run as one-shot kernels over the peers'
  *             memory (CUDA IPC mappings over NVLink, bounded flag waits), NCCL where the peers could
  *             not be mapped; 0 NCCL
+ *   "tpx"     tensor parallel with "tpar" 1: 1 (default) the decode step's exchanges are fused into the
+ *             kernels around them: the attention, gate|up, o and down kernels write their row maxima /
+ *             partial sums into every peer's memory and raise a flag; the o / down GEMV prologues and
+ *             the norm kernels wait for the peers' flags (bounded) and reduce; 0: all-reduce kernels
+ *             (trace, Freivalds and commitment captures always use those)
  * Cached step graphs are dropped. */
 int exb_set_option(exb_model* m, const char* name, int64_t value);
 

@@ -99,6 +99,17 @@ def test_tp2_matches_reference_fixture(golden, key):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["allreduce", "nccl"])
+def test_tp2_exchange_variants_match_reference_fixture(golden, mode):
+    """The same decode with the step's exchanges as separate one-shot all-reduce kernels, or NCCL,
+    instead of fused into the producing and consuming kernels: the same bits."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    _run_tp("qwen2.5-7b-L2", mode, 29735)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("key", ["qwen2.5-7b-L2", "qwen2.5-14b-L1"])
 def test_tp2_trace_and_freivalds_match_reference(golden, key):
     """BASELINE config 5's capture under tensor parallelism: global trace hashes, step digests and

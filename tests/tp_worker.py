@@ -87,6 +87,12 @@ def main():
     from exact_llm_b200._lib import check, lib
     check(lib.exb_model_generate(m.h, int(g["seed"])))
     m.finalize()
+    # the decode step's exchanges: fused into the producing / consuming kernels (default), the
+    # one-shot all-reduce kernels ("allreduce"), or NCCL ("nccl")
+    if mode == "allreduce":
+        m.set_option("tpx", 0)
+    elif mode == "nccl":
+        m.set_option("tpar", 0)
     if mode == "trace":
         parts = trace_mode(m, g, G, key, rank, world)
         ok = all(v for k, v in parts.items() if not k.endswith("_bad"))
