@@ -553,8 +553,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
   }
   cluster.sync();                                        // peers' shared memory stays alive until read
   // tensor parallel: the last CTA publishes the complete row maxima to every rank (TPX_AMAX_O)
-  if (a.tpx_pub && last_cta(a.tpx_ticket, gridDim.x * gridDim.y * gridDim.z))
-    tpx_publish_max(a.tpx, TPX_AMAX_O, a.amax_out, a.R);
+  if (a.tpx && last_cta(a.tpx_ticket, gridDim.x * gridDim.y * gridDim.z))
+    tpx_publish_max(*a.tpx, TPX_AMAX_O, a.amax_out, a.R);
   tl_exit();
 }
 

@@ -152,6 +152,7 @@ struct exb_model {
   // fused exchanges (tpx.cuh) in the same mapped buffers, after the all-reduce area; "tpx" 0: the
   // all-reduce kernels instead
   TpX tpx;
+  TpX* tpx_dev = nullptr;                   // the same description in device memory (kernel arguments)
   bool tpx_opt = true;
   unsigned long long* tpx_ep = nullptr;     // (4) exchange counters
   unsigned int* tpx_tickets = nullptr;      // (2) last-CTA tickets: attention, GEMVs
@@ -546,7 +547,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
   //   quant         xq = qrow(h)
   //   down GEMV     x += down(h)
   aa.amax_out = m->amax_o;
-  if (tpf) { aa.tpx = m->tpx; aa.tpx_pub = true; aa.tpx_ticket = m->tpx_tickets; }
+  if (tpf) { aa.tpx = m->tpx_dev; aa.tpx_ticket = m->tpx_tickets; }
   for (int i = 0; i < c.NL; ++i) {
     LayerDev& Ld = m->L[i];
     const size_t kvoff = m->kv_layer_elems * i;
@@ -646,7 +647,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       }
       if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own heads
       if (tpf) {
-        g.tpx = m->tpx; g.tpx_in = TPX_AMAX_O; g.tpx_out = TPX_SUM_O; g.tpx_ticket = m->tpx_tickets + 1;
+        g.tpx = m->tpx_dev; g.tpx_in = TPX_AMAX_O; g.tpx_out = TPX_SUM_O; g.tpx_ticket = m->tpx_tickets + 1;
         g.raw = own_slot(0);
       }
       set_fr(g, {Ld.li[3]});
@@ -671,7 +672,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       if (ftail) { g.zero2 = m->nstat_a; g.nzero2 = 2 * RMAX; }
       g.epi = EPI_SWIGLU; g.out = m->hb; g.ldo = c.I; g.silu_t = m->silu_t; g.amax_out = m->amax_h;
       g.raw = trace_ptr(Ld.li[4]); g.raw2 = trace_ptr(Ld.li[5]);
-      if (tpf) { g.tpx = m->tpx; g.tpx_out = TPX_AMAX_H; g.tpx_ticket = m->tpx_tickets + 1; }
+      if (tpf) { g.tpx = m->tpx_dev; g.tpx_out = TPX_AMAX_H; g.tpx_ticket = m->tpx_tickets + 1; }
       set_fr(g, {Ld.li[4], Ld.li[5]});
       RUN(launch_gemv(g, st, pdl));
     }
@@ -689,7 +690,7 @@ static cudaError_t enqueue_step(exb_model* m, int R, const int32_t* ids, const i
       }
       if (tp) { g.epi = EPI_RAW; g.out = nullptr; g.raw = m->tp_tot; g.ldr = c.D; }   // partial sums over own groups
       if (tpf) {
-        g.tpx = m->tpx; g.tpx_in = TPX_AMAX_H; g.tpx_out = TPX_SUM_D; g.tpx_ticket = m->tpx_tickets + 1;
+        g.tpx = m->tpx_dev; g.tpx_in = TPX_AMAX_H; g.tpx_out = TPX_SUM_D; g.tpx_ticket = m->tpx_tickets + 1;
         g.raw = own_slot(1);
       }
       set_fr(g, {Ld.li[6]});
@@ -1002,6 +1003,7 @@ static void tp_comm_setup(exb_model* m) {
             cudaMalloc(&m->tpc_epoch, sizeof(unsigned long long) * nblk) == cudaSuccess &&
             cudaMalloc(&m->tpx_ep, sizeof(unsigned long long) * 4) == cudaSuccess &&
             cudaMalloc(&m->tpx_tickets, sizeof(unsigned int) * 2) == cudaSuccess &&
+            cudaMalloc(&m->tpx_dev, sizeof(TpX)) == cudaSuccess &&
             cudaMemset(m->tpc_local, 0, bytes) == cudaSuccess &&
             cudaMemset(m->tpc_epoch, 0, sizeof(unsigned long long) * nblk) == cudaSuccess &&
             cudaMemset(m->tpx_ep, 0, sizeof(unsigned long long) * 4) == cudaSuccess &&
@@ -1052,6 +1054,7 @@ static void tp_comm_setup(exb_model* m) {
   m->tpx.rank = m->tp_rank; m->tpx.size = P; m->tpx.D = m->c.D;
   for (int q = 0; q < P; ++q) m->tpx.base[q] = m->tpc.base[q] ? m->tpc.base[q] + ar_bytes : nullptr;
   m->tpx.ep = m->tpx_ep; m->tpx.err = m->err;
+  if (m->tpc_on) m->tpc_on = cudaMemcpy(m->tpx_dev, &m->tpx, sizeof(TpX), cudaMemcpyHostToDevice) == cudaSuccess;
 }
 
 static int create_impl(const exb_config* cfg, int rank, int size, const uint8_t* uid, exb_model** out) {
@@ -1136,6 +1139,7 @@ void exb_model_destroy(exb_model* m) {
   cudaFree(m->tpc_epoch);
   cudaFree(m->tpx_ep);
   cudaFree(m->tpx_tickets);
+  cudaFree(m->tpx_dev);
   for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
   if (m->st) cudaStreamSynchronize(m->st);
   cudaFree(m->warena);

@@ -79,8 +79,8 @@ struct AttnArgs {
   int64_t* kr_out = nullptr; int64_t ldkr = 0;  // trace commitment: roped K | V rows (R, 2 KV hd)
   int* err = nullptr;
   // tensor parallel: the last CTA publishes the final amax_out rows as exchange TPX_AMAX_O
-  TpX tpx;
-  bool tpx_pub = false;
+  // (the exchange description lives in device memory: the argument block stays small)
+  const TpX* tpx = nullptr;
   unsigned int* tpx_ticket = nullptr;
 };
 enum Epi {
@@ -163,7 +163,7 @@ struct GemvArgs {
   // exchange TPX_AMAX_O / TPX_AMAX_H; tpx_out publishes this kernel's result as exchange tpx_out:
   // TPX_SUM_O / TPX_SUM_D (EPI_RAW: `raw` is this rank's own slot, the peers' slots are written
   // from the epilogue) or TPX_AMAX_H (the final amax_out rows, from the last CTA)
-  TpX tpx;
+  const TpX* tpx = nullptr;                     // device memory
   int tpx_in = -1, tpx_out = -1;
   unsigned int* tpx_ticket = nullptr;
 };

@@ -35,7 +35,9 @@ constexpr int PREFETCH_BYTES = 64 * 1024;       // per-CTA L2 prefetch before th
 constexpr int DYN_SMEM_MAX = 200 * 1024;        // dynamic shared memory budget of one CTA
 constexpr int PRE_SMEM_MAX = 104 * 1024;        // with the pre-wait area: two CTAs still fit one SM
 
-template <int R, int RPU, bool GROUP, int RB>
+// TPX: the tensor-parallel exchange code (a separate instantiation, so that the single-GPU kernels
+// carry none of it)
+template <int R, int RPU, bool GROUP, int RB, bool TPX>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   int16_t* xs = reinterpret_cast<int16_t*>(smem_raw);                    // R x K int16 (tail: D int64 x 2)
@@ -143,9 +145,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   } else {
     // xq = clip(shr(x, s)) with s from the producer's published row max (exact_llm.py:41-46); under
     // tensor parallelism the max over every rank's rows, from the fused exchange
-    if (a.tpx_in >= 0) tpx_wait(a.tpx, a.tpx_in, R);
+    if (TPX && a.tpx_in >= 0) tpx_wait(*a.tpx, a.tpx_in, R);
     for (int r = 0; r < R; ++r) {
-      const int s = a.tpx_in >= 0 ? tpx_shift(a.tpx, a.tpx_in == TPX_AMAX_O ? 0 : 1, r) : qrow_shift(__ldcg(a.amax_in + r));
+      const int s = TPX && a.tpx_in >= 0 ? tpx_shift(*a.tpx, a.tpx_in == TPX_AMAX_O ? 0 : 1, r)
+                                         : qrow_shift(__ldcg(a.amax_in + r));
       row_quant_known<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, K, s, xs + (size_t)r * K);
       if (threadIdx.x == 0) sh_s[r] = s;
     }
@@ -230,6 +233,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
 #pragma unroll
           for (int q = 0; q < RPU; ++q) t2[q] = acc[0][r * RPU + q];
           unit_epilogue<RPU>(a, ug, r, t2, sh[r], est[warp][b][r]);
+          if constexpr (TPX && RPU == 1)
+            if (a.tpx_out == TPX_SUM_O || a.tpx_out == TPX_SUM_D) {   // partial sums into every peer's slot
+              const TpX& x = *a.tpx;
+              const int which = a.tpx_out == TPX_SUM_O ? 0 : 1;
+              for (int q = 0; q < x.size; ++q)
+                if (q != x.rank) tpx_sum_slot(x, q, which, x.rank)[(size_t)r * x.D + ug] = t2[0];
+            }
         }
       }
     }
@@ -350,10 +360,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   }
   // ---- tensor parallel: the last CTA publishes this kernel's exchange (every CTA's peer stores
   // are ordered before its ticket by the election's fence and barrier)
-  if (a.tpx_out >= 0) {
+  if (TPX && a.tpx_out >= 0) {
     if (last_cta(a.tpx_ticket, gridDim.x)) {
-      if (a.tpx_out == TPX_AMAX_H) tpx_publish_max(a.tpx, TPX_AMAX_H, a.amax_out, R);
-      else tpx_signal(a.tpx, a.tpx_out);
+      if (a.tpx_out == TPX_AMAX_H) tpx_publish_max(*a.tpx, TPX_AMAX_H, a.amax_out, R);
+      else tpx_signal(*a.tpx, a.tpx_out);
     }
   }
   // ---- last CTA: build the next GEMV's int16 input rows from this kernel's complete output;
@@ -385,9 +395,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   tl_exit();
 }
 
-template <int R, int RPU, bool GROUP, int RB>
+template <int R, int RPU, bool GROUP, int RB, bool TPX = false>
 static cudaError_t launch_t(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
-  auto kern = k_gemv<R, RPU, GROUP, RB>;
+  auto kern = k_gemv<R, RPU, GROUP, RB, TPX>;
   // The max-dynamic-shared-memory attribute is raised once to the full budget and never lowered:
   // launches of one instantiation use different sizes, and a captured graph node (or a profiler
   // replay) must never find a smaller maximum than it was launched with.
@@ -412,6 +422,18 @@ static cudaError_t launch_t(const GemvArgs& a, size_t smem, cudaStream_t st, boo
 
 template <int RPU, bool GROUP>
 static cudaError_t launch_r(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
+  if constexpr (GROUP) {
+    if (a.tpx) switch (a.R) {      // tensor-parallel decode (group-128 models only)
+        case 1: return a.rb == 1 ? launch_t<1, RPU, GROUP, 1, true>(a, smem, st, pdl)
+                                 : launch_t<1, RPU, GROUP, 4, true>(a, smem, st, pdl);
+        case 2: return launch_t<2, RPU, GROUP, 2, true>(a, smem, st, pdl);
+        case 3: return launch_t<3, RPU, GROUP, 1, true>(a, smem, st, pdl);
+        case 4: return launch_t<4, RPU, GROUP, 1, true>(a, smem, st, pdl);
+        default: return cudaErrorInvalidValue;
+      }
+  } else {
+    if (a.tpx) return cudaErrorInvalidValue;
+  }
   switch (a.R) {
     case 1: return a.rb == 1 ? launch_t<1, RPU, GROUP, 1>(a, smem, st, pdl) : launch_t<1, RPU, GROUP, 4>(a, smem, st, pdl);
     case 2: return launch_t<2, RPU, GROUP, 2>(a, smem, st, pdl);

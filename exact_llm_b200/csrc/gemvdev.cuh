@@ -4,7 +4,6 @@
 #pragma once
 #include "common.cuh"
 #include "exb_internal.h"
-#include "tpx.cuh"
 
 namespace exb {
 
@@ -81,11 +80,6 @@ EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, 
   const int n = ug;
   const int64_t t = t2[0];
   if (a.raw) a.raw[(size_t)r * a.ldr + n] = t;
-  if (a.tpx_out == TPX_SUM_O || a.tpx_out == TPX_SUM_D) {    // row-split partial sums into every peer's slot
-    const int which = a.tpx_out == TPX_SUM_O ? 0 : 1;
-    for (int q = 0; q < a.tpx.size; ++q)
-      if (q != a.tpx.rank) tpx_sum_slot(a.tpx, q, which, a.tpx.rank)[(size_t)r * a.tpx.D + n] = t;
-  }
   if (a.fr_nseg) {
     const int sg = (a.fr_nseg > 2 && n >= a.fr_seg_start[2]) ? 2 : (a.fr_nseg > 1 && n >= a.fr_seg_start[1]) ? 1 : 0;
     const int ncols = (sg + 1 < a.fr_nseg ? a.fr_seg_start[sg + 1] : a.L.N) - a.fr_seg_start[sg];

@@ -12,6 +12,12 @@ namespace exb {
 
 constexpr int ROW_THREADS = 512;
 
+// The norm gains are weights: pull them into L2 before the dependent-launch wait, so the norm reads
+// them from L2 instead of HBM once the row is ready.
+EXB_DEV void prefetch_gains(const int64_t* g, int D) {
+  if (threadIdx.x == 0 && !((uintptr_t)g & 15) && !(D & 1)) prefetch_l2_bulk(g, (uint32_t)D * 8);
+}
+
 static cudaError_t launch_simple(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
                                  void** args) {
   cudaLaunchConfig_t cfg = {};
@@ -131,6 +137,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restric
                                                         int64_t ldcap) {
   extern __shared__ int64_t ys[];
   __shared__ uint64_t red[33];
+  prefetch_gains(g, D);
   pdl_wait();
   pdl_launch_dependents();
   const int r = blockIdx.x;
@@ -192,6 +199,8 @@ __global__ void __launch_bounds__(ROW_THREADS) k_tpx_norm(const TpX x, int sum_t
                                                           int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs) {
   extern __shared__ int64_t ys[];
   __shared__ uint64_t red[33];
+  prefetch_gains(g, D);
+  if (bias && threadIdx.x == 32 && !((uintptr_t)bias & 15)) prefetch_l2_bulk(bias, (uint32_t)D * 8);
   pdl_wait();
   pdl_launch_dependents();
   tpx_wait(x, sum_type, 1);
