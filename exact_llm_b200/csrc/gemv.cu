@@ -35,10 +35,13 @@ constexpr int PREFETCH_BYTES = 64 * 1024;       // per-CTA L2 prefetch before th
 constexpr int DYN_SMEM_MAX = 200 * 1024;        // dynamic shared memory budget of one CTA
 constexpr int PRE_SMEM_MAX = 104 * 1024;        // with the pre-wait area: two CTAs still fit one SM
 
-// TPX: the tensor-parallel exchange code (a separate instantiation, so that the single-GPU kernels
-// carry none of it)
-template <int R, int RPU, bool GROUP, int RB, bool TPX>
+// MODE: 0 lean (the decode hot path: int16 or qrow inputs, store / residual / SwiGLU / raw
+// epilogues, no Freivalds, tails, norm prologues, row statistics or argmax), 1 full, 2 full with the
+// tensor-parallel exchanges.  Each is its own instantiation: code a launch never runs still costs
+// registers (spills) in the streaming loop.
+template <int R, int RPU, bool GROUP, int RB, int MODE>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
+  constexpr bool LEAN = MODE == 0, TPX = MODE == 2;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   int16_t* xs = reinterpret_cast<int16_t*>(smem_raw);                    // R x K int16 (tail: D int64 x 2)
   __shared__ unsigned long long red[NCW][R][6];
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
       reinterpret_cast<int4*>(xs + (size_t)r * K)[c] = reinterpret_cast<const int4*>(a.xq + (size_t)r * a.ldx)[c];
     }
     if (threadIdx.x < R) sh_s[threadIdx.x] = a.xs[threadIdx.x];
-  } else if (a.xin == XIN_NORMST) {
+  } else if (!LEAN && a.xin == XIN_NORMST) {
     // the norm from the row statistics the producers published (max |x|, sum x^2); the full
     // routine when irms would shift the row (max |x| >= 2^24) or the row is too long for registers
     int64_t* ys = reinterpret_cast<int64_t*>(smem_raw + (((size_t)R * K * 2 + 127) & ~(size_t)127));
@@ -137,7 +140,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
                                           rred))
         row_norm_q_any<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, xs + (size_t)r * K, &sh_s[r], ys, rred);
     }
-  } else if (a.xin == XIN_NORM) {
+  } else if (!LEAN && a.xin == XIN_NORM) {
     // xq, s = qrow(irms(x, g)) for every row, computed by this CTA (exact_llm.py:100-106, 41-46)
     int64_t* ys = reinterpret_cast<int64_t*>(smem_raw + (((size_t)R * K * 2 + 127) & ~(size_t)127));
     for (int r = 0; r < R; ++r)
@@ -232,7 +235,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
           int64_t t2[RPU];
 #pragma unroll
           for (int q = 0; q < RPU; ++q) t2[q] = acc[0][r * RPU + q];
-          unit_epilogue<RPU>(a, ug, r, t2, sh[r], est[warp][b][r]);
+          unit_epilogue<RPU, LEAN>(a, ug, r, t2, sh[r], est[warp][b][r]);
           if constexpr (TPX && RPU == 1)
             if (a.tpx_out == TPX_SUM_O || a.tpx_out == TPX_SUM_D) {   // partial sums into every peer's slot
               const TpX& x = *a.tpx;
@@ -281,7 +284,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     }
   }
   // ---- residual row statistics for the next norm (max |x_new|, sum x_new^2), one atomic each per CTA
-  if (a.nstat_out) {
+  if (!LEAN && a.nstat_out) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const uint64_t v = block_max_u64<GEMV_THREADS>(lane == 0 ? omax[r] : 0, rred);
@@ -291,7 +294,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     }
   }
   // ---- Freivalds: per-CTA partial sums -> one atomic per (segment, row, prime)
-  if (a.fr_nseg) {
+  if (!LEAN && a.fr_nseg) {
     if (lane == 0) {
 #pragma unroll
       for (int r = 0; r < R; ++r)
@@ -324,7 +327,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     }
   }
   // ---- greedy argmax (first index on ties, exact_llm.py:267): last-CTA reduction
-  if (a.epi == EPI_HEAD && a.next_tok) {
+  if (!LEAN && a.epi == EPI_HEAD && a.next_tok) {
     if (lane == 0) {
 #pragma unroll
       for (int r = 0; r < R; ++r) {
@@ -368,7 +371,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   }
   // ---- last CTA: build the next GEMV's int16 input rows from this kernel's complete output;
   // the activation staging area and the ring (contiguous) are free now and stage the row.
-  if (a.tail != TAIL_NONE && last_cta(a.ticket, gridDim.x)) {
+  if (!LEAN && a.tail != TAIL_NONE && last_cta(a.ticket, gridDim.x)) {
     int64_t* ys = reinterpret_cast<int64_t*>(smem_raw);
     if (a.tail == TAIL_ROPE) {
       rope_cache_rows<GEMV_THREADS>(a.rope);
@@ -395,9 +398,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   tl_exit();
 }
 
-template <int R, int RPU, bool GROUP, int RB, bool TPX = false>
+template <int R, int RPU, bool GROUP, int RB, int MODE>
 static cudaError_t launch_t(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
-  auto kern = k_gemv<R, RPU, GROUP, RB, TPX>;
+  auto kern = k_gemv<R, RPU, GROUP, RB, MODE>;
   // The max-dynamic-shared-memory attribute is raised once to the full budget and never lowered:
   // launches of one instantiation use different sizes, and a captured graph node (or a profiler
   // replay) must never find a smaller maximum than it was launched with.
@@ -420,27 +423,27 @@ static cudaError_t launch_t(const GemvArgs& a, size_t smem, cudaStream_t st, boo
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <int RPU, bool GROUP>
-static cudaError_t launch_r(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
-  if constexpr (GROUP) {
-    if (a.tpx) switch (a.R) {      // tensor-parallel decode (group-128 models only)
-        case 1: return a.rb == 1 ? launch_t<1, RPU, GROUP, 1, true>(a, smem, st, pdl)
-                                 : launch_t<1, RPU, GROUP, 4, true>(a, smem, st, pdl);
-        case 2: return launch_t<2, RPU, GROUP, 2, true>(a, smem, st, pdl);
-        case 3: return launch_t<3, RPU, GROUP, 1, true>(a, smem, st, pdl);
-        case 4: return launch_t<4, RPU, GROUP, 1, true>(a, smem, st, pdl);
-        default: return cudaErrorInvalidValue;
-      }
-  } else {
-    if (a.tpx) return cudaErrorInvalidValue;
-  }
+template <int RPU, bool GROUP, int MODE>
+static cudaError_t launch_m(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
   switch (a.R) {
-    case 1: return a.rb == 1 ? launch_t<1, RPU, GROUP, 1>(a, smem, st, pdl) : launch_t<1, RPU, GROUP, 4>(a, smem, st, pdl);
-    case 2: return launch_t<2, RPU, GROUP, 2>(a, smem, st, pdl);
-    case 3: return launch_t<3, RPU, GROUP, 1>(a, smem, st, pdl);
-    case 4: return launch_t<4, RPU, GROUP, 1>(a, smem, st, pdl);
+    case 1: return a.rb == 1 ? launch_t<1, RPU, GROUP, 1, MODE>(a, smem, st, pdl)
+                             : launch_t<1, RPU, GROUP, 4, MODE>(a, smem, st, pdl);
+    case 2: return launch_t<2, RPU, GROUP, 2, MODE>(a, smem, st, pdl);
+    case 3: return launch_t<3, RPU, GROUP, 1, MODE>(a, smem, st, pdl);
+    case 4: return launch_t<4, RPU, GROUP, 1, MODE>(a, smem, st, pdl);
     default: return cudaErrorInvalidValue;
   }
+}
+
+template <int RPU, bool GROUP>
+static cudaError_t launch_r(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
+  if (a.tpx) {                       // tensor-parallel decode (group-128 models only)
+    if constexpr (GROUP) return launch_m<RPU, GROUP, 2>(a, smem, st, pdl);
+    return cudaErrorInvalidValue;
+  }
+  const bool lean = a.fr_nseg == 0 && a.tail == TAIL_NONE && (a.xin == XIN_Q16 || a.xin == XIN_QUANT) &&
+                    !a.nstat_out && a.epi != EPI_HEAD;
+  return lean ? launch_m<RPU, GROUP, 0>(a, smem, st, pdl) : launch_m<RPU, GROUP, 1>(a, smem, st, pdl);
 }
 
 static int sm_count() {

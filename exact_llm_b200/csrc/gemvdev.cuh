@@ -51,7 +51,8 @@ struct EpiState {
 };
 
 // Epilogue of one output unit (1 column, or a gate/up pair) for activation row r.
-template <int RPU>
+// LEAN: no Freivalds, residual statistics or argmax (the launch guarantees none is asked for)
+template <int RPU, bool LEAN = false>
 EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, int sh, EpiState& E) {
   uint64_t& omax = E.omax;
   unsigned long long (&frl)[3][2] = E.frl;
@@ -67,7 +68,7 @@ EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, 
     omax = ah > omax ? ah : omax;
     if (a.raw) a.raw[(size_t)r * a.ldr + ug] = t2[0];
     if (a.raw2) a.raw2[(size_t)r * a.ldr + ug] = t2[RPU - 1];
-    if (a.fr_nseg) {
+    if (!LEAN && a.fr_nseg) {
       const int I = a.L.N / 2;
 #pragma unroll
       for (int pi = 0; pi < 2; ++pi) {
@@ -80,7 +81,7 @@ EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, 
   const int n = ug;
   const int64_t t = t2[0];
   if (a.raw) a.raw[(size_t)r * a.ldr + n] = t;
-  if (a.fr_nseg) {
+  if (!LEAN && a.fr_nseg) {
     const int sg = (a.fr_nseg > 2 && n >= a.fr_seg_start[2]) ? 2 : (a.fr_nseg > 1 && n >= a.fr_seg_start[1]) ? 1 : 0;
     const int ncols = (sg + 1 < a.fr_nseg ? a.fr_seg_start[sg + 1] : a.L.N) - a.fr_seg_start[sg];
     const int loc = n - a.fr_seg_start[sg];
@@ -97,7 +98,7 @@ EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, 
     int64_t* o = a.out + (size_t)r * a.ldo + n;
     const int64_t xn = (int64_t)((uint64_t)__ldcg(reinterpret_cast<const long long*>(o)) + (uint64_t)y);
     *o = xn;
-    if (a.nstat_out) {
+    if (!LEAN && a.nstat_out) {
       const uint64_t ax = uabs64(xn);
       omax = ax > omax ? ax : omax;
       E.ssq += (uint64_t)xn * (uint64_t)xn;          // wraps harmlessly when max |x_new| >= 2^24 (unused then)
@@ -105,7 +106,7 @@ EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, 
   } else if (a.out) {
     a.out[(size_t)r * a.ldo + n] = y;
   }
-  if (a.epi == EPI_HEAD && (y > best_v || (y == best_v && n < best_n))) {
+  if (!LEAN && a.epi == EPI_HEAD && (y > best_v || (y == best_v && n < best_n))) {
     best_v = y;
     best_n = n;
   }
