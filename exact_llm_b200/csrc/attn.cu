@@ -284,7 +284,9 @@ EXB_DEV int64_t rope_value(const int64_t* row, int d, int half, int64_t c, int64
   return shr64((int64_t)((uint64_t)x * (uint64_t)c + (uint64_t)rot * (uint64_t)s), 16);
 }
 
-template <int HD, int TILE>
+// EXTRA: the trace-commitment capture of the roped K / V rows and the tensor-parallel publication of
+// the row maxima (a separate instantiation keeps them out of the single-GPU decode kernel)
+template <int HD, int TILE, bool EXTRA>
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn_rope(const AttnArgs a, int SCmax) {
   extern __shared__ __align__(16) unsigned char sm[];
   constexpr int TP = HD + 8;                 // padded K row (int16): 8 consecutive rows hit distinct banks
@@ -393,7 +395,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
               const int16_t v16 = qrow_value(kv[q], sh);
               ktile[(size_t)t * TP + d] = v16;
               if (writer) a.kc[cidx * HD + d] = v16;
-              if (writer && a.kr_out) a.kr_out[(size_t)r2 * a.ldkr + (size_t)j * HD + d] = kv[q];   // roped K
+              if (EXTRA && writer && a.kr_out) a.kr_out[(size_t)r2 * a.ldkr + (size_t)j * HD + d] = kv[q];   // roped K
             }
           }
           if (lane == 0) {
@@ -411,7 +413,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
               if (v > INT32_MAX || v < INT32_MIN) set_err(a.err, ERR_V_RANGE);
               vtile[(size_t)t * HD + d] = (int32_t)v;
               if (writer) a.vc[cidx * HD + d] = (int32_t)v;
-              if (writer && a.kr_out) a.kr_out[(size_t)r2 * a.ldkr + (size_t)(a.KV + j) * HD + d] = v;
+              if (EXTRA && writer && a.kr_out) a.kr_out[(size_t)r2 * a.ldkr + (size_t)(a.KV + j) * HD + d] = v;
             }
           }
         }
@@ -553,7 +555,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(ATT_THREADS) k_attn
   }
   cluster.sync();                                        // peers' shared memory stays alive until read
   // tensor parallel: the last CTA publishes the complete row maxima to every rank (TPX_AMAX_O)
-  if (a.tpx && last_cta(a.tpx_ticket, gridDim.x * gridDim.y * gridDim.z))
+  if (EXTRA && a.tpx && last_cta(a.tpx_ticket, gridDim.x * gridDim.y * gridDim.z))
     tpx_publish_max(*a.tpx, TPX_AMAX_O, a.amax_out, a.R);
   tl_exit();
 }
@@ -569,12 +571,17 @@ cudaError_t launch_attn_rope(const AttnArgs& a, cudaStream_t st, bool pdl) {
                       tile * (a.hd + 8) * 2 + tile * a.hd * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   void (*kern)(const AttnArgs, int) =
-      longc ? (a.hd == 128 ? k_attn_rope<128, 64> : a.hd == 64 ? k_attn_rope<64, 64>
-               : a.hd == 32 ? k_attn_rope<32, 64> : k_attn_rope<16, 64>)
-            : (a.hd == 128 ? k_attn_rope<128, 128> : a.hd == 64 ? k_attn_rope<64, 128>
-               : a.hd == 32 ? k_attn_rope<32, 128> : k_attn_rope<16, 128>);
-  static DevOnce attr_set[8];
-  const int ti = (a.hd == 128 ? 0 : a.hd == 64 ? 1 : a.hd == 32 ? 2 : 3) + (longc ? 4 : 0);
+      !(a.kr_out || a.tpx)
+          ? (longc ? (a.hd == 128 ? k_attn_rope<128, 64, false> : a.hd == 64 ? k_attn_rope<64, 64, false>
+                      : a.hd == 32 ? k_attn_rope<32, 64, false> : k_attn_rope<16, 64, false>)
+                   : (a.hd == 128 ? k_attn_rope<128, 128, false> : a.hd == 64 ? k_attn_rope<64, 128, false>
+                      : a.hd == 32 ? k_attn_rope<32, 128, false> : k_attn_rope<16, 128, false>))
+          : (longc ? (a.hd == 128 ? k_attn_rope<128, 64, true> : a.hd == 64 ? k_attn_rope<64, 64, true>
+                      : a.hd == 32 ? k_attn_rope<32, 64, true> : k_attn_rope<16, 64, true>)
+                   : (a.hd == 128 ? k_attn_rope<128, 128, true> : a.hd == 64 ? k_attn_rope<64, 128, true>
+                      : a.hd == 32 ? k_attn_rope<32, 128, true> : k_attn_rope<16, 128, true>));
+  static DevOnce attr_set[16];
+  const int ti = (a.hd == 128 ? 0 : a.hd == 64 ? 1 : a.hd == 32 ? 2 : 3) + (longc ? 4 : 0) + (a.kr_out || a.tpx ? 8 : 0);
   if (!attr_set[ti].done()) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;

@@ -130,6 +130,9 @@ EXB_DEV void put_digits(uint8_t* dig, int K, int r, int i, int16_t v) {
   dig[(size_t)(TC_DECODE_ROWS + r) * K + i] = (uint8_t)(int8_t)(v >> 8);
 }
 
+// EPT: elements per thread of the register variant (D <= EPT * ROW_THREADS), 0 = the row staged in
+// shared memory; one instantiation per variant keeps the others' registers out of it
+template <int EPT>
 __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restrict__ x, int ldx,
                                                         const int64_t* __restrict__ g, int D,
                                                         int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs,
@@ -141,7 +144,8 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restric
   pdl_wait();
   pdl_launch_dependents();
   const int r = blockIdx.x;
-  row_norm_q_any<ROW_THREADS>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, ys, red);
+  if constexpr (EPT > 0) row_norm_q_regs<ROW_THREADS, EPT>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, red);
+  else row_norm_q<ROW_THREADS>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, ys, red);
   if (dig)   // the row was written by this CTA (visible after the function's final barrier)
     for (int i = threadIdx.x; i < D; i += ROW_THREADS) put_digits(dig, D, r, i, xq[(size_t)r * ldq + i]);
   if (xcap)
@@ -151,16 +155,20 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restric
 
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
                           int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig, int64_t* xcap, int64_t ldcap) {
-  const size_t smem = (size_t)D * 16;
+  const int v = D <= 4 * ROW_THREADS ? 0 : D <= 8 * ROW_THREADS ? 1 : D <= 12 * ROW_THREADS ? 2 : 3;
+  const void* fn = v == 0 ? (const void*)k_norm_q<4> : v == 1 ? (const void*)k_norm_q<8>
+                 : v == 2 ? (const void*)k_norm_q<12> : (const void*)k_norm_q<0>;
+  const size_t smem = v == 3 ? (size_t)D * 16 : 0;
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
   static DevOnce attr_set;   // raised once to the full budget, never lowered
-  if (!attr_set.done()) {
-    cudaError_t e = cudaFuncSetAttribute(k_norm_q, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (v == 3 && !attr_set.done()) {
+    cudaError_t e = cudaFuncSetAttribute(k_norm_q<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     attr_set.set();
   }
   void* args[] = {(void*)&x,  (void*)&ldx, (void*)&g,   (void*)&D,    (void*)&xq,
                   (void*)&ldq, (void*)&xs,  (void*)&dig, (void*)&xcap, (void*)&ldcap};
-  return launch_simple((const void*)k_norm_q, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
+  return launch_simple(fn, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
 }
 
 __global__ void __launch_bounds__(ROW_THREADS) k_quant(const int64_t* __restrict__ x, int ldx, int K,
