@@ -2237,6 +2237,7 @@ int exb_set_option(exb_model* m, const char* name, int64_t value) {
   else if (n == "fuse") m->fuse_in = (int)value;
   else if (n == "tpar") m->tpar = value != 0;
   else if (n == "tpx") m->tpx_opt = value != 0;
+  else if (n == "tcp") gemm_tc_set_persist(value != 0 ? 1 : 0);
   else if (n == "tail") m->tail_norm = value != 0;
 
   else if (n == "attn") m->attn_fused = value != 0;

@@ -350,6 +350,7 @@ size_t gemm_tc_digit_bytes(int T, int K);
 // int8 digit planes (lo = xq & 255, hi = xq >> 8) of T int16 rows, padded to the tile height
 cudaError_t launch_digits(const int16_t* xq, int ldx, int T, int K, void* digits, cudaStream_t st);
 bool gemm_tc_supported(const LinW& L, int epi);
+void gemm_tc_set_persist(int on);     // multi-row GEMM on a persistent grid (default 1), process-wide
 // Decode steps (T <= TC_DECODE_ROWS rows, digit planes of exactly TC_DECODE_ROWS rows): 8-row
 // activation tiles, optional split over the 128-groups (int64 partial sums in tot_buf, the last
 // CTA of each 128-row tile finishes it; tot_buf and tickets are zero between uses), SwiGLU row

@@ -66,6 +66,8 @@ struct TcArgs {
   // decode extras
   int act_fast = 0;                   // grid.x indexes activation tiles (CTAs resident together
                                       // share a weight tile, read from HBM once), grid.y weight tiles
+  int persist = 0;                    // persistent grid: CTA c takes tiles c, c + gridDim.x, ... of the
+  int ntn = 0, ntiles = 0;            // ntiles tiles (activation tiles fastest, ntn per weight tile)
   int ksplit = 1;                     // CTAs sharing one 128-row tile over the 128-groups
   int64_t* tot_buf = nullptr;         // (T, N) int64 partial sums (zero between uses)
   unsigned int* tickets = nullptr;    // (N / 128) last-CTA counters (zero between uses)
@@ -194,12 +196,26 @@ __global__ void __launch_bounds__(TcGeo<BN>::THREADS, 1)
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool af = a.act_fast && a.ksplit <= 1;
-  const int tm = af ? (int)blockIdx.y : (int)blockIdx.x;
-  const int tn = a.ksplit > 1 ? 0 : (af ? (int)blockIdx.x : (int)blockIdx.y);   // split-K: grid.y = K ranges
-  const int ks = a.ksplit > 1 ? (int)blockIdx.y : 0;
   const int G = a.K >> 7;
-  const int g0 = (int)((long long)G * ks / a.ksplit), g1 = (int)((long long)G * (ks + 1) / a.ksplit);
-  const int ng = g1 - g0;
+  // Tiles of this CTA: one (from the grid position) or, with a persistent grid, tiles w0, w0 +
+  // wstep, ... of the activation-fastest order.  Every role walks the same sequence; `it` counts
+  // the CTA's (tile, 128-group) iterations, which index the stage ring and the TMEM buffers.
+  const int w0 = a.persist ? (int)blockIdx.x : 0;
+  const int wend = a.persist ? a.ntiles : 1;
+  const int wstep = a.persist ? (int)gridDim.x : 1;
+  auto tile_of = [&](int w, int& tm, int& tn, int& g0, int& ng) {
+    int ks = 0;
+    if (a.persist) {
+      tn = w % a.ntn;
+      tm = w / a.ntn;
+    } else {
+      tm = af ? (int)blockIdx.y : (int)blockIdx.x;
+      tn = a.ksplit > 1 ? 0 : (af ? (int)blockIdx.x : (int)blockIdx.y);   // split-K: grid.y = K ranges
+      ks = a.ksplit > 1 ? (int)blockIdx.y : 0;
+    }
+    g0 = (int)((long long)G * ks / a.ksplit);
+    ng = (int)((long long)G * (ks + 1) / a.ksplit) - g0;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -222,6 +238,8 @@ __global__ void __launch_bounds__(TcGeo<BN>::THREADS, 1)
     // ---- TMA producer: the weight tiles of the first stages do not depend on the previous
     // kernel and go out before the programmatic-dependent-launch wait; activation digits after it
     if (lane == 0) {
+      int tm, tn, g0, ng;
+      tile_of(w0, tm, tn, g0, ng);
       const int pre = ng < TC_STAGES ? ng : TC_STAGES;
       for (int i = 0; i < pre; ++i) {
         unsigned char* st = smem + (size_t)i * STAGE_BYTES;
@@ -235,27 +253,43 @@ __global__ void __launch_bounds__(TcGeo<BN>::THREADS, 1)
         tma_load_2d(st + TC_A_BYTES + B_BYTES, &tmHi, (g0 + i) * 128, tn * BN, &full[i]);
       }
       *(volatile int*)&issued_sh = pre;
-      for (int i = pre; i < ng; ++i) {
-        const int s = i % TC_STAGES;
-        if (!tc_wait(&empty[s], ((i / TC_STAGES) - 1) & 1)) {
-          abort_sh = 1;
-          set_err(a.err, ERR_WAIT_TIMEOUT);
-          break;
+      // the ring runs on across tile boundaries: the next tile's first groups load while the
+      // epilogue finishes the current one (on a fresh barrier the parity-1 wait returns at once)
+      int it = pre, i = pre;
+      for (int w = w0;;) {
+        for (; i < ng; ++i, ++it) {
+          const int s = it % TC_STAGES;
+          if (!tc_wait(&empty[s], ((it / TC_STAGES) - 1) & 1)) {
+            abort_sh = 1;
+            set_err(a.err, ERR_WAIT_TIMEOUT);
+            break;
+          }
+          if (*(volatile int*)&abort_sh) break;
+          unsigned char* st = smem + (size_t)s * STAGE_BYTES;
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(st, &tmA, (g0 + i) * 128, tm * TC_BM, &full[s]);
+          tma_load_2d(st + TC_A_BYTES, &tmLo, (g0 + i) * 128, tn * BN, &full[s]);
+          tma_load_2d(st + TC_A_BYTES + B_BYTES, &tmHi, (g0 + i) * 128, tn * BN, &full[s]);
+          *(volatile int*)&issued_sh = it + 1;
         }
         if (*(volatile int*)&abort_sh) break;
-        unsigned char* st = smem + (size_t)s * STAGE_BYTES;
-        mbar_expect_tx(&full[s], STAGE_BYTES);
-        tma_load_2d(st, &tmA, (g0 + i) * 128, tm * TC_BM, &full[s]);
-        tma_load_2d(st + TC_A_BYTES, &tmLo, (g0 + i) * 128, tn * BN, &full[s]);
-        tma_load_2d(st + TC_A_BYTES + B_BYTES, &tmHi, (g0 + i) * 128, tn * BN, &full[s]);
-        *(volatile int*)&issued_sh = i + 1;
+        w += wstep;
+        if (w >= wend) break;
+        tile_of(w, tm, tn, g0, ng);
+        i = 0;
       }
     }
   } else if (warp == 1) {
     // ---- MMA issuer
     if (lane == 0) {
       const uint32_t id_lo = tc_idesc<BN>(false), id_hi = tc_idesc<BN>(true);
-      for (int i = 0; i < ng; ++i) {
+      int ntot = 0;                     // this CTA's (tile, group) iterations
+      for (int w = w0; w < wend; w += wstep) {
+        int tm, tn, g0, ng;
+        tile_of(w, tm, tn, g0, ng);
+        ntot += ng;
+      }
+      for (int i = 0; i < ntot; ++i) {
         const int s = i % TC_STAGES, b = i & 1;
         if (!tc_wait(&full[s], (i / TC_STAGES) & 1) || !tc_wait(&acce[b], ((i >> 1) & 1) ^ 1)) {
           abort_sh = 1;
@@ -284,93 +318,98 @@ __global__ void __launch_bounds__(TcGeo<BN>::THREADS, 1)
     const int q = warp & 3;
     const int hc = (warp - 2) >> 2;
     const int row = q * 32 + lane;
-    const int n = tm * TC_BM + row;
-    int64_t tot[CW];
-#pragma unroll
-    for (int j = 0; j < CW; ++j) tot[j] = 0;
-    const int32_t* mrow = a.Mg ? a.Mg + (size_t)n * a.ldm : nullptr;
-    int32_t mnext = (mrow && ng > 0) ? __ldg(mrow + g0) : 1;
     bool ok = true;
-    for (int i = 0; i < ng; ++i) {
-      const int b = i & 1;
-      const int32_t mv = mnext;
-      if (mrow && i + 1 < ng) mnext = __ldg(mrow + g0 + i + 1);
-      // warp-uniform outcome: the TMEM loads below are .sync.aligned over the whole warp
-      if (!__all_sync(0xffffffffu, tc_wait(&accf[b], (i >> 1) & 1))) {
-        ok = false;
-        set_err(a.err, ERR_WAIT_TIMEOUT);
-        abort_sh = 1;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t t_lo = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * BN + hc * CW);
-      // TMEM columns per load: 16 where the registers allow (BN = 64), else 8 (the 16-warp epilogue
-      // of BN = 128 runs at 96 registers per thread and would spill)
-      constexpr int CH = (CW >= 16 && BN < 128) ? 16 : 8;
+    int it = 0;                         // this CTA's (tile, group) iterations so far
+    for (int w = w0; w < wend && ok; w += wstep) {
+      int tm, tn, g0, ng;
+      tile_of(w, tm, tn, g0, ng);
+      const int n = tm * TC_BM + row;
+      int64_t tot[CW];
 #pragma unroll
-      for (int c = 0; c < CW / CH; ++c) {
-        int32_t lo[CH], hi[CH];
-        if constexpr (CH == 16) {
-          tmem_ld16(t_lo + c * CH, lo);
-          tmem_ld16(t_lo + BN + c * CH, hi);
-        } else {
-          tmem_ld8(t_lo + c * CH, lo);
-          tmem_ld8(t_lo + BN + c * CH, hi);
+      for (int j = 0; j < CW; ++j) tot[j] = 0;
+      const int32_t* mrow = a.Mg ? a.Mg + (size_t)n * a.ldm : nullptr;
+      int32_t mnext = (mrow && ng > 0) ? __ldg(mrow + g0) : 1;
+      for (int i = 0; i < ng; ++i, ++it) {
+        const int b = it & 1;
+        const int32_t mv = mnext;
+        if (mrow && i + 1 < ng) mnext = __ldg(mrow + g0 + i + 1);
+        // warp-uniform outcome: the TMEM loads below are .sync.aligned over the whole warp
+        if (!__all_sync(0xffffffffu, tc_wait(&accf[b], (it >> 1) & 1))) {
+          ok = false;
+          set_err(a.err, ERR_WAIT_TIMEOUT);
+          abort_sh = 1;
+          break;
         }
-        tmem_wait_ld();
-        if (c == CW / CH - 1) {
-          tc_fence_before();
-          mbar_arrive(&acce[b]);        // buffer b may be overwritten by the next-but-one group
+        tc_fence_after();
+        const uint32_t t_lo = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 2 * BN + hc * CW);
+        // TMEM columns per load: 16 where the registers allow (BN = 64), else 8 (the 16-warp epilogue
+        // of BN = 128 runs at 96 registers per thread and would spill)
+        constexpr int CH = (CW >= 16 && BN < 128) ? 16 : 8;
+#pragma unroll
+        for (int c = 0; c < CW / CH; ++c) {
+          int32_t lo[CH], hi[CH];
+          if constexpr (CH == 16) {
+            tmem_ld16(t_lo + c * CH, lo);
+            tmem_ld16(t_lo + BN + c * CH, hi);
+          } else {
+            tmem_ld8(t_lo + c * CH, lo);
+            tmem_ld8(t_lo + BN + c * CH, hi);
+          }
+          tmem_wait_ld();
+          if (c == CW / CH - 1) {
+            tc_fence_before();
+            mbar_arrive(&acce[b]);        // buffer b may be overwritten by the next-but-one group
+          }
+#pragma unroll
+          for (int e = 0; e < CH; ++e)    // exact group sum 256 hi + lo (|.| < 2^30), times the scale
+            tot[c * CH + e] = mad_wide(hi[e] * 256 + lo[e], mv, tot[c * CH + e]);
         }
-#pragma unroll
-        for (int e = 0; e < CH; ++e)    // exact group sum 256 hi + lo (|.| < 2^30), times the scale
-          tot[c * CH + e] = mad_wide(hi[e] * 256 + lo[e], mv, tot[c * CH + e]);
       }
-    }
-    pdl_launch_dependents();
-    // every epilogue thread reaches this point (finished or timed out): one decision for all
-    named_sync(1, NEPI);
-    ok = ok && !*(volatile int*)&abort_sh;
-    ok = __all_sync(0xffffffffu, ok);
-    named_sync(1, NEPI);
-    if (ok && a.ksplit == 1) {
-#pragma unroll
-      for (int j = 0; j < CW; ++j) {
-        const int t = tn * BN + hc * CW + j;
-        uint64_t hm = 0;
-        tc_finish(a, t, n, tot[j], t < a.T, hm);
-        if (a.amax_out) tc_publish_hmax(a, t, hm);
-      }
-    } else if (ok) {
-      // split-K: add this CTA's partial sums, the last CTA of the tile finishes it
-#pragma unroll
-      for (int j = 0; j < CW; ++j) {
-        const int t = hc * CW + j;
-        if (t < a.T) atomicAdd(reinterpret_cast<unsigned long long*>(a.tot_buf + (size_t)t * a.N + n),
-                               (unsigned long long)tot[j]);
-      }
-      __threadfence();
+      if (w == w0) pdl_launch_dependents();
+      // every epilogue thread reaches this point (finished or timed out): one decision for all
       named_sync(1, NEPI);
-      if (threadIdx.x == 64) {
-        const unsigned prev = atomicAdd(a.tickets + tm, 1u);
-        last_sh = prev == (unsigned)(a.ksplit - 1);
-        if (last_sh) a.tickets[tm] = 0;
-      }
+      ok = ok && !*(volatile int*)&abort_sh;
+      ok = __all_sync(0xffffffffu, ok);
       named_sync(1, NEPI);
-      if (last_sh) {
-        __threadfence();
+      if (ok && a.ksplit == 1) {
+#pragma unroll
+        for (int j = 0; j < CW; ++j) {
+          const int t = tn * BN + hc * CW + j;
+          uint64_t hm = 0;
+          tc_finish(a, t, n, tot[j], t < a.T, hm);
+          if (a.amax_out) tc_publish_hmax(a, t, hm);
+        }
+      } else if (ok) {
+        // split-K: add this CTA's partial sums, the last CTA of the tile finishes it
 #pragma unroll
         for (int j = 0; j < CW; ++j) {
           const int t = hc * CW + j;
-          int64_t v = 0;
-          if (t < a.T) {
-            int64_t* p = a.tot_buf + (size_t)t * a.N + n;
-            v = (int64_t)__ldcg(reinterpret_cast<const long long*>(p));
-            *p = 0;                     // ready for the next use
+          if (t < a.T) atomicAdd(reinterpret_cast<unsigned long long*>(a.tot_buf + (size_t)t * a.N + n),
+                                 (unsigned long long)tot[j]);
+        }
+        __threadfence();
+        named_sync(1, NEPI);
+        if (threadIdx.x == 64) {
+          const unsigned prev = atomicAdd(a.tickets + tm, 1u);
+          last_sh = prev == (unsigned)(a.ksplit - 1);
+          if (last_sh) a.tickets[tm] = 0;
+        }
+        named_sync(1, NEPI);
+        if (last_sh) {
+          __threadfence();
+#pragma unroll
+          for (int j = 0; j < CW; ++j) {
+            const int t = hc * CW + j;
+            int64_t v = 0;
+            if (t < a.T) {
+              int64_t* p = a.tot_buf + (size_t)t * a.N + n;
+              v = (int64_t)__ldcg(reinterpret_cast<const long long*>(p));
+              *p = 0;                     // ready for the next use
+            }
+            uint64_t hm = 0;
+            tc_finish(a, t, n, v, t < a.T, hm);
+            if (a.amax_out) tc_publish_hmax(a, t, hm);
           }
-          uint64_t hm = 0;
-          tc_finish(a, t, n, v, t < a.T, hm);
-          if (a.amax_out) tc_publish_hmax(a, t, hm);
         }
       }
     }
@@ -482,6 +521,19 @@ static cudaError_t tc_launch(dim3 grid, const CUtensorMap& mA, const CUtensorMap
   return cudaLaunchKernelEx(&cfg, k_gemm_tc<BN>, mA, mLo, mHi, a);
 }
 
+// process-wide choice of the persistent grid for the multi-row GEMM (engine option "tcp")
+#ifndef EXB_TC_PERSIST
+#define EXB_TC_PERSIST 1
+#endif
+static int g_tc_persist = EXB_TC_PERSIST;
+void gemm_tc_set_persist(int on) { g_tc_persist = on; }
+static int tc_sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
 cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32_t* xs, int epi, int64_t* out, int ldo,
                            int64_t* raw, int64_t* raw2, int ldr, const int32_t* silu_t, int* err, cudaStream_t st,
                            const TcDecode* dec) {
@@ -510,8 +562,17 @@ cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32
   // activation tiles fastest: the CTAs resident together cover a few weight tiles x every
   // activation tile, so each weight byte comes from HBM once and the activations stay in L2
   a.act_fast = 1;
-  if (BN == 128) return tc_launch<128>(dim3(Tpad / 128, L.N / TC_BM), mA, mLo, mHi, a, false, st);
-  return tc_launch<64>(dim3((T + 63) / 64, L.N / TC_BM), mA, mLo, mHi, a, false, st);
+  const int ntn = BN == 128 ? Tpad / 128 : (T + 63) / 64, ntm = L.N / TC_BM;
+  if (g_tc_persist) {
+    // persistent grid: one CTA per SM walks the tiles in the same activation-fastest order, so
+    // the TMA ring and the TMEM allocation carry over from tile to tile
+    a.persist = 1; a.ntn = ntn; a.ntiles = ntn * ntm;
+    const int grid = a.ntiles < tc_sm_count() ? a.ntiles : tc_sm_count();
+    if (BN == 128) return tc_launch<128>(dim3(grid, 1), mA, mLo, mHi, a, false, st);
+    return tc_launch<64>(dim3(grid, 1), mA, mLo, mHi, a, false, st);
+  }
+  if (BN == 128) return tc_launch<128>(dim3(ntn, ntm), mA, mLo, mHi, a, false, st);
+  return tc_launch<64>(dim3(ntn, ntm), mA, mLo, mHi, a, false, st);
 }
 
 }  // namespace exb

@@ -249,6 +249,8 @@ int exb_model_create_tp(const exb_config* cfg, int rank, int size, const uint8_t
  *             partial sums into every peer's memory and raise a flag; the o / down GEMV prologues and
  *             the norm kernels wait for the peers' flags (bounded) and reduce; 0: all-reduce kernels
  *             (trace, Freivalds and commitment captures always use those)
+ *   "tcp"     1 (default): the multi-row tcgen05 GEMM runs on a persistent grid (one CTA per SM walking
+ *             the tiles); 0: one CTA per tile.  Process-wide (every model and exb_linear_g128).
  * Cached step graphs are dropped. */
 int exb_set_option(exb_model* m, const char* name, int64_t value);
 
