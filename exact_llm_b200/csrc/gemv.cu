@@ -36,12 +36,12 @@ constexpr int DYN_SMEM_MAX = 200 * 1024;        // dynamic shared memory budget 
 constexpr int PRE_SMEM_MAX = 104 * 1024;        // with the pre-wait area: two CTAs still fit one SM
 
 // MODE: 0 lean (the decode hot path: int16 or qrow inputs, store / residual / SwiGLU / raw
-// epilogues, no Freivalds, tails, norm prologues, row statistics or argmax), 1 full, 2 full with the
+// epilogues, no Freivalds, tails, norm prologues, row statistics or argmax), 1 full, 2 lean with the
 // tensor-parallel exchanges.  Each is its own instantiation: code a launch never runs still costs
 // registers (spills) in the streaming loop.
 template <int R, int RPU, bool GROUP, int RB, int MODE>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
-  constexpr bool LEAN = MODE == 0, TPX = MODE == 2;
+  constexpr bool LEAN = MODE != 1, TPX = MODE == 2;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   int16_t* xs = reinterpret_cast<int16_t*>(smem_raw);                    // R x K int16 (tail: D int64 x 2)
   __shared__ unsigned long long red[NCW][R][6];
@@ -437,12 +437,14 @@ static cudaError_t launch_m(const GemvArgs& a, size_t smem, cudaStream_t st, boo
 
 template <int RPU, bool GROUP>
 static cudaError_t launch_r(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
-  if (a.tpx) {                       // tensor-parallel decode (group-128 models only)
-    if constexpr (GROUP) return launch_m<RPU, GROUP, 2>(a, smem, st, pdl);
-    return cudaErrorInvalidValue;
-  }
   const bool lean = a.fr_nseg == 0 && a.tail == TAIL_NONE && (a.xin == XIN_Q16 || a.xin == XIN_QUANT) &&
                     !a.nstat_out && a.epi != EPI_HEAD;
+  if (a.tpx) {                       // tensor-parallel decode exchanges (group-128 models, lean launches)
+    if constexpr (GROUP) {
+      if (lean) return launch_m<RPU, GROUP, 2>(a, smem, st, pdl);
+    }
+    return cudaErrorInvalidValue;
+  }
   return lean ? launch_m<RPU, GROUP, 0>(a, smem, st, pdl) : launch_m<RPU, GROUP, 1>(a, smem, st, pdl);
 }
 
