@@ -773,66 +773,173 @@ __global__ void __launch_bounds__(PA_THREADS, 3) k_attn_prefill(const AttnArgs a
       if (tq == 0 && sacc) atomicAdd(reinterpret_cast<unsigned long long*>(&ssum[srow(i)]), (unsigned long long)sacc);
     }
   }
-  // pass 3: p = (e << 20) // sum (exact floor division through a per-row reciprocal and integer
-  // corrections; p <= 2^20), then out += p . v as 32 x 32 -> 64-bit products (thread: row tid / 8,
-  // dims 32 i + 4 (tid % 8) + (0..3): int4 reads of V, the 8 threads of a row on 32 distinct banks;
-  // head dim 16: dims tid % 8 + 8 i)
-  __syncthreads();
-  if (tid < PRT) sinv[tid] = ssum[tid] > 0 ? __drcp_rn((double)ssum[tid]) : 0.0;
-  constexpr int DPT = HD / 8;
-  constexpr bool VEC = DPT % 4 == 0;                   // int4 runs of V (head dims >= 32)
-  const int orow = tid >> 3, od = tid & 7;
-  auto dim_of = [&](int jd) { return VEC ? (jd >> 2) * 32 + od * 4 + (jd & 3) : od + 8 * jd; };
-  int64_t oacc[DPT];
-#pragma unroll
-  for (int i = 0; i < DPT; ++i) oacc[i] = 0;
-  for (int t0 = 0; t0 < pend; t0 += PKT) {
+  if constexpr (HD >= 32) {
+    // pass 3 on the tensor cores: p = (e << 20) // sum (exact floor division through a per-row
+    // reciprocal and integer corrections; 0 <= p <= 2^20) as three unsigned byte digits, V (int32) as
+    // three unsigned bytes and a signed top byte; out = sum over the 12 digit products of
+    // (p_i . v_j) << 8 (i + j), each an int8 MMA over the 64 keys of a tile (|.| < 2^23), the products
+    // of one weight 8 s summed in int32 (< 2^25) and shifted into int64 per tile.  Warp w: rows
+    // 16 (w % 2) .. + 15, dims (w / 2) HD/4 .. + HD/4 - 1 (HD/32 tiles of 8 dims).
+    constexpr int TBV = PKT + 16;                      // plane row of 64 keys: 20 words, conflict-free
+    constexpr int NTW = HD / 32;
+    uint8_t* vpl = reinterpret_cast<uint8_t*>(vt);     // 4 planes x HD dims x TBV (over V and P tiles)
+    uint8_t* ppl = klo;                                // 3 planes x PRT rows x TBV (over the key planes)
     __syncthreads();
-    const int nk = min(PKT, pend - t0);
-    for (int e = tid; e < PKT * (HD / 4); e += PA_THREADS) {     // V tile lands during the scores
-      const int t = e / (HD / 4), c4 = e - t * (HD / 4);
-      if (t < nk) cp_async16(reinterpret_cast<int4*>(vt) + e, reinterpret_cast<const int4*>(a.vc + (cbase + t0 + t) * HD) + c4);
-      else reinterpret_cast<int4*>(vt)[e] = make_int4(0, 0, 0, 0);
-    }
-    cp_async_commit();
-    load_k(t0);
-    __syncthreads();
-    int64_t sc[2][4];
-    bool valid[2][4];
-    scores(t0, sc, valid);
+    if (tid < PRT) sinv[tid] = ssum[tid] > 0 ? __drcp_rn((double)ssum[tid]) : 0.0;
+    const int mtw = warp & 1, dq = warp >> 1;
+    int64_t o64[NTW][4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int nt = 0; nt < NTW; ++nt)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int row = srow(i);
-        int32_t p = 0;
-        if (valid[i][k])
-          p = (int32_t)floordiv_small_q(exp_lookup(a.exp_t, mx[row] - sc[i][k]) << 20, ssum[row], sinv[row]);
-        pt[row * PKT + skey(k)] = p;
-      }
-    cp_async_wait<0>();
-    __syncthreads();
-#pragma unroll 2
-    for (int t = 0; t < nk; ++t) {
-      const int64_t p = pt[orow * PKT + t];
-      if constexpr (VEC) {
+      for (int f = 0; f < 4; ++f) o64[nt][f] = 0;
+    for (int t0 = 0; t0 < pend; t0 += PKT) {
+      __syncthreads();
+      const int nk = min(PKT, pend - t0);
+      // V tile -> byte planes, keys contiguous per dim (dims fastest over the threads: every warp
+      // reads 128 contiguous bytes of a cached row); keys t >= nk are zero
+      for (int e = tid; e < (PKT / 4) * HD; e += PA_THREADS) {
+        const int d = e % HD, kg = e / HD;
+        uint32_t v[4];
 #pragma unroll
-        for (int i = 0; i < DPT / 4; ++i) {
-          const int4 v = *reinterpret_cast<const int4*>(vt + t * HD + dim_of(4 * i));
-          oacc[4 * i] += p * v.x;
-          oacc[4 * i + 1] += p * v.y;
-          oacc[4 * i + 2] += p * v.z;
-          oacc[4 * i + 3] += p * v.w;
+        for (int u = 0; u < 4; ++u) {
+          const int t = 4 * kg + u;
+          v[u] = t < nk ? (uint32_t)a.vc[(cbase + t0 + t) * HD + d] : 0u;
         }
-      } else {
+        const uint32_t lo01 = __byte_perm(v[0], v[1], 0x5140), lo23 = __byte_perm(v[2], v[3], 0x5140);
+        const uint32_t hi01 = __byte_perm(v[0], v[1], 0x7362), hi23 = __byte_perm(v[2], v[3], 0x7362);
+        *reinterpret_cast<uint32_t*>(vpl + (0 * HD + d) * TBV + 4 * kg) = __byte_perm(lo01, lo23, 0x5410);
+        *reinterpret_cast<uint32_t*>(vpl + (1 * HD + d) * TBV + 4 * kg) = __byte_perm(lo01, lo23, 0x7632);
+        *reinterpret_cast<uint32_t*>(vpl + (2 * HD + d) * TBV + 4 * kg) = __byte_perm(hi01, hi23, 0x5410);
+        *reinterpret_cast<uint32_t*>(vpl + (3 * HD + d) * TBV + 4 * kg) = __byte_perm(hi01, hi23, 0x7632);
+      }
+      load_k(t0);
+      __syncthreads();
+      int64_t sc[2][4];
+      bool valid[2][4];
+      scores(t0, sc, valid);
+      uint32_t pv[2][4];
 #pragma unroll
-        for (int i = 0; i < DPT; ++i) oacc[i] += p * (int64_t)vt[t * HD + dim_of(i)];
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int row = srow(i);
+          pv[i][k] = valid[i][k]
+                         ? (uint32_t)floordiv_small_q(exp_lookup(a.exp_t, mx[row] - sc[i][k]) << 20, ssum[row], sinv[row])
+                         : 0u;
+        }
+      __syncthreads();                                 // every warp's scores have read the key planes
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+          const int row = srow(i), key = nq * 16 + n * 8 + 2 * tq;
+          const uint32_t pa = pv[i][2 * n], pb = pv[i][2 * n + 1];
+#pragma unroll
+          for (int d = 0; d < 3; ++d)                  // digit d of the two keys, little-endian
+            *reinterpret_cast<uint16_t*>(ppl + (d * PRT + row) * TBV + key) =
+                (uint16_t)(((pa >> (8 * d)) & 255u) | (((pb >> (8 * d)) & 255u) << 8));
+        }
+      __syncthreads();
+#pragma unroll 1
+      for (int sft = 0; sft < 6; ++sft) {
+        int acc[NTW][4];
+#pragma unroll
+        for (int nt = 0; nt < NTW; ++nt)
+#pragma unroll
+          for (int f = 0; f < 4; ++f) acc[nt][f] = 0;
+#pragma unroll 1
+        for (int pi = 0; pi < 3; ++pi) {
+          const int vj = sft - pi;
+          if (vj < 0 || vj > 3) continue;
+#pragma unroll
+          for (int ks = 0; ks < PKT / 32; ++ks) {
+            const int ra = (pi * PRT + mtw * 16 + g) * TBV + ks * 32 + 4 * tq, rb = ra + 8 * TBV;
+            const uint32_t af[4] = {ld_s32(ppl + ra), ld_s32(ppl + rb), ld_s32(ppl + ra + 16), ld_s32(ppl + rb + 16)};
+#pragma unroll
+            for (int nt = 0; nt < NTW; ++nt) {
+              const int kb = (vj * HD + dq * (HD / 4) + nt * 8 + g) * TBV + ks * 32 + 4 * tq;
+              const uint32_t b0 = ld_s32(vpl + kb), b1 = ld_s32(vpl + kb + 16);
+              if (vj == 3) mma_i8<false, true>(acc[nt], af, b0, b1);
+              else mma_i8<false, false>(acc[nt], af, b0, b1);
+            }
+          }
+        }
+#pragma unroll
+        for (int nt = 0; nt < NTW; ++nt)
+#pragma unroll
+          for (int f = 0; f < 4; ++f)
+            o64[nt][f] = (int64_t)((uint64_t)o64[nt][f] + ((uint64_t)(int64_t)acc[nt][f] << (8 * sft)));
       }
     }
-  }
-  if (orow < nr)
 #pragma unroll
-    for (int i = 0; i < DPT; ++i) a.out[(size_t)(r0 + orow) * a.ldo + (size_t)h * HD + dim_of(i)] = shr64(oacc[i], 20);
+    for (int nt = 0; nt < NTW; ++nt)
+#pragma unroll
+      for (int f = 0; f < 4; ++f) {
+        const int row = mtw * 16 + g + 8 * (f >> 1), dim = dq * (HD / 4) + nt * 8 + 2 * tq + (f & 1);
+        if (row < nr) a.out[(size_t)(r0 + row) * a.ldo + (size_t)h * HD + dim] = shr64(o64[nt][f], 20);
+      }
+  } else {
+    // pass 3: p = (e << 20) // sum (exact floor division through a per-row reciprocal and integer
+    // corrections; p <= 2^20), then out += p . v as 32 x 32 -> 64-bit products (thread: row tid / 8,
+    // dims 32 i + 4 (tid % 8) + (0..3): int4 reads of V, the 8 threads of a row on 32 distinct banks;
+    // head dim 16: dims tid % 8 + 8 i)
+    __syncthreads();
+    if (tid < PRT) sinv[tid] = ssum[tid] > 0 ? __drcp_rn((double)ssum[tid]) : 0.0;
+    constexpr int DPT = HD / 8;
+    constexpr bool VEC = DPT % 4 == 0;                   // int4 runs of V (head dims >= 32)
+    const int orow = tid >> 3, od = tid & 7;
+    auto dim_of = [&](int jd) { return VEC ? (jd >> 2) * 32 + od * 4 + (jd & 3) : od + 8 * jd; };
+    int64_t oacc[DPT];
+  #pragma unroll
+    for (int i = 0; i < DPT; ++i) oacc[i] = 0;
+    for (int t0 = 0; t0 < pend; t0 += PKT) {
+      __syncthreads();
+      const int nk = min(PKT, pend - t0);
+      for (int e = tid; e < PKT * (HD / 4); e += PA_THREADS) {     // V tile lands during the scores
+        const int t = e / (HD / 4), c4 = e - t * (HD / 4);
+        if (t < nk) cp_async16(reinterpret_cast<int4*>(vt) + e, reinterpret_cast<const int4*>(a.vc + (cbase + t0 + t) * HD) + c4);
+        else reinterpret_cast<int4*>(vt)[e] = make_int4(0, 0, 0, 0);
+      }
+      cp_async_commit();
+      load_k(t0);
+      __syncthreads();
+      int64_t sc[2][4];
+      bool valid[2][4];
+      scores(t0, sc, valid);
+  #pragma unroll
+      for (int i = 0; i < 2; ++i)
+  #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int row = srow(i);
+          int32_t p = 0;
+          if (valid[i][k])
+            p = (int32_t)floordiv_small_q(exp_lookup(a.exp_t, mx[row] - sc[i][k]) << 20, ssum[row], sinv[row]);
+          pt[row * PKT + skey(k)] = p;
+        }
+      cp_async_wait<0>();
+      __syncthreads();
+  #pragma unroll 2
+      for (int t = 0; t < nk; ++t) {
+        const int64_t p = pt[orow * PKT + t];
+        if constexpr (VEC) {
+  #pragma unroll
+          for (int i = 0; i < DPT / 4; ++i) {
+            const int4 v = *reinterpret_cast<const int4*>(vt + t * HD + dim_of(4 * i));
+            oacc[4 * i] += p * v.x;
+            oacc[4 * i + 1] += p * v.y;
+            oacc[4 * i + 2] += p * v.z;
+            oacc[4 * i + 3] += p * v.w;
+          }
+        } else {
+  #pragma unroll
+          for (int i = 0; i < DPT; ++i) oacc[i] += p * (int64_t)vt[t * HD + dim_of(i)];
+        }
+      }
+    }
+    if (orow < nr)
+  #pragma unroll
+      for (int i = 0; i < DPT; ++i) a.out[(size_t)(r0 + orow) * a.ldo + (size_t)h * HD + dim_of(i)] = shr64(oacc[i], 20);
+  }
   tl_exit();
 }
 
