@@ -37,11 +37,11 @@ constexpr int PRE_SMEM_MAX = 104 * 1024;        // with the pre-wait area: two C
 
 // MODE: 0 lean (the decode hot path: int16 or qrow inputs, store / residual / SwiGLU / raw
 // epilogues, no Freivalds, tails, norm prologues, row statistics or argmax), 1 full, 2 lean with the
-// tensor-parallel exchanges.  Each is its own instantiation: code a launch never runs still costs
+// tensor-parallel exchanges, 3 lean with the norm prologue (row staged in shared memory).  Each is its own instantiation: code a launch never runs still costs
 // registers (spills) in the streaming loop.
 template <int R, int RPU, bool GROUP, int RB, int MODE>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
-  constexpr bool LEAN = MODE != 1, TPX = MODE == 2;
+  constexpr bool LEAN = MODE != 1, TPX = MODE == 2, NORMP = MODE == 1 || MODE == 3;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   int16_t* xs = reinterpret_cast<int16_t*>(smem_raw);                    // R x K int16 (tail: D int64 x 2)
   __shared__ unsigned long long red[NCW][R][6];
@@ -140,11 +140,15 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
                                           rred))
         row_norm_q_any<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, xs + (size_t)r * K, &sh_s[r], ys, rred);
     }
-  } else if (!LEAN && a.xin == XIN_NORM) {
+  } else if (NORMP && a.xin == XIN_NORM) {
     // xq, s = qrow(irms(x, g)) for every row, computed by this CTA (exact_llm.py:100-106, 41-46)
     int64_t* ys = reinterpret_cast<int64_t*>(smem_raw + (((size_t)R * K * 2 + 127) & ~(size_t)127));
-    for (int r = 0; r < R; ++r)
-      row_norm_q_any<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, xs + (size_t)r * K, &sh_s[r], ys, rred);
+    for (int r = 0; r < R; ++r) {
+      if constexpr (LEAN)     // one routine only: the row and gains staged in shared memory
+        row_norm_q<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, xs + (size_t)r * K, &sh_s[r], ys, rred);
+      else
+        row_norm_q_any<GEMV_THREADS>(a.x64 + (size_t)r * a.ldx64, a.gain, K, xs + (size_t)r * K, &sh_s[r], ys, rred);
+    }
   } else {
     // xq = clip(shr(x, s)) with s from the producer's published row max (exact_llm.py:41-46); under
     // tensor parallelism the max over every rank's rows, from the fused exchange
@@ -445,7 +449,10 @@ static cudaError_t launch_r(const GemvArgs& a, size_t smem, cudaStream_t st, boo
     }
     return cudaErrorInvalidValue;
   }
-  return lean ? launch_m<RPU, GROUP, 0>(a, smem, st, pdl) : launch_m<RPU, GROUP, 1>(a, smem, st, pdl);
+  if (lean) return launch_m<RPU, GROUP, 0>(a, smem, st, pdl);
+  const bool norm_lean = a.fr_nseg == 0 && a.tail == TAIL_NONE && a.xin == XIN_NORM && !a.nstat_out &&
+                         a.epi != EPI_HEAD;
+  return norm_lean ? launch_m<RPU, GROUP, 3>(a, smem, st, pdl) : launch_m<RPU, GROUP, 1>(a, smem, st, pdl);
 }
 
 static int sm_count() {
