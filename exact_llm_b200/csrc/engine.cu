@@ -175,6 +175,7 @@ struct exb_model {
   int16_t *p_xq = nullptr, *p_qq = nullptr;
   int32_t *p_xs = nullptr, *p_qs = nullptr, *p_next = nullptr;
   void* p_dig = nullptr;
+  unsigned long long* p_amax = nullptr;     // per-row max |h| published by the gate|up GEMM
   // persistent decode-step kernel (step.cu): per-layer descriptors and accumulators
   bool tc_on = true;                    // multi-row chunks on the tensor-core GEMM
   bool tail_norm = false;               // decode: the o and down GEMVs finish the next norm in their last CTA
@@ -1481,7 +1482,8 @@ static int prefill_alloc(exb_model* m) {
   const size_t o_rows = take(sizeof(int32_t) * 3 * PCH), o_x = take(8ull * P * c.D), o_qkv = take(8ull * P * m->Nqkv),
                o_ao = take(8ull * P * Hd), o_hb = take(8ull * P * c.I), o_raw = take(8ull * P * c.V),
                o_xq = take(2ull * P * m->KMAX), o_qq = take(2ull * P * Hd), o_xs = take(4ull * P),
-               o_qs = take(4ull * P * c.H), o_next = take(4ull * P), o_dig = take(gemm_tc_digit_bytes(P, m->KMAX));
+               o_qs = take(4ull * P * c.H), o_next = take(4ull * P), o_dig = take(gemm_tc_digit_bytes(P, m->KMAX)),
+               o_amax = take(8ull * P);
   CK(cudaMalloc(&m->p_arena, off));
   CK(cudaMallocHost(&m->p_hrows, sizeof(int32_t) * 3 * PCH));
   char* b = m->p_arena;
@@ -1489,6 +1491,7 @@ static int prefill_alloc(exb_model* m) {
   m->p_ao = (int64_t*)(b + o_ao); m->p_hb = (int64_t*)(b + o_hb); m->p_raw = (int64_t*)(b + o_raw);
   m->p_xq = (int16_t*)(b + o_xq); m->p_qq = (int16_t*)(b + o_qq); m->p_xs = (int32_t*)(b + o_xs);
   m->p_qs = (int32_t*)(b + o_qs); m->p_next = (int32_t*)(b + o_next); m->p_dig = b + o_dig;
+  m->p_amax = (unsigned long long*)(b + o_amax);
   m->pch = P;
   return EXB_OK;
 }
@@ -1514,12 +1517,18 @@ static int prefill_chunk(exb_model* m, int R, int64_t* logits_host, int32_t* nex
   bool one_seq = m->attn_prefill;
   for (int r = 1; r < R && one_seq; ++r)
     one_seq = m->p_hrows[PCH + r] == m->p_hrows[PCH] && m->p_hrows[2 * PCH + r] == m->p_hrows[2 * PCH] + r;
-  auto lin = [&](const int16_t* xq, int K, const LinW& L, int epi, int64_t* out, int ldo) -> cudaError_t {
-    cudaError_t e = launch_digits(xq, K, R, K, m->p_dig, st);
+  // the row kernels before the group-128 linears write the int8 digit planes themselves (planes of
+  // Tpad rows; the padding rows' sums are never stored); per-channel linears take the digit kernel
+  const int Tpad = (R + TC_PAD_ROWS - 1) / TC_PAD_ROWS * TC_PAD_ROWS;
+  uint8_t* dig = m->group ? static_cast<uint8_t*>(m->p_dig) : nullptr;
+  auto lin = [&](const int16_t* xq, int K, const LinW& L, int epi, int64_t* out, int ldo,
+                 unsigned long long* amax = nullptr) -> cudaError_t {
+    cudaError_t e = cudaSuccess;
+    if (!dig) e = launch_digits(xq, K, R, K, m->p_dig, st);
     if (e != cudaSuccess) return e;
     if (L.Mg || epi == EPI_RAW)
       return launch_gemm_tc(m->p_dig, R, L, m->p_xs, epi, out, ldo, epi == EPI_RAW ? out : nullptr, nullptr, ldo,
-                            m->silu_t, m->err, st);
+                            m->silu_t, m->err, st, nullptr, amax);
     // per-channel linear: raw sums on the tensor cores, then the QLin requant (exact_llm.py:89-96)
     e = launch_gemm_tc(m->p_dig, R, L, m->p_xs, EPI_RAW, m->p_raw, L.N, m->p_raw, nullptr, L.N, nullptr, m->err, st);
     if (e != cudaSuccess) return e;
@@ -1530,23 +1539,31 @@ static int prefill_chunk(exb_model* m, int R, int64_t* logits_host, int32_t* nex
     const size_t kvoff = m->kv_layer_elems * i;
     aa.kc = m->kc + kvoff; aa.vc = m->vc + kvoff;
     aa.ks = m->ks + (size_t)c.max_batch * c.KV * c.max_seq * i;
-    CK(launch_norm_q(m->p_x, D, Ld.g1, R, D, m->p_xq, D, m->p_xs, st, false));
+    CK(launch_norm_q(m->p_x, D, Ld.g1, R, D, m->p_xq, D, m->p_xs, st, false, dig, nullptr, 0, Tpad));
     CK(lin(m->p_xq, D, Ld.qkv, EPI_STORE, m->p_qkv, m->Nqkv));
     CK(launch_rope_cache(aa, st, false));
     if (one_seq) CK(launch_attn_prefill(aa, st));       // query tiles share the cached K/V rows
     else CK(launch_attn_decode(aa, st, false));
-    CK(launch_quant(m->p_ao, Hd, R, Hd, m->p_xq, Hd, m->p_xs, st, false));
+    CK(launch_quant(m->p_ao, Hd, R, Hd, m->p_xq, Hd, m->p_xs, st, false, dig, Tpad));
     CK(lin(m->p_xq, Hd, Ld.o, EPI_RESID, m->p_x, D));
-    CK(launch_norm_q(m->p_x, D, Ld.g2, R, D, m->p_xq, D, m->p_xs, st, false));
+    CK(launch_norm_q(m->p_x, D, Ld.g2, R, D, m->p_xq, D, m->p_xs, st, false, c.n_experts ? nullptr : dig, nullptr, 0,
+                     Tpad));
     if (c.n_experts) {
       CK(launch_moe(moe_args(m, i, R, m->p_xq, D, m->p_xs, g_hist_row0), m->p_x, D, st));
       continue;
     }
-    CK(lin(m->p_xq, D, Ld.gu, EPI_SWIGLU, m->p_hb, I));
-    CK(launch_quant(m->p_hb, I, R, I, m->p_xq, I, m->p_xs, st, false));
+    if (dig) {
+      // gate|up publishes each row's max |h|; the qrow of h then runs split over slices of the row
+      CK(cudaMemsetAsync(m->p_amax, 0, sizeof(unsigned long long) * R, st));
+      CK(lin(m->p_xq, D, Ld.gu, EPI_SWIGLU, m->p_hb, I, m->p_amax));
+      CK(launch_quant_known(m->p_hb, I, R, I, m->p_amax, m->p_xq, I, m->p_xs, st, false, dig, Tpad));
+    } else {
+      CK(lin(m->p_xq, D, Ld.gu, EPI_SWIGLU, m->p_hb, I));
+      CK(launch_quant(m->p_hb, I, R, I, m->p_xq, I, m->p_xs, st, false));
+    }
     CK(lin(m->p_xq, I, Ld.down, EPI_RESID, m->p_x, D));
   }
-  CK(launch_norm_q(m->p_x, D, m->gf, R, D, m->p_xq, D, m->p_xs, st, false));
+  CK(launch_norm_q(m->p_x, D, m->gf, R, D, m->p_xq, D, m->p_xs, st, false, dig, nullptr, 0, Tpad));
   // head: unscaled per-group sums on the tensor cores, then the per-channel requant + argmax per row
   CK(lin(m->p_xq, D, m->head, EPI_RAW, m->p_raw, c.V));
   int64_t* lg = logits_host ? m->p_raw : nullptr;             // requant in place (row by row, read before write)

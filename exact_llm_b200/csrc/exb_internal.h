@@ -212,11 +212,13 @@ cudaError_t launch_embed(const int8_t* emb, int emb_shift, const int32_t* ids, i
                          cudaStream_t st, bool pdl, unsigned long long* nstat = nullptr);
 cudaError_t launch_embed64(const int64_t* emb_q16, const int32_t* ids, int R, int D, int64_t* x, cudaStream_t st,
                            bool pdl);
-// dig (optional): int8 digit planes of the rows for the tensor-core decode GEMM (TC_DECODE_ROWS-row planes)
+constexpr int TC_DECODE_ROWS = 8;
+constexpr int TC_PAD_ROWS = 128;      // multi-row digit planes are padded to a multiple of this
+// dig (optional): int8 digit planes of the rows for the tensor-core GEMM (planes of dig_rows rows)
 // xcap (optional): a copy of each input row x (row stride ldcap), for the trace commitment
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
                           int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig = nullptr, int64_t* xcap = nullptr,
-                          int64_t ldcap = 0);
+                          int64_t ldcap = 0, int dig_rows = TC_DECODE_ROWS);
 
 // ---- Merkle trace commitment (csrc/commit.cu)
 struct CommitLayout {
@@ -284,9 +286,10 @@ cudaError_t launch_commit_log(int R, const int32_t* row_seq, const int32_t* row_
 cudaError_t commit_root(const int64_t* log, int64_t row, int T, const CommitLayout& c, uint8_t* leaves,
                         uint8_t* lv_a, uint8_t* lv_b, uint8_t** root_dev, cudaStream_t st);
 cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, int ldq, int32_t* xs,
-                         cudaStream_t st, bool pdl);
+                         cudaStream_t st, bool pdl, uint8_t* dig = nullptr, int dig_rows = TC_DECODE_ROWS);
 cudaError_t launch_quant_known(const int64_t* x, int ldx, int R, int K, const unsigned long long* amax, int16_t* xq,
-                               int ldq, int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig = nullptr);
+                               int ldq, int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig = nullptr,
+                               int dig_rows = TC_DECODE_ROWS);
 cudaError_t launch_requant_channel(const int64_t* acc, int ld, int R, const LinW& L, int64_t* out, int ldo,
                                    const int32_t* xs, int epi, cudaStream_t st, bool pdl);
 
@@ -355,7 +358,6 @@ void gemm_tc_set_persist(int on);     // multi-row GEMM on a persistent grid (de
 // activation tiles, optional split over the 128-groups (int64 partial sums in tot_buf, the last
 // CTA of each 128-row tile finishes it; tot_buf and tickets are zero between uses), SwiGLU row
 // max published to amax_out, words cleared for a later producer, programmatic dependent launch.
-constexpr int TC_DECODE_ROWS = 8;
 struct TcDecode {
   int ksplit = 1;
   int64_t* tot_buf = nullptr;           // (TC_DECODE_ROWS, N) int64
@@ -367,7 +369,7 @@ struct TcDecode {
 // tot / requant epilogue of a group-128 linear over T activation rows given as digit planes
 cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32_t* xs, int epi, int64_t* out, int ldo,
                            int64_t* raw, int64_t* raw2, int ldr, const int32_t* silu_t, int* err, cudaStream_t st,
-                           const TcDecode* dec = nullptr);
+                           const TcDecode* dec = nullptr, unsigned long long* amax_out = nullptr);
 
 
 }  // namespace exb

@@ -28,7 +28,7 @@
 namespace exb {
 
 constexpr int TC_BM = 128;                              // output rows per tile (MMA M)
-constexpr int TC_PAD = 128;                             // activation rows are padded to this
+constexpr int TC_PAD = TC_PAD_ROWS;                     // activation rows are padded to this
 constexpr int TC_STAGES = 4;
 constexpr int TC_A_BYTES = TC_BM * 128;                 // one group of 128 weight rows
 constexpr uint32_t TC_WAIT_LIMIT = 1u << 24;
@@ -536,7 +536,7 @@ static int tc_sm_count() {
 
 cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32_t* xs, int epi, int64_t* out, int ldo,
                            int64_t* raw, int64_t* raw2, int ldr, const int32_t* silu_t, int* err, cudaStream_t st,
-                           const TcDecode* dec) {
+                           const TcDecode* dec, unsigned long long* amax_out) {
   if (!gemm_tc_supported(L, epi) || T <= 0) return cudaErrorInvalidValue;
   // activation-row tile: 8 for decode steps (digit planes of TC_DECODE_ROWS rows), else 64 / 128
   const int BN = dec ? 8 : (T > 64 ? 128 : 64);
@@ -562,6 +562,7 @@ cudaError_t launch_gemm_tc(const void* digits, int T, const LinW& L, const int32
   // activation tiles fastest: the CTAs resident together cover a few weight tiles x every
   // activation tile, so each weight byte comes from HBM once and the activations stay in L2
   a.act_fast = 1;
+  a.amax_out = amax_out;                // SwiGLU: per-row max |h| (zero before the launch)
   const int ntn = BN == 128 ? Tpad / 128 : (T + 63) / 64, ntm = L.N / TC_BM;
   if (g_tc_persist) {
     // persistent grid: one CTA per SM walks the tiles in the same activation-fastest order, so

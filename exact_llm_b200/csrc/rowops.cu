@@ -124,10 +124,11 @@ cudaError_t launch_embed_norm(const int8_t* emb, const int64_t* emb_q16, int emb
 
 // ---------------------------------------------------------------- irms + qrow, qrow (one CTA per row)
 // int8 digit planes (lo = xq & 255, hi = xq >> 8) of row r for the tensor-core GEMM: planes of
-// TC_DECODE_ROWS rows of K bytes, the hi plane right after the lo plane
-EXB_DEV void put_digits(uint8_t* dig, int K, int r, int i, int16_t v) {
+// prow rows of K bytes (TC_DECODE_ROWS for decode steps, the padded chunk for prefill), the hi plane
+// right after the lo plane
+EXB_DEV void put_digits(uint8_t* dig, int prow, int K, int r, int i, int16_t v) {
   dig[(size_t)r * K + i] = (uint8_t)(v & 255);
-  dig[(size_t)(TC_DECODE_ROWS + r) * K + i] = (uint8_t)(int8_t)(v >> 8);
+  dig[(size_t)(prow + r) * K + i] = (uint8_t)(int8_t)(v >> 8);
 }
 
 // EPT: elements per thread of the register variant (D <= EPT * ROW_THREADS), 0 = the row staged in
@@ -137,7 +138,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restric
                                                         const int64_t* __restrict__ g, int D,
                                                         int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs,
                                                         uint8_t* __restrict__ dig, int64_t* __restrict__ xcap,
-                                                        int64_t ldcap) {
+                                                        int64_t ldcap, int dig_rows) {
   extern __shared__ int64_t ys[];
   __shared__ uint64_t red[33];
   prefetch_gains(g, D);
@@ -147,14 +148,15 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_q(const int64_t* __restric
   if constexpr (EPT > 0) row_norm_q_regs<ROW_THREADS, EPT>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, red);
   else row_norm_q<ROW_THREADS>(x + (size_t)r * ldx, g, D, xq + (size_t)r * ldq, xs + r, ys, red);
   if (dig)   // the row was written by this CTA (visible after the function's final barrier)
-    for (int i = threadIdx.x; i < D; i += ROW_THREADS) put_digits(dig, D, r, i, xq[(size_t)r * ldq + i]);
+    for (int i = threadIdx.x; i < D; i += ROW_THREADS) put_digits(dig, dig_rows, D, r, i, xq[(size_t)r * ldq + i]);
   if (xcap)
     for (int i = threadIdx.x; i < D; i += ROW_THREADS) xcap[(size_t)r * ldcap + i] = ld_cg(x + (size_t)r * ldx + i);
   tl_exit();
 }
 
 cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, int D, int16_t* xq, int ldq,
-                          int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig, int64_t* xcap, int64_t ldcap) {
+                          int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig, int64_t* xcap, int64_t ldcap,
+                          int dig_rows) {
   const int v = D <= 4 * ROW_THREADS ? 0 : D <= 8 * ROW_THREADS ? 1 : D <= 12 * ROW_THREADS ? 2 : 3;
   const void* fn = v == 0 ? (const void*)k_norm_q<4> : v == 1 ? (const void*)k_norm_q<8>
                  : v == 2 ? (const void*)k_norm_q<12> : (const void*)k_norm_q<0>;
@@ -166,24 +168,27 @@ cudaError_t launch_norm_q(const int64_t* x, int ldx, const int64_t* g, int R, in
     if (e != cudaSuccess) return e;
     attr_set.set();
   }
-  void* args[] = {(void*)&x,  (void*)&ldx, (void*)&g,   (void*)&D,    (void*)&xq,
-                  (void*)&ldq, (void*)&xs,  (void*)&dig, (void*)&xcap, (void*)&ldcap};
+  void* args[] = {(void*)&x,   (void*)&ldx, (void*)&g,   (void*)&D,     (void*)&xq,      (void*)&ldq,
+                  (void*)&xs,  (void*)&dig, (void*)&xcap, (void*)&ldcap, (void*)&dig_rows};
   return launch_simple(fn, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
 }
 
 __global__ void __launch_bounds__(ROW_THREADS) k_quant(const int64_t* __restrict__ x, int ldx, int K,
-                                                       int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs) {
+                                                       int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs,
+                                                       uint8_t* __restrict__ dig, int dig_rows) {
   extern __shared__ int64_t ys[];
   __shared__ uint64_t red[33];
   pdl_wait();
   pdl_launch_dependents();
   const int r = blockIdx.x;
   row_quant<ROW_THREADS>(x + (size_t)r * ldx, K, xq + (size_t)r * ldq, xs + r, ys, red);
+  if (dig)   // the row was written by this CTA (visible after the function's final barrier)
+    for (int i = threadIdx.x; i < K; i += ROW_THREADS) put_digits(dig, dig_rows, K, r, i, xq[(size_t)r * ldq + i]);
   tl_exit();
 }
 
 cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, int ldq, int32_t* xs,
-                         cudaStream_t st, bool pdl) {
+                         cudaStream_t st, bool pdl, uint8_t* dig, int dig_rows) {
   const size_t smem = (size_t)K * 8;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;   // one row staged in shared memory
   static DevOnce attr_set;   // raised once to the full budget, never lowered
@@ -192,7 +197,7 @@ cudaError_t launch_quant(const int64_t* x, int ldx, int R, int K, int16_t* xq, i
     if (e != cudaSuccess) return e;
     attr_set.set();
   }
-  void* args[] = {(void*)&x, (void*)&ldx, (void*)&K, (void*)&xq, (void*)&ldq, (void*)&xs};
+  void* args[] = {(void*)&x, (void*)&ldx, (void*)&K, (void*)&xq, (void*)&ldq, (void*)&xs, (void*)&dig, (void*)&dig_rows};
   return launch_simple((const void*)k_quant, dim3(R), dim3(ROW_THREADS), smem, st, pdl, args);
 }
 
@@ -251,7 +256,7 @@ cudaError_t launch_tpx_norm(const TpX& x, int sum_type, const int64_t* bias, int
 __global__ void __launch_bounds__(256) k_quant_known(const int64_t* __restrict__ x, int ldx, int K,
                                                      const unsigned long long* __restrict__ amax,
                                                      int16_t* __restrict__ xq, int ldq, int32_t* __restrict__ xs,
-                                                     uint8_t* __restrict__ dig) {
+                                                     uint8_t* __restrict__ dig, int dig_rows) {
   pdl_wait();
   pdl_launch_dependents();
   const int r = blockIdx.y;
@@ -264,17 +269,18 @@ __global__ void __launch_bounds__(256) k_quant_known(const int64_t* __restrict__
     const longlong2 v = __ldcg(x2 + i);
     const short2 q = make_short2(qrow_value(v.x, s), qrow_value(v.y, s));
     q2[i] = q;
-    if (dig) { put_digits(dig, K, r, 2 * i, q.x); put_digits(dig, K, r, 2 * i + 1, q.y); }
+    if (dig) { put_digits(dig, dig_rows, K, r, 2 * i, q.x); put_digits(dig, dig_rows, K, r, 2 * i + 1, q.y); }
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) xs[r] = s;
   tl_exit();
 }
 
 cudaError_t launch_quant_known(const int64_t* x, int ldx, int R, int K, const unsigned long long* amax, int16_t* xq,
-                               int ldq, int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig) {
+                               int ldq, int32_t* xs, cudaStream_t st, bool pdl, uint8_t* dig, int dig_rows) {
   if ((K & 1) || (ldx & 1) || (ldq & 1)) return cudaErrorInvalidValue;
   int slices = (K + 2047) / 2048;
-  void* args[] = {(void*)&x, (void*)&ldx, (void*)&K, (void*)&amax, (void*)&xq, (void*)&ldq, (void*)&xs, (void*)&dig};
+  void* args[] = {(void*)&x,   (void*)&ldx, (void*)&K,   (void*)&amax,    (void*)&xq,
+                  (void*)&ldq, (void*)&xs,  (void*)&dig, (void*)&dig_rows};
   return launch_simple((const void*)k_quant_known, dim3(slices, R), dim3(256), 0, st, pdl, args);
 }
 
