@@ -439,7 +439,7 @@ def run_ours(a, rank, world, local_rank):
     # prefill: the whole forward (every op) and the tcgen05 linear alone at the 7B gate|up shape
     prefill = {"tokens": PROMPT * B, "seconds": prefill_s, "tok_s": PROMPT * B / prefill_s,
                "effective_tops": lin_flops_fn(c) * PROMPT * B / prefill_s / 1e12,
-               "path": "linears on the tcgen05 int8 GEMM (int16 activations as 2 int8 digits), 256-row chunks"}
+               "path": "linears on the tcgen05 int8 GEMM (int16 activations as 2 int8 digits), 512-row chunks"}
     if PROMPT * B >= 16 and not a.no_gemm:
         tops, gms = gemm_tc_tops(c["D"], 2 * c["I"], 2048)
         peak8 = int8_peak_tops()
