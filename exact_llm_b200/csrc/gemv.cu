@@ -37,11 +37,12 @@ constexpr int PRE_SMEM_MAX = 104 * 1024;        // with the pre-wait area: two C
 
 // MODE: 0 lean (the decode hot path: int16 or qrow inputs, store / residual / SwiGLU / raw
 // epilogues, no Freivalds, tails, norm prologues, row statistics or argmax), 1 full, 2 lean with the
-// tensor-parallel exchanges, 3 lean with the norm prologue (row staged in shared memory).  Each is its own instantiation: code a launch never runs still costs
+// tensor-parallel exchanges, 3 lean with the norm prologue (row staged in shared memory), 4 lean with
+// the greedy argmax (the decode head).  Each is its own instantiation: code a launch never runs still costs
 // registers (spills) in the streaming loop.
 template <int R, int RPU, bool GROUP, int RB, int MODE>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
-  constexpr bool LEAN = MODE != 1, TPX = MODE == 2, NORMP = MODE == 1 || MODE == 3;
+  constexpr bool LEAN = MODE != 1, TPX = MODE == 2, NORMP = MODE == 1 || MODE == 3, HEADA = MODE == 1 || MODE == 4;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   int16_t* xs = reinterpret_cast<int16_t*>(smem_raw);                    // R x K int16 (tail: D int64 x 2)
   __shared__ unsigned long long red[NCW][R][6];
@@ -239,7 +240,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
           int64_t t2[RPU];
 #pragma unroll
           for (int q = 0; q < RPU; ++q) t2[q] = acc[0][r * RPU + q];
-          unit_epilogue<RPU, LEAN>(a, ug, r, t2, sh[r], est[warp][b][r]);
+          unit_epilogue<RPU, LEAN, HEADA>(a, ug, r, t2, sh[r], est[warp][b][r]);
           if constexpr (TPX && RPU == 1)
             if (a.tpx_out == TPX_SUM_O || a.tpx_out == TPX_SUM_D) {   // partial sums into every peer's slot
               const TpX& x = *a.tpx;
@@ -331,7 +332,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     }
   }
   // ---- greedy argmax (first index on ties, exact_llm.py:267): last-CTA reduction
-  if (!LEAN && a.epi == EPI_HEAD && a.next_tok) {
+  if (HEADA && a.epi == EPI_HEAD && a.next_tok) {
     if (lane == 0) {
 #pragma unroll
       for (int r = 0; r < R; ++r) {
@@ -450,6 +451,9 @@ static cudaError_t launch_r(const GemvArgs& a, size_t smem, cudaStream_t st, boo
     return cudaErrorInvalidValue;
   }
   if (lean) return launch_m<RPU, GROUP, 0>(a, smem, st, pdl);
+  const bool head_lean = a.fr_nseg == 0 && a.tail == TAIL_NONE && (a.xin == XIN_Q16 || a.xin == XIN_QUANT) &&
+                         !a.nstat_out && a.epi == EPI_HEAD;
+  if (head_lean) return launch_m<RPU, GROUP, 4>(a, smem, st, pdl);
   const bool norm_lean = a.fr_nseg == 0 && a.tail == TAIL_NONE && a.xin == XIN_NORM && !a.nstat_out &&
                          a.epi != EPI_HEAD;
   return norm_lean ? launch_m<RPU, GROUP, 3>(a, smem, st, pdl) : launch_m<RPU, GROUP, 1>(a, smem, st, pdl);

@@ -51,9 +51,9 @@ struct EpiState {
 };
 
 // Epilogue of one output unit (1 column, or a gate/up pair) for activation row r.
-// LEAN: no Freivalds or argmax; STATS: the residual row statistics (the launch guarantees nothing
-// compiled out is asked for)
-template <int RPU, bool LEAN = false, bool STATS = !LEAN>
+// LEAN: no Freivalds or residual row statistics; HEADA: the greedy argmax (the launch guarantees
+// nothing compiled out is asked for)
+template <int RPU, bool LEAN = false, bool HEADA = !LEAN>
 EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, int sh, EpiState& E) {
   uint64_t& omax = E.omax;
   unsigned long long (&frl)[3][2] = E.frl;
@@ -99,7 +99,7 @@ EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, 
     int64_t* o = a.out + (size_t)r * a.ldo + n;
     const int64_t xn = (int64_t)((uint64_t)__ldcg(reinterpret_cast<const long long*>(o)) + (uint64_t)y);
     *o = xn;
-    if (STATS && a.nstat_out) {
+    if (!LEAN && a.nstat_out) {
       const uint64_t ax = uabs64(xn);
       omax = ax > omax ? ax : omax;
       E.ssq += (uint64_t)xn * (uint64_t)xn;          // wraps harmlessly when max |x_new| >= 2^24 (unused then)
@@ -107,7 +107,7 @@ EXB_DEV void unit_epilogue(const GemvArgs& a, int ug, int r, const int64_t* t2, 
   } else if (a.out) {
     a.out[(size_t)r * a.ldo + n] = y;
   }
-  if (!LEAN && a.epi == EPI_HEAD && (y > best_v || (y == best_v && n < best_n))) {
+  if (HEADA && a.epi == EPI_HEAD && (y > best_v || (y == best_v && n < best_n))) {
     best_v = y;
     best_n = n;
   }
