@@ -268,15 +268,21 @@ def run_reference(a, rank, world):
     c = arch_config(a)
     tp = world > 1 and not a.replicas
     smp = CpuDecodeSample(c, PROMPT + 1)
-    for _ in range(max(1, a.warmup)):                         # untimed warm-up samples
+    # bounded so the whole arm ends within a few minutes whatever --steps / --warmup say: at most 2
+    # untimed warm-up samples, then timed samples until --steps or about 90 s of sampling (at least
+    # 3); the line reports the samples actually timed
+    for _ in range(min(2, max(1, a.warmup))):                 # untimed warm-up samples
         smp.layer()
     smp.head_time()
-    times = [smp.layer() for _ in range(max(1, a.steps))]     # each timed step: one whole decoder layer
+    times = []
+    while len(times) < max(1, a.steps) and (len(times) < 3 or sum(times) < 90.0):
+        times.append(smp.layer())                             # each timed step: one whole decoder layer
     t_layer = float(np.median(times))
     per_tok = c["NL"] * t_layer + smp.t_head
     val = 1.0 / per_tok                                       # IntModel decodes one sequence at a time
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": world,
-            "steps": len(times), "warmup": max(1, a.warmup), "ms_per_step": t_layer * 1e3, "higher_is_better": True,
+            "steps": len(times), "warmup": min(2, max(1, a.warmup)), "ms_per_step": t_layer * 1e3,
+            "higher_is_better": True,
             "scaling": "strong" if tp else "weak", "vs_baseline": None,
             "dtype": "int64 (float64 BLAS, exact < 2^53)", "data": "synthetic",
             "config": workload_config(a, c, world, tp),
